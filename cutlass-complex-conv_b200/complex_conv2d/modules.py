@@ -1,0 +1,279 @@
+"""``ComplexConv2d``: the drop-in module (reference ``complex_conv2d/modules.py``).
+
+Constructor signature, validation, error types and messages, parameters
+(``weight_real``/``weight_imag``, fp32 KCRS, ``requires_grad=False``),
+initialisation and the cache-invalidation rules follow
+``modules.py:21-207`` of the reference.  What changes is what runs:
+
+* the lazy prepack (``modules.py:127-151``) builds the packed weight image of
+  the B200 kernels (per tap: -W_im, W_re, W_im planes, TF32-rounded; 3xTF32
+  adds the rounding remainders) instead of a KRSC copy;
+* ``forward_planar`` calls the tcgen05 kernel on NHWC planes;
+* ``forward`` hands the complex64 NCHW tensor to the native entry point,
+  which does the NCHW->planar conversion and writes complex64 NCHW output
+  itself, instead of the five ATen layout kernels of ``modules.py:198-207``.
+"""
+
+import os
+
+import torch
+from torch import nn
+
+from ._extension import cutlass_complex_conv
+
+_PRECISIONS = {"tf32": 0, "3xtf32": 1}
+_WEIGHT_KCRS = 0
+
+
+def _pair(value, name):
+    """Int or 2-sequence of ints -> tuple (``modules.py:7-18``)."""
+    if isinstance(value, int):
+        return (value, value)
+
+    if (
+        isinstance(value, (tuple, list))
+        and len(value) == 2
+        and all(isinstance(v, int) for v in value)
+    ):
+        return (int(value[0]), int(value[1]))
+
+    raise TypeError(f"{name} must be an int or a pair of ints")
+
+
+def _resolve_precision(precision):
+    if precision is None:
+        precision = os.environ.get("COMPLEX_CONV2D_PRECISION", "tf32")
+    key = str(precision).lower()
+    if key not in _PRECISIONS:
+        raise ValueError(
+            f"precision must be one of {sorted(_PRECISIONS)}, got {precision!r}"
+        )
+    return key
+
+
+def _aligned16(t):
+    return t.data_ptr() % 16 == 0
+
+
+class ComplexConv2d(nn.Module):
+    """Inference-only complex-valued 2D convolution on B200 tensor cores.
+
+    The public ``forward`` method accepts a ``torch.complex64`` tensor in NCHW
+    format. ``forward_planar`` exposes the planar path and accepts separate
+    real/imaginary float32 tensors in contiguous NHWC format.
+
+    ``precision`` selects the tensor-core arithmetic: ``"tf32"`` (default,
+    like the reference) or ``"3xtf32"`` (split-TF32, close to FP32 results).
+    ``None`` reads ``COMPLEX_CONV2D_PRECISION`` from the environment.
+
+    Current limitations (as in the reference):
+      - CUDA only (an sm_100 / B200 device)
+      - torch.complex64 only
+      - forward inference only (no autograd/backward)
+      - bias=False
+      - dilation=1
+      - groups=1
+      - padding_mode="zeros"
+      - in/out channel counts multiples of 4 (reference kernel alignment)
+    """
+
+    def __init__(
+        self,
+        in_channels,
+        out_channels,
+        kernel_size,
+        stride=1,
+        padding=0,
+        dilation=1,
+        groups=1,
+        bias=False,
+        padding_mode="zeros",
+        device=None,
+        dtype=None,
+        precision="tf32",
+    ):
+        super().__init__()
+
+        if in_channels <= 0 or out_channels <= 0:
+            raise ValueError("in_channels and out_channels must be positive")
+
+        kernel_size = _pair(kernel_size, "kernel_size")
+        stride = _pair(stride, "stride")
+        padding = _pair(padding, "padding")
+        dilation = _pair(dilation, "dilation")
+
+        if kernel_size[0] <= 0 or kernel_size[1] <= 0:
+            raise ValueError("kernel_size must be positive")
+        if stride[0] <= 0 or stride[1] <= 0:
+            raise ValueError("stride must be positive")
+        if padding[0] < 0 or padding[1] < 0:
+            raise ValueError("padding must be non-negative")
+
+        if dilation != (1, 1):
+            raise NotImplementedError("dilation != 1 is not supported yet")
+        if groups != 1:
+            raise NotImplementedError("groups != 1 is not supported yet")
+        if bias:
+            raise NotImplementedError("bias=True is not supported yet")
+        if padding_mode != "zeros":
+            raise NotImplementedError(
+                'padding_mode other than "zeros" is not supported yet'
+            )
+        if dtype not in (None, torch.complex64):
+            raise NotImplementedError("only torch.complex64 is supported")
+
+        self.in_channels = int(in_channels)
+        self.out_channels = int(out_channels)
+        self.kernel_size = kernel_size
+        self.stride = stride
+        self.padding = padding
+        self.dilation = dilation
+        self.groups = groups
+        self.padding_mode = padding_mode
+        self.precision = _resolve_precision(precision)
+
+        # PyTorch-facing weights use KCRS layout. They are packed lazily into
+        # the kernel's weight image before the first invocation.
+        weight_shape = (
+            self.out_channels,
+            self.in_channels,
+            self.kernel_size[0],
+            self.kernel_size[1],
+        )
+
+        self.weight_real = nn.Parameter(
+            torch.empty(weight_shape, device=device, dtype=torch.float32),
+            requires_grad=False,
+        )
+        self.weight_imag = nn.Parameter(
+            torch.empty(weight_shape, device=device, dtype=torch.float32),
+            requires_grad=False,
+        )
+
+        nn.init.kaiming_uniform_(self.weight_real)
+        nn.init.kaiming_uniform_(self.weight_imag)
+
+        self._clear_prepacked_weights()
+
+    def extra_repr(self):
+        return (
+            f"{self.in_channels}, {self.out_channels}, kernel_size={self.kernel_size}, "
+            f"stride={self.stride}, padding={self.padding}, precision={self.precision!r}"
+        )
+
+    def _clear_prepacked_weights(self):
+        self._w_packed = None
+        self._packed_precision = None
+        self._weight_version = None
+
+    def _apply(self, fn, recurse=True):
+        # nn.Module.to()/cuda()/cpu() may replace or move Parameter storage.
+        # Cached packed weights must never outlive the storage they came from.
+        self._clear_prepacked_weights()
+        result = super()._apply(fn, recurse=recurse)
+        self._clear_prepacked_weights()
+        return result
+
+    @torch.no_grad()
+    def _prepack_weights(self):
+        if not self.weight_real.is_cuda or not self.weight_imag.is_cuda:
+            raise RuntimeError("ComplexConv2d weights must be on CUDA")
+
+        self._w_packed = cutlass_complex_conv.prepack(
+            self.weight_real.detach().contiguous(),
+            self.weight_imag.detach().contiguous(),
+            _WEIGHT_KCRS,
+            _PRECISIONS[self.precision],
+        )
+        self._packed_precision = self.precision
+        self._weight_version = (
+            self.weight_real._version,
+            self.weight_imag._version,
+        )
+
+    def _ensure_prepacked(self):
+        version = (
+            self.weight_real._version,
+            self.weight_imag._version,
+        )
+
+        if (
+            self._w_packed is None
+            or self._weight_version != version
+            or self._packed_precision != self.precision
+            or self._w_packed.device != self.weight_real.device
+        ):
+            self._prepack_weights()
+
+    def forward_planar(self, x_real, x_imag):
+        """Run the planar path.
+
+        Args:
+            x_real: contiguous CUDA float32 tensor in NHWC layout.
+            x_imag: contiguous CUDA float32 tensor in NHWC layout.
+
+        Returns:
+            ``[y_real, y_imag]`` as contiguous NHWC float32 tensors.
+        """
+        self._ensure_prepacked()
+
+        # TMA needs 16-byte aligned bases; copy the rare misaligned view.
+        if x_real.is_cuda and x_real.is_contiguous() and not _aligned16(x_real):
+            x_real = x_real.clone()
+        if x_imag.is_cuda and x_imag.is_contiguous() and not _aligned16(x_imag):
+            x_imag = x_imag.clone()
+
+        return cutlass_complex_conv.forward_planar_packed(
+            x_real,
+            x_imag,
+            self._w_packed,
+            self.in_channels,
+            self.out_channels,
+            self.kernel_size[0],
+            self.kernel_size[1],
+            self.stride[0],
+            self.stride[1],
+            self.padding[0],
+            self.padding[1],
+            _PRECISIONS[self.precision],
+        )
+
+    def forward(self, x):
+        """Run complex Conv2d on a torch.complex64 NCHW tensor."""
+        if not x.is_cuda:
+            raise ValueError("ComplexConv2d input must be on CUDA")
+        if x.dtype != torch.complex64:
+            raise ValueError(
+                f"ComplexConv2d expects torch.complex64 input, got {x.dtype}"
+            )
+        if x.dim() != 4:
+            raise ValueError(
+                f"ComplexConv2d expects a 4D NCHW tensor, got {x.dim()}D"
+            )
+        if x.size(1) != self.in_channels:
+            raise ValueError(
+                f"expected {self.in_channels} input channels, got {x.size(1)}"
+            )
+        if x.device != self.weight_real.device:
+            raise ValueError(
+                "input and ComplexConv2d weights must be on the same CUDA device"
+            )
+
+        self._ensure_prepacked()
+
+        x = x.contiguous()
+        if not _aligned16(x):
+            x = x.clone()
+
+        return cutlass_complex_conv.forward_complex_packed(
+            x,
+            self._w_packed,
+            self.out_channels,
+            self.kernel_size[0],
+            self.kernel_size[1],
+            self.stride[0],
+            self.stride[1],
+            self.padding[0],
+            self.padding[1],
+            _PRECISIONS[self.precision],
+        )

@@ -1,0 +1,240 @@
+// Python extension `complex_conv2d._C`.
+//
+// Keeps the reference's pybind surface (csrc/bindings.cpp:16-29 of the
+// reference: `forward(x_real, x_imag, w_real, w_imag, stride_h, stride_w,
+// pad_h, pad_w) -> [y_real, y_imag]`, with the argument checks and messages
+// of csrc/complex_conv2d.cu:94-159) and adds the entry points the module
+// uses with cached packed weights.  Every call goes through the C ABI of
+// libccv_b200.so (include/ccv_b200.h); this file only validates torch
+// tensors, allocates outputs/scratch from the caching allocator and picks
+// the current stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "ccv_b200.h"
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK(x.is_cuda(), #x " must be CUDA")
+#define CHECK_FLOAT(x) TORCH_CHECK(x.scalar_type() == at::kFloat, #x " must be float32")
+#define CHECK_CONTIGUOUS(x) TORCH_CHECK(x.is_contiguous(), #x " must be contiguous")
+
+void check_rc(int rc, const char* what) {
+  if (rc == CCV_OK) return;
+  const char* msg = ccv_last_error_message();
+  if (rc == CCV_ERR_UNSUPPORTED) {
+    TORCH_CHECK(false, "complex_conv2d cannot implement this convolution configuration (", what,
+                "): ", msg);
+  }
+  TORCH_CHECK(false, what, " failed (status ", rc, "): ", msg);
+}
+
+ccv_stream_t current_stream() {
+  return reinterpret_cast<ccv_stream_t>(at::cuda::getCurrentCUDAStream().stream());
+}
+
+ccv_conv_shape make_shape(int64_t n, int64_t h, int64_t w, int64_t c, int64_t k, int64_t r,
+                          int64_t s, int64_t sh, int64_t sw, int64_t ph, int64_t pw) {
+  ccv_conv_shape shp;
+  shp.n = n; shp.h = h; shp.w = w; shp.c = c; shp.k = k; shp.r = r; shp.s = s;
+  shp.stride_h = sh; shp.stride_w = sw; shp.pad_h = ph; shp.pad_w = pw;
+  return shp;
+}
+
+// Reference-compatible entry: KRSC weights, fresh NHWC outputs.
+std::vector<torch::Tensor> forward(torch::Tensor x_real, torch::Tensor x_imag,
+                                   torch::Tensor w_real, torch::Tensor w_imag, int64_t stride_h,
+                                   int64_t stride_w, int64_t pad_h, int64_t pad_w) {
+  CHECK_CUDA(x_real); CHECK_CUDA(x_imag); CHECK_CUDA(w_real); CHECK_CUDA(w_imag);
+  CHECK_FLOAT(x_real); CHECK_FLOAT(x_imag); CHECK_FLOAT(w_real); CHECK_FLOAT(w_imag);
+  CHECK_CONTIGUOUS(x_real); CHECK_CONTIGUOUS(x_imag);
+  CHECK_CONTIGUOUS(w_real); CHECK_CONTIGUOUS(w_imag);
+  TORCH_CHECK(x_real.dim() == 4, "x_real must be a 4D NHWC tensor");
+  TORCH_CHECK(x_imag.dim() == 4, "x_imag must be a 4D NHWC tensor");
+  TORCH_CHECK(w_real.dim() == 4, "w_real must be a 4D KRSC tensor");
+  TORCH_CHECK(w_imag.dim() == 4, "w_imag must be a 4D KRSC tensor");
+  TORCH_CHECK(x_real.sizes() == x_imag.sizes(), "x_real and x_imag must have identical shapes");
+  TORCH_CHECK(w_real.sizes() == w_imag.sizes(), "w_real and w_imag must have identical shapes");
+  TORCH_CHECK(x_real.device() == x_imag.device() && x_real.device() == w_real.device() &&
+                  x_real.device() == w_imag.device(),
+              "all inputs and weights must be on the same CUDA device");
+  TORCH_CHECK(stride_h > 0 && stride_w > 0, "stride must be positive");
+  TORCH_CHECK(pad_h >= 0 && pad_w >= 0, "padding must be non-negative");
+  c10::cuda::CUDAGuard guard(x_real.device());
+  const int64_t N = x_real.size(0), H = x_real.size(1), W = x_real.size(2), C = x_real.size(3);
+  const int64_t K = w_real.size(0), R = w_real.size(1), S = w_real.size(2);
+  TORCH_CHECK(w_real.size(3) == C, "input channel count must match the weight channel count");
+  TORCH_CHECK(R > 0 && S > 0, "kernel dimensions must be positive");
+  const int64_t P = (H + 2 * pad_h - R) / stride_h + 1;
+  const int64_t Q = (W + 2 * pad_w - S) / stride_w + 1;
+  TORCH_CHECK(H + 2 * pad_h - R >= 0 && W + 2 * pad_w - S >= 0 && P > 0 && Q > 0,
+              "invalid convolution configuration: output spatial size must be positive");
+  ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
+  check_rc(ccv_check_shape(&shp), "shape check");
+  auto y_real = torch::empty({N, P, Q, K}, x_real.options());
+  auto y_imag = torch::empty({N, P, Q, K}, x_real.options());
+  const size_t ws_bytes = ccv_forward_workspace_bytes(&shp);
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes)},
+                         x_real.options().dtype(torch::kUInt8));
+  check_rc(ccv_forward(x_real.data_ptr<float>(), x_imag.data_ptr<float>(),
+                       w_real.data_ptr<float>(), w_imag.data_ptr<float>(),
+                       y_real.data_ptr<float>(), y_imag.data_ptr<float>(), &shp, ws.data_ptr(),
+                       ws_bytes, current_stream()),
+           "ccv_forward");
+  return {y_real, y_imag};
+}
+
+// Packs KCRS (layout 0) or KRSC (layout 1) weights into the kernel image.
+torch::Tensor prepack(torch::Tensor w_real, torch::Tensor w_imag, int64_t layout,
+                      int64_t precision) {
+  CHECK_CUDA(w_real); CHECK_CUDA(w_imag); CHECK_FLOAT(w_real); CHECK_FLOAT(w_imag);
+  CHECK_CONTIGUOUS(w_real); CHECK_CONTIGUOUS(w_imag);
+  TORCH_CHECK(w_real.dim() == 4 && w_real.sizes() == w_imag.sizes(),
+              "weights must be two 4D tensors of identical shape");
+  TORCH_CHECK(w_real.device() == w_imag.device(), "weights must be on the same CUDA device");
+  c10::cuda::CUDAGuard guard(w_real.device());
+  int64_t K = w_real.size(0), C, R, S;
+  if (layout == CCV_WEIGHT_KCRS) {
+    C = w_real.size(1); R = w_real.size(2); S = w_real.size(3);
+  } else {
+    R = w_real.size(1); S = w_real.size(2); C = w_real.size(3);
+  }
+  // A shape with a 1x1 image and padding that keeps the output positive.
+  ccv_conv_shape shp = make_shape(1, R, S, C, K, R, S, 1, 1, 0, 0);
+  const size_t bytes = ccv_packed_weight_bytes(&shp, static_cast<int>(precision));
+  check_rc(bytes == 0 ? ccv_check_shape(&shp) : CCV_OK, "weight shape check");
+  auto packed = torch::empty({static_cast<int64_t>(bytes / 4)}, w_real.options());
+  check_rc(ccv_prepack_weights(w_real.data_ptr<float>(), w_imag.data_ptr<float>(),
+                               static_cast<int>(layout), &shp, static_cast<int>(precision),
+                               packed.data_ptr(), bytes, current_stream()),
+           "ccv_prepack_weights");
+  return packed;
+}
+
+std::vector<torch::Tensor> forward_planar_packed(torch::Tensor x_real, torch::Tensor x_imag,
+                                                 torch::Tensor w_packed, int64_t in_channels,
+                                                 int64_t K, int64_t R, int64_t S,
+                                                 int64_t stride_h, int64_t stride_w,
+                                                 int64_t pad_h, int64_t pad_w,
+                                                 int64_t precision) {
+  CHECK_CUDA(x_real); CHECK_CUDA(x_imag); CHECK_CUDA(w_packed);
+  CHECK_FLOAT(x_real); CHECK_FLOAT(x_imag); CHECK_FLOAT(w_packed);
+  CHECK_CONTIGUOUS(x_real); CHECK_CONTIGUOUS(x_imag); CHECK_CONTIGUOUS(w_packed);
+  TORCH_CHECK(x_real.dim() == 4, "x_real must be a 4D NHWC tensor");
+  TORCH_CHECK(x_imag.dim() == 4, "x_imag must be a 4D NHWC tensor");
+  TORCH_CHECK(x_real.sizes() == x_imag.sizes(), "x_real and x_imag must have identical shapes");
+  TORCH_CHECK(x_real.device() == x_imag.device() && x_real.device() == w_packed.device(),
+              "all inputs and weights must be on the same CUDA device");
+  c10::cuda::CUDAGuard guard(x_real.device());
+  const int64_t N = x_real.size(0), H = x_real.size(1), W = x_real.size(2), C = x_real.size(3);
+  TORCH_CHECK(C == in_channels, "input channel count must match the weight channel count");
+  TORCH_CHECK(stride_h > 0 && stride_w > 0, "stride must be positive");
+  TORCH_CHECK(pad_h >= 0 && pad_w >= 0, "padding must be non-negative");
+  const int64_t P0 = (H + 2 * pad_h - R) / stride_h + 1;
+  const int64_t Q0 = (W + 2 * pad_w - S) / stride_w + 1;
+  TORCH_CHECK(H + 2 * pad_h - R >= 0 && W + 2 * pad_w - S >= 0 && P0 > 0 && Q0 > 0,
+              "invalid convolution configuration: output spatial size must be positive");
+  ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
+  int64_t P = 0, Q = 0;
+  check_rc(ccv_output_size(&shp, &P, &Q), "shape check");
+  TORCH_CHECK(static_cast<size_t>(w_packed.numel()) * 4 >=
+                  ccv_packed_weight_bytes(&shp, static_cast<int>(precision)),
+              "packed weights do not match the problem");
+  auto y_real = torch::empty({N, P, Q, K}, x_real.options());
+  auto y_imag = torch::empty({N, P, Q, K}, x_real.options());
+  const size_t ws_bytes = ccv_fprop_planar_workspace_bytes(&shp, static_cast<int>(precision));
+  torch::Tensor ws;
+  void* ws_ptr = nullptr;
+  if (ws_bytes > 0) {
+    ws = torch::empty({static_cast<int64_t>(ws_bytes)}, x_real.options().dtype(torch::kUInt8));
+    ws_ptr = ws.data_ptr();
+  }
+  check_rc(ccv_fprop_planar(x_real.data_ptr<float>(), x_imag.data_ptr<float>(),
+                            w_packed.data_ptr(), y_real.data_ptr<float>(),
+                            y_imag.data_ptr<float>(), &shp, static_cast<int>(precision), ws_ptr,
+                            ws_bytes, current_stream()),
+           "ccv_fprop_planar");
+  return {y_real, y_imag};
+}
+
+torch::Tensor forward_complex_packed(torch::Tensor x, torch::Tensor w_packed, int64_t K,
+                                     int64_t R, int64_t S, int64_t stride_h, int64_t stride_w,
+                                     int64_t pad_h, int64_t pad_w, int64_t precision) {
+  CHECK_CUDA(x); CHECK_CUDA(w_packed);
+  TORCH_CHECK(x.scalar_type() == at::kComplexFloat, "x must be complex64");
+  CHECK_FLOAT(w_packed);
+  CHECK_CONTIGUOUS(x); CHECK_CONTIGUOUS(w_packed);
+  TORCH_CHECK(x.dim() == 4, "x must be a 4D NCHW tensor");
+  TORCH_CHECK(x.device() == w_packed.device(),
+              "input and weights must be on the same CUDA device");
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t N = x.size(0), C = x.size(1), H = x.size(2), W = x.size(3);
+  ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
+  int64_t P = 0, Q = 0;
+  check_rc(ccv_output_size(&shp, &P, &Q), "shape check");
+  TORCH_CHECK(static_cast<size_t>(w_packed.numel()) * 4 >=
+                  ccv_packed_weight_bytes(&shp, static_cast<int>(precision)),
+              "packed weights do not match the problem");
+  auto y = torch::empty({N, K, P, Q}, x.options());
+  const size_t ws_bytes = ccv_fprop_complex_workspace_bytes(&shp, static_cast<int>(precision));
+  torch::Tensor ws;
+  void* ws_ptr = nullptr;
+  if (ws_bytes > 0) {
+    ws = torch::empty({static_cast<int64_t>(ws_bytes)}, x.options().dtype(torch::kUInt8));
+    ws_ptr = ws.data_ptr();
+  }
+  check_rc(ccv_fprop_complex(x.data_ptr(), w_packed.data_ptr(), y.data_ptr(), &shp,
+                             static_cast<int>(precision), ws_ptr, ws_bytes, current_stream()),
+           "ccv_fprop_complex");
+  return y;
+}
+
+int64_t device_status(int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  int st = 0;
+  check_rc(ccv_get_device_status(&st), "ccv_get_device_status");
+  return st;
+}
+
+void clear_device_status(int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  check_rc(ccv_clear_device_status(), "ccv_clear_device_status");
+}
+
+int64_t selftest_bounded_wait(int64_t device) {
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  auto st = torch::zeros({1}, torch::TensorOptions()
+                                  .dtype(torch::kInt32)
+                                  .device(torch::kCUDA, static_cast<c10::DeviceIndex>(device)));
+  check_rc(ccv_selftest_bounded_wait(st.data_ptr<int>(), current_stream()),
+           "ccv_selftest_bounded_wait");
+  return st.item<int>();
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("forward", &forward, "B200 tcgen05 planar-complex Conv2d forward (KRSC weights)",
+        pybind11::arg("x_real"), pybind11::arg("x_imag"), pybind11::arg("w_real"),
+        pybind11::arg("w_imag"), pybind11::arg("stride_h"), pybind11::arg("stride_w"),
+        pybind11::arg("pad_h"), pybind11::arg("pad_w"));
+  m.def("prepack", &prepack, "Pack weights into the kernel image", pybind11::arg("w_real"),
+        pybind11::arg("w_imag"), pybind11::arg("layout"), pybind11::arg("precision"));
+  m.def("forward_planar_packed", &forward_planar_packed, "Planar NHWC forward, packed weights",
+        pybind11::arg("x_real"), pybind11::arg("x_imag"), pybind11::arg("w_packed"),
+        pybind11::arg("in_channels"), pybind11::arg("out_channels"), pybind11::arg("kernel_h"), pybind11::arg("kernel_w"),
+        pybind11::arg("stride_h"), pybind11::arg("stride_w"), pybind11::arg("pad_h"),
+        pybind11::arg("pad_w"), pybind11::arg("precision"));
+  m.def("forward_complex_packed", &forward_complex_packed,
+        "complex64 NCHW forward, packed weights", pybind11::arg("x"), pybind11::arg("w_packed"),
+        pybind11::arg("out_channels"), pybind11::arg("kernel_h"), pybind11::arg("kernel_w"),
+        pybind11::arg("stride_h"), pybind11::arg("stride_w"), pybind11::arg("pad_h"),
+        pybind11::arg("pad_w"), pybind11::arg("precision"));
+  m.def("device_status", &device_status, pybind11::arg("device"));
+  m.def("clear_device_status", &clear_device_status, pybind11::arg("device"));
+  m.def("selftest_bounded_wait", &selftest_bounded_wait, pybind11::arg("device"));
+  m.def("version", []() { return std::string(ccv_version()); });
+}

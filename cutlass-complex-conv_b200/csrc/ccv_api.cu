@@ -1,0 +1,350 @@
+// extern "C" entry points of libccv_b200.so (declared in include/ccv_b200.h):
+// argument checking with the reference's error texts, per-device state
+// (status word, SM count, architecture check), tensor-map encoding, and the
+// composition of layout kernels with the fprop kernel.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "ccv_internal.h"
+
+#define CCV_VERSION_STRING "ccv_b200 0.1.0 (sm_100a tcgen05/TMA)"
+
+namespace ccv {
+
+// Per-device status word.  Bounded in-kernel waits that run out write a
+// CCV_ERR_* code here; fprop kernels read it at start and exit without work
+// while it is set.
+__device__ int g_ccv_status = 0;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+constexpr int kMaxDevices = 64;
+std::mutex g_dev_mutex;
+int* g_status_ptr[kMaxDevices] = {};
+int g_sm_count[kMaxDevices] = {};
+int g_arch_ok[kMaxDevices] = {};  // 0 unknown, 1 ok, -1 not sm_100
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode_tiled = nullptr;
+std::once_flag g_encode_once;
+
+int current_device(int* dev) {
+  const cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return cuda_error(e, "cudaGetDevice");
+  if (*dev < 0 || *dev >= kMaxDevices) return set_error(CCV_ERR_DEVICE, "device index out of range");
+  return CCV_OK;
+}
+
+int check_device() {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != CCV_OK) return rc;
+  std::lock_guard<std::mutex> lk(g_dev_mutex);
+  if (g_arch_ok[dev] == 0) {
+    int major = 0, minor = 0, sms = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_error(e, "cudaDeviceGetAttribute");
+    g_sm_count[dev] = sms;
+    g_arch_ok[dev] = (major == 10 && minor == 0) ? 1 : -1;
+  }
+  if (g_arch_ok[dev] != 1) {
+    return set_error(CCV_ERR_DEVICE,
+                     "complex_conv2d B200 kernels need an sm_100 (B200/GB200) device");
+  }
+  return CCV_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+int set_error(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+  return set_error(CCV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int* device_status_ptr() {
+  int dev = 0;
+  if (current_device(&dev) != CCV_OK) return nullptr;
+  std::lock_guard<std::mutex> lk(g_dev_mutex);
+  if (g_status_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_ccv_status);
+    if (e != cudaSuccess) {
+      cuda_error(e, "cudaGetSymbolAddress(status)");
+      return nullptr;
+    }
+    g_status_ptr[dev] = static_cast<int*>(p);
+  }
+  return g_status_ptr[dev];
+}
+
+int device_sm_count() {
+  int dev = 0;
+  if (current_device(&dev) != CCV_OK) return 148;
+  std::lock_guard<std::mutex> lk(g_dev_mutex);
+  return g_sm_count[dev] > 0 ? g_sm_count[dev] : 148;
+}
+
+int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides) {
+  std::call_once(g_encode_once, []() {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode_tiled = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+  });
+  if (g_encode_tiled == nullptr) {
+    return set_error(CCV_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  }
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t bx[5], es[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    es[i] = elem_strides[i];
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  const CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base),
+                                    d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return set_error(CCV_ERR_UNSUPPORTED,
+                     "cuTensorMapEncodeTiled rejected the problem (error " + std::to_string(r) + ")");
+  }
+  return CCV_OK;
+}
+
+int make_problem(const ccv_conv_shape* shape, Problem* out) {
+  if (shape == nullptr) return set_error(CCV_ERR_INVALID_ARGUMENT, "shape is null");
+  const ccv_conv_shape& s = *shape;
+  if (s.n <= 0 || s.h <= 0 || s.w <= 0 || s.c <= 0 || s.k <= 0) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor dimensions must be positive");
+  }
+  if (s.r <= 0 || s.s <= 0) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "kernel dimensions must be positive");
+  }
+  if (s.stride_h <= 0 || s.stride_w <= 0) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "stride must be positive");
+  }
+  if (s.pad_h < 0 || s.pad_w < 0) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "padding must be non-negative");
+  }
+  const int64_t lim = 0x7fffffffLL;
+  if (s.n > lim || s.h > lim || s.w > lim || s.c > lim || s.k > lim || s.r > lim || s.s > lim ||
+      s.pad_h > (1 << 20) || s.pad_w > (1 << 20) || s.stride_h > lim || s.stride_w > lim) {
+    return set_error(CCV_ERR_UNSUPPORTED, "cannot implement this convolution configuration: "
+                                          "dimension exceeds 32-bit range");
+  }
+  const int64_t p = (s.h + 2 * s.pad_h - s.r) / s.stride_h + 1;
+  const int64_t q = (s.w + 2 * s.pad_w - s.s) / s.stride_w + 1;
+  if (s.h + 2 * s.pad_h - s.r < 0 || s.w + 2 * s.pad_w - s.s < 0 || p <= 0 || q <= 0) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT,
+                     "invalid convolution configuration: output spatial size must be positive");
+  }
+  if (s.c % 4 != 0 || s.k % 4 != 0) {
+    return set_error(CCV_ERR_UNSUPPORTED,
+                     "cannot implement this convolution configuration: input and output "
+                     "channel counts must be multiples of 4");
+  }
+  if (s.stride_h > 8 || s.stride_w > 8) {
+    return set_error(CCV_ERR_UNSUPPORTED,
+                     "cannot implement this convolution configuration: stride above 8");
+  }
+  if (s.n * s.h * s.w * s.c * 4 >= (1LL << 40) || s.n * p * q * s.k * 8 >= (1LL << 40)) {
+    return set_error(CCV_ERR_UNSUPPORTED,
+                     "cannot implement this convolution configuration: tensor too large");
+  }
+  Problem pb;
+  pb.n = static_cast<int>(s.n); pb.h = static_cast<int>(s.h); pb.w = static_cast<int>(s.w);
+  pb.c = static_cast<int>(s.c); pb.k = static_cast<int>(s.k); pb.r = static_cast<int>(s.r);
+  pb.s = static_cast<int>(s.s); pb.p = static_cast<int>(p); pb.q = static_cast<int>(q);
+  pb.sh = static_cast<int>(s.stride_h); pb.sw = static_cast<int>(s.stride_w);
+  pb.ph = static_cast<int>(s.pad_h); pb.pw = static_cast<int>(s.pad_w);
+  *out = pb;
+  return CCV_OK;
+}
+
+}  // namespace ccv
+
+using namespace ccv;
+
+extern "C" {
+
+const char* ccv_version(void) { return CCV_VERSION_STRING; }
+
+const char* ccv_last_error_message(void) { return g_last_error.c_str(); }
+
+int ccv_output_size(const ccv_conv_shape* shape, int64_t* p, int64_t* q) {
+  Problem pb;
+  const int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if (p) *p = pb.p;
+  if (q) *q = pb.q;
+  return CCV_OK;
+}
+
+int ccv_check_shape(const ccv_conv_shape* shape) {
+  Problem pb;
+  return make_problem(shape, &pb);
+}
+
+size_t ccv_packed_weight_bytes(const ccv_conv_shape* shape, int precision) {
+  Problem pb;
+  if (make_problem(shape, &pb) != CCV_OK) return 0;
+  const size_t img = packed_image_floats(pb) * sizeof(float);
+  return precision == CCV_PRECISION_3XTF32 ? 2 * img : img;
+}
+
+int ccv_prepack_weights(const float* w_real, const float* w_imag, int layout,
+                        const ccv_conv_shape* shape, int precision, void* packed,
+                        size_t packed_bytes, ccv_stream_t stream) {
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if (layout != CCV_WEIGHT_KCRS && layout != CCV_WEIGHT_KRSC) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "unknown weight layout");
+  }
+  if (precision != CCV_PRECISION_TF32 && precision != CCV_PRECISION_3XTF32) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "unknown precision");
+  }
+  if (w_real == nullptr || w_imag == nullptr || packed == nullptr) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "null weight pointer");
+  }
+  if (!aligned16(packed)) return set_error(CCV_ERR_INVALID_ARGUMENT, "packed weights must be 16-byte aligned");
+  if (packed_bytes < ccv_packed_weight_bytes(shape, precision)) {
+    return set_error(CCV_ERR_WORKSPACE, "packed weight buffer too small");
+  }
+  if ((rc = check_device()) != CCV_OK) return rc;
+  return launch_prepack(w_real, w_imag, layout, pb, precision, static_cast<float*>(packed),
+                        reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t ccv_fprop_planar_workspace_bytes(const ccv_conv_shape* shape, int precision) {
+  (void)shape;
+  (void)precision;
+  return 0;
+}
+
+size_t ccv_fprop_complex_workspace_bytes(const ccv_conv_shape* shape, int precision) {
+  Problem pb;
+  if (make_problem(shape, &pb) != CCV_OK) return 0;
+  (void)precision;
+  // fp32 NHWC planes of the input (real, imaginary), 256-byte aligned halves.
+  const size_t plane = static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c * sizeof(float);
+  const size_t plane_al = (plane + 255) & ~static_cast<size_t>(255);
+  return 2 * plane_al;
+}
+
+int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_packed,
+                     float* y_real, float* y_imag, const ccv_conv_shape* shape, int precision,
+                     void* workspace, size_t workspace_bytes, ccv_stream_t stream) {
+  (void)workspace;
+  (void)workspace_bytes;
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if (!x_real || !x_imag || !w_packed || !y_real || !y_imag) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  }
+  if (!aligned16(x_real) || !aligned16(x_imag) || !aligned16(w_packed) || !aligned16(y_real) ||
+      !aligned16(y_imag)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  }
+  if ((rc = check_device()) != CCV_OK) return rc;
+  return launch_fprop(x_real, x_imag, static_cast<const float*>(w_packed), y_real, y_imag, pb,
+                      precision, OUT_PLANAR_NHWC, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_conv_shape* shape,
+                      int precision, void* workspace, size_t workspace_bytes,
+                      ccv_stream_t stream) {
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if (!x || !w_packed || !y) return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  }
+  const size_t need = ccv_fprop_complex_workspace_bytes(shape, precision);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
+  }
+  if ((rc = check_device()) != CCV_OK) return rc;
+  const size_t plane = static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c * sizeof(float);
+  const size_t plane_al = (plane + 255) & ~static_cast<size_t>(255);
+  float* xr = static_cast<float*>(workspace);
+  float* xi = reinterpret_cast<float*>(static_cast<char*>(workspace) + plane_al);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = launch_nchw_complex_to_planar(static_cast<const float*>(x), xr, xi, pb, st);
+  if (rc != CCV_OK) return rc;
+  return launch_fprop(xr, xi, static_cast<const float*>(w_packed), static_cast<float*>(y), nullptr,
+                      pb, precision, OUT_COMPLEX_NCHW, st);
+}
+
+size_t ccv_forward_workspace_bytes(const ccv_conv_shape* shape) {
+  const size_t b = ccv_packed_weight_bytes(shape, CCV_PRECISION_TF32);
+  return (b + 255) & ~static_cast<size_t>(255);
+}
+
+int ccv_forward(const float* x_real, const float* x_imag, const float* w_real_krsc,
+                const float* w_imag_krsc, float* y_real, float* y_imag,
+                const ccv_conv_shape* shape, void* workspace, size_t workspace_bytes,
+                ccv_stream_t stream) {
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if (workspace == nullptr || workspace_bytes < ccv_forward_workspace_bytes(shape)) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing or too small");
+  }
+  rc = ccv_prepack_weights(w_real_krsc, w_imag_krsc, CCV_WEIGHT_KRSC, shape, CCV_PRECISION_TF32,
+                           workspace, workspace_bytes, stream);
+  if (rc != CCV_OK) return rc;
+  return ccv_fprop_planar(x_real, x_imag, workspace, y_real, y_imag, shape, CCV_PRECISION_TF32,
+                          nullptr, 0, stream);
+}
+
+int ccv_get_device_status(int* status) {
+  if (status == nullptr) return set_error(CCV_ERR_INVALID_ARGUMENT, "status is null");
+  int v = 0;
+  const cudaError_t e = cudaMemcpyFromSymbol(&v, g_ccv_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyFromSymbol(status)");
+  *status = v;
+  return CCV_OK;
+}
+
+int ccv_clear_device_status(void) {
+  const int zero = 0;
+  const cudaError_t e = cudaMemcpyToSymbol(g_ccv_status, &zero, sizeof(int));
+  if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyToSymbol(status)");
+  return CCV_OK;
+}
+
+int ccv_selftest_bounded_wait(int* status_dev, ccv_stream_t stream) {
+  if (status_dev == nullptr) return set_error(CCV_ERR_INVALID_ARGUMENT, "status is null");
+  const int rc = check_device();
+  if (rc != CCV_OK) return rc;
+  return launch_selftest_wait(status_dev, reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

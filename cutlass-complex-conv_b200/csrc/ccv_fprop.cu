@@ -1,0 +1,497 @@
+// Complex Conv2d forward as an implicit planar-complex GEMM on sm_100a.
+//
+// GEMM view (same as the reference kernel, csrc/cutlass_ext/cutlass/conv/
+// kernel/implicit_planar_cgemm_convolution.h:286-505): M = N*P*Q output
+// pixels, N = K output channels, reduction = R*S*C.  The reference's
+// mainloop (threadblock/implicit_planar_cgemm_multistage.h:251-271) issues
+// four real products per fragment:
+//     re += Ar*Br,  re += Ai*(-Bi),  im += Ar*Bi,  im += Ai*Br.
+// Here the same four products are two tcgen05 MMAs per 8-deep K step, each
+// M=128 x N=2*KT, accumulating [re | im] side by side in Tensor Memory:
+//     D[:, 0:2KT] += Ar * [Wr ; Wi]^T      (B rows KT..3KT of the packed tile)
+//     D[:, 0:2KT] += Ai * [-Wi ; Wr]^T     (B rows 0..2KT of the packed tile)
+// The packed weight tile per (tap, 16 input channels) is the three planes
+// (-Wi, Wr, Wi) stacked along N, so both B operands are windows of one TMA
+// box and every activation/weight byte is loaded into shared memory once.
+//
+// Warp roles (192 threads, one CTA per SM):
+//   warp 0      TMA producer: activation boxes (both planes) + weight box
+//   warp 1      TMEM allocator and single-thread MMA issuer
+//   warps 2..5  epilogue: tcgen05.ld -> registers -> global (NHWC planes or
+//               complex64 NCHW), one output pixel per thread
+//
+// Activation tiles: the 128 GEMM rows of a tile are NB spatial boxes of
+// box_p x box_q output pixels (box_p*box_q*NB = 128).  For tap (r, s) the
+// box is one strided TMA load of the NHWC plane; TMA's out-of-bounds zero
+// fill provides the padding (the reference uses cp.async zero-fill,
+// threadblock/implicit_planar_cgemm_multistage.h:170-239).  1x1/stride-1/
+// pad-0 problems use a flat 2-D view instead (128 consecutive pixels).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "ccv_internal.h"
+#include "ccv_ptx.cuh"
+
+namespace ccv {
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kBlockM = 128;     // GEMM rows (output pixels) per tile
+constexpr int kBlockC = 16;      // input channels per K step (64-byte rows)
+constexpr int kRowBytes = kBlockC * 4;
+constexpr int kABytes = kBlockM * kRowBytes;  // one activation plane per stage
+
+// Error codes written into the device status word by bounded waits.
+constexpr int kTimeoutProducer = CCV_ERR_DEVICE_TIMEOUT;
+constexpr int kTimeoutMma = CCV_ERR_DEVICE_TIMEOUT;
+constexpr int kTimeoutEpilogue = CCV_ERR_DEVICE_TIMEOUT;
+
+struct alignas(64) FpropParams {
+  CUtensorMap tm_xr;  // activation real plane
+  CUtensorMap tm_xi;  // activation imaginary plane
+  CUtensorMap tm_w;   // packed weights [R*S][3][K][C]
+  float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
+  float* y1;          // planar: y_imag (NPQK); complex: unused
+  int* status;        // device status word
+  int n, h, w, c, k, r, s, p, q;
+  int sh, sw, ph, pw;
+  int box_p, box_q, box_q_log2, box_px_log2, nb;  // spatial box tiling
+  int tiles_bp, tiles_bq, total_boxes;
+  int tiles_m, tiles_n;
+  int ksteps;         // ceil(C/16) * R * S
+  long long m_total;  // N*P*Q (flat mode)
+};
+
+template <int KT>
+struct Cfg {
+  static constexpr int kWBytes = 3 * KT * kRowBytes;
+  static constexpr int kStageBytes = 2 * kABytes + kWBytes;
+  static constexpr int kStages = KT == 128 ? 5 : (KT == 64 ? 7 : 9);
+  static constexpr int kTmemCols = 2 * KT < 32 ? 32 : 2 * KT;
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
+};
+
+__device__ __forceinline__ float4 u4f(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return make_float4(__uint_as_float(a), __uint_as_float(b), __uint_as_float(c),
+                     __uint_as_float(d));
+}
+
+template <int KT, bool FLAT, bool OUT_COMPLEX>
+__global__ void __launch_bounds__(kThreads, 1)
+    ccv_fprop_tf32_kernel(const __grid_constant__ FpropParams prm) {
+  using C = Cfg<KT>;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment keeps every stage buffer on a swizzle-pattern boundary.
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  // bars[0..S) full, bars[S..2S) empty, bars[2S] accumulator ready
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [0] skip, [1] abort
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t smem_base = ptx::smem_u32(smem);
+  const uint32_t bar_base = ptx::smem_u32(bars);
+  auto full_bar = [&](int i) { return bar_base + 8u * i; };
+  auto empty_bar = [&](int i) { return bar_base + 8u * (C::kStages + i); };
+  const uint32_t acc_bar = bar_base + 8u * (2 * C::kStages);
+
+  if (threadIdx.x == 0) {
+    flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
+    flags[1] = 0;
+    for (int i = 0; i < C::kStages; ++i) {
+      ptx::mbar_init(full_bar(i), 1);
+      ptx::mbar_init(empty_bar(i), 1);
+    }
+    ptx::mbar_init(acc_bar, 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&prm.tm_xr);
+    ptx::prefetch_tmap(&prm.tm_xi);
+    ptx::prefetch_tmap(&prm.tm_w);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), C::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const bool skip = flags[0] != 0;
+
+  const int n_tile = blockIdx.x % prm.tiles_n;
+  const int m_tile = blockIdx.x / prm.tiles_n;
+  const int k0 = n_tile * KT;
+  const int rs = prm.r * prm.s;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && !skip) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int t = 0; t < prm.ksteps; ++t) {
+        if (!ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, prm.status, kTimeoutProducer)) {
+          flags[1] = 1;
+          break;
+        }
+        if (flags[1]) break;
+        const uint32_t fb = full_bar(stage);
+        ptx::mbar_arrive_expect_tx(fb, C::kStageBytes);
+        const int cb = t / rs;
+        const int tap = t - cb * rs;
+        const int rr = tap / prm.s;
+        const int ss = tap - rr * prm.s;
+        const int c0 = cb * kBlockC;
+        const uint32_t a_r = smem_base + stage * C::kStageBytes;
+        const uint32_t a_i = a_r + kABytes;
+        const uint32_t w_s = a_i + kABytes;
+        if constexpr (FLAT) {
+          ptx::tma_load_2d(a_r, &prm.tm_xr, fb, c0, m_tile * kBlockM);
+          ptx::tma_load_2d(a_i, &prm.tm_xi, fb, c0, m_tile * kBlockM);
+        } else {
+          const int per_img = prm.tiles_bp * prm.tiles_bq;
+          const uint32_t box_bytes = (1u << prm.box_px_log2) * kRowBytes;
+          for (int b = 0; b < prm.nb; ++b) {
+            // Boxes past the end repeat the last box; their rows are not stored.
+            const int gb = min(m_tile * prm.nb + b, prm.total_boxes - 1);
+            const int img = gb / per_img;
+            const int rem = gb - img * per_img;
+            const int bp = rem / prm.tiles_bq;
+            const int bq = rem - bp * prm.tiles_bq;
+            const int wc = bq * prm.box_q * prm.sw - prm.pw + ss;
+            const int hc = bp * prm.box_p * prm.sh - prm.ph + rr;
+            ptx::tma_load_4d(a_r + b * box_bytes, &prm.tm_xr, fb, c0, wc, hc, img);
+            ptx::tma_load_4d(a_i + b * box_bytes, &prm.tm_xi, fb, c0, wc, hc, img);
+          }
+        }
+        ptx::tma_load_4d(w_s, &prm.tm_w, fb, c0, k0, 0, tap);
+        ++issued;
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      // Drain: make sure no TMA write into this CTA's shared memory is still
+      // in flight before the CTA can exit (matters only after an abort).
+      const int last = issued;
+      for (int j = 0; j < C::kStages && j < last; ++j) {
+        const int t = last - 1 - j;
+        const int st = t % C::kStages;
+        const uint32_t ph = static_cast<uint32_t>((t / C::kStages) & 1);
+        ptx::mbar_wait_bounded(full_bar(st), ph, prm.status, kTimeoutProducer);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && !skip) {
+      constexpr uint32_t idesc = ptx::idesc_tf32(kBlockM, 2 * KT, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = 0; t < prm.ksteps; ++t) {
+        if (!ptx::mbar_wait_bounded(full_bar(stage), phase, prm.status, kTimeoutMma)) {
+          flags[1] = 1;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t a_r = smem_base + stage * C::kStageBytes;
+        const uint32_t a_i = a_r + kABytes;
+        const uint32_t w_s = a_i + kABytes;
+#pragma unroll
+        for (int kk = 0; kk < kBlockC / 8; ++kk) {
+          const uint32_t koff = kk * 32;
+          const uint64_t da_r = ptx::desc_kmajor_sw64(a_r + koff);
+          const uint64_t da_i = ptx::desc_kmajor_sw64(a_i + koff);
+          const uint64_t db_top = ptx::desc_kmajor_sw64(w_s + KT * kRowBytes + koff);  // [Wr; Wi]
+          const uint64_t db_bot = ptx::desc_kmajor_sw64(w_s + koff);                   // [-Wi; Wr]
+          ptx::mma_tf32_ss(tmem_base, da_r, db_top, idesc, (t | kk) != 0 ? 1u : 0u);
+          ptx::mma_tf32_ss(tmem_base, da_i, db_bot, idesc, 1u);
+        }
+        ptx::mma_commit(empty_bar(stage));
+        if (++stage == C::kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      // Accumulator complete (or abandoned): release the epilogue, then wait
+      // ourselves so no MMA is in flight when TMEM is freed.
+      ptx::mma_commit(acc_bar);
+      ptx::mbar_wait_bounded(acc_bar, 0, prm.status, kTimeoutMma);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    bool ok = false;
+    if (!skip) {
+      ok = ptx::mbar_wait_bounded(acc_bar, 0, prm.status, kTimeoutEpilogue);
+      ptx::tc_fence_after();
+    }
+    // Map the GEMM row to an output pixel.
+    bool valid = ok;
+    int img = 0, op = 0, oq = 0;
+    if constexpr (FLAT) {
+      const long long m = static_cast<long long>(m_tile) * kBlockM + row;
+      valid = valid && (m < prm.m_total);
+      const long long pq = static_cast<long long>(prm.p) * prm.q;
+      img = static_cast<int>(m / pq);
+      const long long rem = m - static_cast<long long>(img) * pq;
+      op = static_cast<int>(rem / prm.q);
+      oq = static_cast<int>(rem - static_cast<long long>(op) * prm.q);
+    } else {
+      const int b = row >> prm.box_px_log2;
+      const int local = row & ((1 << prm.box_px_log2) - 1);
+      const int pi = local >> prm.box_q_log2;
+      const int qi = local & ((1 << prm.box_q_log2) - 1);
+      const int gb = m_tile * prm.nb + b;
+      valid = valid && (gb < prm.total_boxes);
+      const int per_img = prm.tiles_bp * prm.tiles_bq;
+      img = gb / per_img;
+      const int rem = gb - img * per_img;
+      const int bp = rem / prm.tiles_bq;
+      const int bq = rem - bp * prm.tiles_bq;
+      op = bp * prm.box_p + pi;
+      oq = bq * prm.box_q + qi;
+      valid = valid && (op < prm.p) && (oq < prm.q);
+    }
+    if (flags[1]) valid = false;
+    if (!skip) {
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      const long long pix = (static_cast<long long>(img) * prm.p + op) * prm.q + oq;
+#pragma unroll 1
+      for (int ch = 0; ch < KT; ch += 32) {
+        uint32_t vr[32], vi[32];
+        ptx::tmem_ld_32x32b_x32(t_row + ch, vr);
+        ptx::tmem_ld_32x32b_x32(t_row + KT + ch, vi);
+        ptx::tmem_wait_ld();
+        const int kb = k0 + ch;
+        if (valid && kb < prm.k) {
+          if constexpr (!OUT_COMPLEX) {
+            float* dr = prm.y0 + pix * prm.k + kb;
+            float* di = prm.y1 + pix * prm.k + kb;
+            if (kb + 32 <= prm.k) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                *reinterpret_cast<float4*>(dr + j) = u4f(vr[j], vr[j + 1], vr[j + 2], vr[j + 3]);
+                *reinterpret_cast<float4*>(di + j) = u4f(vi[j], vi[j + 1], vi[j + 2], vi[j + 3]);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                if (kb + j < prm.k) {
+                  *reinterpret_cast<float4*>(dr + j) = u4f(vr[j], vr[j + 1], vr[j + 2], vr[j + 3]);
+                  *reinterpret_cast<float4*>(di + j) = u4f(vi[j], vi[j + 1], vi[j + 2], vi[j + 3]);
+                }
+              }
+            }
+          } else {
+            // complex64 NKPQ: element (img, k, op, oq) as (re, im)
+            const long long pq = static_cast<long long>(prm.p) * prm.q;
+            float2* y = reinterpret_cast<float2*>(prm.y0);
+            const long long base = static_cast<long long>(img) * prm.k * pq +
+                                   static_cast<long long>(op) * prm.q + oq;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (kb + j < prm.k) {
+                y[base + static_cast<long long>(kb + j) * pq] =
+                    make_float2(__uint_as_float(vr[j]), __uint_as_float(vi[j]));
+              }
+            }
+          }
+        }
+      }
+    }
+    ptx::tc_fence_before();
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+struct Tiling {
+  bool flat = false;
+  int kt = 128;
+  int box_p = 1, box_q = 1, nb = 1;
+  int tiles_bp = 1, tiles_bq = 1, total_boxes = 1;
+  int tiles_m = 1, tiles_n = 1;
+};
+
+int ilog2(int v) {
+  int l = 0;
+  while ((1 << l) < v) ++l;
+  return l;
+}
+
+Tiling choose_tiling(const Problem& pb) {
+  Tiling t;
+  t.kt = pb.k > 64 ? 128 : (pb.k > 32 ? 64 : 32);
+  t.tiles_n = (pb.k + t.kt - 1) / t.kt;
+  t.flat = (pb.r == 1 && pb.s == 1 && pb.sh == 1 && pb.sw == 1 && pb.ph == 0 && pb.pw == 0);
+  if (t.flat) {
+    const long long m = static_cast<long long>(pb.n) * pb.p * pb.q;
+    t.tiles_m = static_cast<int>((m + kBlockM - 1) / kBlockM);
+    return t;
+  }
+  // Spatial boxes: box_p x box_q (powers of two, product 8..128, at most 4
+  // boxes per tile), chosen to cover P x Q with the fewest computed rows.
+  long long best_cost = -1;
+  for (int px = 32; px <= 128; px *= 2) {
+    const int nb = kBlockM / px;
+    for (int bq = 1; bq <= px; bq *= 2) {
+      const int bp = px / bq;
+      if (bq * pb.sw > 256 || bp * pb.sh > 256) continue;
+      const long long tbq = (pb.q + bq - 1) / bq;
+      const long long tbp = (pb.p + bp - 1) / bp;
+      const long long boxes = static_cast<long long>(pb.n) * tbq * tbp;
+      const long long tiles = (boxes + nb - 1) / nb;
+      const long long cost = tiles * kBlockM * 4 + nb;  // rows computed, then fewer boxes
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        t.box_p = bp;
+        t.box_q = bq;
+        t.nb = nb;
+        t.tiles_bp = static_cast<int>(tbp);
+        t.tiles_bq = static_cast<int>(tbq);
+        t.total_boxes = static_cast<int>(boxes);
+        t.tiles_m = static_cast<int>(tiles);
+      }
+    }
+  }
+  return t;
+}
+
+template <int KT, bool FLAT, bool OUT_COMPLEX>
+int launch_variant(const FpropParams& prm, int grid, cudaStream_t stream) {
+  using C = Cfg<KT>;
+  auto kern = ccv_fprop_tf32_kernel<KT, FLAT, OUT_COMPLEX>;
+  static std::once_flag once[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(once[dev & 63], [&]() {
+    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    C::kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(fprop)");
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(prm);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "fprop kernel launch");
+  return CCV_OK;
+}
+
+template <bool FLAT, bool OUT_COMPLEX>
+int launch_kt(int kt, const FpropParams& prm, int grid, cudaStream_t stream) {
+  switch (kt) {
+    case 128: return launch_variant<128, FLAT, OUT_COMPLEX>(prm, grid, stream);
+    case 64: return launch_variant<64, FLAT, OUT_COMPLEX>(prm, grid, stream);
+    default: return launch_variant<32, FLAT, OUT_COMPLEX>(prm, grid, stream);
+  }
+}
+
+}  // namespace
+
+int launch_fprop(const float* xr, const float* xi, const float* w_packed, float* y0, float* y1,
+                 const Problem& pb, int precision, OutLayout out_layout, cudaStream_t stream) {
+  if (precision != CCV_PRECISION_TF32) {
+    return set_error(CCV_ERR_UNSUPPORTED, "3xTF32 fprop is not available in this build");
+  }
+  const Tiling t = choose_tiling(pb);
+  FpropParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.y0 = y0;
+  prm.y1 = y1;
+  prm.status = device_status_ptr();
+  if (prm.status == nullptr) return CCV_ERR_CUDA;
+  prm.n = pb.n; prm.h = pb.h; prm.w = pb.w; prm.c = pb.c; prm.k = pb.k;
+  prm.r = pb.r; prm.s = pb.s; prm.p = pb.p; prm.q = pb.q;
+  prm.sh = pb.sh; prm.sw = pb.sw; prm.ph = pb.ph; prm.pw = pb.pw;
+  prm.box_p = t.box_p; prm.box_q = t.box_q;
+  prm.box_q_log2 = ilog2(t.box_q);
+  prm.box_px_log2 = ilog2(t.box_p * t.box_q);
+  prm.nb = t.nb;
+  prm.tiles_bp = t.tiles_bp; prm.tiles_bq = t.tiles_bq; prm.total_boxes = t.total_boxes;
+  prm.tiles_m = t.tiles_m; prm.tiles_n = t.tiles_n;
+  prm.ksteps = ((pb.c + kBlockC - 1) / kBlockC) * pb.r * pb.s;
+  prm.m_total = static_cast<long long>(pb.n) * pb.p * pb.q;
+
+  int rc;
+  const uint64_t cb = static_cast<uint64_t>(pb.c) * 4;
+  if (t.flat) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(pb.c),
+                              static_cast<uint64_t>(pb.n) * pb.h * pb.w};
+    const uint64_t strides[1] = {cb};
+    const uint32_t box[2] = {kBlockC, kBlockM};
+    const uint32_t es[2] = {1, 1};
+    if ((rc = encode_tiled(&prm.tm_xr, xr, 2, dims, strides, box, es)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_xi, xi, 2, dims, strides, box, es)) != CCV_OK) return rc;
+  } else {
+    const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.w),
+                              static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
+    const uint64_t strides[3] = {cb, cb * pb.w, cb * pb.w * pb.h};
+    const uint32_t box[4] = {kBlockC, static_cast<uint32_t>(t.box_q * pb.sw),
+                             static_cast<uint32_t>(t.box_p * pb.sh), 1};
+    const uint32_t es[4] = {1, static_cast<uint32_t>(pb.sw), static_cast<uint32_t>(pb.sh), 1};
+    if ((rc = encode_tiled(&prm.tm_xr, xr, 4, dims, strides, box, es)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_xi, xi, 4, dims, strides, box, es)) != CCV_OK) return rc;
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.k), 3,
+                              static_cast<uint64_t>(pb.r) * pb.s};
+    const uint64_t strides[3] = {cb, cb * pb.k, cb * pb.k * 3};
+    const uint32_t box[4] = {kBlockC, static_cast<uint32_t>(t.kt), 3, 1};
+    const uint32_t es[4] = {1, 1, 1, 1};
+    if ((rc = encode_tiled(&prm.tm_w, w_packed, 4, dims, strides, box, es)) != CCV_OK) return rc;
+  }
+  const long long grid = static_cast<long long>(t.tiles_m) * t.tiles_n;
+  if (grid <= 0 || grid > 0x7fffffffLL) {
+    return set_error(CCV_ERR_UNSUPPORTED, "problem too large for the grid");
+  }
+  const bool cplx = out_layout == OUT_COMPLEX_NCHW;
+  if (t.flat) {
+    return cplx ? launch_kt<true, true>(t.kt, prm, static_cast<int>(grid), stream)
+                : launch_kt<true, false>(t.kt, prm, static_cast<int>(grid), stream);
+  }
+  return cplx ? launch_kt<false, true>(t.kt, prm, static_cast<int>(grid), stream)
+              : launch_kt<false, false>(t.kt, prm, static_cast<int>(grid), stream);
+}
+
+// ------------------------------------------------------------------ self-test
+namespace {
+__global__ void ccv_selftest_wait_kernel(int* status) {
+  __shared__ uint64_t bar;
+  const uint32_t b = ptx::smem_u32(&bar);
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(b, 1);
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // Nothing ever arrives on `bar`: the bounded wait must give up.
+    const bool ok = ptx::mbar_wait_bounded(b, 0, status, CCV_ERR_DEVICE_TIMEOUT);
+    if (ok) atomicExch(status, -1);  // impossible completion is itself an error
+  }
+}
+}  // namespace
+
+int launch_selftest_wait(int* status_dev, cudaStream_t stream) {
+  ccv_selftest_wait_kernel<<<1, 32, 0, stream>>>(status_dev);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "selftest kernel launch");
+  return CCV_OK;
+}
+
+}  // namespace ccv

@@ -1,0 +1,56 @@
+// Internal declarations shared by the translation units of libccv_b200.so.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "ccv_b200.h"
+
+namespace ccv {
+
+// Records `msg` as the calling thread's last error and returns `code`.
+int set_error(int code, const std::string& msg);
+
+// Converts a CUDA runtime error into CCV_ERR_CUDA with context.
+int cuda_error(cudaError_t e, const char* what);
+
+// Device pointer of the per-device status word (the current device).
+int* device_status_ptr();
+
+// Number of SMs of the current device (cached per device).
+int device_sm_count();
+
+// Validated problem with derived sizes.
+struct Problem {
+  int n, h, w, c, k, r, s, p, q;
+  int sh, sw, ph, pw;
+};
+
+int make_problem(const ccv_conv_shape* shape, Problem* out);
+
+// Packed weight image: per precision "image" of [R*S][3][K][C] floats.
+inline size_t packed_image_floats(const Problem& pb) {
+  return static_cast<size_t>(pb.r) * pb.s * 3ull * pb.k * pb.c;
+}
+
+// Kernels of ccv_layout.cu.
+int launch_prepack(const float* w_real, const float* w_imag, int layout, const Problem& pb,
+                   int precision, float* packed, cudaStream_t stream);
+int launch_nchw_complex_to_planar(const float* x, float* xr, float* xi, const Problem& pb,
+                                  cudaStream_t stream);
+
+// Kernels of ccv_fprop.cu.
+enum OutLayout { OUT_PLANAR_NHWC = 0, OUT_COMPLEX_NCHW = 1 };
+int launch_fprop(const float* xr, const float* xi, const float* w_packed, float* y0, float* y1,
+                 const Problem& pb, int precision, OutLayout out_layout, cudaStream_t stream);
+
+// Encodes a tiled tensor map through the driver entry point.
+int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                 const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides);
+
+int launch_selftest_wait(int* status_dev, cudaStream_t stream);
+
+}  // namespace ccv

@@ -1,0 +1,121 @@
+// Layout kernels around the fprop kernel:
+//   * weight prepack: KCRS or KRSC real/imag planes -> per-tap (-Wi, Wr, Wi)
+//     planes of [K][C], TF32-rounded (and, for 3xTF32, the rounding
+//     remainders as a second image).  Replaces the per-version KCRS->KRSC
+//     copy of the reference module (modules.py:127-151).
+//   * complex64 NCHW -> fp32 NHWC planes (the two permute+contiguous copies
+//     of modules.py:198-199), used by the complex entry point.
+#include <cuda_runtime.h>
+
+#include "ccv_internal.h"
+
+namespace ccv {
+
+namespace {
+
+// Round-to-nearest (ties away from zero) conversion to TF32, kept in an fp32
+// container with the 13 low mantissa bits cleared.
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// out image layout: [tap = r*S + s][plane][K][C], plane 0 = -Wi, 1 = Wr, 2 = Wi.
+__global__ void ccv_prepack_kernel(const float* __restrict__ wr, const float* __restrict__ wi,
+                                   float* __restrict__ out, int K, int C, int R, int S, int krsc,
+                                   int split) {
+  const long long total = static_cast<long long>(R) * S * K * C;
+  const long long image = total * 3;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % C);
+    long long t = i / C;
+    const int k = static_cast<int>(t % K);
+    const int tap = static_cast<int>(t / K);
+    const int r = tap / S;
+    const int s = tap - r * S;
+    const long long src = krsc ? ((static_cast<long long>(k) * R + r) * S + s) * C + c
+                               : ((static_cast<long long>(k) * C + c) * R + r) * S + s;
+    const float xr = wr[src];
+    const float xi = wi[src];
+    const float hr = to_tf32(xr);
+    const float hi = to_tf32(xi);
+    const long long kc = static_cast<long long>(K) * C;
+    const long long o = static_cast<long long>(tap) * 3 * kc + static_cast<long long>(k) * C + c;
+    out[o] = -hi;
+    out[o + kc] = hr;
+    out[o + 2 * kc] = hi;
+    if (split) {
+      const float lr = to_tf32(xr - hr);
+      const float li = to_tf32(xi - hi);
+      out[image + o] = -li;
+      out[image + o + kc] = lr;
+      out[image + o + 2 * kc] = li;
+    }
+  }
+}
+
+// complex64 NCHW -> two fp32 NHWC planes, 32x32 (C x W) tiles per (n, h).
+__global__ void ccv_nchw_to_planar_kernel(const float2* __restrict__ x, float* __restrict__ xr,
+                                          float* __restrict__ xi, int C, int H, int W) {
+  __shared__ float tr[32][33];
+  __shared__ float ti[32][33];
+  const int nh = blockIdx.z;
+  const int n = nh / H;
+  const int h = nh - n * H;
+  const int w0 = blockIdx.x * 32;
+  const int c0 = blockIdx.y * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int c = c0 + ty + i;
+    const int w = w0 + tx;
+    if (c < C && w < W) {
+      const float2 v = x[((static_cast<long long>(n) * C + c) * H + h) * W + w];
+      tr[ty + i][tx] = v.x;
+      ti[ty + i][tx] = v.y;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    const int w = w0 + ty + i;
+    const int c = c0 + tx;
+    if (c < C && w < W) {
+      const long long o = ((static_cast<long long>(n) * H + h) * W + w) * C + c;
+      xr[o] = tr[tx][ty + i];
+      xi[o] = ti[tx][ty + i];
+    }
+  }
+}
+
+}  // namespace
+
+int launch_prepack(const float* w_real, const float* w_imag, int layout, const Problem& pb,
+                   int precision, float* packed, cudaStream_t stream) {
+  const long long total = static_cast<long long>(pb.r) * pb.s * pb.k * pb.c;
+  const int threads = 256;
+  const long long blocks = std::min<long long>((total + threads - 1) / threads, 148LL * 16);
+  ccv_prepack_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(
+      w_real, w_imag, packed, pb.k, pb.c, pb.r, pb.s, layout == CCV_WEIGHT_KRSC ? 1 : 0,
+      precision == CCV_PRECISION_3XTF32 ? 1 : 0);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "prepack kernel launch");
+  return CCV_OK;
+}
+
+int launch_nchw_complex_to_planar(const float* x, float* xr, float* xi, const Problem& pb,
+                                  cudaStream_t stream) {
+  const long long nh = static_cast<long long>(pb.n) * pb.h;
+  if (nh > 65535) return set_error(CCV_ERR_UNSUPPORTED, "N*H too large for the layout kernel");
+  dim3 grid((pb.w + 31) / 32, (pb.c + 31) / 32, static_cast<unsigned>(nh));
+  dim3 block(32, 8);
+  ccv_nchw_to_planar_kernel<<<grid, block, 0, stream>>>(reinterpret_cast<const float2*>(x), xr,
+                                                         xi, pb.c, pb.h, pb.w);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "layout kernel launch");
+  return CCV_OK;
+}
+
+}  // namespace ccv

@@ -1,0 +1,142 @@
+/*
+ * ccv_b200.h - C ABI of the B200 (sm_100a) complex-valued Conv2d forward.
+ *
+ * This is the drop-in boundary that replaces the reference's compiled
+ * extension `complex_conv2d._C` (pybind module defined in
+ * csrc/bindings.cpp:16-29 of jaeeunHwang/cutlass-complex-conv, whose body is
+ * `complex_conv2d_cuda` in csrc/complex_conv2d.cu:84-309).  All entry points
+ * take plain device pointers and sizes; none allocates memory.  Callers that
+ * need scratch memory get its size from the matching *_workspace_bytes query
+ * and pass it in.  Every launch is asynchronous on the given stream.
+ *
+ * Conventions
+ *   - Activation planes x_real/x_imag: fp32 NHWC, contiguous
+ *     (reference: modules.py:153-174, complex_conv2d.cu:134-138).
+ *   - Complex activations: complex64 NCHW, interleaved (re, im) fp32 pairs
+ *     (reference: modules.py:176-207).
+ *   - Output planes y_real/y_imag: fp32 NPQK (NHWC), contiguous
+ *     (reference: complex_conv2d.cu:161-165).  Complex output: complex64
+ *     NKPQ (NCHW) interleaved.
+ *   - Cross-correlation, zero padding, dilation 1, groups 1
+ *     (reference: complex_conv2d.cu:173-195).
+ *   - P = (H + 2*pad_h - R) / stride_h + 1, Q likewise
+ *     (reference: complex_conv2d.cu:151-155).
+ *   - Constraints (reference: device/implicit_planar_cgemm_convolution.h
+ *     can_implement, :71-187): C % 4 == 0, K % 4 == 0, every tensor below
+ *     2^31 bytes per plane; additionally stride <= 8 (TMA traversal stride).
+ *   - All pointers 16-byte aligned.
+ *
+ * Return value of every int function: CCV_OK or a CCV_ERR_* code; the text
+ * of the last error on the calling thread is ccv_last_error_message().
+ */
+#ifndef CCV_B200_H_
+#define CCV_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream. */
+typedef struct CUstream_st* ccv_stream_t;
+
+enum ccv_status {
+  CCV_OK = 0,
+  CCV_ERR_INVALID_ARGUMENT = 1, /* bad shape, pointer, alignment or size  */
+  CCV_ERR_UNSUPPORTED = 2,      /* reference: "CUTLASS cannot implement"   */
+  CCV_ERR_WORKSPACE = 3,        /* workspace missing or too small          */
+  CCV_ERR_CUDA = 4,             /* a CUDA runtime/driver call failed       */
+  CCV_ERR_DEVICE = 5,           /* device not sm_100 or status word set    */
+  CCV_ERR_DEVICE_TIMEOUT = 6    /* a bounded in-kernel wait ran out        */
+};
+
+enum ccv_precision {
+  CCV_PRECISION_TF32 = 0,  /* TF32 tensor-core products, FP32 accumulate   */
+  CCV_PRECISION_3XTF32 = 1 /* split-TF32 (hi*hi + hi*lo + lo*hi), ~FP32  */
+};
+
+enum ccv_weight_layout {
+  CCV_WEIGHT_KCRS = 0, /* nn.Module parameter layout (modules.py:93-107)   */
+  CCV_WEIGHT_KRSC = 1  /* extension layout (complex_conv2d.cu:140-143)     */
+};
+
+typedef struct ccv_conv_shape {
+  int64_t n, h, w, c; /* input batch, height, width, channels */
+  int64_t k, r, s;    /* output channels, filter height, filter width */
+  int64_t stride_h, stride_w;
+  int64_t pad_h, pad_w;
+} ccv_conv_shape;
+
+/* Output spatial size; reference complex_conv2d.cu:151-159. */
+int ccv_output_size(const ccv_conv_shape* shape, int64_t* p, int64_t* q);
+
+/* Validate a problem the way can_implement does (complex_conv2d.cu:94-159,
+ * device/implicit_planar_cgemm_convolution.h:71-187). */
+int ccv_check_shape(const ccv_conv_shape* shape);
+
+/* Bytes of the packed weight image used by the fprop kernels. */
+size_t ccv_packed_weight_bytes(const ccv_conv_shape* shape, int precision);
+
+/* Repack real/imag weight planes (KCRS or KRSC fp32) into the kernel's
+ * packed image: per filter tap, planes (-W_im, W_re, W_im) of [K][C], each
+ * value rounded to TF32 (3xTF32 adds a second image of the rounding
+ * remainders).  Replaces the KCRS->KRSC prepack of modules.py:127-151. */
+int ccv_prepack_weights(const float* w_real, const float* w_imag, int layout,
+                        const ccv_conv_shape* shape, int precision,
+                        void* packed, size_t packed_bytes, ccv_stream_t stream);
+
+/* Scratch bytes the fprop entry points below need for this problem. */
+size_t ccv_fprop_planar_workspace_bytes(const ccv_conv_shape* shape, int precision);
+size_t ccv_fprop_complex_workspace_bytes(const ccv_conv_shape* shape, int precision);
+
+/* Planar fprop: fp32 NHWC planes in, fp32 NPQK planes out, packed weights.
+ * Replaces complex_conv2d_cuda (csrc/complex_conv2d.cu:84-309) behind
+ * ComplexConv2d.forward_planar (modules.py:153-174). */
+int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_packed,
+                     float* y_real, float* y_imag, const ccv_conv_shape* shape,
+                     int precision, void* workspace, size_t workspace_bytes,
+                     ccv_stream_t stream);
+
+/* Complex fprop: complex64 NCHW in, complex64 NKPQ out, packed weights.
+ * Replaces the layout conversions plus kernel of ComplexConv2d.forward
+ * (modules.py:176-207). */
+int ccv_fprop_complex(const void* x, const void* w_packed, void* y,
+                      const ccv_conv_shape* shape, int precision, void* workspace,
+                      size_t workspace_bytes, ccv_stream_t stream);
+
+/* The reference extension call itself: `_C.forward(x_real, x_imag, w_real,
+ * w_imag, stride_h, stride_w, pad_h, pad_w)` (csrc/bindings.cpp:16-29) with
+ * KRSC weights, TF32.  Needs ccv_forward_workspace_bytes() of scratch (the
+ * packed weights). */
+size_t ccv_forward_workspace_bytes(const ccv_conv_shape* shape);
+int ccv_forward(const float* x_real, const float* x_imag, const float* w_real_krsc,
+                const float* w_imag_krsc, float* y_real, float* y_imag,
+                const ccv_conv_shape* shape, void* workspace, size_t workspace_bytes,
+                ccv_stream_t stream);
+
+/* Device status word of the current device: nonzero after an in-kernel
+ * bounded wait ran out (a CCV_ERR_* code).  While it is set, fprop kernels
+ * on that device exit without work.  get copies it to the host
+ * (synchronizes the device); clear resets it. */
+int ccv_get_device_status(int* status);
+int ccv_clear_device_status(void);
+
+/* Self-test of the bounded wait: launches one CTA that waits on an mbarrier
+ * nothing arrives on.  The wait gives up after its time limit and the
+ * kernel writes CCV_ERR_DEVICE_TIMEOUT into *status_dev (a device int the
+ * caller zeroed), leaving the context usable. */
+int ccv_selftest_bounded_wait(int* status_dev, ccv_stream_t stream);
+
+/* Text of the last error raised on the calling host thread. */
+const char* ccv_last_error_message(void);
+
+/* Library version string. */
+const char* ccv_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CCV_B200_H_ */

@@ -1,0 +1,85 @@
+"""Host-side behaviour of the drop-in module that needs no GPU: constructor
+validation and messages (modules.py:54-80 of the reference), parameter
+layout and state_dict keys (modules.py:93-107), input validation order
+(modules.py:176-195)."""
+
+import pytest
+import torch
+
+from complex_conv2d import ComplexConv2d
+from complex_conv2d.modules import _pair
+
+
+def test_rejects_unsupported_options():
+    with pytest.raises(NotImplementedError, match="bias"):
+        ComplexConv2d(32, 64, 3, bias=True)
+    with pytest.raises(NotImplementedError, match="groups"):
+        ComplexConv2d(32, 64, 3, groups=2)
+    with pytest.raises(NotImplementedError, match="dilation"):
+        ComplexConv2d(32, 64, 3, dilation=2)
+    with pytest.raises(NotImplementedError, match="padding_mode"):
+        ComplexConv2d(32, 64, 3, padding_mode="reflect")
+    with pytest.raises(NotImplementedError, match="complex64"):
+        ComplexConv2d(32, 64, 3, dtype=torch.complex128)
+
+
+def test_rejects_bad_sizes():
+    with pytest.raises(ValueError, match="positive"):
+        ComplexConv2d(0, 4, 3)
+    with pytest.raises(ValueError, match="kernel_size must be positive"):
+        ComplexConv2d(4, 4, 0)
+    with pytest.raises(ValueError, match="stride must be positive"):
+        ComplexConv2d(4, 4, 3, stride=0)
+    with pytest.raises(ValueError, match="padding must be non-negative"):
+        ComplexConv2d(4, 4, 3, padding=-1)
+    with pytest.raises(TypeError, match="kernel_size must be an int or a pair of ints"):
+        ComplexConv2d(4, 4, 3.0)
+
+
+def test_pair_helper():
+    assert _pair(3, "x") == (3, 3)
+    assert _pair((2, 5), "x") == (2, 5)
+    assert _pair([1, 2], "x") == (1, 2)
+    with pytest.raises(TypeError):
+        _pair((1, 2, 3), "x")
+    with pytest.raises(TypeError):
+        _pair((1.0, 2), "x")
+
+
+def test_parameters_and_state_dict():
+    m = ComplexConv2d(8, 12, (3, 5), stride=(2, 1), padding=(1, 2))
+    assert m.weight_real.shape == (12, 8, 3, 5)
+    assert m.weight_real.dtype == torch.float32
+    assert not m.weight_real.requires_grad and not m.weight_imag.requires_grad
+    assert set(m.state_dict()) == {"weight_real", "weight_imag"}
+    assert m.kernel_size == (3, 5) and m.stride == (2, 1) and m.padding == (1, 2)
+    # kaiming_uniform_ default (a=0): U(+-sqrt(6/fan_in))
+    bound = (6.0 / (8 * 15)) ** 0.5
+    assert m.weight_real.abs().max().item() <= bound
+
+
+def test_precision_selector():
+    assert ComplexConv2d(4, 4, 3).precision == "tf32"
+    assert ComplexConv2d(4, 4, 3, precision="3xTF32").precision == "3xtf32"
+    with pytest.raises(ValueError, match="precision"):
+        ComplexConv2d(4, 4, 3, precision="fp16")
+
+
+def test_forward_validation_before_any_cuda_use():
+    m = ComplexConv2d(4, 4, 3)
+    with pytest.raises(ValueError, match="must be on CUDA"):
+        m(torch.zeros(1, 4, 5, 5, dtype=torch.complex64))
+
+
+def test_prepack_requires_cuda_weights():
+    m = ComplexConv2d(4, 4, 3)
+    with pytest.raises(RuntimeError, match="weights must be on CUDA"):
+        m._ensure_prepacked()
+
+
+def test_apply_clears_cache():
+    m = ComplexConv2d(4, 4, 3)
+    m._w_packed = torch.zeros(1)
+    m._weight_version = (0, 0)
+    m.float()
+    assert m._w_packed is None and m._weight_version is None
