@@ -25,7 +25,7 @@ PKG = os.path.join(HERE, "complex_conv2d")
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(REPO, "include")
 
-CU_SOURCES = ["ccv_api.cu", "ccv_fprop.cu", "ccv_layout.cu"]
+CU_SOURCES = ["ccv_api.cu", "ccv_fprop.cu", "ccv_layout.cu", "ccv_noalloc.cu"]
 CU_HEADERS = ["ccv_internal.h", "ccv_ptx.cuh"]
 NVCC_ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -116,6 +116,23 @@ int ccv_forward(const float* x_real, const float* x_imag, const float* w_real_kr
                 const ccv_conv_shape* shape, void* workspace, size_t workspace_bytes,
                 ccv_stream_t stream);
 
+/* ccv_forward without scratch allocation - no counterpart in the reference.
+ * For callers that may not allocate device memory at all (code running in
+ * another framework's enqueue/execute callback, where that framework owns
+ * the memory pool and a cudaMalloc/cudaFree could synchronize the device).
+ * Same contract and results as ccv_forward, but the packed weights live in
+ * a fixed device array of CCV_NOALLOC_MAX_WEIGHT_BYTES inside the library
+ * (reserved on every GPU that loads it, until process exit).  Problems whose
+ * packed weights (3 * R*S*K*C * 4 bytes) exceed it return CCV_ERR_WORKSPACE.
+ * All calls on a device share that array: calls that overlap on the GPU race,
+ * so order them on one stream.  The first call on a device looks up the
+ * array's address and must come before any stream capture. */
+#define CCV_NOALLOC_MAX_WEIGHT_BYTES (16u * 1024u * 1024u)
+int ccv_forward_noalloc(const float* x_real, const float* x_imag,
+                        const float* w_real_krsc, const float* w_imag_krsc,
+                        float* y_real, float* y_imag, const ccv_conv_shape* shape,
+                        ccv_stream_t stream);
+
 /* Device status word of the current device: nonzero after an in-kernel
  * bounded wait ran out (a CCV_ERR_* code).  While it is set, fprop kernels
  * on that device exit without work.  get copies it to the host
