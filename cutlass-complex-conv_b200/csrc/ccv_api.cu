@@ -102,7 +102,8 @@ int device_sm_count() {
 }
 
 int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                 const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides) {
+                 const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides,
+                 int swizzle_bytes) {
   std::call_once(g_encode_once, []() {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -126,7 +127,9 @@ int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* d
   }
   const CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base),
                                     d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                    CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                                    swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                                         : CU_TENSOR_MAP_SWIZZLE_64B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     return set_error(CCV_ERR_UNSUPPORTED,

@@ -31,9 +31,11 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "ccv_internal.h"
+#include "ccv_fprop_common.cuh"
 #include "ccv_ptx.cuh"
 
 namespace ccv {
@@ -41,7 +43,6 @@ namespace ccv {
 namespace {
 
 constexpr int kThreads = 192;
-constexpr int kBlockM = 128;     // GEMM rows (output pixels) per tile
 constexpr int kBlockC = 16;      // input channels per K step (64-byte rows)
 constexpr int kRowBytes = kBlockC * 4;
 constexpr int kABytes = kBlockM * kRowBytes;  // one activation plane per stage
@@ -51,21 +52,7 @@ constexpr int kTimeoutProducer = CCV_ERR_DEVICE_TIMEOUT;
 constexpr int kTimeoutMma = CCV_ERR_DEVICE_TIMEOUT;
 constexpr int kTimeoutEpilogue = CCV_ERR_DEVICE_TIMEOUT;
 
-struct alignas(64) FpropParams {
-  CUtensorMap tm_xr;  // activation real plane
-  CUtensorMap tm_xi;  // activation imaginary plane
-  CUtensorMap tm_w;   // packed weights [R*S][3][K][C]
-  float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
-  float* y1;          // planar: y_imag (NPQK); complex: unused
-  int* status;        // device status word
-  int n, h, w, c, k, r, s, p, q;
-  int sh, sw, ph, pw;
-  int box_p, box_q, box_q_log2, box_px_log2, nb;  // spatial box tiling
-  int tiles_bp, tiles_bq, total_boxes;
-  int tiles_m, tiles_n;
-  int ksteps;         // ceil(C/16) * R * S
-  long long m_total;  // N*P*Q (flat mode)
-};
+
 
 template <int KT>
 struct Cfg {
@@ -322,58 +309,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
-struct Tiling {
-  bool flat = false;
-  int kt = 128;
-  int box_p = 1, box_q = 1, nb = 1;
-  int tiles_bp = 1, tiles_bq = 1, total_boxes = 1;
-  int tiles_m = 1, tiles_n = 1;
-};
-
-int ilog2(int v) {
-  int l = 0;
-  while ((1 << l) < v) ++l;
-  return l;
-}
-
-Tiling choose_tiling(const Problem& pb) {
-  Tiling t;
-  t.kt = pb.k > 64 ? 128 : (pb.k > 32 ? 64 : 32);
-  t.tiles_n = (pb.k + t.kt - 1) / t.kt;
-  t.flat = (pb.r == 1 && pb.s == 1 && pb.sh == 1 && pb.sw == 1 && pb.ph == 0 && pb.pw == 0);
-  if (t.flat) {
-    const long long m = static_cast<long long>(pb.n) * pb.p * pb.q;
-    t.tiles_m = static_cast<int>((m + kBlockM - 1) / kBlockM);
-    return t;
-  }
-  // Spatial boxes: box_p x box_q (powers of two, product 8..128, at most 4
-  // boxes per tile), chosen to cover P x Q with the fewest computed rows.
-  long long best_cost = -1;
-  for (int px = 32; px <= 128; px *= 2) {
-    const int nb = kBlockM / px;
-    for (int bq = 1; bq <= px; bq *= 2) {
-      const int bp = px / bq;
-      if (bq * pb.sw > 256 || bp * pb.sh > 256) continue;
-      const long long tbq = (pb.q + bq - 1) / bq;
-      const long long tbp = (pb.p + bp - 1) / bp;
-      const long long boxes = static_cast<long long>(pb.n) * tbq * tbp;
-      const long long tiles = (boxes + nb - 1) / nb;
-      const long long cost = tiles * kBlockM * 4 + nb;  // rows computed, then fewer boxes
-      if (best_cost < 0 || cost < best_cost) {
-        best_cost = cost;
-        t.box_p = bp;
-        t.box_q = bq;
-        t.nb = nb;
-        t.tiles_bp = static_cast<int>(tbp);
-        t.tiles_bq = static_cast<int>(tbq);
-        t.total_boxes = static_cast<int>(boxes);
-        t.tiles_m = static_cast<int>(tiles);
-      }
-    }
-  }
-  return t;
-}
-
 template <int KT, bool FLAT, bool OUT_COMPLEX>
 int launch_variant(const FpropParams& prm, int grid, cudaStream_t stream) {
   using C = Cfg<KT>;
@@ -410,6 +345,13 @@ int launch_fprop(const float* xr, const float* xi, const float* w_packed, float*
     return set_error(CCV_ERR_UNSUPPORTED, "3xTF32 fprop is not available in this build");
   }
   const Tiling t = choose_tiling(pb);
+  // Large problems go to the persistent CTA-pair kernel; small ones (fewer
+  // pair tiles than half the SMs) to the single-CTA kernel.
+  // CCV_FORCE_KERNEL=1 or 2 pins the family (testing/benchmarking knob).
+  const char* force_env = getenv("CCV_FORCE_KERNEL");
+  const int forced = force_env ? atoi(force_env) : 0;
+  const bool use_pair = forced == 2 || (forced != 1 && pair_tiles(t) * 2 >= device_sm_count());
+  if (use_pair) return launch_fprop_pair(xr, xi, w_packed, y0, y1, pb, t, out_layout, stream);
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;

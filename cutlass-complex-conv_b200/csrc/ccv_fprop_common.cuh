@@ -1,0 +1,92 @@
+// Shared by the fprop kernel families: kernel parameters and the spatial
+// tiling of the GEMM M dimension (output pixels) into TMA boxes.
+#pragma once
+
+#include <cuda.h>
+
+#include "ccv_internal.h"
+
+namespace ccv {
+
+constexpr int kBlockM = 128;  // GEMM rows (output pixels) per CTA tile
+
+struct alignas(64) FpropParams {
+  CUtensorMap tm_xr;  // activation real plane
+  CUtensorMap tm_xi;  // activation imaginary plane
+  CUtensorMap tm_w;   // packed weights [R*S][3][K][C]
+  float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
+  float* y1;          // planar: y_imag (NPQK); complex: unused
+  int* status;        // device status word
+  int n, h, w, c, k, r, s, p, q;
+  int sh, sw, ph, pw;
+  int box_p, box_q, box_q_log2, box_px_log2, nb;  // spatial box tiling
+  int tiles_bp, tiles_bq, total_boxes;
+  int tiles_m, tiles_n;
+  int ksteps;         // ceil(C/16) * R * S
+  long long m_total;  // N*P*Q (flat mode)
+  int num_tiles;      // work units of the persistent kernel
+};
+
+// Tiling of the output pixels: 128-row tiles made of NB boxes of
+// box_p x box_q output pixels (powers of two), or flat 128-pixel runs for
+// 1x1 / stride-1 / pad-0 problems.
+struct Tiling {
+  bool flat = false;
+  int kt = 128;
+  int box_p = 1, box_q = 1, nb = 1;
+  int tiles_bp = 1, tiles_bq = 1, total_boxes = 1;
+  int tiles_m = 1, tiles_n = 1;
+};
+
+inline int ilog2(int v) {
+  int l = 0;
+  while ((1 << l) < v) ++l;
+  return l;
+}
+
+inline Tiling choose_tiling(const Problem& pb) {
+  Tiling t;
+  t.kt = pb.k > 64 ? 128 : (pb.k > 32 ? 64 : 32);
+  t.tiles_n = (pb.k + t.kt - 1) / t.kt;
+  t.flat = (pb.r == 1 && pb.s == 1 && pb.sh == 1 && pb.sw == 1 && pb.ph == 0 && pb.pw == 0);
+  if (t.flat) {
+    const long long m = static_cast<long long>(pb.n) * pb.p * pb.q;
+    t.tiles_m = static_cast<int>((m + kBlockM - 1) / kBlockM);
+    return t;
+  }
+  // Spatial boxes: box_p x box_q (powers of two, product 8..128, at most 4
+  // boxes per tile), chosen to cover P x Q with the fewest computed rows.
+  long long best_cost = -1;
+  for (int px = 32; px <= 128; px *= 2) {
+    const int nb = kBlockM / px;
+    for (int bq = 1; bq <= px; bq *= 2) {
+      const int bp = px / bq;
+      if (bq * pb.sw > 256 || bp * pb.sh > 256) continue;
+      const long long tbq = (pb.q + bq - 1) / bq;
+      const long long tbp = (pb.p + bp - 1) / bp;
+      const long long boxes = static_cast<long long>(pb.n) * tbq * tbp;
+      const long long tiles = (boxes + nb - 1) / nb;
+      const long long cost = tiles * kBlockM * 4 + nb;  // rows computed, then fewer boxes
+      if (best_cost < 0 || cost < best_cost) {
+        best_cost = cost;
+        t.box_p = bp;
+        t.box_q = bq;
+        t.nb = nb;
+        t.tiles_bp = static_cast<int>(tbp);
+        t.tiles_bq = static_cast<int>(tbq);
+        t.total_boxes = static_cast<int>(boxes);
+        t.tiles_m = static_cast<int>(tiles);
+      }
+    }
+  }
+  return t;
+}
+
+// CTA-pair kernel family (ccv_fprop2.cu): work units are pairs of 128-row
+// tiles; returns the number of such units.
+int pair_tiles(const Tiling& t);
+int launch_fprop_pair(const float* xr, const float* xi, const float* w_packed, float* y0,
+                      float* y1, const Problem& pb, const Tiling& t, OutLayout out_layout,
+                      cudaStream_t stream);
+
+}  // namespace ccv

@@ -48,8 +48,10 @@ int launch_fprop(const float* xr, const float* xi, const float* w_packed, float*
                  const Problem& pb, int precision, OutLayout out_layout, cudaStream_t stream);
 
 // Encodes a tiled tensor map through the driver entry point.
+// `swizzle_bytes` is 64 or 128 (the box's inner extent in bytes).
 int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
-                 const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides);
+                 const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides,
+                 int swizzle_bytes = 64);
 
 int launch_selftest_wait(int* status_dev, cudaStream_t stream);
 
