@@ -67,6 +67,12 @@ int check_device() {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Bytes of one fp32 NHWC input plane, rounded up to 256.
+size_t plane_bytes_aligned(const Problem& pb) {
+  const size_t plane = static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c * sizeof(float);
+  return (plane + 255) & ~static_cast<size_t>(255);
+}
+
 }  // namespace
 
 int set_error(int code, const std::string& msg) {
@@ -244,29 +250,28 @@ int ccv_prepack_weights(const float* w_real, const float* w_imag, int layout,
 }
 
 size_t ccv_fprop_planar_workspace_bytes(const ccv_conv_shape* shape, int precision) {
-  (void)shape;
-  (void)precision;
-  return 0;
+  Problem pb;
+  if (make_problem(shape, &pb) != CCV_OK) return 0;
+  // 3xTF32 splits the input planes into TF32 parts and remainders (4 planes).
+  return precision == CCV_PRECISION_3XTF32 ? 4 * plane_bytes_aligned(pb) : 0;
 }
 
 size_t ccv_fprop_complex_workspace_bytes(const ccv_conv_shape* shape, int precision) {
   Problem pb;
   if (make_problem(shape, &pb) != CCV_OK) return 0;
-  (void)precision;
-  // fp32 NHWC planes of the input (real, imaginary), 256-byte aligned halves.
-  const size_t plane = static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c * sizeof(float);
-  const size_t plane_al = (plane + 255) & ~static_cast<size_t>(255);
-  return 2 * plane_al;
+  // fp32 NHWC planes of the input (real, imaginary; 3xTF32: also remainders).
+  return (precision == CCV_PRECISION_3XTF32 ? 4 : 2) * plane_bytes_aligned(pb);
 }
 
 int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_packed,
                      float* y_real, float* y_imag, const ccv_conv_shape* shape, int precision,
                      void* workspace, size_t workspace_bytes, ccv_stream_t stream) {
-  (void)workspace;
-  (void)workspace_bytes;
   Problem pb;
   int rc = make_problem(shape, &pb);
   if (rc != CCV_OK) return rc;
+  if (precision != CCV_PRECISION_TF32 && precision != CCV_PRECISION_3XTF32) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "unknown precision");
+  }
   if (!x_real || !x_imag || !w_packed || !y_real || !y_imag) {
     return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
   }
@@ -274,9 +279,27 @@ int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_pac
       !aligned16(y_imag)) {
     return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
   }
+  const size_t need = ccv_fprop_planar_workspace_bytes(shape, precision);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
+  }
   if ((rc = check_device()) != CCV_OK) return rc;
-  return launch_fprop(x_real, x_imag, static_cast<const float*>(w_packed), y_real, y_imag, pb,
-                      precision, OUT_PLANAR_NHWC, reinterpret_cast<cudaStream_t>(stream));
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (precision == CCV_PRECISION_3XTF32) {
+    const size_t pl = plane_bytes_aligned(pb);
+    char* ws = static_cast<char*>(workspace);
+    float* hr = reinterpret_cast<float*>(ws);
+    float* hi = reinterpret_cast<float*>(ws + pl);
+    float* lr = reinterpret_cast<float*>(ws + 2 * pl);
+    float* li = reinterpret_cast<float*>(ws + 3 * pl);
+    rc = launch_split_planes(x_real, x_imag, hr, hi, lr, li,
+                             static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c, st);
+    if (rc != CCV_OK) return rc;
+    return launch_fprop(hr, hi, lr, li, static_cast<const float*>(w_packed), y_real, y_imag, pb,
+                        precision, OUT_PLANAR_NHWC, st);
+  }
+  return launch_fprop(x_real, x_imag, nullptr, nullptr, static_cast<const float*>(w_packed),
+                      y_real, y_imag, pb, precision, OUT_PLANAR_NHWC, st);
 }
 
 int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_conv_shape* shape,
@@ -285,6 +308,9 @@ int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_co
   Problem pb;
   int rc = make_problem(shape, &pb);
   if (rc != CCV_OK) return rc;
+  if (precision != CCV_PRECISION_TF32 && precision != CCV_PRECISION_3XTF32) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "unknown precision");
+  }
   if (!x || !w_packed || !y) return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
   if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y)) {
     return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
@@ -294,15 +320,18 @@ int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_co
     return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
   }
   if ((rc = check_device()) != CCV_OK) return rc;
-  const size_t plane = static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c * sizeof(float);
-  const size_t plane_al = (plane + 255) & ~static_cast<size_t>(255);
-  float* xr = static_cast<float*>(workspace);
-  float* xi = reinterpret_cast<float*>(static_cast<char*>(workspace) + plane_al);
+  const size_t pl = plane_bytes_aligned(pb);
+  char* ws = static_cast<char*>(workspace);
+  float* xr = reinterpret_cast<float*>(ws);
+  float* xi = reinterpret_cast<float*>(ws + pl);
+  const bool split = precision == CCV_PRECISION_3XTF32;
+  float* lr = split ? reinterpret_cast<float*>(ws + 2 * pl) : nullptr;
+  float* li = split ? reinterpret_cast<float*>(ws + 3 * pl) : nullptr;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  rc = launch_nchw_complex_to_planar(static_cast<const float*>(x), xr, xi, pb, st);
+  rc = launch_nchw_complex_to_planar(static_cast<const float*>(x), xr, xi, lr, li, pb, st);
   if (rc != CCV_OK) return rc;
-  return launch_fprop(xr, xi, static_cast<const float*>(w_packed), static_cast<float*>(y), nullptr,
-                      pb, precision, OUT_COMPLEX_NCHW, st);
+  return launch_fprop(xr, xi, lr, li, static_cast<const float*>(w_packed), static_cast<float*>(y),
+                      nullptr, pb, precision, OUT_COMPLEX_NCHW, st);
 }
 
 size_t ccv_forward_workspace_bytes(const ccv_conv_shape* shape) {

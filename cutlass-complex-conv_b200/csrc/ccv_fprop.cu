@@ -339,10 +339,16 @@ int launch_kt(int kt, const FpropParams& prm, int grid, cudaStream_t stream) {
 
 }  // namespace
 
-int launch_fprop(const float* xr, const float* xi, const float* w_packed, float* y0, float* y1,
-                 const Problem& pb, int precision, OutLayout out_layout, cudaStream_t stream) {
-  if (precision != CCV_PRECISION_TF32) {
-    return set_error(CCV_ERR_UNSUPPORTED, "3xTF32 fprop is not available in this build");
+int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
+                 const float* w_packed, float* y0, float* y1, const Problem& pb, int precision,
+                 OutLayout out_layout, cudaStream_t stream) {
+  const bool split = precision == CCV_PRECISION_3XTF32;
+  if (split && (xr_lo == nullptr || xi_lo == nullptr)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "3xTF32 needs the activation remainder planes");
+  }
+  if (!split) {
+    xr_lo = nullptr;
+    xi_lo = nullptr;
   }
   const Tiling t = choose_tiling(pb);
   // Large problems go to the persistent CTA-pair kernel; small ones (fewer
@@ -350,8 +356,26 @@ int launch_fprop(const float* xr, const float* xi, const float* w_packed, float*
   // CCV_FORCE_KERNEL=1 or 2 pins the family (testing/benchmarking knob).
   const char* force_env = getenv("CCV_FORCE_KERNEL");
   const int forced = force_env ? atoi(force_env) : 0;
-  const bool use_pair = forced == 2 || (forced != 1 && pair_tiles(t) * 2 >= device_sm_count());
-  if (use_pair) return launch_fprop_pair(xr, xi, w_packed, y0, y1, pb, t, out_layout, stream);
+  // 3xTF32 runs only on the pair kernels (they take the precision passes).
+  const bool use_pair =
+      split || forced == 2 || (forced != 1 && pair_tiles(t) * 2 >= device_sm_count());
+  if (use_pair) {
+    // Halo reuse for stride-1 filters, unless its one-box tiles compute
+    // clearly more rows than the tap kernel's multi-box tiles.
+    // CCV_HALO=0/1 pins the choice (testing/benchmarking knob).
+    const char* halo_env = getenv("CCV_HALO");
+    const int halo_forced = halo_env ? atoi(halo_env) : -1;
+    if (halo_forced != 0 && halo_applicable(pb)) {
+      const Tiling th = choose_halo_tiling(pb);
+      const long long rows_tap = static_cast<long long>(t.tiles_m) * t.tiles_n;
+      const long long rows_halo = static_cast<long long>(th.tiles_m) * th.tiles_n;
+      if (halo_forced == 1 || rows_halo * 100 <= rows_tap * 115) {
+        return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, w_packed, y0, y1, pb, th, out_layout,
+                                      stream);
+      }
+    }
+    return launch_fprop_pair(xr, xi, xr_lo, xi_lo, w_packed, y0, y1, pb, t, out_layout, stream);
+  }
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;

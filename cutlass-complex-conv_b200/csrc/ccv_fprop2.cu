@@ -25,6 +25,7 @@
 
 #include <mutex>
 
+#include "ccv_epilogue.cuh"
 #include "ccv_fprop_common.cuh"
 #include "ccv_internal.h"
 #include "ccv_ptx.cuh"
@@ -50,11 +51,6 @@ struct Cfg2 {
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;
   static_assert(kStages >= 3, "pipeline too shallow");
 };
-
-__device__ __forceinline__ float4 u4f2(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  return make_float4(__uint_as_float(a), __uint_as_float(b), __uint_as_float(c),
-                     __uint_as_float(d));
-}
 
 template <int KT, bool FLAT, bool OUT_COMPLEX>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
@@ -100,6 +96,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     ptx::prefetch_tmap(&prm.tm_xr);
     ptx::prefetch_tmap(&prm.tm_xi);
     ptx::prefetch_tmap(&prm.tm_w);
+    if (prm.passes > 1) {
+      ptx::prefetch_tmap(&prm.tm_xr_lo);
+      ptx::prefetch_tmap(&prm.tm_xi_lo);
+    }
   }
   if (warp == 1) {
     ptx::tmem_alloc_pair(ptx::smem_u32(tmem_holder), C::kTmemCols);
@@ -122,7 +122,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         const int n_tile = t % prm.tiles_n;
         const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
         const int k0 = n_tile * KT;
-        for (int ks = 0; ks < prm.ksteps; ++ks, ++g) {
+        for (int v = 0; v < prm.ksteps * prm.passes; ++v, ++g) {
+          const int ks = v / prm.passes;
+          const int pass = v - ks * prm.passes;
+          const CUtensorMap* mr = pass == 2 ? &prm.tm_xr_lo : &prm.tm_xr;
+          const CUtensorMap* mi = pass == 2 ? &prm.tm_xi_lo : &prm.tm_xi;
           const int stage = static_cast<int>(g % C::kStages);
           const uint32_t phase = (g / C::kStages) & 1u;
           if (!ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, prm.status, kTimeout) ||
@@ -143,8 +147,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
           const uint32_t w_x = a_i + kA2;
           const uint32_t w_y = w_x + C::kWSlot;
           if constexpr (FLAT) {
-            ptx::tma_load_2d_pair(a_r, &prm.tm_xr, fb, c0, half * kBlockM);
-            ptx::tma_load_2d_pair(a_i, &prm.tm_xi, fb, c0, half * kBlockM);
+            ptx::tma_load_2d_pair(a_r, mr, fb, c0, half * kBlockM);
+            ptx::tma_load_2d_pair(a_i, mi, fb, c0, half * kBlockM);
           } else {
             const uint32_t box_bytes = (1u << prm.box_px_log2) * kRow2;
             for (int b = 0; b < prm.nb; ++b) {
@@ -156,14 +160,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
               const int bq = rem - bp * prm.tiles_bq;
               const int wc = bq * prm.box_q * prm.sw - prm.pw + ss;
               const int hc = bp * prm.box_p * prm.sh - prm.ph + rr;
-              ptx::tma_load_4d_pair(a_r + b * box_bytes, &prm.tm_xr, fb, c0, wc, hc, img);
-              ptx::tma_load_4d_pair(a_i + b * box_bytes, &prm.tm_xi, fb, c0, wc, hc, img);
+              ptx::tma_load_4d_pair(a_r + b * box_bytes, mr, fb, c0, wc, hc, img);
+              ptx::tma_load_4d_pair(a_i + b * box_bytes, mi, fb, c0, wc, hc, img);
             }
           }
           // Packed planes per tap: 0 = -W_im, 1 = W_re, 2 = W_im.
           // CTA0: X = W_re, Y = -W_im.  CTA1: X = W_im, Y = W_re.
-          ptx::tma_load_4d_pair(w_x, &prm.tm_w, fb, c0, k0, leader ? 1 : 2, tap);
-          ptx::tma_load_4d_pair(w_y, &prm.tm_w, fb, c0, k0, leader ? 0 : 1, tap);
+          // Pass 1 of 3xTF32 reads the weight remainder image.
+          const int wtap = pass == 1 ? tap + rs : tap;
+          ptx::tma_load_4d_pair(w_x, &prm.tm_w, fb, c0, k0, leader ? 1 : 2, wtap);
+          ptx::tma_load_4d_pair(w_y, &prm.tm_w, fb, c0, k0, leader ? 0 : 1, wtap);
         }
       }
       if (leader) {
@@ -191,7 +197,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         }
         ptx::tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(buf * C::kAccCols);
-        for (int ks = 0; ks < prm.ksteps; ++ks, ++g) {
+        for (int ks = 0; ks < prm.ksteps * prm.passes; ++ks, ++g) {
           const int stage = static_cast<int>(g % C::kStages);
           const uint32_t phase = (g / C::kStages) & 1u;
           if (!ptx::mbar_wait_bounded(full_bar(stage), phase, prm.status, kTimeout)) {
@@ -238,65 +244,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       if (!ok) flags[1] = 1;
       const int n_tile = t % prm.tiles_n;
       const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
-      const int k0 = n_tile * KT;
-      bool valid = ok && !flags[1];
       int img = 0, op = 0, oq = 0;
-      if constexpr (FLAT) {
-        const long long m = static_cast<long long>(half) * kBlockM + row;
-        valid = valid && (m < prm.m_total);
-        const long long pq = static_cast<long long>(prm.p) * prm.q;
-        img = static_cast<int>(m / pq);
-        const long long rem = m - static_cast<long long>(img) * pq;
-        op = static_cast<int>(rem / prm.q);
-        oq = static_cast<int>(rem - static_cast<long long>(op) * prm.q);
-      } else {
-        const int b = row >> prm.box_px_log2;
-        const int local = row & ((1 << prm.box_px_log2) - 1);
-        const int gb = half * prm.nb + b;
-        valid = valid && (gb < prm.total_boxes);
-        img = gb / per_img;
-        const int rem = gb - img * per_img;
-        const int bp = rem / prm.tiles_bq;
-        const int bq = rem - bp * prm.tiles_bq;
-        op = bp * prm.box_p + (local >> prm.box_q_log2);
-        oq = bq * prm.box_q + (local & ((1 << prm.box_q_log2) - 1));
-        valid = valid && (op < prm.p) && (oq < prm.q);
-      }
-      const long long pix = (static_cast<long long>(img) * prm.p + op) * prm.q + oq;
-      const uint32_t t_acc = t_row + static_cast<uint32_t>(buf * C::kAccCols);
-#pragma unroll 1
-      for (int ch = 0; ch < KT; ch += 32) {
-        uint32_t vr[32], vi[32];
-        ptx::tmem_ld_32x32b_x32(t_acc + ch, vr);
-        ptx::tmem_ld_32x32b_x32(t_acc + KT + ch, vi);
-        ptx::tmem_wait_ld();
-        const int kb = k0 + ch;
-        if (valid && kb < prm.k) {
-          if constexpr (!OUT_COMPLEX) {
-            float* dr = prm.y0 + pix * prm.k + kb;
-            float* di = prm.y1 + pix * prm.k + kb;
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              if (kb + j < prm.k) {
-                *reinterpret_cast<float4*>(dr + j) = u4f2(vr[j], vr[j + 1], vr[j + 2], vr[j + 3]);
-                *reinterpret_cast<float4*>(di + j) = u4f2(vi[j], vi[j + 1], vi[j + 2], vi[j + 3]);
-              }
-            }
-          } else {
-            const long long pq = static_cast<long long>(prm.p) * prm.q;
-            float2* y = reinterpret_cast<float2*>(prm.y0);
-            const long long base = static_cast<long long>(img) * prm.k * pq +
-                                   static_cast<long long>(op) * prm.q + oq;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (kb + j < prm.k) {
-                y[base + static_cast<long long>(kb + j) * pq] =
-                    make_float2(__uint_as_float(vr[j]), __uint_as_float(vi[j]));
-              }
-            }
-          }
-        }
-      }
+      const bool valid = tile_row_pixel<FLAT>(prm, half, row, img, op, oq) && ok && !flags[1];
+      store_accumulator<KT, OUT_COMPLEX>(prm, t_row + static_cast<uint32_t>(buf * C::kAccCols),
+                                         n_tile * KT, valid, img, op, oq);
       // This warp is done with the accumulator buffer: release it to the MMA.
       ptx::tc_fence_before();
       __syncwarp();
@@ -360,9 +311,9 @@ int launch2_kt(int kt, const FpropParams& prm, cudaStream_t stream) {
 
 int pair_tiles(const Tiling& t) { return ((t.tiles_m + 1) / 2) * t.tiles_n; }
 
-int launch_fprop_pair(const float* xr, const float* xi, const float* w_packed, float* y0,
-                      float* y1, const Problem& pb, const Tiling& t, OutLayout out_layout,
-                      cudaStream_t stream) {
+int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
+                      const float* w_packed, float* y0, float* y1, const Problem& pb,
+                      const Tiling& t, OutLayout out_layout, cudaStream_t stream) {
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;
@@ -381,6 +332,12 @@ int launch_fprop_pair(const float* xr, const float* xi, const float* w_packed, f
   prm.ksteps = ((pb.c + kC2 - 1) / kC2) * pb.r * pb.s;
   prm.m_total = static_cast<long long>(pb.n) * pb.p * pb.q;
   prm.num_tiles = pair_tiles(t);
+  const bool split = xr_lo != nullptr;
+  prm.passes = split ? 3 : 1;
+  if (!split) {
+    xr_lo = xr;
+    xi_lo = xi;
+  }
 
   int rc;
   const uint64_t cb = static_cast<uint64_t>(pb.c) * 4;
@@ -392,6 +349,8 @@ int launch_fprop_pair(const float* xr, const float* xi, const float* w_packed, f
     const uint32_t es[2] = {1, 1};
     if ((rc = encode_tiled(&prm.tm_xr, xr, 2, dims, strides, box, es, 128)) != CCV_OK) return rc;
     if ((rc = encode_tiled(&prm.tm_xi, xi, 2, dims, strides, box, es, 128)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_xr_lo, xr_lo, 2, dims, strides, box, es, 128)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_xi_lo, xi_lo, 2, dims, strides, box, es, 128)) != CCV_OK) return rc;
   } else {
     const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.w),
                               static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
@@ -401,10 +360,12 @@ int launch_fprop_pair(const float* xr, const float* xi, const float* w_packed, f
     const uint32_t es[4] = {1, static_cast<uint32_t>(pb.sw), static_cast<uint32_t>(pb.sh), 1};
     if ((rc = encode_tiled(&prm.tm_xr, xr, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
     if ((rc = encode_tiled(&prm.tm_xi, xi, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_xr_lo, xr_lo, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_xi_lo, xi_lo, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
   }
   {
     const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.k), 3,
-                              static_cast<uint64_t>(pb.r) * pb.s};
+                              static_cast<uint64_t>(pb.r) * pb.s * (split ? 2 : 1)};
     const uint64_t strides[3] = {cb, cb * pb.k, cb * pb.k * 3};
     const uint32_t box[4] = {kC2, static_cast<uint32_t>(t.kt), 1, 1};
     const uint32_t es[4] = {1, 1, 1, 1};

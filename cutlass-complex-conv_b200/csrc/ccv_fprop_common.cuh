@@ -13,7 +13,9 @@ constexpr int kBlockM = 128;  // GEMM rows (output pixels) per CTA tile
 struct alignas(64) FpropParams {
   CUtensorMap tm_xr;  // activation real plane
   CUtensorMap tm_xi;  // activation imaginary plane
-  CUtensorMap tm_w;   // packed weights [R*S][3][K][C]
+  CUtensorMap tm_w;   // packed weights [image][R*S][3][K][C] (image 1 = 3xTF32 remainders)
+  CUtensorMap tm_xr_lo;  // 3xTF32: activation remainder planes (x - tf32(x))
+  CUtensorMap tm_xi_lo;
   float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
   float* y1;          // planar: y_imag (NPQK); complex: unused
   int* status;        // device status word
@@ -25,6 +27,10 @@ struct alignas(64) FpropParams {
   int ksteps;         // ceil(C/16) * R * S
   long long m_total;  // N*P*Q (flat mode)
   int num_tiles;      // work units of the persistent kernel
+  // halo kernel: rows of one shifted activation copy, ring depths and sizes
+  int halo_rows, a_slots, w_stages, a_slot_bytes, w_stage_bytes;
+  // precision passes per K step: 1 (TF32) or 3 (3xTF32: hi*hi, hi*lo, lo*hi)
+  int passes;
 };
 
 // Tiling of the output pixels: 128-row tiles made of NB boxes of
@@ -85,8 +91,21 @@ inline Tiling choose_tiling(const Problem& pb) {
 // CTA-pair kernel family (ccv_fprop2.cu): work units are pairs of 128-row
 // tiles; returns the number of such units.
 int pair_tiles(const Tiling& t);
-int launch_fprop_pair(const float* xr, const float* xi, const float* w_packed, float* y0,
-                      float* y1, const Problem& pb, const Tiling& t, OutLayout out_layout,
-                      cudaStream_t stream);
+// xr_lo/xi_lo: 3xTF32 remainder planes (nullptr for TF32); xr/xi then hold
+// the TF32-rounded parts.
+int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
+                      const float* w_packed, float* y0, float* y1, const Problem& pb,
+                      const Tiling& t, OutLayout out_layout, cudaStream_t stream);
+
+// Halo variant of the pair kernel (ccv_fprop2h.cu): stride-1 problems with a
+// filter wider than 1x1.  Each CTA tile is one box of box_p x box_q pixels
+// (box_q a multiple of 8); per 32-channel block the S column-shifted halo
+// copies of the box are loaded once and reused by the R filter rows.
+bool halo_applicable(const Problem& pb);
+Tiling choose_halo_tiling(const Problem& pb);
+int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
+                           const float* xi_lo, const float* w_packed, float* y0, float* y1,
+                           const Problem& pb, const Tiling& t, OutLayout out_layout,
+                           cudaStream_t stream);
 
 }  // namespace ccv

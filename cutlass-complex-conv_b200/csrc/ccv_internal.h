@@ -39,13 +39,21 @@ inline size_t packed_image_floats(const Problem& pb) {
 // Kernels of ccv_layout.cu.
 int launch_prepack(const float* w_real, const float* w_imag, int layout, const Problem& pb,
                    int precision, float* packed, cudaStream_t stream);
-int launch_nchw_complex_to_planar(const float* x, float* xr, float* xi, const Problem& pb,
-                                  cudaStream_t stream);
+// complex64 NCHW -> fp32 NHWC planes.  With xr_lo/xi_lo non-null (3xTF32),
+// xr/xi receive tf32(x) and xr_lo/xi_lo the remainders x - tf32(x).
+int launch_nchw_complex_to_planar(const float* x, float* xr, float* xi, float* xr_lo,
+                                  float* xi_lo, const Problem& pb, cudaStream_t stream);
+// fp32 planes -> (tf32(x), x - tf32(x)) planes, for 3xTF32 on planar inputs.
+int launch_split_planes(const float* xr, const float* xi, float* hr, float* hi, float* lr,
+                        float* li, size_t count, cudaStream_t stream);
 
 // Kernels of ccv_fprop.cu.
 enum OutLayout { OUT_PLANAR_NHWC = 0, OUT_COMPLEX_NCHW = 1 };
-int launch_fprop(const float* xr, const float* xi, const float* w_packed, float* y0, float* y1,
-                 const Problem& pb, int precision, OutLayout out_layout, cudaStream_t stream);
+// For 3xTF32, xr/xi are the TF32-rounded activation planes and xr_lo/xi_lo
+// the remainders (x - tf32(x)); for TF32 the *_lo pointers are ignored.
+int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
+                 const float* w_packed, float* y0, float* y1, const Problem& pb, int precision,
+                 OutLayout out_layout, cudaStream_t stream);
 
 // Encodes a tiled tensor map through the driver entry point.
 // `swizzle_bytes` is 64 or 128 (the box's inner extent in bytes).

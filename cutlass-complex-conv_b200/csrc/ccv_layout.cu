@@ -7,6 +7,8 @@
 //     of modules.py:198-199), used by the complex entry point.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "ccv_internal.h"
 
 namespace ccv {
@@ -56,9 +58,30 @@ __global__ void ccv_prepack_kernel(const float* __restrict__ wr, const float* __
   }
 }
 
+// fp32 planes -> TF32-rounded parts and exact remainders (x - tf32(x)), the
+// activation split of 3xTF32.
+__global__ void ccv_split_planes_kernel(const float4* __restrict__ xr, const float4* __restrict__ xi,
+                                        float4* __restrict__ hr, float4* __restrict__ hi,
+                                        float4* __restrict__ lr, float4* __restrict__ li,
+                                        long long count4) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 a = xr[i];
+    const float4 b = xi[i];
+    const float4 ah = make_float4(to_tf32(a.x), to_tf32(a.y), to_tf32(a.z), to_tf32(a.w));
+    const float4 bh = make_float4(to_tf32(b.x), to_tf32(b.y), to_tf32(b.z), to_tf32(b.w));
+    hr[i] = ah;
+    hi[i] = bh;
+    lr[i] = make_float4(a.x - ah.x, a.y - ah.y, a.z - ah.z, a.w - ah.w);
+    li[i] = make_float4(b.x - bh.x, b.y - bh.y, b.z - bh.z, b.w - bh.w);
+  }
+}
+
 // complex64 NCHW -> two fp32 NHWC planes, 32x32 (C x W) tiles per (n, h).
+// With xr_lo/xi_lo set, writes tf32(x) and x - tf32(x) instead (3xTF32).
 __global__ void ccv_nchw_to_planar_kernel(const float2* __restrict__ x, float* __restrict__ xr,
-                                          float* __restrict__ xi, int C, int H, int W) {
+                                          float* __restrict__ xi, float* __restrict__ xr_lo,
+                                          float* __restrict__ xi_lo, int C, int H, int W) {
   __shared__ float tr[32][33];
   __shared__ float ti[32][33];
   const int nh = blockIdx.z;
@@ -84,8 +107,19 @@ __global__ void ccv_nchw_to_planar_kernel(const float2* __restrict__ x, float* _
     const int c = c0 + tx;
     if (c < C && w < W) {
       const long long o = ((static_cast<long long>(n) * H + h) * W + w) * C + c;
-      xr[o] = tr[tx][ty + i];
-      xi[o] = ti[tx][ty + i];
+      const float a = tr[tx][ty + i];
+      const float b = ti[tx][ty + i];
+      if (xr_lo != nullptr) {
+        const float ah = to_tf32(a);
+        const float bh = to_tf32(b);
+        xr[o] = ah;
+        xi[o] = bh;
+        xr_lo[o] = a - ah;
+        xi_lo[o] = b - bh;
+      } else {
+        xr[o] = a;
+        xi[o] = b;
+      }
     }
   }
 }
@@ -105,16 +139,31 @@ int launch_prepack(const float* w_real, const float* w_imag, int layout, const P
   return CCV_OK;
 }
 
-int launch_nchw_complex_to_planar(const float* x, float* xr, float* xi, const Problem& pb,
-                                  cudaStream_t stream) {
+int launch_nchw_complex_to_planar(const float* x, float* xr, float* xi, float* xr_lo,
+                                  float* xi_lo, const Problem& pb, cudaStream_t stream) {
   const long long nh = static_cast<long long>(pb.n) * pb.h;
   if (nh > 65535) return set_error(CCV_ERR_UNSUPPORTED, "N*H too large for the layout kernel");
   dim3 grid((pb.w + 31) / 32, (pb.c + 31) / 32, static_cast<unsigned>(nh));
   dim3 block(32, 8);
   ccv_nchw_to_planar_kernel<<<grid, block, 0, stream>>>(reinterpret_cast<const float2*>(x), xr,
-                                                         xi, pb.c, pb.h, pb.w);
+                                                         xi, xr_lo, xi_lo, pb.c, pb.h, pb.w);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "layout kernel launch");
+  return CCV_OK;
+}
+
+int launch_split_planes(const float* xr, const float* xi, float* hr, float* hi, float* lr,
+                        float* li, size_t count, cudaStream_t stream) {
+  // count is a multiple of 4 (C % 4 == 0); all pointers 16-byte aligned.
+  const long long c4 = static_cast<long long>(count / 4);
+  const int threads = 256;
+  const long long blocks = std::min<long long>((c4 + threads - 1) / threads, 148LL * 16);
+  ccv_split_planes_kernel<<<static_cast<int>(std::max<long long>(blocks, 1)), threads, 0, stream>>>(
+      reinterpret_cast<const float4*>(xr), reinterpret_cast<const float4*>(xi),
+      reinterpret_cast<float4*>(hr), reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lr),
+      reinterpret_cast<float4*>(li), c4);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "split kernel launch");
   return CCV_OK;
 }
 

@@ -93,7 +93,9 @@ size_t ccv_fprop_complex_workspace_bytes(const ccv_conv_shape* shape, int precis
 
 /* Planar fprop: fp32 NHWC planes in, fp32 NPQK planes out, packed weights.
  * Replaces complex_conv2d_cuda (csrc/complex_conv2d.cu:84-309) behind
- * ComplexConv2d.forward_planar (modules.py:153-174). */
+ * ComplexConv2d.forward_planar (modules.py:153-174).  TF32 needs no
+ * workspace; 3xTF32 needs ccv_fprop_planar_workspace_bytes() (the inputs
+ * split into TF32 parts and remainders) and weights packed for 3xTF32. */
 int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_packed,
                      float* y_real, float* y_imag, const ccv_conv_shape* shape,
                      int precision, void* workspace, size_t workspace_bytes,

@@ -1,0 +1,77 @@
+"""3xTF32 parity: relative Frobenius error <= 1e-5 against the fp64 oracle
+(north-star tolerance for the FP32-faithful path), through the C ABI and the
+module, including the MRI-style configuration it is benchmarked on."""
+
+import pytest
+import torch
+
+import ccv_abi
+import oracle
+from oracle.configs import BASELINE_CASES
+from test_oracle import CASES as GOLDEN_CASES
+from test_parity_gpu import EDGE, abi_fprop_complex, abi_fprop_planar, abi_prepack
+
+pytestmark = pytest.mark.gpu
+
+TOL_3XTF32 = 1e-5
+P3 = ccv_abi.CCV_PRECISION_3XTF32
+
+
+@pytest.mark.parametrize("name,case,x,wr,wi,y32,y64", GOLDEN_CASES, ids=[c[0] for c in GOLDEN_CASES])
+def test_golden_3xtf32(name, case, x, wr, wi, y32, y64):
+    packed = abi_prepack(case, torch.from_numpy(wr), torch.from_numpy(wi), precision=P3)
+    xt = torch.from_numpy(x)
+    y = abi_fprop_planar(case, xt, packed, precision=P3, poison=True)
+    ref = oracle.oracle_fp64(case, xt, torch.from_numpy(wr), torch.from_numpy(wi))
+    err = oracle.rel_frobenius(y, ref)
+    assert err <= TOL_3XTF32, (name, err)
+    yc = abi_fprop_complex(case, xt, packed, precision=P3, poison=True)
+    assert torch.equal(yc, y.to(torch.complex64))
+
+
+@pytest.mark.parametrize("case", EDGE, ids=[str(i) for i in range(len(EDGE))])
+def test_edges_3xtf32(case):
+    x, wr, wi = oracle.make_inputs(case, input_seed=13)
+    packed = abi_prepack(case, wr, wi, precision=P3)
+    y = abi_fprop_complex(case, x, packed, precision=P3, poison=True)
+    assert oracle.rel_frobenius(y, oracle.oracle_fp64(case, x, wr, wi)) <= TOL_3XTF32
+
+
+def test_mri_config_3xtf32_sampled_images():
+    name, case, std, precs = [c for c in BASELINE_CASES if c[0] == "b32_64_64_320"][0]
+    assert "3xtf32" in precs
+    x, wr, wi = oracle.make_inputs(case, input_std=std)
+    packed = abi_prepack(case, wr, wi, precision=P3)
+    y = abi_fprop_complex(case, x, packed, precision=P3, poison=True)
+    sub = oracle.ConvCase(1, case.c, case.h, case.w, case.k, case.r, case.s,
+                          case.stride_h, case.stride_w, case.pad_h, case.pad_w)
+    for img in (0, case.n - 1):
+        ref = oracle.oracle_fp64(sub, x[img:img + 1], wr, wi)
+        err = oracle.rel_frobenius(y[img:img + 1], ref)
+        assert err <= TOL_3XTF32, (img, err)
+
+
+def test_tf32_is_measurably_less_accurate_than_3xtf32():
+    case = oracle.ConvCase(2, 64, 16, 16, 64, 3, 3, 1, 1, 1, 1)
+    x, wr, wi = oracle.make_inputs(case, input_seed=5)
+    ref = oracle.oracle_fp64(case, x, wr, wi)
+    e1 = oracle.rel_frobenius(abi_fprop_complex(case, x, abi_prepack(case, wr, wi)), ref)
+    e3 = oracle.rel_frobenius(abi_fprop_complex(case, x, abi_prepack(case, wr, wi, precision=P3),
+                                                precision=P3), ref)
+    assert e3 < e1 / 50, (e1, e3)
+
+
+def test_module_3xtf32_forward_and_planar():
+    from complex_conv2d import ComplexConv2d
+    case = oracle.ConvCase(2, 32, 20, 20, 48, 3, 3, 1, 1, 1, 1)
+    x, wr, wi = oracle.make_inputs(case, input_seed=6)
+    m = ComplexConv2d(32, 48, 3, padding=1, device="cuda", precision="3xtf32")
+    with torch.no_grad():
+        m.weight_real.copy_(wr)
+        m.weight_imag.copy_(wi)
+        y = m(x.cuda())
+        yr, yi = m.forward_planar(x.real.permute(0, 2, 3, 1).contiguous().cuda(),
+                                  x.imag.permute(0, 2, 3, 1).contiguous().cuda())
+    ref = oracle.oracle_fp64(case, x, wr, wi)
+    assert oracle.rel_frobenius(y.cpu(), ref) <= TOL_3XTF32
+    assert torch.equal(oracle.planar_nhwc_to_complex_nchw(yr, yi), y)

@@ -1,5 +1,5 @@
-"""Both kernel families on the same problems: the CTA-pair kernel
-(ccv_fprop2.cu) is pinned with CCV_FORCE_KERNEL=2 on the golden and edge
+"""All kernel families on the same problems: the CTA-pair kernels
+(ccv_fprop2.cu tap, ccv_fprop2h.cu halo) are pinned with CCV_FORCE_KERNEL=2 / CCV_HALO on the golden and edge
 shapes that would normally go to the single-CTA kernel, and against the
 fp64 oracle; and the single-CTA kernel (CCV_FORCE_KERNEL=1) on a shape that
 would normally go to the pair kernel."""
@@ -18,21 +18,34 @@ pytestmark = pytest.mark.gpu
 
 @pytest.fixture
 def force_kernel():
-    old = os.environ.get("CCV_FORCE_KERNEL")
+    """Pin the kernel family (1 = single CTA, 2 = CTA pair; 'halo' = CTA pair
+    with halo reuse, 'tap' = CTA pair without) through the library's env knobs."""
+    keys = ("CCV_FORCE_KERNEL", "CCV_HALO")
+    old = {k: os.environ.get(k) for k in keys}
 
     def set_(v):
-        os.environ["CCV_FORCE_KERNEL"] = str(v)
+        if v == "halo":
+            os.environ["CCV_FORCE_KERNEL"] = "2"
+            os.environ["CCV_HALO"] = "1"
+        elif v == "tap":
+            os.environ["CCV_FORCE_KERNEL"] = "2"
+            os.environ["CCV_HALO"] = "0"
+        else:
+            os.environ["CCV_FORCE_KERNEL"] = str(v)
+            os.environ.pop("CCV_HALO", None)
 
     yield set_
-    if old is None:
-        os.environ.pop("CCV_FORCE_KERNEL", None)
-    else:
-        os.environ["CCV_FORCE_KERNEL"] = old
+    for k, v in old.items():
+        if v is None:
+            os.environ.pop(k, None)
+        else:
+            os.environ[k] = v
 
 
 @pytest.mark.parametrize("name,case,x,wr,wi,y32,y64", GOLDEN_CASES, ids=[c[0] for c in GOLDEN_CASES])
-def test_pair_kernel_golden(force_kernel, name, case, x, wr, wi, y32, y64):
-    force_kernel(2)
+@pytest.mark.parametrize("family", ["tap", "halo"])
+def test_pair_kernel_golden(force_kernel, family, name, case, x, wr, wi, y32, y64):
+    force_kernel(family)
     packed = abi_prepack(case, torch.from_numpy(wr), torch.from_numpy(wi))
     y = abi_fprop_planar(case, torch.from_numpy(x), packed, poison=True)
     assert not torch.isnan(y.real).any() and not torch.isnan(y.imag).any()
@@ -42,8 +55,9 @@ def test_pair_kernel_golden(force_kernel, name, case, x, wr, wi, y32, y64):
 
 
 @pytest.mark.parametrize("case", EDGE, ids=[str(i) for i in range(len(EDGE))])
-def test_pair_kernel_edges(force_kernel, case):
-    force_kernel(2)
+@pytest.mark.parametrize("family", ["tap", "halo"])
+def test_pair_kernel_edges(force_kernel, family, case):
+    force_kernel(family)
     x, wr, wi = oracle.make_inputs(case, input_seed=9)
     packed = abi_prepack(case, wr, wi)
     y = abi_fprop_planar(case, x, packed, poison=True)
@@ -51,7 +65,7 @@ def test_pair_kernel_edges(force_kernel, case):
     assert oracle.rel_frobenius(y, oracle.oracle_fp64(case, x, wr, wi)) <= TF32_TOL
 
 
-@pytest.mark.parametrize("family", [1, 2])
+@pytest.mark.parametrize("family", [1, "tap", "halo"])
 def test_families_agree_on_a_mid_size_problem(force_kernel, family):
     case = oracle.ConvCase(6, 64, 30, 30, 132, 3, 3, 1, 1, 1, 1)
     x, wr, wi = oracle.make_inputs(case, input_seed=21)

@@ -55,8 +55,12 @@ def abi_fprop_planar(case, x, packed, precision=ccv_abi.CCV_PRECISION_TF32, pois
     fill = float("nan") if poison else 0.0
     yr = torch.full((case.n, case.p, case.q, case.k), fill, dtype=torch.float32, device=DEV)
     yi = torch.full_like(yr, fill)
+    ws_bytes = lib.ccv_fprop_planar_workspace_bytes(ctypes.byref(shp), precision)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=DEV)
     ccv_abi.check(lib.ccv_fprop_planar(_ptr(xr), _ptr(xi), _ptr(packed), _ptr(yr), _ptr(yi),
-                                       ctypes.byref(shp), precision, None, 0, _stream()), "fprop_planar")
+                                       ctypes.byref(shp), precision,
+                                       _ptr(ws) if ws_bytes else None, ws_bytes, _stream()),
+                  "fprop_planar")
     torch.cuda.synchronize()
     return oracle.planar_nhwc_to_complex_nchw(yr, yi).cpu()
 
