@@ -259,7 +259,9 @@ size_t ccv_fprop_planar_workspace_bytes(const ccv_conv_shape* shape, int precisi
 size_t ccv_fprop_complex_workspace_bytes(const ccv_conv_shape* shape, int precision) {
   Problem pb;
   if (make_problem(shape, &pb) != CCV_OK) return 0;
-  // fp32 NHWC planes of the input (real, imaginary; 3xTF32: also remainders).
+  // The fused kernel reads complex64 directly; otherwise fp32 NHWC planes of
+  // the input (real, imaginary; 3xTF32: also remainders).
+  if (fused_complex_available(pb, precision)) return 0;
   return (precision == CCV_PRECISION_3XTF32 ? 4 : 2) * plane_bytes_aligned(pb);
 }
 
@@ -316,10 +318,15 @@ int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_co
     return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
   }
   const size_t need = ccv_fprop_complex_workspace_bytes(shape, precision);
-  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) {
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) {
     return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
   }
   if ((rc = check_device()) != CCV_OK) return rc;
+  if (need == 0) {
+    return launch_fprop_fused_complex(static_cast<const float*>(x),
+                                      static_cast<const float*>(w_packed), static_cast<float*>(y),
+                                      pb, precision, reinterpret_cast<cudaStream_t>(stream));
+  }
   const size_t pl = plane_bytes_aligned(pb);
   char* ws = static_cast<char*>(workspace);
   float* xr = reinterpret_cast<float*>(ws);

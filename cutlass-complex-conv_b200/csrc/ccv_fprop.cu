@@ -339,6 +339,55 @@ int launch_kt(int kt, const FpropParams& prm, int grid, cudaStream_t stream) {
 
 }  // namespace
 
+namespace {
+
+enum KernelFamily { kSingleCta = 0, kPairTap = 1, kPairHalo = 2 };
+
+// Kernel family for a problem.  Large problems go to the persistent CTA-pair
+// kernels; small ones (fewer pair tiles than half the SMs) to the single-CTA
+// kernel.  Among the pair kernels, halo reuse serves stride-1 filters unless
+// its one-box tiles compute clearly more rows than the tap kernel's multi-box
+// tiles.  3xTF32 runs only on the pair kernels (they take precision passes).
+// Testing/benchmarking knobs: CCV_FORCE_KERNEL=1|2 pins single-CTA / pair,
+// CCV_HALO=0|1 pins the pair variant.
+KernelFamily choose_family(const Problem& pb, bool split, const Tiling& t, Tiling* th) {
+  const char* force_env = getenv("CCV_FORCE_KERNEL");
+  const int forced = force_env ? atoi(force_env) : 0;
+  const bool use_pair =
+      split || forced == 2 || (forced != 1 && pair_tiles(t) * 2 >= device_sm_count());
+  if (!use_pair) return kSingleCta;
+  const char* halo_env = getenv("CCV_HALO");
+  const int halo_forced = halo_env ? atoi(halo_env) : -1;
+  if (halo_forced != 0 && halo_applicable(pb)) {
+    *th = choose_halo_tiling(pb);
+    const long long rows_tap = static_cast<long long>(t.tiles_m) * t.tiles_n;
+    const long long rows_halo = static_cast<long long>(th->tiles_m) * th->tiles_n;
+    if (halo_forced == 1 || rows_halo * 100 <= rows_tap * 115) return kPairHalo;
+  }
+  return kPairTap;
+}
+
+}  // namespace
+
+bool fused_complex_available(const Problem& pb, int precision) {
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  return choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th) == kPairHalo &&
+         halo_fused_supported(pb, th);
+}
+
+int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
+                               const Problem& pb, int precision, cudaStream_t stream) {
+  const bool split = precision == CCV_PRECISION_3XTF32;
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  if (choose_family(pb, split, t, &th) != kPairHalo || !halo_fused_supported(pb, th)) {
+    return set_error(CCV_ERR_UNSUPPORTED, "no fused complex kernel for this problem");
+  }
+  return launch_fprop_pair_halo(nullptr, nullptr, nullptr, nullptr, xc, split, w_packed, y,
+                                nullptr, pb, th, OUT_COMPLEX_NCHW, stream);
+}
+
 int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                  const float* w_packed, float* y0, float* y1, const Problem& pb, int precision,
                  OutLayout out_layout, cudaStream_t stream) {
@@ -351,30 +400,15 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
     xi_lo = nullptr;
   }
   const Tiling t = choose_tiling(pb);
-  // Large problems go to the persistent CTA-pair kernel; small ones (fewer
-  // pair tiles than half the SMs) to the single-CTA kernel.
-  // CCV_FORCE_KERNEL=1 or 2 pins the family (testing/benchmarking knob).
-  const char* force_env = getenv("CCV_FORCE_KERNEL");
-  const int forced = force_env ? atoi(force_env) : 0;
-  // 3xTF32 runs only on the pair kernels (they take the precision passes).
-  const bool use_pair =
-      split || forced == 2 || (forced != 1 && pair_tiles(t) * 2 >= device_sm_count());
-  if (use_pair) {
-    // Halo reuse for stride-1 filters, unless its one-box tiles compute
-    // clearly more rows than the tap kernel's multi-box tiles.
-    // CCV_HALO=0/1 pins the choice (testing/benchmarking knob).
-    const char* halo_env = getenv("CCV_HALO");
-    const int halo_forced = halo_env ? atoi(halo_env) : -1;
-    if (halo_forced != 0 && halo_applicable(pb)) {
-      const Tiling th = choose_halo_tiling(pb);
-      const long long rows_tap = static_cast<long long>(t.tiles_m) * t.tiles_n;
-      const long long rows_halo = static_cast<long long>(th.tiles_m) * th.tiles_n;
-      if (halo_forced == 1 || rows_halo * 100 <= rows_tap * 115) {
-        return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, w_packed, y0, y1, pb, th, out_layout,
-                                      stream);
-      }
-    }
-    return launch_fprop_pair(xr, xi, xr_lo, xi_lo, w_packed, y0, y1, pb, t, out_layout, stream);
+  Tiling th;
+  switch (choose_family(pb, split, t, &th)) {
+    case kPairHalo:
+      return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, nullptr, split, w_packed, y0, y1, pb,
+                                    th, out_layout, stream);
+    case kPairTap:
+      return launch_fprop_pair(xr, xi, xr_lo, xi_lo, w_packed, y0, y1, pb, t, out_layout, stream);
+    default:
+      break;
   }
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));

@@ -239,7 +239,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     for (int t = cid; t < prm.num_tiles && !skip; t += ncl, ++i) {
       const int buf = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
-      const bool ok = ptx::mbar_wait_bounded(tfull_bar(buf), use & 1u, prm.status, kTimeout);
+      const bool ok = ptx::mbar_wait_bounded_backoff(tfull_bar(buf), use & 1u, prm.status, kTimeout);
       ptx::tc_fence_after();
       if (!ok) flags[1] = 1;
       const int n_tile = t % prm.tiles_n;

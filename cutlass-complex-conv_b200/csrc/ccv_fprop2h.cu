@@ -10,12 +10,18 @@
 // read one slot, so activation bytes per K step drop from 128 rows per plane
 // to (box_p+R-1)*box_q/R.  Weights stream per tap as in the tap kernel.
 // Two rings: A slots (one per (cb, s)) and weight stages (one per tap).
+//
+// IN_COMPLEX: eight extra converter warps per CTA fill the A slots from the
+// complex64 NCHW input (de-interleave + NCHW->K-major transpose in the
+// producer), so forward() needs no separate layout pass; they release each
+// slot to the even CTA's barrier with a cluster-scope release.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <mutex>
 
+#include "ccv_convert.cuh"
 #include "ccv_epilogue.cuh"
 #include "ccv_fprop_common.cuh"
 #include "ccv_internal.h"
@@ -41,8 +47,12 @@ struct CfgH {
   static constexpr int kWStageBytes = 2 * KT * kRowH;
 };
 
-template <int KT, bool OUT_COMPLEX>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsH, 1)
+constexpr int kConvWarps = 8;
+constexpr int kConvUnits = 5;   // (32-row block, channel quad) units per converter lane
+
+template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX>
+__global__ void __cluster_dims__(2, 1, 1)
+    __launch_bounds__(IN_COMPLEX ? kThreadsH + 32 * kConvWarps : kThreadsH, 1)
     ccv_fprop2h_tf32_kernel(const __grid_constant__ FpropParams prm) {
   using C = CfgH<KT>;
   extern __shared__ uint8_t smem_raw[];
@@ -79,7 +89,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsH, 1)
     flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
     flags[1] = 0;
     for (int i = 0; i < SA; ++i) {
-      ptx::mbar_init(afull(i), 1);
+      // Fused complex path: one arrival per converter warp of both CTAs.
+      ptx::mbar_init(afull(i), IN_COMPLEX ? 2 * kConvWarps : 1);
       ptx::mbar_init(aempty(i), 1);
     }
     for (int i = 0; i < SW; ++i) {
@@ -94,10 +105,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsH, 1)
     ptx::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    ptx::prefetch_tmap(&prm.tm_xr);
-    ptx::prefetch_tmap(&prm.tm_xi);
+    if (!IN_COMPLEX) {
+      ptx::prefetch_tmap(&prm.tm_xr);
+      ptx::prefetch_tmap(&prm.tm_xi);
+    }
     ptx::prefetch_tmap(&prm.tm_w);
-    if (prm.passes > 1) {
+    if (!IN_COMPLEX && prm.passes > 1) {
       ptx::prefetch_tmap(&prm.tm_xr_lo);
       ptx::prefetch_tmap(&prm.tm_xi_lo);
     }
@@ -139,18 +152,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsH, 1)
             const int pass = sp - ss * prm.passes;
             const CUtensorMap* mr = pass == 2 ? &prm.tm_xr_lo : &prm.tm_xr;
             const CUtensorMap* mi = pass == 2 ? &prm.tm_xi_lo : &prm.tm_xi;
-            const int slot = static_cast<int>(ga % SA);
-            const uint32_t ph = (ga / SA) & 1u;
-            if (!ptx::mbar_wait_bounded(aempty(slot), ph ^ 1u, prm.status, kTimeoutH) || flags[1]) {
-              flags[1] = 1;
-              abort = true;
-              break;
+            if (!IN_COMPLEX) {
+              const int slot = static_cast<int>(ga % SA);
+              const uint32_t ph = (ga / SA) & 1u;
+              if (!ptx::mbar_wait_bounded(aempty(slot), ph ^ 1u, prm.status, kTimeoutH) ||
+                  flags[1]) {
+                flags[1] = 1;
+                abort = true;
+                break;
+              }
+              if (leader) ptx::mbar_arrive_expect_tx(afull(slot), 2u * prm.a_slot_bytes);
+              const uint32_t fb = ptx::mapa_shared(afull(slot), 0);
+              const uint32_t a_r = a_base + static_cast<uint32_t>(slot * prm.a_slot_bytes);
+              ptx::tma_load_4d_pair(a_r, mr, fb, c0, w0 + ss, h0, img);
+              ptx::tma_load_4d_pair(a_r + a_plane_bytes, mi, fb, c0, w0 + ss, h0, img);
             }
-            if (leader) ptx::mbar_arrive_expect_tx(afull(slot), 2u * prm.a_slot_bytes);
-            const uint32_t fb = ptx::mapa_shared(afull(slot), 0);
-            const uint32_t a_r = a_base + static_cast<uint32_t>(slot * prm.a_slot_bytes);
-            ptx::tma_load_4d_pair(a_r, mr, fb, c0, w0 + ss, h0, img);
-            ptx::tma_load_4d_pair(a_r + a_plane_bytes, mi, fb, c0, w0 + ss, h0, img);
             for (int rr = 0; rr < prm.r; ++rr, ++gw) {
               const int st = static_cast<int>(gw % SW);
               const uint32_t pw_ = (gw / SW) & 1u;
@@ -175,7 +191,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsH, 1)
       }
       if (leader) {
         // Drain: every issued slot and stage (both CTAs) has landed.
-        for (uint32_t j = 0; j < static_cast<uint32_t>(SA) && j < ga; ++j) {
+        for (uint32_t j = 0; !IN_COMPLEX && j < static_cast<uint32_t>(SA) && j < ga; ++j) {
           const uint32_t g = ga - 1 - j;
           ptx::mbar_wait_bounded(afull(static_cast<int>(g % SA)), (g / SA) & 1u, prm.status,
                                  kTimeoutH);
@@ -208,7 +224,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsH, 1)
         for (int cb = 0; cb < ncb && !abort; ++cb) {
           for (int sp = 0; sp < prm.s * prm.passes && !abort; ++sp, ++ga) {
             const int slot = static_cast<int>(ga % SA);
-            if (!ptx::mbar_wait_bounded(afull(slot), (ga / SA) & 1u, prm.status, kTimeoutH)) {
+            if (!ptx::mbar_wait_bounded<IN_COMPLEX>(afull(slot), (ga / SA) & 1u, prm.status,
+                                                    kTimeoutH)) {
               flags[1] = 1;
               abort = true;
               break;
@@ -247,7 +264,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsH, 1)
       ptx::mbar_wait_bounded(done_bar, 0, prm.status, kTimeoutH);
     }
     __syncwarp();
-  } else {
+  } else if (warp <= 5) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
@@ -258,7 +275,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsH, 1)
     for (int t = cid; t < prm.num_tiles && !skip; t += ncl, ++i) {
       const int buf = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
-      const bool ok = ptx::mbar_wait_bounded(tfull(buf), use & 1u, prm.status, kTimeoutH);
+      const bool ok = ptx::mbar_wait_bounded_backoff(tfull(buf), use & 1u, prm.status, kTimeoutH);
       ptx::tc_fence_after();
       if (!ok) flags[1] = 1;
       const int n_tile = t % prm.tiles_n;
@@ -274,6 +291,68 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsH, 1)
     }
   }
 
+  if constexpr (IN_COMPLEX) {
+    if (warp > 5 && !skip) {
+      // ---------------------------------------------------------- converters
+      // Jobs in MMA order: (tile, channel block, filter column, pass).  The
+      // loads of job j+1 are issued before waiting for job j+1's slot.
+      const int wid = warp - 6;
+      const float2* xc = reinterpret_cast<const float2*>(prm.xc);
+      const int jobs_per_tile = ncb * prm.s * prm.passes;
+      auto make_job = [&](int t, int jt, SlotJob& jb) {
+        const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
+        const int gb = min(half, prm.total_boxes - 1);
+        const int img = gb / per_img;
+        const int rem = gb - img * per_img;
+        const int bp = rem / prm.tiles_bq;
+        const int bq = rem - bp * prm.tiles_bq;
+        const int cb = jt / (prm.s * prm.passes);
+        const int sp = jt - cb * (prm.s * prm.passes);
+        const int ss = sp / prm.passes;
+        const int pass = sp - ss * prm.passes;
+        jb.img = img;
+        jb.h0 = bp * prm.box_p - prm.ph;
+        jb.w0 = bq * prm.box_q - prm.pw + ss;
+        jb.c0 = cb * kCH;
+        jb.mode = prm.passes == 1 ? kConvRaw : (pass == 2 ? kConvLo : kConvHi);
+      };
+      int t = cid, jt = 0;
+      SlotJob jb;
+      float2 v[kConvUnits][4];
+      if (t < prm.num_tiles) {
+        make_job(t, jt, jb);
+        slot_job_load(v, jb, xc, prm.c, prm.h, prm.w, prm.halo_rows, prm.box_q_log2, wid,
+                      kConvWarps, lane);
+      }
+      uint32_t ga = 0;
+      while (t < prm.num_tiles) {
+        const int slot = static_cast<int>(ga % SA);
+        if (!ptx::mbar_wait_bounded_backoff(aempty(slot), ((ga / SA) & 1u) ^ 1u, prm.status,
+                                    kTimeoutH) ||
+            flags[1]) {
+          flags[1] = 1;
+          break;
+        }
+        uint8_t* pr = data + slot * prm.a_slot_bytes;
+        slot_job_store(v, jb.mode, prm.halo_rows, pr, pr + a_plane_bytes, wid, kConvWarps,
+                       lane);
+        ptx::fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(afull(slot), 0));
+        ++ga;
+        if (++jt == jobs_per_tile) {
+          jt = 0;
+          t += ncl;
+        }
+        if (t < prm.num_tiles) {
+          make_job(t, jt, jb);
+          slot_job_load(v, jb, xc, prm.c, prm.h, prm.w, prm.halo_rows, prm.box_q_log2, wid,
+                        kConvWarps, lane);
+        }
+      }
+    }
+  }
+
   __syncthreads();
   if (flags[1]) ptx::nanosleep(100000);  // let stray copies of an aborted tile land
   ptx::tc_fence_before();
@@ -284,9 +363,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsH, 1)
   }
 }
 
-template <int KT, bool OUT_COMPLEX>
+template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX>
 int launchh_variant(const FpropParams& prm, int smem_bytes, cudaStream_t stream) {
-  auto kern = ccv_fprop2h_tf32_kernel<KT, OUT_COMPLEX>;
+  auto kern = ccv_fprop2h_tf32_kernel<KT, OUT_COMPLEX, IN_COMPLEX>;
+  constexpr int threads = IN_COMPLEX ? kThreadsH + 32 * kConvWarps : kThreadsH;
   static std::once_flag once[64];
   static int max_clusters[64] = {};
   int dev = 0;
@@ -297,7 +377,7 @@ int launchh_variant(const FpropParams& prm, int smem_bytes, cudaStream_t stream)
     if (err != cudaSuccess) return;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 148, 1, 1);
-    cfg.blockDim = dim3(kThreadsH, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
     cfg.dynamicSmemBytes = 232448;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) {
@@ -309,7 +389,7 @@ int launchh_variant(const FpropParams& prm, int smem_bytes, cudaStream_t stream)
   });
   if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(fprop2h)");
   const int clusters = std::max(1, std::min(prm.num_tiles, max_clusters[dev & 63]));
-  kern<<<2 * clusters, kThreadsH, smem_bytes, stream>>>(prm);
+  kern<<<2 * clusters, threads, smem_bytes, stream>>>(prm);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "fprop2h kernel launch");
   return CCV_OK;
@@ -330,6 +410,11 @@ bool halo_applicable(const Problem& pb) {
   if (pb.sh != 1 || pb.sw != 1 || pb.r * pb.s <= 1 || pb.r > 64 || pb.s > 64) return false;
   const Tiling t = choose_halo_tiling(pb);
   return t.total_boxes > 0 && halo_fits(t, pb.r);
+}
+
+bool halo_fused_supported(const Problem& pb, const Tiling& th) {
+  const int rows = (th.box_p + pb.r - 1) * th.box_q;
+  return ((rows + 31) / 32) * 8 <= kConvUnits * kConvWarps;
 }
 
 Tiling choose_halo_tiling(const Problem& pb) {
@@ -365,9 +450,9 @@ Tiling choose_halo_tiling(const Problem& pb) {
 }
 
 int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
-                           const float* xi_lo, const float* w_packed, float* y0, float* y1,
-                           const Problem& pb, const Tiling& t, OutLayout out_layout,
-                           cudaStream_t stream) {
+                           const float* xi_lo, const float* xc, bool split,
+                           const float* w_packed, float* y0, float* y1, const Problem& pb,
+                           const Tiling& t, OutLayout out_layout, cudaStream_t stream) {
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;
@@ -386,7 +471,11 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
   prm.ksteps = ((pb.c + kCH - 1) / kCH) * pb.r * pb.s;
   prm.m_total = static_cast<long long>(pb.n) * pb.p * pb.q;
   prm.num_tiles = pair_tiles(t);
-  const bool split = xr_lo != nullptr;
+  const bool fused = xc != nullptr;
+  if (fused && !halo_fused_supported(pb, t)) {
+    return set_error(CCV_ERR_UNSUPPORTED, "halo slot too tall for the fused converters");
+  }
+  prm.xc = xc;
   prm.passes = split ? 3 : 1;
   if (!split) {
     xr_lo = xr;
@@ -411,7 +500,7 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
 
   int rc;
   const uint64_t cb = static_cast<uint64_t>(pb.c) * 4;
-  {
+  if (!fused) {
     const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.w),
                               static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
     const uint64_t strides[3] = {cb, cb * pb.w, cb * pb.w * pb.h};
@@ -432,16 +521,25 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
     if ((rc = encode_tiled(&prm.tm_w, w_packed, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
   }
   const bool cplx = out_layout == OUT_COMPLEX_NCHW;
+  if (fused) {
+    // The fused path always writes complex64 NCHW.
+    if (!cplx) return set_error(CCV_ERR_INVALID_ARGUMENT, "fused complex input needs complex output");
+    switch (t.kt) {
+      case 128: return launchh_variant<128, true, true>(prm, smem_bytes, stream);
+      case 64: return launchh_variant<64, true, true>(prm, smem_bytes, stream);
+      default: return launchh_variant<32, true, true>(prm, smem_bytes, stream);
+    }
+  }
   switch (t.kt) {
     case 128:
-      return cplx ? launchh_variant<128, true>(prm, smem_bytes, stream)
-                  : launchh_variant<128, false>(prm, smem_bytes, stream);
+      return cplx ? launchh_variant<128, true, false>(prm, smem_bytes, stream)
+                  : launchh_variant<128, false, false>(prm, smem_bytes, stream);
     case 64:
-      return cplx ? launchh_variant<64, true>(prm, smem_bytes, stream)
-                  : launchh_variant<64, false>(prm, smem_bytes, stream);
+      return cplx ? launchh_variant<64, true, false>(prm, smem_bytes, stream)
+                  : launchh_variant<64, false, false>(prm, smem_bytes, stream);
     default:
-      return cplx ? launchh_variant<32, true>(prm, smem_bytes, stream)
-                  : launchh_variant<32, false>(prm, smem_bytes, stream);
+      return cplx ? launchh_variant<32, true, false>(prm, smem_bytes, stream)
+                  : launchh_variant<32, false, false>(prm, smem_bytes, stream);
   }
 }
 

@@ -16,6 +16,7 @@ struct alignas(64) FpropParams {
   CUtensorMap tm_w;   // packed weights [image][R*S][3][K][C] (image 1 = 3xTF32 remainders)
   CUtensorMap tm_xr_lo;  // 3xTF32: activation remainder planes (x - tf32(x))
   CUtensorMap tm_xi_lo;
+  const float* xc;    // fused complex path: complex64 NCHW input (interleaved)
   float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
   float* y1;          // planar: y_imag (NPQK); complex: unused
   int* status;        // device status word
@@ -102,10 +103,15 @@ int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, cons
 // (box_q a multiple of 8); per 32-channel block the S column-shifted halo
 // copies of the box are loaded once and reused by the R filter rows.
 bool halo_applicable(const Problem& pb);
+// Whether the converter warps of the fused complex path cover one A slot of
+// this halo tiling (their register batch bounds the slot's rows).
+bool halo_fused_supported(const Problem& pb, const Tiling& th);
 Tiling choose_halo_tiling(const Problem& pb);
+// xc non-null: fused complex path (converter warps read complex64 NCHW; the
+// planar pointers are ignored and `split` selects 3xTF32).
 int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
-                           const float* xi_lo, const float* w_packed, float* y0, float* y1,
-                           const Problem& pb, const Tiling& t, OutLayout out_layout,
-                           cudaStream_t stream);
+                           const float* xi_lo, const float* xc, bool split,
+                           const float* w_packed, float* y0, float* y1, const Problem& pb,
+                           const Tiling& t, OutLayout out_layout, cudaStream_t stream);
 
 }  // namespace ccv

@@ -55,6 +55,12 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
                  const float* w_packed, float* y0, float* y1, const Problem& pb, int precision,
                  OutLayout out_layout, cudaStream_t stream);
 
+// Fused complex path: complex64 NCHW in, complex64 NKPQ out, one launch, no
+// workspace.  Available when the problem runs on the halo pair kernel.
+bool fused_complex_available(const Problem& pb, int precision);
+int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
+                               const Problem& pb, int precision, cudaStream_t stream);
+
 // Encodes a tiled tensor map through the driver entry point.
 // `swizzle_bytes` is 64 or 128 (the box's inner extent in bytes).
 int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,

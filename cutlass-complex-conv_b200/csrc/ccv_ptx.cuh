@@ -67,23 +67,74 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with cluster-scope acquire: orders the waiter after writes that
+// other CTAs of the cluster released with mbarrier.arrive.release.cluster.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Makes this thread's generic-proxy shared-memory writes visible to the
+// async proxy (TMA, tcgen05.mma operand reads).
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Wait for the phase with the given parity to complete, for at most
 // CCV_WAIT_TIMEOUT_NS.  On timeout, writes `code` into *status (first error
 // wins) and returns false.
+template <bool CLUSTER_ACQUIRE = false>
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int* status,
                                                   int code) {
+  auto test = [&]() {
+    return CLUSTER_ACQUIRE ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+  };
 #pragma unroll 1
   for (int i = 0; i < 256; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (test()) return true;
   }
   const uint64_t t0 = globaltimer();
 #pragma unroll 1
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (test()) return true;
     if (globaltimer() - t0 > CCV_WAIT_TIMEOUT_NS) {
       if (status != nullptr) atomicCAS(status, 0, code);
       return false;
     }
+  }
+}
+
+// Same bound, for warps off the critical path (epilogue, converters): after
+// a short poll they sleep between tests, leaving issue slots to the
+// single-thread TMA producer and MMA issuer warps of the same SM.
+template <bool CLUSTER_ACQUIRE = false>
+__device__ __forceinline__ bool mbar_wait_bounded_backoff(uint32_t bar, uint32_t parity,
+                                                          int* status, int code) {
+  auto test = [&]() {
+    return CLUSTER_ACQUIRE ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity);
+  };
+#pragma unroll 1
+  for (int i = 0; i < 8; ++i) {
+    if (test()) return true;
+  }
+  const uint64_t t0 = globaltimer();
+  uint32_t ns = 32;
+#pragma unroll 1
+  while (true) {
+    if (test()) return true;
+    if (globaltimer() - t0 > CCV_WAIT_TIMEOUT_NS) {
+      if (status != nullptr) atomicCAS(status, 0, code);
+      return false;
+    }
+    asm volatile("nanosleep.u32 %0;" ::"r"(ns));
+    if (ns < 256) ns <<= 1;
   }
 }
 
