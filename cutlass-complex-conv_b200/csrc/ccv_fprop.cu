@@ -43,7 +43,7 @@ namespace ccv {
 namespace {
 
 constexpr int kThreads = 192;
-constexpr int kBlockC = 16;      // input channels per K step (64-byte rows)
+constexpr int kBlockC = 32;      // input channels per K step (128-byte rows)
 constexpr int kRowBytes = kBlockC * 4;
 constexpr int kABytes = kBlockM * kRowBytes;  // one activation plane per stage
 
@@ -58,7 +58,8 @@ template <int KT>
 struct Cfg {
   static constexpr int kWBytes = 3 * KT * kRowBytes;
   static constexpr int kStageBytes = 2 * kABytes + kWBytes;
-  static constexpr int kStages = KT == 128 ? 5 : (KT == 64 ? 7 : 9);
+  static constexpr int kStages = (200 * 1024) / kStageBytes;  // 2 / 3 / 4 for KT 128 / 64 / 32
+  static_assert(kStages >= 2, "pipeline too shallow");
   static constexpr int kTmemCols = 2 * KT < 32 ? 32 : 2 * KT;
   static constexpr int kBarOffset = kStages * kStageBytes;
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
@@ -115,8 +116,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
 
-  const int n_tile = blockIdx.x % prm.tiles_n;
-  const int m_tile = blockIdx.x / prm.tiles_n;
+  // Split-K: a cluster of `splits` CTAs shares one output tile; CTA `split`
+  // runs K steps [kbeg, kend) and the partial sums are reduced through
+  // distributed shared memory after the mainloop (splits == 1: no cluster).
+  const int splits = prm.splits;
+  const int tile = blockIdx.x / splits;
+  const int split = blockIdx.x - tile * splits;
+  const int kbeg = static_cast<int>(static_cast<long long>(split) * prm.ksteps / splits);
+  const int kend = static_cast<int>(static_cast<long long>(split + 1) * prm.ksteps / splits);
+  const int n_tile = tile % prm.tiles_n;
+  const int m_tile = tile / prm.tiles_n;
   const int k0 = n_tile * KT;
   const int rs = prm.r * prm.s;
 
@@ -126,7 +135,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int t = 0; t < prm.ksteps; ++t) {
+      for (int t = kbeg; t < kend; ++t) {
         if (!ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, prm.status, kTimeoutProducer)) {
           flags[1] = 1;
           break;
@@ -172,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // in flight before the CTA can exit (matters only after an abort).
       const int last = issued;
       for (int j = 0; j < C::kStages && j < last; ++j) {
-        const int t = last - 1 - j;
+        const int t = last - 1 - j;  // issue index (0-based within this CTA)
         const int st = t % C::kStages;
         const uint32_t ph = static_cast<uint32_t>((t / C::kStages) & 1);
         ptx::mbar_wait_bounded(full_bar(st), ph, prm.status, kTimeoutProducer);
@@ -184,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = ptx::idesc_tf32(kBlockM, 2 * KT, false);
       int stage = 0;
       uint32_t phase = 0;
-      for (int t = 0; t < prm.ksteps; ++t) {
+      for (int t = kbeg; t < kend; ++t) {
         if (!ptx::mbar_wait_bounded(full_bar(stage), phase, prm.status, kTimeoutMma)) {
           flags[1] = 1;
           break;
@@ -196,11 +205,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kBlockC / 8; ++kk) {
           const uint32_t koff = kk * 32;
-          const uint64_t da_r = ptx::desc_kmajor_sw64(a_r + koff);
-          const uint64_t da_i = ptx::desc_kmajor_sw64(a_i + koff);
-          const uint64_t db_top = ptx::desc_kmajor_sw64(w_s + KT * kRowBytes + koff);  // [Wr; Wi]
-          const uint64_t db_bot = ptx::desc_kmajor_sw64(w_s + koff);                   // [-Wi; Wr]
-          ptx::mma_tf32_ss(tmem_base, da_r, db_top, idesc, (t | kk) != 0 ? 1u : 0u);
+          const uint64_t da_r = ptx::desc_kmajor_sw128(a_r + koff);
+          const uint64_t da_i = ptx::desc_kmajor_sw128(a_i + koff);
+          const uint64_t db_top = ptx::desc_kmajor_sw128(w_s + KT * kRowBytes + koff);  // [Wr; Wi]
+          const uint64_t db_bot = ptx::desc_kmajor_sw128(w_s + koff);                   // [-Wi; Wr]
+          ptx::mma_tf32_ss(tmem_base, da_r, db_top, idesc, (t != kbeg || kk != 0) ? 1u : 0u);
           ptx::mma_tf32_ss(tmem_base, da_i, db_bot, idesc, 1u);
         }
         ptx::mma_commit(empty_bar(stage));
@@ -252,7 +261,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       valid = valid && (op < prm.p) && (oq < prm.q);
     }
     if (flags[1]) valid = false;
-    if (!skip) {
+    if (!skip && splits > 1) {
+      // Split-K: park this CTA's partial accumulator row in shared memory
+      // (the pipeline buffers are idle now) for the cluster reduction;
+      // 16-byte columns XOR-swizzled by row to spread banks.
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+      float4* part = reinterpret_cast<float4*>(smem) + static_cast<size_t>(row) * (KT / 2);
+#pragma unroll 1
+      for (int ch = 0; ch < 2 * KT; ch += 32) {
+        uint32_t v[32];
+        ptx::tmem_ld_32x32b_x32(t_row + ch, v);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          const int c4 = (ch + j) >> 2;
+          part[c4 ^ (row & 7)] = u4f(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        }
+      }
+    } else if (!skip) {
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
       const long long pix = (static_cast<long long>(img) * prm.p + op) * prm.q + oq;
 #pragma unroll 1
@@ -302,6 +328,82 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   __syncthreads();
+  if (splits > 1) {
+    // ---------------------------------------------------------- cluster reduce
+    // Every partial is parked; CTA `split` sums rows [split*128/S, ...) over
+    // the S partials in rank order (deterministic) and writes them out.
+    ptx::cluster_sync();
+    const int rows_per = kBlockM / splits;
+    const int r0 = split * rows_per;
+    const int quads = KT / 4;
+    const uint32_t part_base = smem_base;
+    const bool do_store = !skip && !flags[1];
+    for (int it = threadIdx.x; it < rows_per * quads; it += kThreads) {
+      const int row = r0 + it / quads;
+      const int q = it - (it / quads) * quads;
+      const uint32_t off_r =
+          static_cast<uint32_t>(row * (KT / 2) + (q ^ (row & 7))) * 16u;
+      const uint32_t off_i =
+          static_cast<uint32_t>(row * (KT / 2) + ((quads + q) ^ (row & 7))) * 16u;
+      // All remote loads first (they overlap), then the sums in rank order.
+      float4 pa[16], pb[16];
+#pragma unroll
+      for (int s2 = 0; s2 < 16; ++s2) {
+        if (s2 < splits) {
+          pa[s2] = ptx::ld_shared_cluster_v4(ptx::mapa_shared(part_base + off_r, s2));
+          pb[s2] = ptx::ld_shared_cluster_v4(ptx::mapa_shared(part_base + off_i, s2));
+        }
+      }
+      float4 sr = make_float4(0.f, 0.f, 0.f, 0.f), si = sr;
+#pragma unroll
+      for (int s2 = 0; s2 < 16; ++s2) {
+        if (s2 < splits) {
+          sr.x += pa[s2].x; sr.y += pa[s2].y; sr.z += pa[s2].z; sr.w += pa[s2].w;
+          si.x += pb[s2].x; si.y += pb[s2].y; si.z += pb[s2].z; si.w += pb[s2].w;
+        }
+      }
+      int img = 0, op = 0, oq = 0;
+      bool valid = do_store;
+      if constexpr (FLAT) {
+        const long long m = static_cast<long long>(m_tile) * kBlockM + row;
+        valid = valid && (m < prm.m_total);
+        const long long pq = static_cast<long long>(prm.p) * prm.q;
+        img = static_cast<int>(m / pq);
+        const long long rem = m - static_cast<long long>(img) * pq;
+        op = static_cast<int>(rem / prm.q);
+        oq = static_cast<int>(rem - static_cast<long long>(op) * prm.q);
+      } else {
+        const int b = row >> prm.box_px_log2;
+        const int local = row & ((1 << prm.box_px_log2) - 1);
+        const int gb = m_tile * prm.nb + b;
+        const int per_img = prm.tiles_bp * prm.tiles_bq;
+        img = gb / per_img;
+        const int rem = gb - img * per_img;
+        const int bp = rem / prm.tiles_bq;
+        const int bq = rem - bp * prm.tiles_bq;
+        op = bp * prm.box_p + (local >> prm.box_q_log2);
+        oq = bq * prm.box_q + (local & ((1 << prm.box_q_log2) - 1));
+        valid = valid && (gb < prm.total_boxes) && (op < prm.p) && (oq < prm.q);
+      }
+      const int kb = k0 + 4 * q;
+      if (!valid || kb >= prm.k) continue;
+      const long long pix = (static_cast<long long>(img) * prm.p + op) * prm.q + oq;
+      if constexpr (!OUT_COMPLEX) {
+        *reinterpret_cast<float4*>(prm.y0 + pix * prm.k + kb) = sr;
+        *reinterpret_cast<float4*>(prm.y1 + pix * prm.k + kb) = si;
+      } else {
+        const long long pq = static_cast<long long>(prm.p) * prm.q;
+        float2* y = reinterpret_cast<float2*>(prm.y0) + static_cast<long long>(img) * prm.k * pq +
+                    static_cast<long long>(op) * prm.q + oq;
+        y[static_cast<long long>(kb) * pq] = make_float2(sr.x, si.x);
+        y[static_cast<long long>(kb + 1) * pq] = make_float2(sr.y, si.y);
+        y[static_cast<long long>(kb + 2) * pq] = make_float2(sr.z, si.z);
+        y[static_cast<long long>(kb + 3) * pq] = make_float2(sr.w, si.w);
+      }
+    }
+    // Keep every partial alive until all CTAs finished reading.
+    ptx::cluster_sync();
+  }
   if (warp == 1) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, C::kTmemCols);
@@ -309,31 +411,81 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
+// Largest power-of-two cluster (<= want) the device can co-schedule for this
+// kernel; 1 if clusters are unavailable.
+template <class K>
+int max_split(K kern, int smem, int want) {
+  for (int s = want; s >= 2; s >>= 1) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(s, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = s;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) return s;
+    cudaGetLastError();
+  }
+  return 1;
+}
+
 template <int KT, bool FLAT, bool OUT_COMPLEX>
-int launch_variant(const FpropParams& prm, int grid, cudaStream_t stream) {
+int launch_variant(FpropParams& prm, int tiles, int want_split, cudaStream_t stream) {
   using C = Cfg<KT>;
   auto kern = ccv_fprop_tf32_kernel<KT, FLAT, OUT_COMPLEX>;
   static std::once_flag once[64];
+  static int split_cap[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&]() {
     attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     C::kSmemBytes);
+    if (attr_err != cudaSuccess) return;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaGetLastError();
+    split_cap[dev & 63] = max_split(kern, C::kSmemBytes, 16);
   });
   if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(fprop)");
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(prm);
+  int splits = 1;
+  while (splits * 2 <= want_split && splits * 2 <= split_cap[dev & 63]) splits *= 2;
+  prm.splits = splits;
+  const long long grid = static_cast<long long>(tiles) * splits;
+  if (grid > 0x7fffffffLL) return set_error(CCV_ERR_UNSUPPORTED, "problem too large for the grid");
+  if (splits == 1) {
+    kern<<<static_cast<int>(grid), kThreads, C::kSmemBytes, stream>>>(prm);
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, prm);
+    if (le != cudaSuccess) return cuda_error(le, "fprop split-K kernel launch");
+  }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "fprop kernel launch");
   return CCV_OK;
 }
 
 template <bool FLAT, bool OUT_COMPLEX>
-int launch_kt(int kt, const FpropParams& prm, int grid, cudaStream_t stream) {
+int launch_kt(int kt, FpropParams& prm, int tiles, int want_split, cudaStream_t stream) {
   switch (kt) {
-    case 128: return launch_variant<128, FLAT, OUT_COMPLEX>(prm, grid, stream);
-    case 64: return launch_variant<64, FLAT, OUT_COMPLEX>(prm, grid, stream);
-    default: return launch_variant<32, FLAT, OUT_COMPLEX>(prm, grid, stream);
+    case 128: return launch_variant<128, FLAT, OUT_COMPLEX>(prm, tiles, want_split, stream);
+    case 64: return launch_variant<64, FLAT, OUT_COMPLEX>(prm, tiles, want_split, stream);
+    default: return launch_variant<32, FLAT, OUT_COMPLEX>(prm, tiles, want_split, stream);
   }
 }
 
@@ -436,8 +588,8 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
     const uint64_t strides[1] = {cb};
     const uint32_t box[2] = {kBlockC, kBlockM};
     const uint32_t es[2] = {1, 1};
-    if ((rc = encode_tiled(&prm.tm_xr, xr, 2, dims, strides, box, es)) != CCV_OK) return rc;
-    if ((rc = encode_tiled(&prm.tm_xi, xi, 2, dims, strides, box, es)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_xr, xr, 2, dims, strides, box, es, 128)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_xi, xi, 2, dims, strides, box, es, 128)) != CCV_OK) return rc;
   } else {
     const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.w),
                               static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
@@ -445,8 +597,8 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
     const uint32_t box[4] = {kBlockC, static_cast<uint32_t>(t.box_q * pb.sw),
                              static_cast<uint32_t>(t.box_p * pb.sh), 1};
     const uint32_t es[4] = {1, static_cast<uint32_t>(pb.sw), static_cast<uint32_t>(pb.sh), 1};
-    if ((rc = encode_tiled(&prm.tm_xr, xr, 4, dims, strides, box, es)) != CCV_OK) return rc;
-    if ((rc = encode_tiled(&prm.tm_xi, xi, 4, dims, strides, box, es)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_xr, xr, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_xi, xi, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
   }
   {
     const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.k), 3,
@@ -454,19 +606,34 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
     const uint64_t strides[3] = {cb, cb * pb.k, cb * pb.k * 3};
     const uint32_t box[4] = {kBlockC, static_cast<uint32_t>(t.kt), 3, 1};
     const uint32_t es[4] = {1, 1, 1, 1};
-    if ((rc = encode_tiled(&prm.tm_w, w_packed, 4, dims, strides, box, es)) != CCV_OK) return rc;
+    if ((rc = encode_tiled(&prm.tm_w, w_packed, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
   }
   const long long grid = static_cast<long long>(t.tiles_m) * t.tiles_n;
   if (grid <= 0 || grid > 0x7fffffffLL) {
     return set_error(CCV_ERR_UNSUPPORTED, "problem too large for the grid");
   }
-  const bool cplx = out_layout == OUT_COMPLEX_NCHW;
-  if (t.flat) {
-    return cplx ? launch_kt<true, true>(t.kt, prm, static_cast<int>(grid), stream)
-                : launch_kt<true, false>(t.kt, prm, static_cast<int>(grid), stream);
+  // Split-K across a cluster when the tiles alone leave most SMs idle: aim
+  // for about one CTA per SM, at most 16 CTAs per tile and one K step each.
+  // CCV_SPLITK=n caps the split (testing/benchmarking knob; 1 disables).
+  int want_split = 1;
+  {
+    const int sms = device_sm_count();
+    const long long per_tile = sms / std::max<long long>(grid, 1);
+    want_split = static_cast<int>(std::min<long long>(std::min<long long>(per_tile, 16),
+                                                      prm.ksteps));
+    const char* env = getenv("CCV_SPLITK");
+    if (env != nullptr) want_split = std::min(want_split, std::max(1, atoi(env)));
+    if (want_split < 2) want_split = 1;
   }
-  return cplx ? launch_kt<false, true>(t.kt, prm, static_cast<int>(grid), stream)
-              : launch_kt<false, false>(t.kt, prm, static_cast<int>(grid), stream);
+  prm.splits = 1;
+  const bool cplx = out_layout == OUT_COMPLEX_NCHW;
+  const int tiles = static_cast<int>(grid);
+  if (t.flat) {
+    return cplx ? launch_kt<true, true>(t.kt, prm, tiles, want_split, stream)
+                : launch_kt<true, false>(t.kt, prm, tiles, want_split, stream);
+  }
+  return cplx ? launch_kt<false, true>(t.kt, prm, tiles, want_split, stream)
+              : launch_kt<false, false>(t.kt, prm, tiles, want_split, stream);
 }
 
 // ------------------------------------------------------------------ self-test

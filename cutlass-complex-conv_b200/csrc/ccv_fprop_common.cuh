@@ -32,6 +32,8 @@ struct alignas(64) FpropParams {
   int halo_rows, a_slots, w_stages, a_slot_bytes, w_stage_bytes;
   // precision passes per K step: 1 (TF32) or 3 (3xTF32: hi*hi, hi*lo, lo*hi)
   int passes;
+  // single-CTA kernel: CTAs per output tile (a cluster splitting the K loop)
+  int splits;
 };
 
 // Tiling of the output pixels: 128-row tiles made of NB boxes of
