@@ -192,6 +192,16 @@ torch::Tensor forward_complex_packed(torch::Tensor x, torch::Tensor w_packed, in
   return y;
 }
 
+// Kernel launches of one forward_complex_packed call: 1 when the fused
+// complex-input kernel serves the problem, 2 with the layout pass.
+int64_t complex_forward_launches(int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t R,
+                                 int64_t S, int64_t stride_h, int64_t stride_w, int64_t pad_h,
+                                 int64_t pad_w, int64_t precision) {
+  ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
+  check_rc(ccv_check_shape(&shp), "shape check");
+  return ccv_fprop_complex_workspace_bytes(&shp, static_cast<int>(precision)) == 0 ? 1 : 2;
+}
+
 int64_t device_status(int64_t device) {
   c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
   int st = 0;
@@ -233,6 +243,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("out_channels"), pybind11::arg("kernel_h"), pybind11::arg("kernel_w"),
         pybind11::arg("stride_h"), pybind11::arg("stride_w"), pybind11::arg("pad_h"),
         pybind11::arg("pad_w"), pybind11::arg("precision"));
+  m.def("complex_forward_launches", &complex_forward_launches, pybind11::arg("n"),
+        pybind11::arg("c"), pybind11::arg("h"), pybind11::arg("w"), pybind11::arg("k"),
+        pybind11::arg("r"), pybind11::arg("s"), pybind11::arg("stride_h"),
+        pybind11::arg("stride_w"), pybind11::arg("pad_h"), pybind11::arg("pad_w"),
+        pybind11::arg("precision"));
   m.def("device_status", &device_status, pybind11::arg("device"));
   m.def("clear_device_status", &clear_device_status, pybind11::arg("device"));
   m.def("selftest_bounded_wait", &selftest_bounded_wait, pybind11::arg("device"));
