@@ -157,7 +157,18 @@ def init_pg(world, backend, device=None):
     import torch.distributed as dist
     if world > 1 and not dist.is_initialized():
         kw = {"device_id": device} if device is not None else {}
-        dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120), **kw)
+        # Keep library banners (e.g. NCCL's version line) off stdout, which
+        # carries only the JSON result line.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group(backend=backend, timeout=datetime.timedelta(seconds=120), **kw)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
 
 
 def max_over_ranks(value, world, device):
