@@ -199,7 +199,10 @@ int64_t complex_forward_launches(int64_t N, int64_t C, int64_t H, int64_t W, int
                                  int64_t pad_w, int64_t precision) {
   ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
   check_rc(ccv_check_shape(&shp), "shape check");
-  return ccv_fprop_complex_workspace_bytes(&shp, static_cast<int>(precision)) == 0 ? 1 : 2;
+  int kernels = 0;
+  check_rc(ccv_fprop_kernel_launches(&shp, static_cast<int>(precision), 1, &kernels),
+           "ccv_fprop_kernel_launches");
+  return kernels;
 }
 
 int64_t device_status(int64_t device) {

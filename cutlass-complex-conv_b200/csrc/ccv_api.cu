@@ -249,20 +249,67 @@ int ccv_prepack_weights(const float* w_real, const float* w_imag, int layout,
                         reinterpret_cast<cudaStream_t>(stream));
 }
 
+namespace {
+
+size_t align256(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+// Workspace a planar call cannot run without: 3xTF32 splits the input planes
+// into TF32 parts and remainders (4 planes).
+size_t planar_required_bytes(const Problem& pb, int precision) {
+  return precision == CCV_PRECISION_3XTF32 ? 4 * plane_bytes_aligned(pb) : 0;
+}
+
+// Workspace a complex call cannot run without: none for the fused kernel
+// (it reads complex64 directly); otherwise fp32 NHWC planes of the input
+// (real, imaginary; 3xTF32: also remainders).
+size_t complex_required_bytes(const Problem& pb, int precision) {
+  if (fused_complex_available(pb, precision)) return 0;
+  return (precision == CCV_PRECISION_3XTF32 ? 4 : 2) * plane_bytes_aligned(pb);
+}
+
+// The part of a caller's workspace past the required bytes, handed to the
+// kernels as stream-K scratch (null when nothing usable is left).
+void split_scratch(void* workspace, size_t workspace_bytes, size_t required, void** ws,
+                   size_t* ws_bytes) {
+  *ws = nullptr;
+  *ws_bytes = 0;
+  if (workspace == nullptr) return;
+  const uintptr_t base = reinterpret_cast<uintptr_t>(workspace);
+  const uintptr_t start = (base + align256(required) + 255) & ~static_cast<uintptr_t>(255);
+  const uintptr_t end = base + workspace_bytes;
+  if (start >= end) return;
+  *ws = reinterpret_cast<void*>(start);
+  *ws_bytes = end - start;
+}
+
+}  // namespace
+
 size_t ccv_fprop_planar_workspace_bytes(const ccv_conv_shape* shape, int precision) {
   Problem pb;
   if (make_problem(shape, &pb) != CCV_OK) return 0;
-  // 3xTF32 splits the input planes into TF32 parts and remainders (4 planes).
-  return precision == CCV_PRECISION_3XTF32 ? 4 * plane_bytes_aligned(pb) : 0;
+  const size_t split = split_workspace_bytes(pb, precision);
+  const size_t req = planar_required_bytes(pb, precision);
+  return split > 0 ? align256(req) + 256 + split : req;
 }
 
 size_t ccv_fprop_complex_workspace_bytes(const ccv_conv_shape* shape, int precision) {
   Problem pb;
   if (make_problem(shape, &pb) != CCV_OK) return 0;
-  // The fused kernel reads complex64 directly; otherwise fp32 NHWC planes of
-  // the input (real, imaginary; 3xTF32: also remainders).
-  if (fused_complex_available(pb, precision)) return 0;
-  return (precision == CCV_PRECISION_3XTF32 ? 4 : 2) * plane_bytes_aligned(pb);
+  const size_t split = split_workspace_bytes(pb, precision);
+  const size_t req = complex_required_bytes(pb, precision);
+  return split > 0 ? align256(req) + 256 + split : req;
+}
+
+size_t ccv_fprop_planar_min_workspace_bytes(const ccv_conv_shape* shape, int precision) {
+  Problem pb;
+  if (make_problem(shape, &pb) != CCV_OK) return 0;
+  return planar_required_bytes(pb, precision);
+}
+
+size_t ccv_fprop_complex_min_workspace_bytes(const ccv_conv_shape* shape, int precision) {
+  Problem pb;
+  if (make_problem(shape, &pb) != CCV_OK) return 0;
+  return complex_required_bytes(pb, precision);
 }
 
 int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_packed,
@@ -281,12 +328,15 @@ int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_pac
       !aligned16(y_imag)) {
     return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
   }
-  const size_t need = ccv_fprop_planar_workspace_bytes(shape, precision);
+  const size_t need = planar_required_bytes(pb, precision);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) {
     return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
   }
   if ((rc = check_device()) != CCV_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  void* sk = nullptr;
+  size_t sk_bytes = 0;
+  split_scratch(workspace, workspace_bytes, need, &sk, &sk_bytes);
   if (precision == CCV_PRECISION_3XTF32) {
     const size_t pl = plane_bytes_aligned(pb);
     char* ws = static_cast<char*>(workspace);
@@ -298,10 +348,10 @@ int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_pac
                              static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c, st);
     if (rc != CCV_OK) return rc;
     return launch_fprop(hr, hi, lr, li, static_cast<const float*>(w_packed), y_real, y_imag, pb,
-                        precision, OUT_PLANAR_NHWC, st);
+                        precision, OUT_PLANAR_NHWC, sk, sk_bytes, st);
   }
   return launch_fprop(x_real, x_imag, nullptr, nullptr, static_cast<const float*>(w_packed),
-                      y_real, y_imag, pb, precision, OUT_PLANAR_NHWC, st);
+                      y_real, y_imag, pb, precision, OUT_PLANAR_NHWC, sk, sk_bytes, st);
 }
 
 int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_conv_shape* shape,
@@ -317,15 +367,19 @@ int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_co
   if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y)) {
     return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
   }
-  const size_t need = ccv_fprop_complex_workspace_bytes(shape, precision);
+  const size_t need = complex_required_bytes(pb, precision);
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) {
     return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
   }
   if ((rc = check_device()) != CCV_OK) return rc;
+  void* sk = nullptr;
+  size_t sk_bytes = 0;
+  split_scratch(workspace, workspace_bytes, need, &sk, &sk_bytes);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (need == 0) {
     return launch_fprop_fused_complex(static_cast<const float*>(x),
                                       static_cast<const float*>(w_packed), static_cast<float*>(y),
-                                      pb, precision, reinterpret_cast<cudaStream_t>(stream));
+                                      pb, precision, sk, sk_bytes, st);
   }
   const size_t pl = plane_bytes_aligned(pb);
   char* ws = static_cast<char*>(workspace);
@@ -334,16 +388,31 @@ int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_co
   const bool split = precision == CCV_PRECISION_3XTF32;
   float* lr = split ? reinterpret_cast<float*>(ws + 2 * pl) : nullptr;
   float* li = split ? reinterpret_cast<float*>(ws + 3 * pl) : nullptr;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   rc = launch_nchw_complex_to_planar(static_cast<const float*>(x), xr, xi, lr, li, pb, st);
   if (rc != CCV_OK) return rc;
   return launch_fprop(xr, xi, lr, li, static_cast<const float*>(w_packed), static_cast<float*>(y),
-                      nullptr, pb, precision, OUT_COMPLEX_NCHW, st);
+                      nullptr, pb, precision, OUT_COMPLEX_NCHW, sk, sk_bytes, st);
+}
+
+int ccv_fprop_kernel_launches(const ccv_conv_shape* shape, int precision, int complex_input,
+                              int* kernels) {
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if (kernels == nullptr) return set_error(CCV_ERR_INVALID_ARGUMENT, "null output pointer");
+  const bool split = precision == CCV_PRECISION_3XTF32;
+  if (complex_input) {
+    *kernels = complex_required_bytes(pb, precision) == 0 ? 1 : 2;
+  } else {
+    *kernels = split ? 2 : 1;
+  }
+  return CCV_OK;
 }
 
 size_t ccv_forward_workspace_bytes(const ccv_conv_shape* shape) {
-  const size_t b = ccv_packed_weight_bytes(shape, CCV_PRECISION_TF32);
-  return (b + 255) & ~static_cast<size_t>(255);
+  const size_t b = align256(ccv_packed_weight_bytes(shape, CCV_PRECISION_TF32));
+  if (b == 0) return 0;
+  return b + ccv_fprop_planar_workspace_bytes(shape, CCV_PRECISION_TF32);
 }
 
 int ccv_forward(const float* x_real, const float* x_imag, const float* w_real_krsc,
@@ -353,14 +422,17 @@ int ccv_forward(const float* x_real, const float* x_imag, const float* w_real_kr
   Problem pb;
   int rc = make_problem(shape, &pb);
   if (rc != CCV_OK) return rc;
-  if (workspace == nullptr || workspace_bytes < ccv_forward_workspace_bytes(shape)) {
+  const size_t packed = align256(ccv_packed_weight_bytes(shape, CCV_PRECISION_TF32));
+  if (workspace == nullptr || workspace_bytes < packed) {
     return set_error(CCV_ERR_WORKSPACE, "workspace missing or too small");
   }
   rc = ccv_prepack_weights(w_real_krsc, w_imag_krsc, CCV_WEIGHT_KRSC, shape, CCV_PRECISION_TF32,
-                           workspace, workspace_bytes, stream);
+                           workspace, packed, stream);
   if (rc != CCV_OK) return rc;
+  // Past the packed weights: optional scratch for the fprop kernels.
+  void* rest = workspace_bytes > packed ? static_cast<char*>(workspace) + packed : nullptr;
   return ccv_fprop_planar(x_real, x_imag, workspace, y_real, y_imag, shape, CCV_PRECISION_TF32,
-                          nullptr, 0, stream);
+                          rest, rest ? workspace_bytes - packed : 0, stream);
 }
 
 int ccv_get_device_status(int* status) {

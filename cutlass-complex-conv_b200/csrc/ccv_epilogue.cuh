@@ -41,50 +41,291 @@ __device__ __forceinline__ bool tile_row_pixel(const FpropParams& prm, int half,
   }
 }
 
-// Reads the accumulator row of this thread (TMEM address `t_acc`: lane of
-// the thread, column 0 of the [re | im] block) in 32-column chunks and stores
-// output channels [k0, k0 + KT) of pixel (img, op, oq).  Every thread of the
-// warp must call this (tcgen05.ld is warp-collective); `valid` masks stores.
-template <int KT, bool OUT_COMPLEX>
-__device__ __forceinline__ void store_accumulator(const FpropParams& prm, uint32_t t_acc, int k0,
-                                                  bool valid, int img, int op, int oq) {
-  const long long pix = (static_cast<long long>(img) * prm.p + op) * prm.q + oq;
-#pragma unroll 1
-  for (int ch = 0; ch < KT; ch += 32) {
-    uint32_t vr[32], vi[32];
-    ptx::tmem_ld_32x32b_x32(t_acc + ch, vr);
-    ptx::tmem_ld_32x32b_x32(t_acc + KT + ch, vi);
-    ptx::tmem_wait_ld();
-    const int kb = k0 + ch;
-    if (!valid || kb >= prm.k) continue;
-    if constexpr (!OUT_COMPLEX) {
-      float* dr = prm.y0 + pix * prm.k + kb;
-      float* di = prm.y1 + pix * prm.k + kb;
+// Stores channels [kb, kb + W) of pixel (img, op, oq) from vr (real) and
+// vi (imaginary) as fp32 NPQK planes or complex64 NKPQ (W % 4 == 0).
+template <bool OUT_COMPLEX, int W>
+__device__ __forceinline__ void store_chunk(const FpropParams& prm, int kb, int img, int op,
+                                            int oq, const uint32_t (&vr)[W],
+                                            const uint32_t (&vi)[W]) {
+  if constexpr (!OUT_COMPLEX) {
+    const long long pix = (static_cast<long long>(img) * prm.p + op) * prm.q + oq;
+    float* dr = prm.y0 + pix * prm.k + kb;
+    float* di = prm.y1 + pix * prm.k + kb;
 #pragma unroll
-      for (int j = 0; j < 32; j += 4) {
-        if (kb + j < prm.k) {
-          *reinterpret_cast<float4*>(dr + j) =
-              make_float4(__uint_as_float(vr[j]), __uint_as_float(vr[j + 1]),
-                          __uint_as_float(vr[j + 2]), __uint_as_float(vr[j + 3]));
-          *reinterpret_cast<float4*>(di + j) =
-              make_float4(__uint_as_float(vi[j]), __uint_as_float(vi[j + 1]),
-                          __uint_as_float(vi[j + 2]), __uint_as_float(vi[j + 3]));
-        }
+    for (int j = 0; j < W; j += 4) {
+      if (kb + j < prm.k) {
+        *reinterpret_cast<float4*>(dr + j) =
+            make_float4(__uint_as_float(vr[j]), __uint_as_float(vr[j + 1]),
+                        __uint_as_float(vr[j + 2]), __uint_as_float(vr[j + 3]));
+        *reinterpret_cast<float4*>(di + j) =
+            make_float4(__uint_as_float(vi[j]), __uint_as_float(vi[j + 1]),
+                        __uint_as_float(vi[j + 2]), __uint_as_float(vi[j + 3]));
       }
-    } else {
-      const long long pq = static_cast<long long>(prm.p) * prm.q;
-      float2* y = reinterpret_cast<float2*>(prm.y0);
-      const long long base =
-          static_cast<long long>(img) * prm.k * pq + static_cast<long long>(op) * prm.q + oq;
+    }
+  } else {
+    const long long pq = static_cast<long long>(prm.p) * prm.q;
+    float2* y = reinterpret_cast<float2*>(prm.y0);
+    const long long base =
+        static_cast<long long>(img) * prm.k * pq + static_cast<long long>(op) * prm.q + oq;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        if (kb + j < prm.k) {
-          y[base + static_cast<long long>(kb + j) * pq] =
-              make_float2(__uint_as_float(vr[j]), __uint_as_float(vi[j]));
-        }
+    for (int j = 0; j < W; ++j) {
+      if (kb + j < prm.k) {
+        y[base + static_cast<long long>(kb + j) * pq] =
+            make_float2(__uint_as_float(vr[j]), __uint_as_float(vi[j]));
       }
     }
   }
+}
+
+// Reads the accumulator row of this thread (TMEM address `t_acc`: lane of
+// the thread, column 0 of the [re | im] block) in CW-column chunks (16 or 32;
+// 16 halves the registers it holds) and stores output channels [k0, k0 + KT)
+// of pixel (img, op, oq).  Every thread of the warp must call this
+// (tcgen05.ld is warp-collective); `valid` masks stores.
+template <int KT, bool OUT_COMPLEX, int CW = 32>
+__device__ __forceinline__ void store_accumulator(const FpropParams& prm, uint32_t t_acc, int k0,
+                                                  bool valid, int img, int op, int oq) {
+#pragma unroll 1
+  for (int ch = 0; ch < KT; ch += CW) {
+    uint32_t vr[CW], vi[CW];
+    ptx::tmem_ld_32x32b<CW>(t_acc + ch, vr);
+    ptx::tmem_ld_32x32b<CW>(t_acc + KT + ch, vi);
+    ptx::tmem_wait_ld();
+    const int kb = k0 + ch;
+    if (!valid || kb >= prm.k) continue;
+    store_chunk<OUT_COMPLEX, CW>(prm, kb, img, op, oq, vr, vi);
+  }
+}
+
+// Epilogue of one piece of a split (stream-K) tile, for the 32 rows of one
+// warp (`quarter`) of CTA `rank`.  The warp writes its TMEM accumulator rows
+// to this piece's partial buffer and adds the piece's slot count to the
+// tile's counter.  The warp that completes the count (all L slots summed;
+// nobody waits for anybody) adds every piece's rows in cluster order - its
+// own taken from TMEM, the others from the partial buffers; the same order
+// whichever piece finishes last, so results are deterministic - and stores
+// the output rows.  Then TMEM is released by an arrival on the MMA CTA's
+// barrier `tempty_remote` (cluster address).  Returns whether this warp
+// stored the tile.
+//
+// Partial buffer layout (per CTA: 128 rows x 2*KT fp32): four 32-row blocks,
+// one per epilogue warp.  A block is a sequence of 8-channel granules; a
+// granule holds four float4 "columns" (re 0-3, re 4-7, im 0-3, im 4-7) and
+// column j of row `lane` sits at float4 index j * 32 + lane.  So a warp
+// moves 512 contiguous bytes per access and any run of granules is one
+// contiguous range (2 KB per granule).
+//
+// The sum is staged through shared memory when the caller hands this warp a
+// free region (`stage`, `stage_bytes`; the kernel's operand buffers after its
+// last unit) and kStageBufs mbarriers from `stage_bar` (8 bytes apart): one
+// bulk copy per other piece brings a run of granules in (as long a run as
+// the region allows, so the copies are large), into a ring of up to
+// kStageBufs buffers.  Otherwise the partial rows are read into registers,
+// two granules per step.
+constexpr int kStageBufs = 16;  // staging ring depth (mbarriers per epilogue warp)
+
+template <int KT, bool OUT_COMPLEX>
+__device__ __noinline__ bool split_piece_epilogue(const FpropParams& prm, WorkUnit w, int cid,
+                                                  int rank, int quarter, int lane, uint32_t t_acc,
+                                                  int k0, bool valid, int img, int op, int oq,
+                                                  uint32_t tempty_remote, uint8_t* stage,
+                                                  uint32_t stage_bytes, uint32_t stage_bar) {
+  static_assert(KT % 16 == 0, "KT");
+  constexpr int kRowF4 = 2 * KT / 4;       // float4 per row
+  constexpr uint32_t kGranBytes = 2048u;   // one granule of a 32-row block
+  float4* ws4 = reinterpret_cast<float4*>(prm.split_ws);
+  // float4 index of column 0 of granule 0, row 0 of cluster g's block.
+  auto block0 = [&](int g) {
+    return sk_partial_index(prm, g, w.sk, rank) * (static_cast<long long>(kBlockM) * kRowF4) +
+           static_cast<long long>(quarter) * 32 * kRowF4;
+  };
+  {
+    float4* dst = ws4 + block0(cid) + lane;
+#pragma unroll 1
+    for (int ch = 0; ch < KT; ch += 16) {
+      uint32_t vr[16], vi[16];
+      ptx::tmem_ld_32x32b_x16(t_acc + ch, vr);
+      ptx::tmem_ld_32x32b_x16(t_acc + KT + ch, vi);
+      ptx::tmem_wait_ld();
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float4* gd = dst + ((ch / 8 + h) * 4) * 32;
+        const uint32_t* r = vr + 8 * h;
+        const uint32_t* m = vi + 8 * h;
+        __stcg(gd, make_float4(__uint_as_float(r[0]), __uint_as_float(r[1]),
+                               __uint_as_float(r[2]), __uint_as_float(r[3])));
+        __stcg(gd + 32, make_float4(__uint_as_float(r[4]), __uint_as_float(r[5]),
+                                    __uint_as_float(r[6]), __uint_as_float(r[7])));
+        __stcg(gd + 64, make_float4(__uint_as_float(m[0]), __uint_as_float(m[1]),
+                                    __uint_as_float(m[2]), __uint_as_float(m[3])));
+        __stcg(gd + 96, make_float4(__uint_as_float(m[4]), __uint_as_float(m[5]),
+                                    __uint_as_float(m[6]), __uint_as_float(m[7])));
+      }
+    }
+  }
+  // Publish this warp's rows, then count its slots.
+  __threadfence();
+  __syncwarp();
+  unsigned old = 0;
+  if (lane == 0) {
+    unsigned* cnt = prm.split_count + (static_cast<long long>(w.sk) * 2 + rank) * 4 + quarter;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
+                 : "=r"(old)
+                 : "l"(cnt), "r"(static_cast<unsigned>(w.jend - w.jbeg))
+                 : "memory");
+  }
+  old = __shfl_sync(0xffffffffu, old, 0);
+  const bool last =
+      old + static_cast<unsigned>(w.jend - w.jbeg) == static_cast<unsigned>(prm.slots_per_tile);
+  if (last) {
+    __threadfence();
+    int g0 = 0, g1 = 0;
+    sk_tile_clusters(prm, w.sk, g0, g1);
+    const int ng = g1 - g0 + 1;
+    const int ngran = min(KT / 8, (prm.k - k0 + 7) / 8);  // granules with output channels
+    // Largest run of granules per copy with at least two buffers in the
+    // region (or one buffer holding every granule).
+    int run = 0, nbuf = 0;
+    if (stage != nullptr && ng > 1) {
+      for (int cand = ngran; cand >= 1; cand = cand > 1 ? (cand + 1) / 2 : 0) {
+        const uint32_t per_buf = static_cast<uint32_t>(ng - 1) * cand * kGranBytes;
+        const int nchunk = (ngran + cand - 1) / cand;
+        const int fit = min(kStageBufs, static_cast<int>(stage_bytes / per_buf));
+        if (fit >= min(nchunk, 2)) {
+          run = cand;
+          nbuf = min(fit, nchunk);
+          break;
+        }
+        if (cand == 1) break;
+      }
+    }
+    if (run > 0) {
+      const uint32_t per_buf = static_cast<uint32_t>(ng - 1) * run * kGranBytes;
+      const int nchunk = (ngran + run - 1) / run;
+      const uint32_t s_base = ptx::smem_u32(stage);
+      // Chunk k (granules k*run ..) goes to buffer k % nbuf.
+      auto issue = [&](int k) {
+        if (lane == 0) {
+          const int b = k % nbuf;
+          const uint32_t bar = stage_bar + 8u * static_cast<uint32_t>(b);
+          // First fill: order the counter acquire (generic proxy) before the
+          // copies' global reads.  Refills: order this warp's shared reads of
+          // the buffer before the copies' writes (shared only: a global
+          // proxy fence would also wait for the output stores in flight).
+          if (k < nbuf) {
+            if (k == 0) ptx::fence_proxy_async_all();
+          } else {
+            ptx::fence_proxy_async_shared();
+          }
+          const int q0 = k * run;
+          const int nq = min(run, ngran - q0);
+          const uint32_t bytes = static_cast<uint32_t>(nq) * kGranBytes;
+          ptx::mbar_arrive_expect_tx(bar, static_cast<uint32_t>(ng - 1) * bytes);
+          uint32_t dst = s_base + static_cast<uint32_t>(b) * per_buf;
+          for (int g = g0; g <= g1; ++g) {
+            if (g == cid) continue;
+            ptx::bulk_load(dst, ws4 + block0(g) + q0 * 128, bytes, bar);
+            dst += static_cast<uint32_t>(run) * kGranBytes;
+          }
+        }
+      };
+      for (int k = 0; k < nbuf; ++k) issue(k);
+#pragma unroll 1
+      for (int k = 0; k < nchunk; ++k) {
+        const int b = k % nbuf;
+        if (!ptx::mbar_wait_bounded_backoff(stage_bar + 8u * static_cast<uint32_t>(b),
+                                            static_cast<uint32_t>(k / nbuf) & 1u, prm.status,
+                                            CCV_ERR_DEVICE_TIMEOUT)) {
+          break;
+        }
+        const int q0 = k * run;
+        const int nq = min(run, ngran - q0);
+        const uint8_t* bufp = stage + static_cast<uint32_t>(b) * per_buf;
+#pragma unroll 1
+        for (int q = 0; q < nq; ++q) {
+          const int ch = 8 * (q0 + q);
+          uint32_t vr[8], vi[8];
+          int o = 0;
+#pragma unroll 1
+          for (int g = g0; g <= g1; ++g) {
+            uint32_t ar[8], ai[8];
+            if (g == cid) {
+              ptx::tmem_ld_32x32b_x8(t_acc + ch, ar);
+              ptx::tmem_ld_32x32b_x8(t_acc + KT + ch, ai);
+              ptx::tmem_wait_ld();
+            } else {
+              const float4* sp = reinterpret_cast<const float4*>(
+                  bufp + static_cast<uint32_t>(o) * run * kGranBytes + q * kGranBytes);
+              ++o;
+              const float4 a0 = sp[lane], a1 = sp[32 + lane], b0 = sp[64 + lane],
+                           b1 = sp[96 + lane];
+              const float fa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+              const float fb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                ar[e] = __float_as_uint(fa[e]);
+                ai[e] = __float_as_uint(fb[e]);
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              vr[e] = g == g0 ? ar[e]
+                              : __float_as_uint(__uint_as_float(vr[e]) + __uint_as_float(ar[e]));
+              vi[e] = g == g0 ? ai[e]
+                              : __float_as_uint(__uint_as_float(vi[e]) + __uint_as_float(ai[e]));
+            }
+          }
+          if (valid) store_chunk<OUT_COMPLEX, 8>(prm, k0 + ch, img, op, oq, vr, vi);
+        }
+        // Every lane is done with this buffer before it is refilled.
+        __syncwarp();
+        if (k + nbuf < nchunk) issue(k + nbuf);
+      }
+    } else {
+      // Register path: two granules (16 channels) per step.
+#pragma unroll 1
+      for (int ch = 0; ch < 8 * ngran; ch += 16) {
+        uint32_t vr[16], vi[16];
+#pragma unroll 1
+        for (int g = g0; g <= g1; ++g) {
+          uint32_t ar[16], ai[16];
+          if (g == cid) {
+            ptx::tmem_ld_32x32b_x16(t_acc + ch, ar);
+            ptx::tmem_ld_32x32b_x16(t_acc + KT + ch, ai);
+            ptx::tmem_wait_ld();
+          } else {
+            const float4* src = ws4 + block0(g) + lane + (ch / 8) * 128;
+            float4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + j * 32);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const float4 a0 = v[4 * h], a1 = v[4 * h + 1], b0 = v[4 * h + 2], b1 = v[4 * h + 3];
+              const float fa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+              const float fb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                ar[8 * h + e] = __float_as_uint(fa[e]);
+                ai[8 * h + e] = __float_as_uint(fb[e]);
+              }
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            vr[e] = g == g0 ? ar[e]
+                            : __float_as_uint(__uint_as_float(vr[e]) + __uint_as_float(ar[e]));
+            vi[e] = g == g0 ? ai[e]
+                            : __float_as_uint(__uint_as_float(vi[e]) + __uint_as_float(ai[e]));
+          }
+        }
+        if (valid) store_chunk<OUT_COMPLEX, 16>(prm, k0 + ch, img, op, oq, vr, vi);
+      }
+    }
+  }
+  ptx::tc_fence_before();
+  __syncwarp();
+  if (lane == 0) ptx::mbar_arrive_cluster(tempty_remote);
+  return last;
 }
 
 }  // namespace ccv

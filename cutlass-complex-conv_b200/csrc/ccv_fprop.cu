@@ -521,6 +521,23 @@ KernelFamily choose_family(const Problem& pb, bool split, const Tiling& t, Tilin
 
 }  // namespace
 
+size_t split_workspace_bytes(const Problem& pb, int precision) {
+  const bool split = precision == CCV_PRECISION_3XTF32;
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  const int passes = split ? 3 : 1;
+  switch (choose_family(pb, split, t, &th)) {
+    case kPairHalo:
+      return pair_split_workspace_bytes(th.kt, pair_tiles(th),
+                                        ((pb.c + kBlockC - 1) / kBlockC) * pb.s * passes);
+    case kPairTap:
+      return pair_split_workspace_bytes(t.kt, pair_tiles(t),
+                                        ((pb.c + kBlockC - 1) / kBlockC) * pb.r * pb.s * passes);
+    default:
+      return 0;
+  }
+}
+
 bool fused_complex_available(const Problem& pb, int precision) {
   const Tiling t = choose_tiling(pb);
   Tiling th;
@@ -529,7 +546,8 @@ bool fused_complex_available(const Problem& pb, int precision) {
 }
 
 int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
-                               const Problem& pb, int precision, cudaStream_t stream) {
+                               const Problem& pb, int precision, void* ws, size_t ws_bytes,
+                               cudaStream_t stream) {
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;
@@ -537,12 +555,12 @@ int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
     return set_error(CCV_ERR_UNSUPPORTED, "no fused complex kernel for this problem");
   }
   return launch_fprop_pair_halo(nullptr, nullptr, nullptr, nullptr, xc, split, w_packed, y,
-                                nullptr, pb, th, OUT_COMPLEX_NCHW, stream);
+                                nullptr, pb, th, OUT_COMPLEX_NCHW, ws, ws_bytes, stream);
 }
 
 int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                  const float* w_packed, float* y0, float* y1, const Problem& pb, int precision,
-                 OutLayout out_layout, cudaStream_t stream) {
+                 OutLayout out_layout, void* ws, size_t ws_bytes, cudaStream_t stream) {
   const bool split = precision == CCV_PRECISION_3XTF32;
   if (split && (xr_lo == nullptr || xi_lo == nullptr)) {
     return set_error(CCV_ERR_INVALID_ARGUMENT, "3xTF32 needs the activation remainder planes");
@@ -556,9 +574,10 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
   switch (choose_family(pb, split, t, &th)) {
     case kPairHalo:
       return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, nullptr, split, w_packed, y0, y1, pb,
-                                    th, out_layout, stream);
+                                    th, out_layout, ws, ws_bytes, stream);
     case kPairTap:
-      return launch_fprop_pair(xr, xi, xr_lo, xi_lo, w_packed, y0, y1, pb, t, out_layout, stream);
+      return launch_fprop_pair(xr, xi, xr_lo, xi_lo, w_packed, y0, y1, pb, t, out_layout, ws,
+                               ws_bytes, stream);
     default:
       break;
   }

@@ -48,8 +48,11 @@ struct Cfg2 {
   static constexpr int kAccCols = 2 * KT;                // [re | im]
   static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;
   static constexpr int kBarOffset = kStages * kStageBytes;
-  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;
+  static constexpr int kBarBytes = 1024;
+  static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
   static_assert(kStages >= 3, "pipeline too shallow");
+  static_assert((2 * kStages + 8 + 4 * kStageBufs) * 8 <= kBarBytes, "barrier block overflow");
+  static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
 template <int KT, bool FLAT, bool OUT_COMPLEX>
@@ -60,7 +63,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
-  // full[S] (even CTA), empty[S], tfull[2], tempty[2] (even CTA), done
+  // full[S] (even CTA), empty[S], tfull[2], tempty[2] (even CTA), done, the
+  // TMEM address and flags, then 4 * kStageBufs staging barriers from slot 2S+8.
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * C::kStages + 5);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [0] skip, [1] abort
 
@@ -77,6 +81,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   auto tfull_bar = [&](int b) { return bar_base + 8u * (2 * C::kStages + b); };
   auto tempty_bar = [&](int b) { return bar_base + 8u * (2 * C::kStages + 2 + b); };
   const uint32_t done_bar = bar_base + 8u * (2 * C::kStages + 4);
+  // kStageBufs per epilogue warp: staging of a split tile's sum after the
+  // last unit.
+  const uint32_t stage_bar0 = bar_base + 8u * (2 * C::kStages + 8);
 
   if (threadIdx.x == 0) {
     flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
@@ -90,6 +97,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       ptx::mbar_init(tempty_bar(b), 8);  // 4 epilogue warps x 2 CTAs
     }
     ptx::mbar_init(done_bar, 1);
+    for (int i = 0; i < 4 * kStageBufs; ++i) ptx::mbar_init(stage_bar0 + 8u * i, 1);
     ptx::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -118,11 +126,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     if (lane == 0 && !skip) {
       uint32_t g = 0;
       bool abort = false;
-      for (int t = cid; t < prm.num_tiles && !abort; t += ncl) {
+      UnitCursor cur = unit_cursor(prm, cid);
+      WorkUnit wu;
+      while (!abort && next_unit(prm, ncl, cur, wu)) {
+        const int t = wu.tile;
         const int n_tile = t % prm.tiles_n;
         const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
         const int k0 = n_tile * KT;
-        for (int v = 0; v < prm.ksteps * prm.passes; ++v, ++g) {
+        for (int v = wu.jbeg; v < wu.jend; ++v, ++g) {
           const int ks = v / prm.passes;
           const int pass = v - ks * prm.passes;
           const CUtensorMap* mr = pass == 2 ? &prm.tm_xr_lo : &prm.tm_xr;
@@ -188,16 +199,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       uint32_t g = 0;
       int i = 0;
       bool abort = false;
-      for (int t = cid; t < prm.num_tiles && !abort; t += ncl, ++i) {
+      UnitCursor cur = unit_cursor(prm, cid);
+      WorkUnit wu;
+      while (!abort && next_unit(prm, ncl, cur, wu)) {
         const int buf = i & 1;
         const uint32_t use = static_cast<uint32_t>(i >> 1);
+        ++i;
         if (!ptx::mbar_wait_bounded(tempty_bar(buf), (use & 1u) ^ 1u, prm.status, kTimeout)) {
           flags[1] = 1;
           break;
         }
         ptx::tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(buf * C::kAccCols);
-        for (int ks = 0; ks < prm.ksteps * prm.passes; ++ks, ++g) {
+        for (int ks = wu.jbeg; ks < wu.jend; ++ks, ++g) {
           const int stage = static_cast<int>(g % C::kStages);
           const uint32_t phase = (g / C::kStages) & 1u;
           if (!ptx::mbar_wait_bounded(full_bar(stage), phase, prm.status, kTimeout)) {
@@ -215,7 +229,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             const uint32_t koff = kk * 32;
             ptx::mma_tf32_pair(d, ptx::desc_kmajor_sw128(a_r + koff),
                                ptx::desc_kmajor_sw128(w_x + koff), idesc,
-                               (ks | kk) != 0 ? 1u : 0u);
+                               (ks != wu.jbeg || kk != 0) ? 1u : 0u);
             ptx::mma_tf32_pair(d, ptx::desc_kmajor_sw128(a_i + koff),
                                ptx::desc_kmajor_sw128(w_y + koff), idesc, 1u);
           }
@@ -236,22 +250,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     const uint32_t tempty_leader0 = ptx::mapa_shared(tempty_bar(0), 0);
     const uint32_t tempty_leader1 = ptx::mapa_shared(tempty_bar(1), 0);
     int i = 0;
-    for (int t = cid; t < prm.num_tiles && !skip; t += ncl, ++i) {
+    UnitCursor cur = unit_cursor(prm, cid);
+    WorkUnit wu;
+    while (!skip && next_unit(prm, ncl, cur, wu)) {
       const int buf = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
+      ++i;
       const bool ok = ptx::mbar_wait_bounded_backoff(tfull_bar(buf), use & 1u, prm.status, kTimeout);
       ptx::tc_fence_after();
       if (!ok) flags[1] = 1;
+      const int t = wu.tile;
       const int n_tile = t % prm.tiles_n;
       const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
       int img = 0, op = 0, oq = 0;
-      const bool valid = tile_row_pixel<FLAT>(prm, half, row, img, op, oq) && ok && !flags[1];
-      store_accumulator<KT, OUT_COMPLEX>(prm, t_row + static_cast<uint32_t>(buf * C::kAccCols),
-                                         n_tile * KT, valid, img, op, oq);
-      // This warp is done with the accumulator buffer: release it to the MMA.
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive_cluster(buf == 0 ? tempty_leader0 : tempty_leader1);
+      const bool in_tile = tile_row_pixel<FLAT>(prm, half, row, img, op, oq);
+      const uint32_t t_acc = t_row + static_cast<uint32_t>(buf * C::kAccCols);
+      const uint32_t t_free = buf == 0 ? tempty_leader0 : tempty_leader1;
+      if (wu.split && ok && !flags[1]) {
+        // After the cluster's last unit the pipeline stages are idle: they
+        // stage the split tile's partial sums.
+        const bool final_unit = cursor_done(prm, cur);
+        constexpr uint32_t per_warp = (static_cast<uint32_t>(C::kBarOffset) / 4u) & ~127u;
+        split_piece_epilogue<KT, OUT_COMPLEX>(
+            prm, wu, cid, static_cast<int>(rank), quarter, lane, t_acc, n_tile * KT, in_tile, img,
+            op, oq, t_free, final_unit ? smem + quarter * per_warp : nullptr, per_warp,
+            stage_bar0 + 8u * kStageBufs * static_cast<uint32_t>(quarter));
+      } else {
+        store_accumulator<KT, OUT_COMPLEX>(prm, t_acc, n_tile * KT, in_tile && ok && !flags[1],
+                                           img, op, oq);
+        // This warp is done with the accumulator buffer: release it to the MMA.
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(t_free);
+      }
       if (!ok) break;
     }
   }
@@ -267,7 +298,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
 }
 
 template <int KT, bool FLAT, bool OUT_COMPLEX>
-int launch2_variant(const FpropParams& prm, cudaStream_t stream) {
+int launch2_variant(FpropParams& prm, void* ws, size_t ws_bytes, cudaStream_t stream) {
   using C = Cfg2<KT>;
   auto kern = ccv_fprop2_tf32_kernel<KT, FLAT, OUT_COMPLEX>;
   static std::once_flag once[64];
@@ -291,19 +322,23 @@ int launch2_variant(const FpropParams& prm, cudaStream_t stream) {
     }
   });
   if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(fprop2)");
-  const int clusters = std::max(1, std::min(prm.num_tiles, max_clusters[dev & 63]));
-  kern<<<2 * clusters, kThreads2, C::kSmemBytes, stream>>>(prm);
+  const int clusters = cluster_cap(max_clusters[dev & 63]);
+  int rc;
+  const int launched = launch_clusters(prm, clusters, prm.ksteps * prm.passes, KT, ws, ws_bytes,
+                                       stream, &rc);
+  if (rc != CCV_OK) return rc;
+  kern<<<2 * launched, kThreads2, C::kSmemBytes, stream>>>(prm);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "fprop2 kernel launch");
   return CCV_OK;
 }
 
 template <bool FLAT, bool OUT_COMPLEX>
-int launch2_kt(int kt, const FpropParams& prm, cudaStream_t stream) {
+int launch2_kt(int kt, FpropParams& prm, void* ws, size_t ws_bytes, cudaStream_t stream) {
   switch (kt) {
-    case 128: return launch2_variant<128, FLAT, OUT_COMPLEX>(prm, stream);
-    case 64: return launch2_variant<64, FLAT, OUT_COMPLEX>(prm, stream);
-    default: return launch2_variant<32, FLAT, OUT_COMPLEX>(prm, stream);
+    case 128: return launch2_variant<128, FLAT, OUT_COMPLEX>(prm, ws, ws_bytes, stream);
+    case 64: return launch2_variant<64, FLAT, OUT_COMPLEX>(prm, ws, ws_bytes, stream);
+    default: return launch2_variant<32, FLAT, OUT_COMPLEX>(prm, ws, ws_bytes, stream);
   }
 }
 
@@ -311,9 +346,91 @@ int launch2_kt(int kt, const FpropParams& prm, cudaStream_t stream) {
 
 int pair_tiles(const Tiling& t) { return ((t.tiles_m + 1) / 2) * t.tiles_n; }
 
+namespace {
+constexpr int kMinSkSlots = 2;  // K slots per stream-K range, at least
+
+size_t partial_bytes(int clusters, int kt) {
+  // Two partial buffers per cluster (first and last unit of its range), one
+  // per CTA of the pair, 128 rows x 2*KT fp32 each.
+  return static_cast<size_t>(clusters) * 2 * 2 * kBlockM * 2 * kt * sizeof(float);
+}
+}  // namespace
+
+size_t pair_split_workspace_bytes(int kt, int tiles, int slots) {
+  const int g = std::max(1, device_sm_count() / 2);
+  const long long r = std::min<long long>(tiles, g);  // stream-K tiles, at most
+  const long long gs = std::min<long long>(g, r * slots / kMinSkSlots);
+  if (gs < 2) return 0;
+  // Counters: per stream-K tile x 2 CTAs x 4 epilogue warps.
+  return partial_bytes(static_cast<int>(gs), kt) + static_cast<size_t>(r) * 8 * sizeof(unsigned);
+}
+
+int cluster_cap(int max_clusters) {
+  // CCV_MAX_CLUSTERS=n caps the persistent grid (testing knob: exercises the
+  // stream-K split on small problems).
+  const char* env = getenv("CCV_MAX_CLUSTERS");
+  if (env != nullptr && atoi(env) > 0) return std::min(max_clusters, atoi(env));
+  return max_clusters;
+}
+
+int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes) {
+  prm.slots_per_tile = slots;
+  prm.sk_start = prm.num_tiles;
+  prm.sk_slots = 0;
+  prm.sk_clusters = 1;
+  prm.split_ws = nullptr;
+  prm.split_count = nullptr;
+  // CCV_STREAMK=0 disables the split, =1 takes it whenever it is possible
+  // (testing knob); by default the model below decides.
+  const char* env = getenv("CCV_STREAMK");
+  const int mode = env ? atoi(env) : -1;
+  if (mode == 0 || ws == nullptr || clusters < 2 || slots < kMinSkSlots) return 0;
+  const int T = prm.num_tiles;
+  const int r = T % clusters;
+  if (r == 0) return 0;
+  const long long X = static_cast<long long>(r) * slots;
+  if (X > 0x7fffffffLL) return 0;
+  const int gs = static_cast<int>(std::min<long long>(clusters, X / kMinSkSlots));
+  if (gs < 2) return 0;
+  const long long per_range = (X + gs - 1) / gs;
+  // Default: split when the slot-count model saves at least 10% of the
+  // kernel (whole tiles: (q + 1) * L slot times on the busiest cluster;
+  // split: q * L + per_range).  Below that the partial sums' traffic and
+  // the unit switches eat the gain (measured on B200).
+  const long long q = T / clusters;
+  const long long dp_time = (q + 1) * slots;
+  const long long sk_time = q * slots + per_range;
+  if (mode != 1 && (slots < 4 || (dp_time - sk_time) * 10 < dp_time)) return 0;
+  const size_t pbytes = partial_bytes(gs, kt);
+  const size_t cbytes = static_cast<size_t>(r) * 8 * sizeof(unsigned);
+  if (ws_bytes < pbytes + cbytes || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return 0;
+  prm.sk_start = T - r;
+  prm.sk_slots = X;
+  prm.sk_clusters = gs;
+  prm.split_ws = static_cast<float*>(ws);
+  prm.split_count = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + pbytes);
+  return r * 8;
+}
+
+int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
+                    cudaStream_t stream, int* rc) {
+  *rc = CCV_OK;
+  clusters = std::max(1, clusters);
+  const int counters = plan_stream_k(prm, clusters, slots, kt, ws, ws_bytes);
+  if (counters > 0) {
+    const cudaError_t e =
+        cudaMemsetAsync(prm.split_count, 0, static_cast<size_t>(counters) * sizeof(unsigned),
+                        stream);
+    if (e != cudaSuccess) *rc = cuda_error(e, "cudaMemsetAsync(stream-K counters)");
+    return clusters;
+  }
+  return std::max(1, std::min(prm.num_tiles, clusters));
+}
+
 int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                       const float* w_packed, float* y0, float* y1, const Problem& pb,
-                      const Tiling& t, OutLayout out_layout, cudaStream_t stream) {
+                      const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
+                      cudaStream_t stream) {
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;
@@ -373,11 +490,11 @@ int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, cons
   }
   const bool cplx = out_layout == OUT_COMPLEX_NCHW;
   if (t.flat) {
-    return cplx ? launch2_kt<true, true>(t.kt, prm, stream)
-                : launch2_kt<true, false>(t.kt, prm, stream);
+    return cplx ? launch2_kt<true, true>(t.kt, prm, ws, ws_bytes, stream)
+                : launch2_kt<true, false>(t.kt, prm, ws, ws_bytes, stream);
   }
-  return cplx ? launch2_kt<false, true>(t.kt, prm, stream)
-              : launch2_kt<false, false>(t.kt, prm, stream);
+  return cplx ? launch2_kt<false, true>(t.kt, prm, ws, ws_bytes, stream)
+              : launch2_kt<false, false>(t.kt, prm, ws, ws_bytes, stream);
 }
 
 }  // namespace ccv

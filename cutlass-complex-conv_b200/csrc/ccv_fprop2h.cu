@@ -37,6 +37,7 @@ constexpr int kRowH = kCH * 4;        // 128-byte rows
 constexpr int kMaxASlots = 4;
 constexpr int kMaxWStages = 8;
 constexpr int kBarBytes = 1024;       // barrier block at the start of the carve-out
+static_assert(8 * (32 + 4 * kStageBufs) <= kBarBytes, "barrier block overflow");
 constexpr int kSmemDataBudget = 232448 - kBarBytes - 1024;  // minus alignment slack
 constexpr int kTimeoutH = CCV_ERR_DEVICE_TIMEOUT;
 
@@ -59,7 +60,8 @@ __global__ void __cluster_dims__(2, 1, 1)
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(base);
-  // afull[4], aempty[4], wfull[8], wempty[8], tfull[2], tempty[2], done
+  // afull[4], aempty[4], wfull[8], wempty[8], tfull[2], tempty[2], done,
+  // then the TMEM address and flags; staging barriers from slot 32.
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 29);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [0] skip, [1] abort
   uint8_t* data = base + kBarBytes;
@@ -78,6 +80,9 @@ __global__ void __cluster_dims__(2, 1, 1)
   auto tfull = [&](int b) { return bar_base + 8u * (2 * kMaxASlots + 2 * kMaxWStages + b); };
   auto tempty = [&](int b) { return bar_base + 8u * (2 * kMaxASlots + 2 * kMaxWStages + 2 + b); };
   const uint32_t done_bar = bar_base + 8u * (2 * kMaxASlots + 2 * kMaxWStages + 4);
+  // kStageBufs per epilogue warp: staging of a split tile's sum after the
+  // last unit.
+  const uint32_t stage_bar0 = bar_base + 8u * 32;
 
   const int SA = prm.a_slots;
   const int SW = prm.w_stages;
@@ -102,6 +107,7 @@ __global__ void __cluster_dims__(2, 1, 1)
       ptx::mbar_init(tempty(b), 8);  // 4 epilogue warps x 2 CTAs
     }
     ptx::mbar_init(done_bar, 1);
+    for (int i = 0; i < 4 * kStageBufs; ++i) ptx::mbar_init(stage_bar0 + 8u * i, 1);
     ptx::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -124,15 +130,18 @@ __global__ void __cluster_dims__(2, 1, 1)
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
-  const int ncb = (prm.c + kCH - 1) / kCH;
   const int per_img = prm.tiles_bp * prm.tiles_bq;
+  const int sp_per_cb = prm.s * prm.passes;  // K slots per 32-channel block
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && !skip) {
       uint32_t ga = 0, gw = 0;
       bool abort = false;
-      for (int t = cid; t < prm.num_tiles && !abort; t += ncl) {
+      UnitCursor cur = unit_cursor(prm, cid);
+      WorkUnit wu;
+      while (!abort && next_unit(prm, ncl, cur, wu)) {
+        const int t = wu.tile;
         const int n_tile = t % prm.tiles_n;
         const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
         // Boxes past the end repeat the last box; their rows are not stored.
@@ -144,48 +153,49 @@ __global__ void __cluster_dims__(2, 1, 1)
         const int h0 = bp * prm.box_p - prm.ph;
         const int w0 = bq * prm.box_q - prm.pw;
         const int k0 = n_tile * KT;
-        for (int cb = 0; cb < ncb && !abort; ++cb) {
+        for (int j = wu.jbeg; j < wu.jend && !abort; ++j, ++ga) {
+          // Slot j: channel block cb, filter column ss, precision pass
+          // (3xTF32: hi*hi, hi*lo, lo*hi).
+          const int cb = j / sp_per_cb;
+          const int sp = j - cb * sp_per_cb;
           const int c0 = cb * kCH;
-          for (int sp = 0; sp < prm.s * prm.passes && !abort; ++sp, ++ga) {
-            // Filter column ss, precision pass (3xTF32: hi*hi, hi*lo, lo*hi).
-            const int ss = sp / prm.passes;
-            const int pass = sp - ss * prm.passes;
-            const CUtensorMap* mr = pass == 2 ? &prm.tm_xr_lo : &prm.tm_xr;
-            const CUtensorMap* mi = pass == 2 ? &prm.tm_xi_lo : &prm.tm_xi;
-            if (!IN_COMPLEX) {
-              const int slot = static_cast<int>(ga % SA);
-              const uint32_t ph = (ga / SA) & 1u;
-              if (!ptx::mbar_wait_bounded(aempty(slot), ph ^ 1u, prm.status, kTimeoutH) ||
-                  flags[1]) {
-                flags[1] = 1;
-                abort = true;
-                break;
-              }
-              if (leader) ptx::mbar_arrive_expect_tx(afull(slot), 2u * prm.a_slot_bytes);
-              const uint32_t fb = ptx::mapa_shared(afull(slot), 0);
-              const uint32_t a_r = a_base + static_cast<uint32_t>(slot * prm.a_slot_bytes);
-              ptx::tma_load_4d_pair(a_r, mr, fb, c0, w0 + ss, h0, img);
-              ptx::tma_load_4d_pair(a_r + a_plane_bytes, mi, fb, c0, w0 + ss, h0, img);
+          const int ss = sp / prm.passes;
+          const int pass = sp - ss * prm.passes;
+          const CUtensorMap* mr = pass == 2 ? &prm.tm_xr_lo : &prm.tm_xr;
+          const CUtensorMap* mi = pass == 2 ? &prm.tm_xi_lo : &prm.tm_xi;
+          if (!IN_COMPLEX) {
+            const int slot = static_cast<int>(ga % SA);
+            const uint32_t ph = (ga / SA) & 1u;
+            if (!ptx::mbar_wait_bounded(aempty(slot), ph ^ 1u, prm.status, kTimeoutH) ||
+                flags[1]) {
+              flags[1] = 1;
+              abort = true;
+              break;
             }
-            for (int rr = 0; rr < prm.r; ++rr, ++gw) {
-              const int st = static_cast<int>(gw % SW);
-              const uint32_t pw_ = (gw / SW) & 1u;
-              if (!ptx::mbar_wait_bounded(wempty(st), pw_ ^ 1u, prm.status, kTimeoutH) ||
-                  flags[1]) {
-                flags[1] = 1;
-                abort = true;
-                break;
-              }
-              if (leader) ptx::mbar_arrive_expect_tx(wfull(st), 2u * C::kWStageBytes);
-              const uint32_t wb = ptx::mapa_shared(wfull(st), 0);
-              const uint32_t w_x = w_base + static_cast<uint32_t>(st * C::kWStageBytes);
-              const uint32_t w_y = w_x + C::kWStageBytes / 2;
-              const int tap = rr * prm.s + ss + (pass == 1 ? prm.r * prm.s : 0);
-              // Packed planes per tap: 0 = -W_im, 1 = W_re, 2 = W_im.
-              // CTA0: X = W_re, Y = -W_im.  CTA1: X = W_im, Y = W_re.
-              ptx::tma_load_4d_pair(w_x, &prm.tm_w, wb, c0, k0, leader ? 1 : 2, tap);
-              ptx::tma_load_4d_pair(w_y, &prm.tm_w, wb, c0, k0, leader ? 0 : 1, tap);
+            if (leader) ptx::mbar_arrive_expect_tx(afull(slot), 2u * prm.a_slot_bytes);
+            const uint32_t fb = ptx::mapa_shared(afull(slot), 0);
+            const uint32_t a_r = a_base + static_cast<uint32_t>(slot * prm.a_slot_bytes);
+            ptx::tma_load_4d_pair(a_r, mr, fb, c0, w0 + ss, h0, img);
+            ptx::tma_load_4d_pair(a_r + a_plane_bytes, mi, fb, c0, w0 + ss, h0, img);
+          }
+          for (int rr = 0; rr < prm.r; ++rr, ++gw) {
+            const int st = static_cast<int>(gw % SW);
+            const uint32_t pw_ = (gw / SW) & 1u;
+            if (!ptx::mbar_wait_bounded(wempty(st), pw_ ^ 1u, prm.status, kTimeoutH) ||
+                flags[1]) {
+              flags[1] = 1;
+              abort = true;
+              break;
             }
+            if (leader) ptx::mbar_arrive_expect_tx(wfull(st), 2u * C::kWStageBytes);
+            const uint32_t wb = ptx::mapa_shared(wfull(st), 0);
+            const uint32_t w_x = w_base + static_cast<uint32_t>(st * C::kWStageBytes);
+            const uint32_t w_y = w_x + C::kWStageBytes / 2;
+            const int tap = rr * prm.s + ss + (pass == 1 ? prm.r * prm.s : 0);
+            // Packed planes per tap: 0 = -W_im, 1 = W_re, 2 = W_im.
+            // CTA0: X = W_re, Y = -W_im.  CTA1: X = W_im, Y = W_re.
+            ptx::tma_load_4d_pair(w_x, &prm.tm_w, wb, c0, k0, leader ? 1 : 2, tap);
+            ptx::tma_load_4d_pair(w_y, &prm.tm_w, wb, c0, k0, leader ? 0 : 1, tap);
           }
         }
       }
@@ -211,9 +221,12 @@ __global__ void __cluster_dims__(2, 1, 1)
       uint32_t ga = 0, gw = 0;
       int i = 0;
       bool abort = false;
-      for (int t = cid; t < prm.num_tiles && !abort; t += ncl, ++i) {
+      UnitCursor cur = unit_cursor(prm, cid);
+      WorkUnit wu;
+      while (!abort && next_unit(prm, ncl, cur, wu)) {
         const int buf = i & 1;
         const uint32_t use = static_cast<uint32_t>(i >> 1);
+        ++i;
         if (!ptx::mbar_wait_bounded(tempty(buf), (use & 1u) ^ 1u, prm.status, kTimeoutH)) {
           flags[1] = 1;
           break;
@@ -221,41 +234,39 @@ __global__ void __cluster_dims__(2, 1, 1)
         ptx::tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(buf * C::kAccCols);
         bool first = true;
-        for (int cb = 0; cb < ncb && !abort; ++cb) {
-          for (int sp = 0; sp < prm.s * prm.passes && !abort; ++sp, ++ga) {
-            const int slot = static_cast<int>(ga % SA);
-            if (!ptx::mbar_wait_bounded<IN_COMPLEX>(afull(slot), (ga / SA) & 1u, prm.status,
-                                                    kTimeoutH)) {
+        for (int j = wu.jbeg; j < wu.jend && !abort; ++j, ++ga) {
+          const int slot = static_cast<int>(ga % SA);
+          if (!ptx::mbar_wait_bounded<IN_COMPLEX>(afull(slot), (ga / SA) & 1u, prm.status,
+                                                  kTimeoutH)) {
+            flags[1] = 1;
+            abort = true;
+            break;
+          }
+          const uint32_t a_r0 = a_base + static_cast<uint32_t>(slot * prm.a_slot_bytes);
+          for (int rr = 0; rr < prm.r; ++rr, ++gw) {
+            const int st = static_cast<int>(gw % SW);
+            if (!ptx::mbar_wait_bounded(wfull(st), (gw / SW) & 1u, prm.status, kTimeoutH)) {
               flags[1] = 1;
               abort = true;
               break;
             }
-            const uint32_t a_r0 = a_base + static_cast<uint32_t>(slot * prm.a_slot_bytes);
-            for (int rr = 0; rr < prm.r; ++rr, ++gw) {
-              const int st = static_cast<int>(gw % SW);
-              if (!ptx::mbar_wait_bounded(wfull(st), (gw / SW) & 1u, prm.status, kTimeoutH)) {
-                flags[1] = 1;
-                abort = true;
-                break;
-              }
-              ptx::tc_fence_after();
-              const uint32_t a_r = a_r0 + static_cast<uint32_t>(rr) * tap_row_bytes;
-              const uint32_t a_i = a_r + a_plane_bytes;
-              const uint32_t w_x = w_base + static_cast<uint32_t>(st * C::kWStageBytes);
-              const uint32_t w_y = w_x + C::kWStageBytes / 2;
+            ptx::tc_fence_after();
+            const uint32_t a_r = a_r0 + static_cast<uint32_t>(rr) * tap_row_bytes;
+            const uint32_t a_i = a_r + a_plane_bytes;
+            const uint32_t w_x = w_base + static_cast<uint32_t>(st * C::kWStageBytes);
+            const uint32_t w_y = w_x + C::kWStageBytes / 2;
 #pragma unroll
-              for (int kk = 0; kk < kCH / 8; ++kk) {
-                const uint32_t koff = kk * 32;
-                ptx::mma_tf32_pair(d, ptx::desc_kmajor_sw128(a_r + koff),
-                                   ptx::desc_kmajor_sw128(w_x + koff), idesc, first ? 0u : 1u);
-                first = false;
-                ptx::mma_tf32_pair(d, ptx::desc_kmajor_sw128(a_i + koff),
-                                   ptx::desc_kmajor_sw128(w_y + koff), idesc, 1u);
-              }
-              ptx::mma_commit_pair(wempty(st));
+            for (int kk = 0; kk < kCH / 8; ++kk) {
+              const uint32_t koff = kk * 32;
+              ptx::mma_tf32_pair(d, ptx::desc_kmajor_sw128(a_r + koff),
+                                 ptx::desc_kmajor_sw128(w_x + koff), idesc, first ? 0u : 1u);
+              first = false;
+              ptx::mma_tf32_pair(d, ptx::desc_kmajor_sw128(a_i + koff),
+                                 ptx::desc_kmajor_sw128(w_y + koff), idesc, 1u);
             }
-            ptx::mma_commit_pair(aempty(slot));
+            ptx::mma_commit_pair(wempty(st));
           }
+          ptx::mma_commit_pair(aempty(slot));
         }
         ptx::mma_commit_pair(tfull(buf));
       }
@@ -272,21 +283,41 @@ __global__ void __cluster_dims__(2, 1, 1)
     const uint32_t tempty_leader0 = ptx::mapa_shared(tempty(0), 0);
     const uint32_t tempty_leader1 = ptx::mapa_shared(tempty(1), 0);
     int i = 0;
-    for (int t = cid; t < prm.num_tiles && !skip; t += ncl, ++i) {
+    UnitCursor cur = unit_cursor(prm, cid);
+    WorkUnit wu;
+    while (!skip && next_unit(prm, ncl, cur, wu)) {
       const int buf = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
+      ++i;
       const bool ok = ptx::mbar_wait_bounded_backoff(tfull(buf), use & 1u, prm.status, kTimeoutH);
       ptx::tc_fence_after();
       if (!ok) flags[1] = 1;
+      const int t = wu.tile;
       const int n_tile = t % prm.tiles_n;
       const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
       int img = 0, op = 0, oq = 0;
-      const bool valid = tile_row_pixel<false>(prm, half, row, img, op, oq) && ok && !flags[1];
-      store_accumulator<KT, OUT_COMPLEX>(prm, t_row + static_cast<uint32_t>(buf * C::kAccCols),
-                                         n_tile * KT, valid, img, op, oq);
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive_cluster(buf == 0 ? tempty_leader0 : tempty_leader1);
+      const bool in_tile = tile_row_pixel<false>(prm, half, row, img, op, oq);
+      const uint32_t t_acc = t_row + static_cast<uint32_t>(buf * C::kAccCols);
+      const uint32_t t_free = buf == 0 ? tempty_leader0 : tempty_leader1;
+      if (wu.split && ok && !flags[1]) {
+        // After the cluster's last unit the operand buffers are idle: they
+        // stage the split tile's partial sums.
+        const bool final_unit = cursor_done(prm, cur);
+        const uint32_t stage_per_warp =
+            (static_cast<uint32_t>(SA * prm.a_slot_bytes + SW * prm.w_stage_bytes) / 4u) & ~127u;
+        split_piece_epilogue<KT, OUT_COMPLEX>(
+            prm, wu, cid, static_cast<int>(rank), quarter, lane, t_acc, n_tile * KT, in_tile, img,
+            op, oq, t_free, final_unit ? data + quarter * stage_per_warp : nullptr, stage_per_warp,
+            stage_bar0 + 8u * kStageBufs * static_cast<uint32_t>(quarter));
+      } else {
+        // The fused variant runs 448 threads (128 registers each): 16-column chunks.
+        store_accumulator<KT, OUT_COMPLEX, IN_COMPLEX ? 16 : 32>(
+            prm, t_acc, n_tile * KT, in_tile && ok && !flags[1], img, op, oq);
+        // This warp is done with the accumulator buffer: release it to the MMA.
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive_cluster(t_free);
+      }
       if (!ok) break;
     }
   }
@@ -298,16 +329,15 @@ __global__ void __cluster_dims__(2, 1, 1)
       // loads of job j+1 are issued before waiting for job j+1's slot.
       const int wid = warp - 6;
       const float2* xc = reinterpret_cast<const float2*>(prm.xc);
-      const int jobs_per_tile = ncb * prm.s * prm.passes;
-      auto make_job = [&](int t, int jt, SlotJob& jb) {
+      auto make_job = [&](int t, int j, SlotJob& jb) {
         const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
         const int gb = min(half, prm.total_boxes - 1);
         const int img = gb / per_img;
         const int rem = gb - img * per_img;
         const int bp = rem / prm.tiles_bq;
         const int bq = rem - bp * prm.tiles_bq;
-        const int cb = jt / (prm.s * prm.passes);
-        const int sp = jt - cb * (prm.s * prm.passes);
+        const int cb = j / sp_per_cb;
+        const int sp = j - cb * sp_per_cb;
         const int ss = sp / prm.passes;
         const int pass = sp - ss * prm.passes;
         jb.img = img;
@@ -316,19 +346,22 @@ __global__ void __cluster_dims__(2, 1, 1)
         jb.c0 = cb * kCH;
         jb.mode = prm.passes == 1 ? kConvRaw : (pass == 2 ? kConvLo : kConvHi);
       };
-      int t = cid, jt = 0;
+      UnitCursor cur = unit_cursor(prm, cid);
+      WorkUnit wu;
+      bool have = next_unit(prm, ncl, cur, wu);
+      int j = have ? wu.jbeg : 0;
       SlotJob jb;
       float2 v[kConvUnits][4];
-      if (t < prm.num_tiles) {
-        make_job(t, jt, jb);
+      if (have) {
+        make_job(wu.tile, j, jb);
         slot_job_load(v, jb, xc, prm.c, prm.h, prm.w, prm.halo_rows, prm.box_q_log2, wid,
                       kConvWarps, lane);
       }
       uint32_t ga = 0;
-      while (t < prm.num_tiles) {
+      while (have) {
         const int slot = static_cast<int>(ga % SA);
         if (!ptx::mbar_wait_bounded_backoff(aempty(slot), ((ga / SA) & 1u) ^ 1u, prm.status,
-                                    kTimeoutH) ||
+                                            kTimeoutH) ||
             flags[1]) {
           flags[1] = 1;
           break;
@@ -340,12 +373,12 @@ __global__ void __cluster_dims__(2, 1, 1)
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(afull(slot), 0));
         ++ga;
-        if (++jt == jobs_per_tile) {
-          jt = 0;
-          t += ncl;
+        if (++j == wu.jend) {
+          have = next_unit(prm, ncl, cur, wu);
+          j = have ? wu.jbeg : 0;
         }
-        if (t < prm.num_tiles) {
-          make_job(t, jt, jb);
+        if (have) {
+          make_job(wu.tile, j, jb);
           slot_job_load(v, jb, xc, prm.c, prm.h, prm.w, prm.halo_rows, prm.box_q_log2, wid,
                         kConvWarps, lane);
         }
@@ -364,7 +397,8 @@ __global__ void __cluster_dims__(2, 1, 1)
 }
 
 template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX>
-int launchh_variant(const FpropParams& prm, int smem_bytes, cudaStream_t stream) {
+int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
+                    cudaStream_t stream) {
   auto kern = ccv_fprop2h_tf32_kernel<KT, OUT_COMPLEX, IN_COMPLEX>;
   constexpr int threads = IN_COMPLEX ? kThreadsH + 32 * kConvWarps : kThreadsH;
   static std::once_flag once[64];
@@ -388,8 +422,12 @@ int launchh_variant(const FpropParams& prm, int smem_bytes, cudaStream_t stream)
     }
   });
   if (err != cudaSuccess) return cuda_error(err, "cudaFuncSetAttribute(fprop2h)");
-  const int clusters = std::max(1, std::min(prm.num_tiles, max_clusters[dev & 63]));
-  kern<<<2 * clusters, threads, smem_bytes, stream>>>(prm);
+  const int clusters = cluster_cap(max_clusters[dev & 63]);
+  const int slots = ((prm.c + kCH - 1) / kCH) * prm.s * prm.passes;
+  int rc;
+  const int launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc);
+  if (rc != CCV_OK) return rc;
+  kern<<<2 * launched, threads, smem_bytes, stream>>>(prm);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "fprop2h kernel launch");
   return CCV_OK;
@@ -452,7 +490,8 @@ Tiling choose_halo_tiling(const Problem& pb) {
 int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
                            const float* xi_lo, const float* xc, bool split,
                            const float* w_packed, float* y0, float* y1, const Problem& pb,
-                           const Tiling& t, OutLayout out_layout, cudaStream_t stream) {
+                           const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
+                           cudaStream_t stream) {
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;
@@ -525,21 +564,21 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
     // The fused path always writes complex64 NCHW.
     if (!cplx) return set_error(CCV_ERR_INVALID_ARGUMENT, "fused complex input needs complex output");
     switch (t.kt) {
-      case 128: return launchh_variant<128, true, true>(prm, smem_bytes, stream);
-      case 64: return launchh_variant<64, true, true>(prm, smem_bytes, stream);
-      default: return launchh_variant<32, true, true>(prm, smem_bytes, stream);
+      case 128: return launchh_variant<128, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
+      case 64: return launchh_variant<64, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
+      default: return launchh_variant<32, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
     }
   }
   switch (t.kt) {
     case 128:
-      return cplx ? launchh_variant<128, true, false>(prm, smem_bytes, stream)
-                  : launchh_variant<128, false, false>(prm, smem_bytes, stream);
+      return cplx ? launchh_variant<128, true, false>(prm, smem_bytes, ws, ws_bytes, stream)
+                  : launchh_variant<128, false, false>(prm, smem_bytes, ws, ws_bytes, stream);
     case 64:
-      return cplx ? launchh_variant<64, true, false>(prm, smem_bytes, stream)
-                  : launchh_variant<64, false, false>(prm, smem_bytes, stream);
+      return cplx ? launchh_variant<64, true, false>(prm, smem_bytes, ws, ws_bytes, stream)
+                  : launchh_variant<64, false, false>(prm, smem_bytes, ws, ws_bytes, stream);
     default:
-      return cplx ? launchh_variant<32, true, false>(prm, smem_bytes, stream)
-                  : launchh_variant<32, false, false>(prm, smem_bytes, stream);
+      return cplx ? launchh_variant<32, true, false>(prm, smem_bytes, ws, ws_bytes, stream)
+                  : launchh_variant<32, false, false>(prm, smem_bytes, ws, ws_bytes, stream);
   }
 }
 

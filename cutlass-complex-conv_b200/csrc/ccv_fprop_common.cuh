@@ -34,7 +34,105 @@ struct alignas(64) FpropParams {
   int passes;
   // single-CTA kernel: CTAs per output tile (a cluster splitting the K loop)
   int splits;
+  // Pair kernels, stream-K tail.  Tiles [0, sk_start) run whole, tile t on
+  // cluster t mod G.  The K slots (A-operand loads; slots_per_tile per tile)
+  // of the tiles from sk_start on are numbered s = (t - sk_start) * L + j and
+  // cut into sk_clusters contiguous ranges, range g going to cluster g before
+  // its whole tiles.  A tile covered by several ranges is "split": each piece
+  // writes fp32 partial rows to split_ws and adds its slot count to a counter
+  // in split_count; the piece that brings the count to L (the last to finish;
+  // nobody waits) sums all pieces' partials in cluster order and stores the
+  // output.  sk_slots == 0: no tail split (split_ws unused).
+  int sk_start, sk_clusters, slots_per_tile;
+  long long sk_slots;  // < 2^31 (checked on the host)
+  float* split_ws;
+  unsigned* split_count;
 };
+
+// Work of one persistent cluster: its stream-K range, then whole tiles.
+struct UnitCursor {
+  int dp;       // next whole tile
+  int s, s1;    // remaining stream-K slot range
+};
+
+// One unit: slots [jbeg, jend) of tile `tile`; `split` when the unit is a
+// piece of a split tile (sk = the tile's index among stream-K tiles).
+struct WorkUnit {
+  int tile, jbeg, jend, sk;
+  bool split;
+};
+
+__host__ __device__ inline long long sk_range_begin(const FpropParams& prm, int g) {
+  return static_cast<long long>(g) * prm.sk_slots / prm.sk_clusters;
+}
+
+__host__ __device__ inline UnitCursor unit_cursor(const FpropParams& prm, int cid) {
+  UnitCursor c;
+  c.dp = cid;
+  c.s = c.s1 = 0;
+  if (prm.sk_slots > 0 && cid < prm.sk_clusters) {
+    c.s = static_cast<int>(sk_range_begin(prm, cid));
+    c.s1 = static_cast<int>(sk_range_begin(prm, cid + 1));
+  }
+  return c;
+}
+
+__host__ __device__ inline bool next_unit(const FpropParams& prm, int ncl, UnitCursor& c,
+                                          WorkUnit& w) {
+  const int L = prm.slots_per_tile;
+  // The stream-K range first: a split tile's sum is then finished by
+  // whichever piece ends last while its cluster goes on with whole tiles,
+  // off the kernel's critical path.
+  if (c.s < c.s1) {
+    const int a = c.s / L;
+    const int end = c.s1 < (a + 1) * L ? c.s1 : (a + 1) * L;
+    w.sk = a;
+    w.tile = prm.sk_start + a;
+    w.jbeg = c.s - a * L;
+    w.jend = end - a * L;
+    w.split = !(w.jbeg == 0 && w.jend == L);
+    c.s = end;
+    return true;
+  }
+  if (c.dp < prm.sk_start) {
+    w.tile = c.dp;
+    w.jbeg = 0;
+    w.jend = L;
+    w.sk = -1;
+    w.split = false;
+    c.dp += ncl;
+    return true;
+  }
+  return false;
+}
+
+// True when the cursor has no unit left.
+__host__ __device__ inline bool cursor_done(const FpropParams& prm, const UnitCursor& c) {
+  return c.dp >= prm.sk_start && c.s >= c.s1;
+}
+
+// Clusters whose stream-K ranges cover parts of stream-K tile `a`: g_first
+// .. g_last (every range holds at least one slot).
+__host__ __device__ inline void sk_tile_clusters(const FpropParams& prm, int a, int& g_first,
+                                                 int& g_last) {
+  const long long L = prm.slots_per_tile;
+  const long long G = prm.sk_clusters;
+  const long long X = prm.sk_slots;
+  long long f = ((a * L + 1) * G + X - 1) / X - 1;
+  long long l = (((a + 1) * L) * G + X - 1) / X - 1;
+  g_first = static_cast<int>(f < G - 1 ? f : G - 1);
+  g_last = static_cast<int>(l < G - 1 ? l : G - 1);
+}
+
+// Partial buffer of cluster g's piece of stream-K tile a: index 0 when g's
+// range starts inside the tile, 1 when it started in an earlier tile (then
+// the piece is the range's last unit).  Buffers hold 128 rows x 2*KT fp32
+// per CTA of the pair.
+__host__ __device__ inline long long sk_partial_index(const FpropParams& prm, int g, int a,
+                                                      int rank) {
+  const int idx = sk_range_begin(prm, g) >= static_cast<long long>(a) * prm.slots_per_tile ? 0 : 1;
+  return (static_cast<long long>(g) * 2 + idx) * 2 + rank;
+}
 
 // Tiling of the output pixels: 128-row tiles made of NB boxes of
 // box_p x box_q output pixels (powers of two), or flat 128-pixel runs for
@@ -98,7 +196,8 @@ int pair_tiles(const Tiling& t);
 // the TF32-rounded parts.
 int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                       const float* w_packed, float* y0, float* y1, const Problem& pb,
-                      const Tiling& t, OutLayout out_layout, cudaStream_t stream);
+                      const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
+                      cudaStream_t stream);
 
 // Halo variant of the pair kernel (ccv_fprop2h.cu): stride-1 problems with a
 // filter wider than 1x1.  Each CTA tile is one box of box_p x box_q pixels
@@ -108,12 +207,30 @@ bool halo_applicable(const Problem& pb);
 // Whether the converter warps of the fused complex path cover one A slot of
 // this halo tiling (their register batch bounds the slot's rows).
 bool halo_fused_supported(const Problem& pb, const Tiling& th);
+// Scratch bytes that let a pair kernel with KT-wide tiles, `tiles` pair
+// tiles and `slots` K slots per tile split its last partial wave stream-K
+// style (partials and counters; an upper bound for the current device).
+size_t pair_split_workspace_bytes(int kt, int tiles, int slots);
+// Stream-K plan for a persistent pair kernel: sets prm.sk_* / slots_per_tile
+// for `clusters` co-resident clusters and `slots` K slots per tile, using ws
+// (at least pair_split_workspace_bytes(kt)) when given and worthwhile.
+// Returns the number of counters to zero before the launch (0: no split).
+int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes);
+// Persistent-grid size after the CCV_MAX_CLUSTERS testing cap.
+int cluster_cap(int max_clusters);
+// Plans the stream-K split (zeroing its counters on `stream`) and returns
+// the number of clusters to launch; *rc receives the status.
+int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
+                    cudaStream_t stream, int* rc);
 Tiling choose_halo_tiling(const Problem& pb);
 // xc non-null: fused complex path (converter warps read complex64 NCHW; the
 // planar pointers are ignored and `split` selects 3xTF32).
+// ws/ws_bytes: optional scratch for the tail split (see
+// halo_split_workspace_bytes); without it every tile runs whole.
 int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
                            const float* xi_lo, const float* xc, bool split,
                            const float* w_packed, float* y0, float* y1, const Problem& pb,
-                           const Tiling& t, OutLayout out_layout, cudaStream_t stream);
+                           const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
+                           cudaStream_t stream);
 
 }  // namespace ccv

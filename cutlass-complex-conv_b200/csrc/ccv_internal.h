@@ -51,15 +51,22 @@ int launch_split_planes(const float* xr, const float* xi, float* hr, float* hi, 
 enum OutLayout { OUT_PLANAR_NHWC = 0, OUT_COMPLEX_NCHW = 1 };
 // For 3xTF32, xr/xi are the TF32-rounded activation planes and xr_lo/xi_lo
 // the remainders (x - tf32(x)); for TF32 the *_lo pointers are ignored.
+// ws/ws_bytes: optional scratch (256-byte aligned) for the stream-K split of
+// the pair kernels' last partial wave; null runs every tile whole.
 int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                  const float* w_packed, float* y0, float* y1, const Problem& pb, int precision,
-                 OutLayout out_layout, cudaStream_t stream);
+                 OutLayout out_layout, void* ws, size_t ws_bytes, cudaStream_t stream);
+
+// Scratch bytes the stream-K split of this problem's kernel can use (0 when
+// the problem runs on the single-CTA kernel).
+size_t split_workspace_bytes(const Problem& pb, int precision);
 
 // Fused complex path: complex64 NCHW in, complex64 NKPQ out, one launch, no
-// workspace.  Available when the problem runs on the halo pair kernel.
+// required workspace.  Available when the problem runs on the halo pair kernel.
 bool fused_complex_available(const Problem& pb, int precision);
 int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
-                               const Problem& pb, int precision, cudaStream_t stream);
+                               const Problem& pb, int precision, void* ws, size_t ws_bytes,
+                               cudaStream_t stream);
 
 // Encodes a tiled tensor map through the driver entry point.
 // `swizzle_bytes` is 64 or 128 (the box's inner extent in bytes).

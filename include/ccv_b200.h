@@ -5,9 +5,10 @@
  * extension `complex_conv2d._C` (pybind module defined in
  * csrc/bindings.cpp:16-29 of jaeeunHwang/cutlass-complex-conv, whose body is
  * `complex_conv2d_cuda` in csrc/complex_conv2d.cu:84-309).  All entry points
- * take plain device pointers and sizes; none allocates memory.  Callers that
- * need scratch memory get its size from the matching *_workspace_bytes query
- * and pass it in.  Every launch is asynchronous on the given stream.
+ * take plain device pointers and sizes; none allocates memory.  Scratch
+ * memory comes from the caller: the *_workspace_bytes queries give the size
+ * that enables every optimisation, *_min_workspace_bytes the size a call
+ * cannot run without.  Every launch is asynchronous on the given stream.
  *
  * Conventions
  *   - Activation planes x_real/x_imag: fp32 NHWC, contiguous
@@ -87,15 +88,33 @@ int ccv_prepack_weights(const float* w_real, const float* w_imag, int layout,
                         const ccv_conv_shape* shape, int precision,
                         void* packed, size_t packed_bytes, ccv_stream_t stream);
 
-/* Scratch bytes the fprop entry points below need for this problem. */
+/* Scratch bytes for the fprop entry points below.  *_workspace_bytes: the
+ * recommended size - the required scratch plus room for the stream-K split
+ * of the last partial wave of output tiles (partial sums and counters; an
+ * upper bound for the current device).  *_min_workspace_bytes: the required
+ * part alone; a call given only that runs every tile whole.  The required
+ * part is 0 for TF32 planar calls and for complex calls served by the fused
+ * complex-input kernel. */
 size_t ccv_fprop_planar_workspace_bytes(const ccv_conv_shape* shape, int precision);
 size_t ccv_fprop_complex_workspace_bytes(const ccv_conv_shape* shape, int precision);
+size_t ccv_fprop_planar_min_workspace_bytes(const ccv_conv_shape* shape, int precision);
+size_t ccv_fprop_complex_min_workspace_bytes(const ccv_conv_shape* shape, int precision);
+
+/* Number of library kernels one ccv_fprop_planar (complex_input = 0) or
+ * ccv_fprop_complex (complex_input = 1) call launches: the conv kernel plus
+ * any layout/split pass (a stream-K counter reset, when taken, is one
+ * cudaMemsetAsync on top). */
+int ccv_fprop_kernel_launches(const ccv_conv_shape* shape, int precision, int complex_input,
+                              int* kernels);
 
 /* Planar fprop: fp32 NHWC planes in, fp32 NPQK planes out, packed weights.
  * Replaces complex_conv2d_cuda (csrc/complex_conv2d.cu:84-309) behind
  * ComplexConv2d.forward_planar (modules.py:153-174).  TF32 needs no
- * workspace; 3xTF32 needs ccv_fprop_planar_workspace_bytes() (the inputs
- * split into TF32 parts and remainders) and weights packed for 3xTF32. */
+ * workspace; 3xTF32 needs ccv_fprop_planar_min_workspace_bytes() (the inputs
+ * split into TF32 parts and remainders) and weights packed for 3xTF32.
+ * Workspace past the required part (256-byte aligned) is used for the
+ * stream-K split.  Results do not depend on whether the split is taken
+ * beyond fp32 summation order (deterministic for a given workspace size). */
 int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_packed,
                      float* y_real, float* y_imag, const ccv_conv_shape* shape,
                      int precision, void* workspace, size_t workspace_bytes,
@@ -110,8 +129,8 @@ int ccv_fprop_complex(const void* x, const void* w_packed, void* y,
 
 /* The reference extension call itself: `_C.forward(x_real, x_imag, w_real,
  * w_imag, stride_h, stride_w, pad_h, pad_w)` (csrc/bindings.cpp:16-29) with
- * KRSC weights, TF32.  Needs ccv_forward_workspace_bytes() of scratch (the
- * packed weights). */
+ * KRSC weights, TF32.  Needs the packed weight bytes (256-byte aligned) of
+ * scratch; ccv_forward_workspace_bytes() adds the stream-K room. */
 size_t ccv_forward_workspace_bytes(const ccv_conv_shape* shape);
 int ccv_forward(const float* x_real, const float* x_imag, const float* w_real_krsc,
                 const float* w_imag_krsc, float* y_real, float* y_imag,

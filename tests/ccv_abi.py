@@ -58,6 +58,10 @@ def load():
         "ccv_prepack_weights": (ctypes.c_int, [vp, vp, ctypes.c_int, sp, ctypes.c_int, vp, sz, vp]),
         "ccv_fprop_planar_workspace_bytes": (sz, [sp, ctypes.c_int]),
         "ccv_fprop_complex_workspace_bytes": (sz, [sp, ctypes.c_int]),
+        "ccv_fprop_planar_min_workspace_bytes": (sz, [sp, ctypes.c_int]),
+        "ccv_fprop_complex_min_workspace_bytes": (sz, [sp, ctypes.c_int]),
+        "ccv_fprop_kernel_launches": (ctypes.c_int, [sp, ctypes.c_int, ctypes.c_int,
+                                                     ctypes.POINTER(ctypes.c_int)]),
         "ccv_fprop_planar": (ctypes.c_int, [vp, vp, vp, vp, vp, sp, ctypes.c_int, vp, sz, vp]),
         "ccv_fprop_complex": (ctypes.c_int, [vp, vp, vp, sp, ctypes.c_int, vp, sz, vp]),
         "ccv_forward_workspace_bytes": (sz, [sp]),
