@@ -110,6 +110,13 @@ int device_sm_count() {
 int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                  const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides,
                  int swizzle_bytes) {
+  return encode_tiled_ex(map, base, rank, dims, strides_bytes, box, elem_strides,
+                         swizzle_bytes == 128 ? kSwizzle128 : kSwizzle64, false);
+}
+
+int encode_tiled_ex(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box,
+                    const uint32_t* elem_strides, TmaSwizzle swizzle, bool elem8) {
   std::call_once(g_encode_once, []() {
     void* fn = nullptr;
     cudaDriverEntryPointQueryResult q;
@@ -131,12 +138,14 @@ int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* d
     es[i] = elem_strides[i];
     if (i + 1 < rank) st[i] = strides_bytes[i];
   }
-  const CUresult r = g_encode_tiled(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<void*>(base),
-                                    d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                    swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                                         : CU_TENSOR_MAP_SWIZZLE_64B,
-                                    CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
-                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUtensorMapSwizzle sw = swizzle == kSwizzle128        ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle == kSwizzle128Atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                               : CU_TENSOR_MAP_SWIZZLE_64B;
+  // 8-byte elements (complex64 moved as opaque 64-bit words) or fp32.
+  const CUresult r = g_encode_tiled(
+      map, elem8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT64 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank,
+      const_cast<void*>(base), d, st, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+      CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     return set_error(CCV_ERR_UNSUPPORTED,
                      "cuTensorMapEncodeTiled rejected the problem (error " + std::to_string(r) + ")");
@@ -287,7 +296,7 @@ void split_scratch(void* workspace, size_t workspace_bytes, size_t required, voi
 size_t ccv_fprop_planar_workspace_bytes(const ccv_conv_shape* shape, int precision) {
   Problem pb;
   if (make_problem(shape, &pb) != CCV_OK) return 0;
-  const size_t split = split_workspace_bytes(pb, precision);
+  const size_t split = split_workspace_bytes(pb, precision, false);
   const size_t req = planar_required_bytes(pb, precision);
   return split > 0 ? align256(req) + 256 + split : req;
 }
@@ -295,7 +304,7 @@ size_t ccv_fprop_planar_workspace_bytes(const ccv_conv_shape* shape, int precisi
 size_t ccv_fprop_complex_workspace_bytes(const ccv_conv_shape* shape, int precision) {
   Problem pb;
   if (make_problem(shape, &pb) != CCV_OK) return 0;
-  const size_t split = split_workspace_bytes(pb, precision);
+  const size_t split = split_workspace_bytes(pb, precision, true);
   const size_t req = complex_required_bytes(pb, precision);
   return split > 0 ? align256(req) + 256 + split : req;
 }
@@ -407,6 +416,13 @@ int ccv_fprop_kernel_launches(const ccv_conv_shape* shape, int precision, int co
     *kernels = split ? 2 : 1;
   }
   return CCV_OK;
+}
+
+const char* ccv_fprop_complex_kernel(const ccv_conv_shape* shape, int precision) {
+  Problem pb;
+  if (make_problem(shape, &pb) != CCV_OK) return "invalid";
+  if (precision != CCV_PRECISION_TF32 && precision != CCV_PRECISION_3XTF32) return "invalid";
+  return complex_kernel_name(pb, precision);
 }
 
 size_t ccv_forward_workspace_bytes(const ccv_conv_shape* shape) {

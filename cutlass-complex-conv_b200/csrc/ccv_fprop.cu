@@ -521,7 +521,25 @@ KernelFamily choose_family(const Problem& pb, bool split, const Tiling& t, Tilin
 
 }  // namespace
 
-size_t split_workspace_bytes(const Problem& pb, int precision) {
+// forward() (complex64 in and out) on the complex-direct kernel: TF32,
+// problems the pair kernels serve, stride 1 with an odd filter width.  Opt
+// in with CCV_CD=1: measured on B200 it is slower than the converter-warp
+// halo kernel on every BASELINE layer (b64 128->128 56x56: 548 vs 441 us;
+// 1x1 256->1024 28x28: 217-303 vs 122 us), because all column slots of a
+// channel block must be resident (short weight ring) and the 4x16 box loads
+// 1.5x halo rows.
+bool use_complex_direct(const Problem& pb, int precision) {
+  if (precision != CCV_PRECISION_TF32) return false;
+  const char* env = getenv("CCV_CD");
+  if (env == nullptr || atoi(env) != 1) return false;
+  if (!cd_applicable(pb)) return false;
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  return choose_family(pb, false, t, &th) != kSingleCta;
+}
+
+size_t split_workspace_bytes(const Problem& pb, int precision, bool complex_input) {
+  if (complex_input && use_complex_direct(pb, precision)) return 0;
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;
@@ -539,15 +557,34 @@ size_t split_workspace_bytes(const Problem& pb, int precision) {
 }
 
 bool fused_complex_available(const Problem& pb, int precision) {
+  if (use_complex_direct(pb, precision)) return true;
   const Tiling t = choose_tiling(pb);
   Tiling th;
   return choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th) == kPairHalo &&
          halo_fused_supported(pb, th);
 }
 
+const char* complex_kernel_name(const Problem& pb, int precision) {
+  if (use_complex_direct(pb, precision)) return "complex_direct_pair";
+  const bool split = precision == CCV_PRECISION_3XTF32;
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  switch (choose_family(pb, split, t, &th)) {
+    case kPairHalo:
+      return halo_fused_supported(pb, th) ? "halo_pair_converter_warps" : "layout_pass+halo_pair";
+    case kPairTap:
+      return "layout_pass+tap_pair";
+    default:
+      return "layout_pass+single_cta";
+  }
+}
+
 int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
                                const Problem& pb, int precision, void* ws, size_t ws_bytes,
                                cudaStream_t stream) {
+  if (use_complex_direct(pb, precision)) {
+    return launch_fprop_cd(xc, w_packed, y, pb, ws, ws_bytes, stream);
+  }
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;

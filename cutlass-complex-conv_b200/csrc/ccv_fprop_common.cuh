@@ -225,6 +225,13 @@ int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws,
 Tiling choose_halo_tiling(const Problem& pb);
 // xc non-null: fused complex path (converter warps read complex64 NCHW; the
 // planar pointers are ignored and `split` selects 3xTF32).
+// Complex-direct kernel (ccv_fprop_cd.cu): forward() with the activations
+// read from complex64 NCHW by TMA as an MN-major operand.  Stride 1, odd
+// filter width, even image width.
+bool cd_applicable(const Problem& pb);
+int launch_fprop_cd(const float* xc, const float* w_packed, float* y, const Problem& pb,
+                    void* ws, size_t ws_bytes, cudaStream_t stream);
+
 // ws/ws_bytes: optional scratch for the tail split (see
 // halo_split_workspace_bytes); without it every tile runs whole.
 int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,

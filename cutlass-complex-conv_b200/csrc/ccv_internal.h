@@ -58,12 +58,14 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
                  OutLayout out_layout, void* ws, size_t ws_bytes, cudaStream_t stream);
 
 // Scratch bytes the stream-K split of this problem's kernel can use (0 when
-// the problem runs on the single-CTA kernel).
-size_t split_workspace_bytes(const Problem& pb, int precision);
+// the problem runs on a kernel without the split).
+size_t split_workspace_bytes(const Problem& pb, int precision, bool complex_input);
 
 // Fused complex path: complex64 NCHW in, complex64 NKPQ out, one launch, no
 // required workspace.  Available when the problem runs on the halo pair kernel.
 bool fused_complex_available(const Problem& pb, int precision);
+// Name of the kernel path a complex (forward()) call takes.
+const char* complex_kernel_name(const Problem& pb, int precision);
 int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
                                const Problem& pb, int precision, void* ws, size_t ws_bytes,
                                cudaStream_t stream);
@@ -73,6 +75,13 @@ int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
 int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                  const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides,
                  int swizzle_bytes = 64);
+// Same, with the swizzle mode named and optionally 8-byte elements.
+// kSwizzle128Atom32 swizzles 32-byte chunks within 128-byte rows (the
+// shared-memory layout of MN-major 32-bit tensor-core operands).
+enum TmaSwizzle { kSwizzle64 = 0, kSwizzle128 = 1, kSwizzle128Atom32 = 2 };
+int encode_tiled_ex(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                    const uint64_t* strides_bytes, const uint32_t* box,
+                    const uint32_t* elem_strides, TmaSwizzle swizzle, bool elem8);
 
 int launch_selftest_wait(int* status_dev, cudaStream_t stream);
 

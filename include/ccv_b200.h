@@ -107,6 +107,12 @@ size_t ccv_fprop_complex_min_workspace_bytes(const ccv_conv_shape* shape, int pr
 int ccv_fprop_kernel_launches(const ccv_conv_shape* shape, int precision, int complex_input,
                               int* kernels);
 
+/* Name of the kernel path ccv_fprop_complex takes for this problem (static
+ * string): "complex_direct_pair" (activations read from complex64 NCHW by
+ * TMA, one launch), "halo_pair_converter_warps" (one launch), or
+ * "layout_pass+<kernel>" (a complex64 -> planar pass, then the kernel). */
+const char* ccv_fprop_complex_kernel(const ccv_conv_shape* shape, int precision);
+
 /* Planar fprop: fp32 NHWC planes in, fp32 NPQK planes out, packed weights.
  * Replaces complex_conv2d_cuda (csrc/complex_conv2d.cu:84-309) behind
  * ComplexConv2d.forward_planar (modules.py:153-174).  TF32 needs no

@@ -20,8 +20,11 @@ pytestmark = pytest.mark.gpu
 def force_kernel():
     """Pin the kernel family (1 = single CTA, 2 = CTA pair; 'halo' = CTA pair
     with halo reuse, 'tap' = CTA pair without) through the library's env knobs."""
-    keys = ("CCV_FORCE_KERNEL", "CCV_HALO")
+    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_CD")
     old = {k: os.environ.get(k) for k in keys}
+    # These tests pin the planar-operand kernels; the complex-direct kernel
+    # has its own tests.
+    os.environ["CCV_CD"] = "0"
 
     def set_(v):
         if v == "halo":

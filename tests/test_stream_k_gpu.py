@@ -43,8 +43,10 @@ GRIDS = [3, 7]
 
 @pytest.fixture
 def knobs():
-    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_STREAMK", "CCV_MAX_CLUSTERS")
+    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_STREAMK", "CCV_MAX_CLUSTERS", "CCV_CD")
     old = {k: os.environ.get(k) for k in keys}
+    # The split lives in the planar-operand pair kernels.
+    os.environ["CCV_CD"] = "0"
 
     def set_(family=None, streamk=None, clusters=None):
         if family is not None:
