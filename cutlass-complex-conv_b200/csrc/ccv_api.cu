@@ -5,9 +5,12 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "ccv_internal.h"
 
@@ -19,6 +22,9 @@ namespace ccv {
 // CCV_ERR_* code here; fprop kernels read it at start and exit without work
 // while it is set.
 __device__ int g_ccv_status = 0;
+// Stream-K counter sets (see stream_k_counters); zero-initialized.
+constexpr int kSkRing = 32;
+__device__ unsigned g_ccv_sk_counters[kSkRing * kSkCounterWords];
 
 namespace {
 
@@ -82,6 +88,38 @@ int set_error(int code, const std::string& msg) {
 
 int cuda_error(cudaError_t e, const char* what) {
   return set_error(CCV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+namespace {
+std::atomic<unsigned> g_sk_epoch[kMaxDevices];
+unsigned* g_sk_base[kMaxDevices] = {};
+}  // namespace
+
+unsigned* stream_k_counters() {
+  int dev = 0;
+  if (current_device(&dev) != CCV_OK) return nullptr;
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mutex);
+    if (g_sk_base[dev] == nullptr) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_ccv_sk_counters);
+      if (e != cudaSuccess) {
+        cuda_error(e, "cudaGetSymbolAddress(stream-K counters)");
+        return nullptr;
+      }
+      g_sk_base[dev] = static_cast<unsigned*>(p);
+    }
+  }
+  const unsigned slot = g_sk_epoch[dev].fetch_add(1u) % kSkRing;
+  return g_sk_base[dev] + static_cast<size_t>(slot) * kSkCounterWords;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* env = getenv("CCV_PDL");
+    return env == nullptr || atoi(env) != 0;
+  }();
+  return on;
 }
 
 int* device_status_ptr() {
@@ -462,8 +500,12 @@ int ccv_get_device_status(int* status) {
 
 int ccv_clear_device_status(void) {
   const int zero = 0;
-  const cudaError_t e = cudaMemcpyToSymbol(g_ccv_status, &zero, sizeof(int));
+  cudaError_t e = cudaMemcpyToSymbol(g_ccv_status, &zero, sizeof(int));
   if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyToSymbol(status)");
+  // A kernel that gave up may have left stream-K counters counted.
+  static const std::vector<unsigned> zeros(static_cast<size_t>(kSkRing) * kSkCounterWords, 0u);
+  e = cudaMemcpyToSymbol(g_ccv_sk_counters, zeros.data(), zeros.size() * sizeof(unsigned));
+  if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyToSymbol(stream-K counters)");
   return CCV_OK;
 }
 

@@ -167,8 +167,8 @@ __device__ __noinline__ bool split_piece_epilogue(const FpropParams& prm, WorkUn
   __threadfence();
   __syncwarp();
   unsigned old = 0;
+  unsigned* cnt = prm.split_count + (static_cast<long long>(w.sk) * 2 + rank) * 4 + quarter;
   if (lane == 0) {
-    unsigned* cnt = prm.split_count + (static_cast<long long>(w.sk) * 2 + rank) * 4 + quarter;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;"
                  : "=r"(old)
                  : "l"(cnt), "r"(static_cast<unsigned>(w.jend - w.jbeg))
@@ -177,6 +177,11 @@ __device__ __noinline__ bool split_piece_epilogue(const FpropParams& prm, WorkUn
   old = __shfl_sync(0xffffffffu, old, 0);
   const bool last =
       old + static_cast<unsigned>(w.jend - w.jbeg) == static_cast<unsigned>(prm.slots_per_tile);
+  // Every piece has counted: leave the counter zero for the next launch
+  // that uses this counter set.
+  if (last && lane == 0) {
+    asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(cnt), "r"(0u) : "memory");
+  }
   if (last) {
     __threadfence();
     int g0 = 0, g1 = 0;

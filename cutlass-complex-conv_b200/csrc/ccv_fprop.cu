@@ -92,7 +92,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t acc_bar = bar_base + 8u * (2 * C::kStages);
 
   if (threadIdx.x == 0) {
-    flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
     flags[1] = 0;
     for (int i = 0; i < C::kStages; ++i) {
       ptx::mbar_init(full_bar(i), 1);
@@ -113,6 +112,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
+  // Everything above may overlap the previous kernel on the stream
+  // (programmatic dependent launch); global memory is touched only below.
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
+  __syncthreads();
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
 
@@ -457,24 +462,9 @@ int launch_variant(FpropParams& prm, int tiles, int want_split, cudaStream_t str
   prm.splits = splits;
   const long long grid = static_cast<long long>(tiles) * splits;
   if (grid > 0x7fffffffLL) return set_error(CCV_ERR_UNSUPPORTED, "problem too large for the grid");
-  if (splits == 1) {
-    kern<<<static_cast<int>(grid), kThreads, C::kSmemBytes, stream>>>(prm);
-  } else {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = C::kSmemBytes;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = splits;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, prm);
-    if (le != cudaSuccess) return cuda_error(le, "fprop split-K kernel launch");
-  }
+  const cudaError_t le = launch_kernel(kern, dim3(static_cast<unsigned>(grid)), dim3(kThreads),
+                                       C::kSmemBytes, stream, splits, prm);
+  if (le != cudaSuccess) return cuda_error(le, "fprop kernel launch");
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "fprop kernel launch");
   return CCV_OK;

@@ -86,7 +86,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   const uint32_t stage_bar0 = bar_base + 8u * (2 * C::kStages + 8);
 
   if (threadIdx.x == 0) {
-    flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
     flags[1] = 0;
     for (int i = 0; i < C::kStages; ++i) {
       ptx::mbar_init(full_bar(i), 1);
@@ -116,6 +115,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   ptx::tc_fence_before();
   ptx::cluster_sync();
   ptx::tc_fence_after();
+  // Everything above may overlap the previous kernel on the stream
+  // (programmatic dependent launch); global memory is touched only below.
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
+  __syncthreads();
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
   const int rs = prm.r * prm.s;
@@ -327,8 +332,9 @@ int launch2_variant(FpropParams& prm, void* ws, size_t ws_bytes, cudaStream_t st
   const int launched = launch_clusters(prm, clusters, prm.ksteps * prm.passes, KT, ws, ws_bytes,
                                        stream, &rc);
   if (rc != CCV_OK) return rc;
-  kern<<<2 * launched, kThreads2, C::kSmemBytes, stream>>>(prm);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_kernel(kern, dim3(2 * launched), dim3(kThreads2), C::kSmemBytes, stream,
+                                0, prm);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "fprop2 kernel launch");
   return CCV_OK;
 }
@@ -361,8 +367,7 @@ size_t pair_split_workspace_bytes(int kt, int tiles, int slots) {
   const long long r = std::min<long long>(tiles, g);  // stream-K tiles, at most
   const long long gs = std::min<long long>(g, r * slots / kMinSkSlots);
   if (gs < 2) return 0;
-  // Counters: per stream-K tile x 2 CTAs x 4 epilogue warps.
-  return partial_bytes(static_cast<int>(gs), kt) + static_cast<size_t>(r) * 8 * sizeof(unsigned);
+  return partial_bytes(static_cast<int>(gs), kt);
 }
 
 int cluster_cap(int max_clusters) {
@@ -402,28 +407,25 @@ int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, s
   const long long sk_time = q * slots + per_range;
   if (mode != 1 && (slots < 4 || (dp_time - sk_time) * 10 < dp_time)) return 0;
   const size_t pbytes = partial_bytes(gs, kt);
-  const size_t cbytes = static_cast<size_t>(r) * 8 * sizeof(unsigned);
-  if (ws_bytes < pbytes + cbytes || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return 0;
+  if (ws_bytes < pbytes || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return 0;
+  if (r * 8 > kSkCounterWords) return 0;
+  unsigned* counters = stream_k_counters();
+  if (counters == nullptr) return 0;
   prm.sk_start = T - r;
   prm.sk_slots = X;
   prm.sk_clusters = gs;
   prm.split_ws = static_cast<float*>(ws);
-  prm.split_count = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + pbytes);
+  prm.split_count = counters;
   return r * 8;
 }
 
 int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
                     cudaStream_t stream, int* rc) {
+  (void)stream;
   *rc = CCV_OK;
   clusters = std::max(1, clusters);
-  const int counters = plan_stream_k(prm, clusters, slots, kt, ws, ws_bytes);
-  if (counters > 0) {
-    const cudaError_t e =
-        cudaMemsetAsync(prm.split_count, 0, static_cast<size_t>(counters) * sizeof(unsigned),
-                        stream);
-    if (e != cudaSuccess) *rc = cuda_error(e, "cudaMemsetAsync(stream-K counters)");
-    return clusters;
-  }
+  // Stream-K counters come zeroed from the library's ring (no memset).
+  if (plan_stream_k(prm, clusters, slots, kt, ws, ws_bytes) > 0) return clusters;
   return std::max(1, std::min(prm.num_tiles, clusters));
 }
 

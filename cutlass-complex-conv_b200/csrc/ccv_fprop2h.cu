@@ -91,7 +91,6 @@ __global__ void __cluster_dims__(2, 1, 1)
   const uint32_t a_plane_bytes = static_cast<uint32_t>(prm.a_slot_bytes / 2);
 
   if (threadIdx.x == 0) {
-    flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
     flags[1] = 0;
     for (int i = 0; i < SA; ++i) {
       // Fused complex path: one arrival per converter warp of both CTAs.
@@ -128,6 +127,12 @@ __global__ void __cluster_dims__(2, 1, 1)
   ptx::tc_fence_before();
   ptx::cluster_sync();
   ptx::tc_fence_after();
+  // Everything above may overlap the previous kernel on the stream
+  // (programmatic dependent launch); global memory is touched only below.
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
+  __syncthreads();
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
   const int per_img = prm.tiles_bp * prm.tiles_bq;
@@ -427,8 +432,9 @@ int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
   int rc;
   const int launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc);
   if (rc != CCV_OK) return rc;
-  kern<<<2 * launched, threads, smem_bytes, stream>>>(prm);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_kernel(kern, dim3(2 * launched), dim3(threads), smem_bytes, stream, 0,
+                                prm);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "fprop2h kernel launch");
   return CCV_OK;
 }

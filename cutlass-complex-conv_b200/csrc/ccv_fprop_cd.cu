@@ -135,7 +135,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsCD, 1)
   const int ndirect = (S + 1) / 2;   // even s
 
   if (threadIdx.x == 0) {
-    flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
     flags[1] = 0;
     for (int g = 0; g < G; ++g) {
       ptx::mbar_init(a_dfull(g), 1);
@@ -165,6 +164,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreadsCD, 1)
   ptx::tc_fence_before();
   ptx::cluster_sync();
   ptx::tc_fence_after();
+  // Everything above may overlap the previous kernel on the stream
+  // (programmatic dependent launch); global memory is touched only below.
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
+  __syncthreads();
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
   const int per_img = prm.tiles_bp * prm.tiles_bq;
@@ -496,8 +501,9 @@ int launch_cd_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_byte
       launch_clusters(prm, cluster_cap(max_clusters[dev & 63]), prm.slots_per_tile, KT, nullptr,
                       0, stream, &rc);
   if (rc != CCV_OK) return rc;
-  kern<<<2 * launched, kThreadsCD, smem_bytes, stream>>>(prm);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_kernel(kern, dim3(2 * launched), dim3(kThreadsCD), smem_bytes, stream, 0,
+                                prm);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "fprop_cd kernel launch");
   return CCV_OK;
 }

@@ -40,9 +40,10 @@ struct alignas(64) FpropParams {
   // cut into sk_clusters contiguous ranges, range g going to cluster g before
   // its whole tiles.  A tile covered by several ranges is "split": each piece
   // writes fp32 partial rows to split_ws and adds its slot count to a counter
-  // in split_count; the piece that brings the count to L (the last to finish;
-  // nobody waits) sums all pieces' partials in cluster order and stores the
-  // output.  sk_slots == 0: no tail split (split_ws unused).
+  // in split_count (a zeroed library-owned set); the piece that brings the
+  // count to L (the last to finish; nobody waits) sums all pieces' partials in
+  // cluster order, stores the output and zeroes the counter.  sk_slots == 0:
+  // no tail split (split_ws unused).
   int sk_start, sk_clusters, slots_per_tile;
   long long sk_slots;  // < 2^31 (checked on the host)
   float* split_ws;
@@ -218,8 +219,8 @@ size_t pair_split_workspace_bytes(int kt, int tiles, int slots);
 int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes);
 // Persistent-grid size after the CCV_MAX_CLUSTERS testing cap.
 int cluster_cap(int max_clusters);
-// Plans the stream-K split (zeroing its counters on `stream`) and returns
-// the number of clusters to launch; *rc receives the status.
+// Plans the stream-K split and returns the number of clusters to launch;
+// *rc receives the status.
 int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
                     cudaStream_t stream, int* rc);
 Tiling choose_halo_tiling(const Problem& pb);

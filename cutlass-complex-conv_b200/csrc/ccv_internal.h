@@ -85,4 +85,46 @@ int encode_tiled_ex(CUtensorMap* map, const void* base, int rank, const uint64_t
 
 int launch_selftest_wait(int* status_dev, cudaStream_t stream);
 
+// Stream-K tile counters for one launch: a zeroed set of kSkCounterWords
+// words in library-owned device memory (a ring of sets, so launches in
+// flight at the same time use different sets).  Each split tile's counter is
+// reset by the piece that completes it, so a set is zero again when its
+// kernel ends; ccv_clear_device_status re-zeroes the ring after an abort.
+constexpr int kSkCounterWords = 1024;
+unsigned* stream_k_counters();
+
+// Programmatic dependent launch for the library's kernels (each calls
+// griddepcontrol.wait before its first global-memory access, so its prologue
+// may overlap the previous kernel's tail).  CCV_PDL=0 turns it off.
+bool pdl_enabled();
+
+// cudaLaunchKernelEx with PDL (when enabled) and, for cluster_x > 1, a
+// runtime cluster size.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t stream, int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned na = 0;
+  if (cluster_x > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 }  // namespace ccv

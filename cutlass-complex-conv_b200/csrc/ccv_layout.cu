@@ -10,6 +10,7 @@
 #include <algorithm>
 
 #include "ccv_internal.h"
+#include "ccv_ptx.cuh"
 
 namespace ccv {
 
@@ -27,6 +28,8 @@ __device__ __forceinline__ float to_tf32(float x) {
 __global__ void ccv_prepack_kernel(const float* __restrict__ wr, const float* __restrict__ wi,
                                    float* __restrict__ out, int K, int C, int R, int S, int krsc,
                                    int split) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
   const long long total = static_cast<long long>(R) * S * K * C;
   const long long image = total * 3;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -64,6 +67,8 @@ __global__ void ccv_split_planes_kernel(const float4* __restrict__ xr, const flo
                                         float4* __restrict__ hr, float4* __restrict__ hi,
                                         float4* __restrict__ lr, float4* __restrict__ li,
                                         long long count4) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count4;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const float4 a = xr[i];
@@ -77,38 +82,52 @@ __global__ void ccv_split_planes_kernel(const float4* __restrict__ xr, const flo
   }
 }
 
-// complex64 NCHW -> two fp32 NHWC planes, 32x32 (C x W) tiles per (n, h).
-// With xr_lo/xi_lo set, writes tf32(x) and x - tf32(x) instead (3xTF32).
-__global__ void ccv_nchw_to_planar_kernel(const float2* __restrict__ x, float* __restrict__ xr,
-                                          float* __restrict__ xi, float* __restrict__ xr_lo,
-                                          float* __restrict__ xi_lo, int C, int H, int W) {
-  __shared__ float tr[32][33];
-  __shared__ float ti[32][33];
+// complex64 NCHW -> two fp32 NHWC planes.  One block per (n, h) row and a
+// 32-channel x 64-pixel tile: every thread issues its 8 loads (256-byte runs
+// along W per warp) before touching shared memory, then writes 8 channel-
+// contiguous runs (128 bytes per warp and plane).  With xr_lo/xi_lo set,
+// writes tf32(x) and x - tf32(x) instead (3xTF32).
+constexpr int kLayoutW = 64;
+
+__global__ void __launch_bounds__(256) ccv_nchw_to_planar_kernel(
+    const float2* __restrict__ x, float* __restrict__ xr, float* __restrict__ xi,
+    float* __restrict__ xr_lo, float* __restrict__ xi_lo, int C, int H, int W) {
+  __shared__ float tr[32][kLayoutW + 1];
+  __shared__ float ti[32][kLayoutW + 1];
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
   const int nh = blockIdx.z;
   const int n = nh / H;
   const int h = nh - n * H;
-  const int w0 = blockIdx.x * 32;
+  const int w0 = blockIdx.x * kLayoutW;
   const int c0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;
+  float2 v[8];
 #pragma unroll
-  for (int i = 0; i < 32; i += 8) {
-    const int c = c0 + ty + i;
-    const int w = w0 + tx;
-    if (c < C && w < W) {
-      const float2 v = x[((static_cast<long long>(n) * C + c) * H + h) * W + w];
-      tr[ty + i][tx] = v.x;
-      ti[ty + i][tx] = v.y;
-    }
+  for (int i = 0; i < 8; ++i) {
+    const int c = c0 + ty + 8 * (i & 3);
+    const int w = w0 + tx + 32 * (i >> 2);
+    v[i] = (c < C && w < W) ? __ldg(x + ((static_cast<long long>(n) * C + c) * H + h) * W + w)
+                            : make_float2(0.f, 0.f);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int cl = ty + 8 * (i & 3);
+    const int wl = tx + 32 * (i >> 2);
+    tr[cl][wl] = v[i].x;
+    ti[cl][wl] = v[i].y;
   }
   __syncthreads();
+  const int c = c0 + tx;
+  if (c >= C) return;
 #pragma unroll
-  for (int i = 0; i < 32; i += 8) {
-    const int w = w0 + ty + i;
-    const int c = c0 + tx;
-    if (c < C && w < W) {
+  for (int i = 0; i < 8; ++i) {
+    const int wl = ty + 8 * i;
+    const int w = w0 + wl;
+    if (w < W) {
       const long long o = ((static_cast<long long>(n) * H + h) * W + w) * C + c;
-      const float a = tr[tx][ty + i];
-      const float b = ti[tx][ty + i];
+      const float a = tr[tx][wl];
+      const float b = ti[tx][wl];
       if (xr_lo != nullptr) {
         const float ah = to_tf32(a);
         const float bh = to_tf32(b);
@@ -131,10 +150,11 @@ int launch_prepack(const float* w_real, const float* w_imag, int layout, const P
   const long long total = static_cast<long long>(pb.r) * pb.s * pb.k * pb.c;
   const int threads = 256;
   const long long blocks = std::min<long long>((total + threads - 1) / threads, 148LL * 16);
-  ccv_prepack_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(
-      w_real, w_imag, packed, pb.k, pb.c, pb.r, pb.s, layout == CCV_WEIGHT_KRSC ? 1 : 0,
-      precision == CCV_PRECISION_3XTF32 ? 1 : 0);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_kernel(ccv_prepack_kernel, dim3(static_cast<unsigned>(blocks)),
+                                dim3(threads), 0, stream, 0, w_real, w_imag, packed, pb.k, pb.c,
+                                pb.r, pb.s, layout == CCV_WEIGHT_KRSC ? 1 : 0,
+                                precision == CCV_PRECISION_3XTF32 ? 1 : 0);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "prepack kernel launch");
   return CCV_OK;
 }
@@ -143,11 +163,12 @@ int launch_nchw_complex_to_planar(const float* x, float* xr, float* xi, float* x
                                   float* xi_lo, const Problem& pb, cudaStream_t stream) {
   const long long nh = static_cast<long long>(pb.n) * pb.h;
   if (nh > 65535) return set_error(CCV_ERR_UNSUPPORTED, "N*H too large for the layout kernel");
-  dim3 grid((pb.w + 31) / 32, (pb.c + 31) / 32, static_cast<unsigned>(nh));
+  dim3 grid((pb.w + kLayoutW - 1) / kLayoutW, (pb.c + 31) / 32, static_cast<unsigned>(nh));
   dim3 block(32, 8);
-  ccv_nchw_to_planar_kernel<<<grid, block, 0, stream>>>(reinterpret_cast<const float2*>(x), xr,
-                                                         xi, xr_lo, xi_lo, pb.c, pb.h, pb.w);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_kernel(ccv_nchw_to_planar_kernel, grid, block, 0, stream, 0,
+                                reinterpret_cast<const float2*>(x), xr, xi, xr_lo, xi_lo, pb.c,
+                                pb.h, pb.w);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "layout kernel launch");
   return CCV_OK;
 }
@@ -158,11 +179,13 @@ int launch_split_planes(const float* xr, const float* xi, float* hr, float* hi, 
   const long long c4 = static_cast<long long>(count / 4);
   const int threads = 256;
   const long long blocks = std::min<long long>((c4 + threads - 1) / threads, 148LL * 16);
-  ccv_split_planes_kernel<<<static_cast<int>(std::max<long long>(blocks, 1)), threads, 0, stream>>>(
-      reinterpret_cast<const float4*>(xr), reinterpret_cast<const float4*>(xi),
-      reinterpret_cast<float4*>(hr), reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lr),
-      reinterpret_cast<float4*>(li), c4);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_kernel(
+      ccv_split_planes_kernel, dim3(static_cast<unsigned>(std::max<long long>(blocks, 1))),
+      dim3(threads), 0, stream, 0, reinterpret_cast<const float4*>(xr),
+      reinterpret_cast<const float4*>(xi), reinterpret_cast<float4*>(hr),
+      reinterpret_cast<float4*>(hi), reinterpret_cast<float4*>(lr), reinterpret_cast<float4*>(li),
+      c4);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "split kernel launch");
   return CCV_OK;
 }

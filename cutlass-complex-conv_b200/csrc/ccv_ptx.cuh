@@ -152,6 +152,16 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// Programmatic dependent launch: wait until the grids this launch depends on
+// have completed and their memory is visible (returns at once without PDL),
+// then allow the next PDL launch on the stream to begin its prologue.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Untiled bulk copy global -> this CTA's shared memory (16-byte aligned
 // addresses, size a multiple of 16), completing `bytes` on `bar`.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
