@@ -11,6 +11,7 @@ shapes.
 
     python cutlass-complex-conv_b200/benchmarks/benchmark_conv2d.py [--cases a,b] [--json]
     python .../benchmark_conv2d.py --cases b64_128_128_56 --only planar --iters 1 --warmup 1
+    python .../benchmark_conv2d.py --cases b64_128_128_56 --only forward --iters 2 --warmup 1
 """
 
 import argparse
@@ -154,6 +155,10 @@ def run_case(case, device, warmup, iters, only, precision):
     if not close:
         raise RuntimeError(f"{case.name}: correctness check failed (max_error={err:.3e})")
     res["max_error"] = err
+    if only == "forward":
+        res["forward_ms"] = benchmark_cuda(lambda: mod(x), warmup, iters)
+        res["tflops_forward"] = case.flops / (res["forward_ms"] * 1e-3) / 1e12
+        return res
     res["baseline_ms"] = benchmark_cuda(lambda: base(x), warmup, iters)
     res["forward_ms"] = benchmark_cuda(lambda: mod(x), warmup, iters)
     if case.n == 1:
@@ -174,7 +179,7 @@ def main():
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--device", default="cuda")
     ap.add_argument("--cases", default="all")
-    ap.add_argument("--only", choices=["all", "planar"], default="all")
+    ap.add_argument("--only", choices=["all", "planar", "forward"], default="all")
     ap.add_argument("--precision", default="tf32")
     ap.add_argument("--json", action="store_true")
     args = ap.parse_args()

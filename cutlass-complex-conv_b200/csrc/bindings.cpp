@@ -12,6 +12,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <string>
 #include <vector>
 
 #include "ccv_b200.h"
@@ -192,8 +193,53 @@ torch::Tensor forward_complex_packed(torch::Tensor x, torch::Tensor w_packed, in
   return y;
 }
 
-// Kernel launches of one forward_complex_packed call: 1 when the fused
-// complex-input kernel serves the problem, 2 with the layout pass.
+// Planar NHWC planes in, complex64 NKPQ out (the conv launch of forward()
+// without its layout pass).
+torch::Tensor forward_planar_to_complex_packed(torch::Tensor x_real, torch::Tensor x_imag,
+                                               torch::Tensor w_packed, int64_t in_channels,
+                                               int64_t K, int64_t R, int64_t S, int64_t stride_h,
+                                               int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                               int64_t precision) {
+  CHECK_CUDA(x_real); CHECK_CUDA(x_imag); CHECK_CUDA(w_packed);
+  CHECK_FLOAT(x_real); CHECK_FLOAT(x_imag); CHECK_FLOAT(w_packed);
+  CHECK_CONTIGUOUS(x_real); CHECK_CONTIGUOUS(x_imag); CHECK_CONTIGUOUS(w_packed);
+  TORCH_CHECK(x_real.dim() == 4 && x_real.sizes() == x_imag.sizes(),
+              "x_real and x_imag must be 4D NHWC tensors of identical shape");
+  c10::cuda::CUDAGuard guard(x_real.device());
+  const int64_t N = x_real.size(0), H = x_real.size(1), W = x_real.size(2), C = x_real.size(3);
+  TORCH_CHECK(C == in_channels, "input channel count must match the weight channel count");
+  ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
+  int64_t P = 0, Q = 0;
+  check_rc(ccv_output_size(&shp, &P, &Q), "shape check");
+  TORCH_CHECK(static_cast<size_t>(w_packed.numel()) * 4 >=
+                  ccv_packed_weight_bytes(&shp, static_cast<int>(precision)),
+              "packed weights do not match the problem");
+  auto y = torch::empty({N, K, P, Q}, x_real.options().dtype(at::kComplexFloat));
+  const size_t ws_bytes = ccv_fprop_planar_workspace_bytes(&shp, static_cast<int>(precision));
+  torch::Tensor ws;
+  void* ws_ptr = nullptr;
+  if (ws_bytes > 0) {
+    ws = torch::empty({static_cast<int64_t>(ws_bytes)}, x_real.options().dtype(torch::kUInt8));
+    ws_ptr = ws.data_ptr();
+  }
+  check_rc(ccv_fprop_planar_to_complex(x_real.data_ptr<float>(), x_imag.data_ptr<float>(),
+                                       w_packed.data_ptr(), y.data_ptr(), &shp,
+                                       static_cast<int>(precision), ws_ptr, ws_bytes,
+                                       current_stream()),
+           "ccv_fprop_planar_to_complex");
+  return y;
+}
+
+// Name of the kernel path forward_complex_packed takes.
+std::string complex_forward_kernel(int64_t N, int64_t C, int64_t H, int64_t W, int64_t K,
+                                   int64_t R, int64_t S, int64_t stride_h, int64_t stride_w,
+                                   int64_t pad_h, int64_t pad_w, int64_t precision) {
+  ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
+  return std::string(ccv_fprop_complex_kernel(&shp, static_cast<int>(precision)));
+}
+
+// Kernel launches of one forward_complex_packed call: 1 for the one-launch
+// kernels, 2 with the layout pass (3 for 3xTF32 with a split pass).
 int64_t complex_forward_launches(int64_t N, int64_t C, int64_t H, int64_t W, int64_t K, int64_t R,
                                  int64_t S, int64_t stride_h, int64_t stride_w, int64_t pad_h,
                                  int64_t pad_w, int64_t precision) {
@@ -246,6 +292,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("out_channels"), pybind11::arg("kernel_h"), pybind11::arg("kernel_w"),
         pybind11::arg("stride_h"), pybind11::arg("stride_w"), pybind11::arg("pad_h"),
         pybind11::arg("pad_w"), pybind11::arg("precision"));
+  m.def("forward_planar_to_complex_packed", &forward_planar_to_complex_packed,
+        "planar NHWC in, complex64 NCHW out, packed weights", pybind11::arg("x_real"),
+        pybind11::arg("x_imag"), pybind11::arg("w_packed"), pybind11::arg("in_channels"),
+        pybind11::arg("out_channels"), pybind11::arg("kernel_h"), pybind11::arg("kernel_w"),
+        pybind11::arg("stride_h"), pybind11::arg("stride_w"), pybind11::arg("pad_h"),
+        pybind11::arg("pad_w"), pybind11::arg("precision"));
+  m.def("complex_forward_kernel", &complex_forward_kernel, pybind11::arg("n"),
+        pybind11::arg("c"), pybind11::arg("h"), pybind11::arg("w"), pybind11::arg("k"),
+        pybind11::arg("r"), pybind11::arg("s"), pybind11::arg("stride_h"),
+        pybind11::arg("stride_w"), pybind11::arg("pad_h"), pybind11::arg("pad_w"),
+        pybind11::arg("precision"));
   m.def("complex_forward_launches", &complex_forward_launches, pybind11::arg("n"),
         pybind11::arg("c"), pybind11::arg("h"), pybind11::arg("w"), pybind11::arg("k"),
         pybind11::arg("r"), pybind11::arg("s"), pybind11::arg("stride_h"),

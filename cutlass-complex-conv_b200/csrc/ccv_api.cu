@@ -401,6 +401,53 @@ int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_pac
                       y_real, y_imag, pb, precision, OUT_PLANAR_NHWC, sk, sk_bytes, st);
 }
 
+int ccv_fprop_planar_to_complex(const float* x_real, const float* x_imag, const void* w_packed,
+                                void* y, const ccv_conv_shape* shape, int precision,
+                                void* workspace, size_t workspace_bytes, ccv_stream_t stream) {
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if (precision != CCV_PRECISION_TF32 && precision != CCV_PRECISION_3XTF32) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "unknown precision");
+  }
+  if (!x_real || !x_imag || !w_packed || !y) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  }
+  if (!aligned16(x_real) || !aligned16(x_imag) || !aligned16(w_packed) || !aligned16(y)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  }
+  const size_t need = planar_required_bytes(pb, precision);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
+  }
+  if ((rc = check_device()) != CCV_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  void* sk = nullptr;
+  size_t sk_bytes = 0;
+  split_scratch(workspace, workspace_bytes, need, &sk, &sk_bytes);
+  const float* xr = x_real;
+  const float* xi = x_imag;
+  const float* lr = nullptr;
+  const float* li = nullptr;
+  if (precision == CCV_PRECISION_3XTF32) {
+    const size_t pl = plane_bytes_aligned(pb);
+    char* ws = static_cast<char*>(workspace);
+    float* hr = reinterpret_cast<float*>(ws);
+    float* hi = reinterpret_cast<float*>(ws + pl);
+    float* wlr = reinterpret_cast<float*>(ws + 2 * pl);
+    float* wli = reinterpret_cast<float*>(ws + 3 * pl);
+    rc = launch_split_planes(x_real, x_imag, hr, hi, wlr, wli,
+                             static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c, st);
+    if (rc != CCV_OK) return rc;
+    xr = hr;
+    xi = hi;
+    lr = wlr;
+    li = wli;
+  }
+  return launch_fprop(xr, xi, lr, li, static_cast<const float*>(w_packed), static_cast<float*>(y),
+                      nullptr, pb, precision, OUT_COMPLEX_NCHW, sk, sk_bytes, st);
+}
+
 int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_conv_shape* shape,
                       int precision, void* workspace, size_t workspace_bytes,
                       ccv_stream_t stream) {

@@ -546,12 +546,26 @@ size_t split_workspace_bytes(const Problem& pb, int precision, bool complex_inpu
   }
 }
 
+// The halo kernel with converter warps (one launch, no workspace) or a
+// layout pass plus the planar-input halo kernel.  Opt in with CCV_FUSED=1:
+// measured on B200 the layout pass (~7 TB/s) plus the TMA-fed kernel is
+// faster on every stride-1 layer (b64 128->128 56x56: 420 vs 440 us; b32
+// 64->64 320x320: 2.76 vs 2.88 ms TF32, 7.11 vs 8.24 ms 3xTF32): the
+// converter warps' scattered 8-byte loads (each input element read once per
+// filter column) cost more than one streaming pass.
+bool use_converter_warps(const Problem& pb, int precision, const Tiling& th) {
+  (void)precision;
+  if (!halo_fused_supported(pb, th)) return false;
+  const char* env = getenv("CCV_FUSED");
+  return env != nullptr && atoi(env) == 1;
+}
+
 bool fused_complex_available(const Problem& pb, int precision) {
   if (use_complex_direct(pb, precision)) return true;
   const Tiling t = choose_tiling(pb);
   Tiling th;
   return choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th) == kPairHalo &&
-         halo_fused_supported(pb, th);
+         use_converter_warps(pb, precision, th);
 }
 
 const char* complex_kernel_name(const Problem& pb, int precision) {
@@ -561,7 +575,8 @@ const char* complex_kernel_name(const Problem& pb, int precision) {
   Tiling th;
   switch (choose_family(pb, split, t, &th)) {
     case kPairHalo:
-      return halo_fused_supported(pb, th) ? "halo_pair_converter_warps" : "layout_pass+halo_pair";
+      return use_converter_warps(pb, precision, th) ? "halo_pair_converter_warps"
+                                                    : "layout_pass+halo_pair";
     case kPairTap:
       return "layout_pass+tap_pair";
     default:
@@ -578,7 +593,7 @@ int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;
-  if (choose_family(pb, split, t, &th) != kPairHalo || !halo_fused_supported(pb, th)) {
+  if (choose_family(pb, split, t, &th) != kPairHalo || !use_converter_warps(pb, precision, th)) {
     return set_error(CCV_ERR_UNSUPPORTED, "no fused complex kernel for this problem");
   }
   return launch_fprop_pair_halo(nullptr, nullptr, nullptr, nullptr, xc, split, w_packed, y,

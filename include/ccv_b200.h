@@ -133,6 +133,13 @@ int ccv_fprop_complex(const void* x, const void* w_packed, void* y,
                       const ccv_conv_shape* shape, int precision, void* workspace,
                       size_t workspace_bytes, ccv_stream_t stream);
 
+/* Planar fp32 NHWC in, complex64 NKPQ out: the convolution launch of
+ * ccv_fprop_complex without its layout pass (for callers that hold planar
+ * activations but want complex output).  Workspace as ccv_fprop_planar. */
+int ccv_fprop_planar_to_complex(const float* x_real, const float* x_imag, const void* w_packed,
+                                void* y, const ccv_conv_shape* shape, int precision,
+                                void* workspace, size_t workspace_bytes, ccv_stream_t stream);
+
 /* The reference extension call itself: `_C.forward(x_real, x_imag, w_real,
  * w_imag, stride_h, stride_w, pad_h, pad_w)` (csrc/bindings.cpp:16-29) with
  * KRSC weights, TF32.  Needs the packed weight bytes (256-byte aligned) of

@@ -64,6 +64,8 @@ def load():
                                                      ctypes.POINTER(ctypes.c_int)]),
         "ccv_fprop_planar": (ctypes.c_int, [vp, vp, vp, vp, vp, sp, ctypes.c_int, vp, sz, vp]),
         "ccv_fprop_complex": (ctypes.c_int, [vp, vp, vp, sp, ctypes.c_int, vp, sz, vp]),
+        "ccv_fprop_planar_to_complex": (ctypes.c_int, [vp, vp, vp, vp, sp, ctypes.c_int, vp, sz,
+                                                       vp]),
         "ccv_fprop_complex_kernel": (ctypes.c_char_p, [sp, ctypes.c_int]),
         "ccv_forward_workspace_bytes": (sz, [sp]),
         "ccv_forward": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, sp, vp, sz, vp]),

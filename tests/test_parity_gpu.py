@@ -81,6 +81,24 @@ def abi_fprop_complex(case, x, packed, precision=ccv_abi.CCV_PRECISION_TF32, poi
     return y.cpu()
 
 
+def abi_fprop_planar_to_complex(case, x, packed, precision=ccv_abi.CCV_PRECISION_TF32):
+    """Planar NHWC in (built from complex64 NCHW x), complex64 NKPQ out."""
+    lib = ccv_abi.load()
+    shp = ccv_abi.shape_of(case)
+    xr = x.real.permute(0, 2, 3, 1).contiguous().to(DEV)
+    xi = x.imag.permute(0, 2, 3, 1).contiguous().to(DEV)
+    y = torch.full((case.n, case.k, case.p, case.q), float("nan"), dtype=torch.complex64,
+                   device=DEV)
+    ws_bytes = lib.ccv_fprop_planar_workspace_bytes(ctypes.byref(shp), precision)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=DEV)
+    ccv_abi.check(lib.ccv_fprop_planar_to_complex(_ptr(xr), _ptr(xi), _ptr(packed), _ptr(y),
+                                                  ctypes.byref(shp), precision,
+                                                  _ptr(ws) if ws_bytes else None, ws_bytes,
+                                                  _stream()), "fprop_planar_to_complex")
+    torch.cuda.synchronize()
+    return y.cpu()
+
+
 def device_status():
     lib = ccv_abi.load()
     st = ctypes.c_int(-1)
@@ -113,6 +131,18 @@ def test_golden_complex_matches_planar_bitwise(name, case, x, wr, wi, y32, y64):
     yp = abi_fprop_planar(case, xt, packed)
     assert torch.equal(yc, yp.to(torch.complex64))
     assert oracle.rel_frobenius(yc, y64) <= TF32_TOL
+
+
+@pytest.mark.parametrize("name,case,x,wr,wi,y32,y64", GOLDEN_CASES, ids=[c[0] for c in GOLDEN_CASES])
+def test_golden_planar_to_complex_entry(name, case, x, wr, wi, y32, y64):
+    """Planar input with complex output runs forward()'s convolution launch:
+    bitwise equal to ccv_fprop_complex (which adds the layout pass)."""
+    xt = torch.from_numpy(x)
+    for prec in (ccv_abi.CCV_PRECISION_TF32, ccv_abi.CCV_PRECISION_3XTF32):
+        packed = abi_prepack(case, torch.from_numpy(wr), torch.from_numpy(wi), precision=prec)
+        y = abi_fprop_planar_to_complex(case, xt, packed, precision=prec)
+        assert not torch.isnan(y.real).any() and not torch.isnan(y.imag).any()
+        assert torch.equal(y, abi_fprop_complex(case, xt, packed, precision=prec)), (name, prec)
 
 
 @pytest.mark.parametrize("name,case,x,wr,wi,y32,y64", GOLDEN_CASES[:4], ids=[c[0] for c in GOLDEN_CASES[:4]])
