@@ -178,6 +178,7 @@ int encode_tiled_ex(CUtensorMap* map, const void* base, int rank, const uint64_t
   }
   const CUtensorMapSwizzle sw = swizzle == kSwizzle128        ? CU_TENSOR_MAP_SWIZZLE_128B
                                 : swizzle == kSwizzle128Atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                : swizzle == kSwizzleNone      ? CU_TENSOR_MAP_SWIZZLE_NONE
                                                                : CU_TENSOR_MAP_SWIZZLE_64B;
   // 8-byte elements (complex64 moved as opaque 64-bit words) or fp32.
   const CUresult r = g_encode_tiled(

@@ -97,6 +97,86 @@ __device__ __forceinline__ void store_accumulator(const FpropParams& prm, uint32
   }
 }
 
+// Planar output through TMA stores.  The warp's 32 rows (TMEM lanes) are one
+// box of the output: `stage` (this warp's 4 KB: 32 rows x 16 channels for
+// each plane) is filled from TMEM 16 channels at a time and lane 0 issues the
+// two tensor stores; the next chunk waits until those have read the buffer.
+// (c1, c2, c3) are the box's pixel coordinates in the output tensor map
+// (q, p, n; or m, -, - for flat tiles).  `valid`: the box holds real pixels.
+template <int KT, bool FLAT>
+__device__ __forceinline__ void store_accumulator_tma(const FpropParams& prm, uint32_t t_acc,
+                                                      int k0, bool valid, int c1, int c2, int c3,
+                                                      uint8_t* stage, int lane) {
+  float* sr = reinterpret_cast<float*>(stage);
+  float* si = sr + 32 * 16;
+  const uint32_t ur = ptx::smem_u32(sr);
+  const uint32_t ui = ptx::smem_u32(si);
+#pragma unroll 1
+  for (int ch = 0; ch < KT; ch += 16) {
+    uint32_t vr[16], vi[16];
+    ptx::tmem_ld_32x32b_x16(t_acc + ch, vr);
+    ptx::tmem_ld_32x32b_x16(t_acc + KT + ch, vi);
+    ptx::tmem_wait_ld();
+    const bool go = valid && k0 + ch < prm.k;
+    if (!go) continue;
+    // The previous chunk's stores have read the buffer.
+    if (lane == 0) ptx::bulk_wait_read_all();
+    __syncwarp();
+    // Row `lane`: 16 channels (64 B).  Rotating the float4 order spreads a
+    // warp's writes over all banks.
+    float4 fr[4], fi[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      fr[j] = make_float4(__uint_as_float(vr[4 * j]), __uint_as_float(vr[4 * j + 1]),
+                          __uint_as_float(vr[4 * j + 2]), __uint_as_float(vr[4 * j + 3]));
+      fi[j] = make_float4(__uint_as_float(vi[4 * j]), __uint_as_float(vi[4 * j + 1]),
+                          __uint_as_float(vi[4 * j + 2]), __uint_as_float(vi[4 * j + 3]));
+    }
+    const int rot = (lane >> 1) & 3;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int qd = (j + rot) & 3;
+      // Register selects (a runtime index into fr/fi would go to local memory).
+      const float4 a = qd == 0 ? fr[0] : qd == 1 ? fr[1] : qd == 2 ? fr[2] : fr[3];
+      const float4 b = qd == 0 ? fi[0] : qd == 1 ? fi[1] : qd == 2 ? fi[2] : fi[3];
+      reinterpret_cast<float4*>(sr + lane * 16)[qd] = a;
+      reinterpret_cast<float4*>(si + lane * 16)[qd] = b;
+    }
+    ptx::fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (FLAT) {
+        ptx::tma_store_2d(&prm.tm_y0, ur, k0 + ch, c1);
+        ptx::tma_store_2d(&prm.tm_y1, ui, k0 + ch, c1);
+      } else {
+        ptx::tma_store_4d(&prm.tm_y0, ur, k0 + ch, c1, c2, c3);
+        ptx::tma_store_4d(&prm.tm_y1, ui, k0 + ch, c1, c2, c3);
+      }
+      ptx::bulk_commit_group();
+    }
+  }
+}
+
+// First output pixel of epilogue warp `quarter` of tile half `half` in the
+// coordinates of the planar output maps; false when it holds no output.
+template <bool FLAT>
+__device__ __forceinline__ bool warp_box_origin(const FpropParams& prm, int half, int quarter,
+                                                int& c1, int& c2, int& c3) {
+  if constexpr (FLAT) {
+    const long long m = static_cast<long long>(half) * kBlockM + quarter * 32;
+    c1 = static_cast<int>(m);
+    c2 = c3 = 0;
+    return m < prm.m_total;
+  } else {
+    int img = 0, op = 0, oq = 0;
+    const bool ok = tile_row_pixel<false>(prm, half, quarter * 32, img, op, oq);
+    c1 = oq;
+    c2 = op;
+    c3 = img;
+    return ok;
+  }
+}
+
 // Epilogue of one piece of a split (stream-K) tile, for the 32 rows of one
 // warp (`quarter`) of CTA `rank`.  The warp writes its TMEM accumulator rows
 // to this piece's partial buffer and adds the piece's slot count to the

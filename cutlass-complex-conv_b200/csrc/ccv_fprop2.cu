@@ -49,7 +49,8 @@ struct Cfg2 {
   static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;
   static constexpr int kBarOffset = kStages * kStageBytes;
   static constexpr int kBarBytes = 1024;
-  static constexpr int kSmemBytes = kBarOffset + kBarBytes + 1024;
+  static constexpr int kOutStageOffset = kBarOffset + kBarBytes;  // TMA-store staging
+  static constexpr int kSmemBytes = kOutStageOffset + kOutStageBytes + 1024;
   static_assert(kStages >= 3, "pipeline too shallow");
   static_assert((2 * kStages + 8 + 4 * kStageBufs) * 8 <= kBarBytes, "barrier block overflow");
   static_assert(kSmemBytes <= 232448, "shared memory");
@@ -281,8 +282,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
             op, oq, t_free, final_unit ? smem + quarter * per_warp : nullptr, per_warp,
             stage_bar0 + 8u * kStageBufs * static_cast<uint32_t>(quarter));
       } else {
-        store_accumulator<KT, OUT_COMPLEX>(prm, t_acc, n_tile * KT, in_tile && ok && !flags[1],
-                                           img, op, oq);
+        bool tma_out = false;
+        if constexpr (!OUT_COMPLEX) tma_out = prm.out_tma != 0;
+        if (tma_out) {
+          int c1 = 0, c2 = 0, c3 = 0;
+          const bool wv = warp_box_origin<FLAT>(prm, half, quarter, c1, c2, c3) && ok && !flags[1];
+          store_accumulator_tma<KT, FLAT>(prm, t_acc, n_tile * KT, wv, c1, c2, c3,
+                                          smem + C::kOutStageOffset + quarter * (kOutStageBytes / 4),
+                                          lane);
+        } else {
+          store_accumulator<KT, OUT_COMPLEX>(prm, t_acc, n_tile * KT, in_tile && ok && !flags[1],
+                                             img, op, oq);
+        }
         // This warp is done with the accumulator buffer: release it to the MMA.
         ptx::tc_fence_before();
         __syncwarp();
@@ -290,6 +301,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       }
       if (!ok) break;
     }
+    // Output stores still in flight complete before the CTA exits.
+    if (lane == 0) ptx::bulk_wait_all();
   }
 
   __syncthreads();
@@ -368,6 +381,47 @@ size_t pair_split_workspace_bytes(int kt, int tiles, int slots) {
   const long long gs = std::min<long long>(g, r * slots / kMinSkSlots);
   if (gs < 2) return 0;
   return partial_bytes(static_cast<int>(gs), kt);
+}
+
+int encode_planar_out_maps(FpropParams& prm, float* y0, float* y1, bool flat) {
+  prm.out_tma = 0;
+  const char* env = getenv("CCV_TMA_STORE");
+  if (env != nullptr && atoi(env) == 0) return CCV_OK;
+  const uint64_t kb = static_cast<uint64_t>(prm.k) * 4;
+  int rc;
+  if (flat) {
+    const uint64_t dims[2] = {static_cast<uint64_t>(prm.k), static_cast<uint64_t>(prm.m_total)};
+    const uint64_t strides[1] = {kb};
+    const uint32_t box[2] = {16, 32};
+    const uint32_t es[2] = {1, 1};
+    if ((rc = encode_tiled_ex(&prm.tm_y0, y0, 2, dims, strides, box, es, kSwizzleNone, false)) !=
+        CCV_OK) {
+      return rc;
+    }
+    if ((rc = encode_tiled_ex(&prm.tm_y1, y1, 2, dims, strides, box, es, kSwizzleNone, false)) !=
+        CCV_OK) {
+      return rc;
+    }
+  } else {
+    // Each epilogue warp's 32 rows must lie in one box of the tile.
+    if ((1 << prm.box_px_log2) < 32) return CCV_OK;
+    const uint32_t px = static_cast<uint32_t>(std::min(prm.box_q, 32));
+    const uint64_t dims[4] = {static_cast<uint64_t>(prm.k), static_cast<uint64_t>(prm.q),
+                              static_cast<uint64_t>(prm.p), static_cast<uint64_t>(prm.n)};
+    const uint64_t strides[3] = {kb, kb * prm.q, kb * prm.q * prm.p};
+    const uint32_t box[4] = {16, px, 32u / px, 1};
+    const uint32_t es[4] = {1, 1, 1, 1};
+    if ((rc = encode_tiled_ex(&prm.tm_y0, y0, 4, dims, strides, box, es, kSwizzleNone, false)) !=
+        CCV_OK) {
+      return rc;
+    }
+    if ((rc = encode_tiled_ex(&prm.tm_y1, y1, 4, dims, strides, box, es, kSwizzleNone, false)) !=
+        CCV_OK) {
+      return rc;
+    }
+  }
+  prm.out_tma = 1;
+  return CCV_OK;
 }
 
 int cluster_cap(int max_clusters) {
@@ -491,6 +545,7 @@ int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, cons
     if ((rc = encode_tiled(&prm.tm_w, w_packed, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
   }
   const bool cplx = out_layout == OUT_COMPLEX_NCHW;
+  if (!cplx && (rc = encode_planar_out_maps(prm, y0, y1, t.flat)) != CCV_OK) return rc;
   if (t.flat) {
     return cplx ? launch2_kt<true, true>(t.kt, prm, ws, ws_bytes, stream)
                 : launch2_kt<true, false>(t.kt, prm, ws, ws_bytes, stream);

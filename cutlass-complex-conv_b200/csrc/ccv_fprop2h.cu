@@ -89,6 +89,8 @@ __global__ void __cluster_dims__(2, 1, 1)
   const uint32_t a_base = ptx::smem_u32(data);
   const uint32_t w_base = a_base + static_cast<uint32_t>(SA * prm.a_slot_bytes);
   const uint32_t a_plane_bytes = static_cast<uint32_t>(prm.a_slot_bytes / 2);
+  // TMA-store staging of the planar epilogue, after the weight stages.
+  uint8_t* out_stage = data + SA * prm.a_slot_bytes + SW * prm.w_stage_bytes;
 
   if (threadIdx.x == 0) {
     flags[1] = 0;
@@ -315,9 +317,18 @@ __global__ void __cluster_dims__(2, 1, 1)
             op, oq, t_free, final_unit ? data + quarter * stage_per_warp : nullptr, stage_per_warp,
             stage_bar0 + 8u * kStageBufs * static_cast<uint32_t>(quarter));
       } else {
-        // The fused variant runs 448 threads (128 registers each): 16-column chunks.
-        store_accumulator<KT, OUT_COMPLEX, IN_COMPLEX ? 16 : 32>(
-            prm, t_acc, n_tile * KT, in_tile && ok && !flags[1], img, op, oq);
+        bool tma_out = false;
+        if constexpr (!OUT_COMPLEX) tma_out = prm.out_tma != 0;
+        if (tma_out) {
+          int c1 = 0, c2 = 0, c3 = 0;
+          const bool wv = warp_box_origin<false>(prm, half, quarter, c1, c2, c3) && ok && !flags[1];
+          store_accumulator_tma<KT, false>(prm, t_acc, n_tile * KT, wv, c1, c2, c3,
+                                           out_stage + quarter * (kOutStageBytes / 4), lane);
+        } else {
+          // The fused variant runs 448 threads (128 registers each): 16-column chunks.
+          store_accumulator<KT, OUT_COMPLEX, IN_COMPLEX ? 16 : 32>(
+              prm, t_acc, n_tile * KT, in_tile && ok && !flags[1], img, op, oq);
+        }
         // This warp is done with the accumulator buffer: release it to the MMA.
         ptx::tc_fence_before();
         __syncwarp();
@@ -325,6 +336,8 @@ __global__ void __cluster_dims__(2, 1, 1)
       }
       if (!ok) break;
     }
+    // Output stores still in flight complete before the CTA exits.
+    if (lane == 0) ptx::bulk_wait_all();
   }
 
   if constexpr (IN_COMPLEX) {
@@ -446,7 +459,7 @@ namespace {
 bool halo_fits(const Tiling& t, int r) {
   const long long slot = 2LL * (t.box_p + r - 1) * t.box_q * kRowH;
   const long long wst = 2LL * t.kt * kRowH;
-  return 2 * slot + 3 * wst <= kSmemDataBudget;
+  return 2 * slot + 3 * wst <= kSmemDataBudget - kOutStageBytes;
 }
 }  // namespace
 
@@ -526,22 +539,27 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
     xr_lo = xr;
     xi_lo = xi;
   }
+  int rc0;
   prm.halo_rows = (t.box_p + pb.r - 1) * t.box_q;
   prm.a_slot_bytes = 2 * prm.halo_rows * kRowH;
   prm.w_stage_bytes = 2 * t.kt * kRowH;
   // Ring depths: at least 2 A slots and 3 weight stages; prefer 4+ weight
   // stages, then a third A slot.
+  const bool cplx_out = out_layout == OUT_COMPLEX_NCHW;
+  if (!cplx_out && (rc0 = encode_planar_out_maps(prm, y0, y1, false)) != CCV_OK) return rc0;
+  const int budget = kSmemDataBudget - (prm.out_tma ? kOutStageBytes : 0);
   int sa = 2;
-  int sw = (kSmemDataBudget - sa * prm.a_slot_bytes) / prm.w_stage_bytes;
-  if (sw > 4 && kSmemDataBudget - 3 * prm.a_slot_bytes >= 4 * prm.w_stage_bytes) {
+  int sw = (budget - sa * prm.a_slot_bytes) / prm.w_stage_bytes;
+  if (sw > 4 && budget - 3 * prm.a_slot_bytes >= 4 * prm.w_stage_bytes) {
     sa = 3;
-    sw = (kSmemDataBudget - sa * prm.a_slot_bytes) / prm.w_stage_bytes;
+    sw = (budget - sa * prm.a_slot_bytes) / prm.w_stage_bytes;
   }
   sw = std::min(sw, kMaxWStages);
   if (sw < 3) return set_error(CCV_ERR_UNSUPPORTED, "halo tile does not fit in shared memory");
   prm.a_slots = sa;
   prm.w_stages = sw;
-  const int smem_bytes = 1024 + kBarBytes + sa * prm.a_slot_bytes + sw * prm.w_stage_bytes;
+  const int smem_bytes = 1024 + kBarBytes + sa * prm.a_slot_bytes + sw * prm.w_stage_bytes +
+                         (prm.out_tma ? kOutStageBytes : 0);
 
   int rc;
   const uint64_t cb = static_cast<uint64_t>(pb.c) * 4;

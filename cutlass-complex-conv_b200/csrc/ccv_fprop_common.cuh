@@ -16,6 +16,11 @@ struct alignas(64) FpropParams {
   CUtensorMap tm_w;   // packed weights [image][R*S][3][K][C] (image 1 = 3xTF32 remainders)
   CUtensorMap tm_xr_lo;  // 3xTF32: activation remainder planes (x - tf32(x))
   CUtensorMap tm_xi_lo;
+  // Planar output through TMA stores (out_tma != 0): y_real / y_imag as
+  // (K, Q, P, N) boxes of 16 channels x out_px pixels x out_rows rows, or
+  // (K, N*P*Q) boxes of 16 channels x 32 pixels for flat tiles.
+  CUtensorMap tm_y0;
+  CUtensorMap tm_y1;
   const float* xc;    // fused complex path: complex64 NCHW input (interleaved)
   float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
   float* y1;          // planar: y_imag (NPQK); complex: unused
@@ -44,6 +49,7 @@ struct alignas(64) FpropParams {
   // count to L (the last to finish; nobody waits) sums all pieces' partials in
   // cluster order, stores the output and zeroes the counter.  sk_slots == 0:
   // no tail split (split_ws unused).
+  int out_tma;
   int sk_start, sk_clusters, slots_per_tile;
   long long sk_slots;  // < 2^31 (checked on the host)
   float* split_ws;
@@ -230,6 +236,13 @@ Tiling choose_halo_tiling(const Problem& pb);
 // read from complex64 NCHW by TMA as an MN-major operand.  Stride 1, odd
 // filter width, even image width.
 bool cd_applicable(const Problem& pb);
+
+// Bytes of shared memory a pair kernel sets aside for the TMA-store epilogue
+// (4 warps x 32 rows x 16 channels x 2 planes).
+constexpr int kOutStageBytes = 4 * 32 * 16 * 4 * 2;
+// Encodes prm.tm_y0 / tm_y1 for planar output and sets prm.out_tma when the
+// tiling lets each epilogue warp's 32 rows form one TMA box.
+int encode_planar_out_maps(FpropParams& prm, float* y0, float* y1, bool flat);
 int launch_fprop_cd(const float* xc, const float* w_packed, float* y, const Problem& pb,
                     void* ws, size_t ws_bytes, cudaStream_t stream);
 

@@ -78,7 +78,7 @@ int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* d
 // Same, with the swizzle mode named and optionally 8-byte elements.
 // kSwizzle128Atom32 swizzles 32-byte chunks within 128-byte rows (the
 // shared-memory layout of MN-major 32-bit tensor-core operands).
-enum TmaSwizzle { kSwizzle64 = 0, kSwizzle128 = 1, kSwizzle128Atom32 = 2 };
+enum TmaSwizzle { kSwizzle64 = 0, kSwizzle128 = 1, kSwizzle128Atom32 = 2, kSwizzleNone = 3 };
 int encode_tiled_ex(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                     const uint64_t* strides_bytes, const uint32_t* box,
                     const uint32_t* elem_strides, TmaSwizzle swizzle, bool elem8);
