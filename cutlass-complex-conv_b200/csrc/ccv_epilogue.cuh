@@ -157,19 +157,20 @@ __device__ __forceinline__ void store_accumulator_tma(const FpropParams& prm, ui
   }
 }
 
-// First output pixel of epilogue warp `quarter` of tile half `half` in the
-// coordinates of the planar output maps; false when it holds no output.
+// Output pixel of tile row `row0` (the first of an epilogue warp's 32 rows)
+// of tile half `half` in the coordinates of the planar output maps; false
+// when it holds no output.
 template <bool FLAT>
-__device__ __forceinline__ bool warp_box_origin(const FpropParams& prm, int half, int quarter,
+__device__ __forceinline__ bool warp_box_origin(const FpropParams& prm, int half, int row0,
                                                 int& c1, int& c2, int& c3) {
   if constexpr (FLAT) {
-    const long long m = static_cast<long long>(half) * kBlockM + quarter * 32;
+    const long long m = static_cast<long long>(half) * kBlockM + row0;
     c1 = static_cast<int>(m);
     c2 = c3 = 0;
     return m < prm.m_total;
   } else {
     int img = 0, op = 0, oq = 0;
-    const bool ok = tile_row_pixel<false>(prm, half, quarter * 32, img, op, oq);
+    const bool ok = tile_row_pixel<false>(prm, half, row0, img, op, oq);
     c1 = oq;
     c2 = op;
     c3 = img;

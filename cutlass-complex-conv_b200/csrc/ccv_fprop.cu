@@ -485,6 +485,22 @@ namespace {
 
 enum KernelFamily { kSingleCta = 0, kPairTap = 1, kPairHalo = 2 };
 
+// Output-channel tile of the single-CTA kernel.  CCV_KT=32|64|128 pins it
+// (testing knob).  Otherwise the widest tile, except that 65..128 output
+// channels over fewer than SMs/16 pixel tiles take two 64-wide tiles: more
+// CTAs to spread the split-K over (measured on B200, batch-1 64->128 @ 28x28:
+// 13.5 -> 10.9 us; deeper layers keep 128, e.g. 128->256 @ 14x14 14.5 us vs
+// 20.1 us with 64).
+int single_cta_kt(const Problem& pb, const Tiling& t) {
+  const char* env = getenv("CCV_KT");
+  if (env != nullptr) {
+    const int v = atoi(env);
+    if (v == 32 || v == 64 || v == 128) return v;
+  }
+  if (t.kt == 128 && pb.k <= 128 && t.tiles_m * 16 < device_sm_count()) return 64;
+  return t.kt;
+}
+
 // Kernel family for a problem.  Large problems go to the persistent CTA-pair
 // kernels; small ones (fewer pair tiles than half the SMs) to the single-CTA
 // kernel.  Among the pair kernels, halo reuse serves stride-1 filters unless
@@ -611,7 +627,7 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
     xr_lo = nullptr;
     xi_lo = nullptr;
   }
-  const Tiling t = choose_tiling(pb);
+  Tiling t = choose_tiling(pb);
   Tiling th;
   switch (choose_family(pb, split, t, &th)) {
     case kPairHalo:
@@ -623,6 +639,8 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
     default:
       break;
   }
+  t.kt = single_cta_kt(pb, t);
+  t.tiles_n = (pb.k + t.kt - 1) / t.kt;
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;

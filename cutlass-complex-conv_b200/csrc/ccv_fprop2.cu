@@ -286,7 +286,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         if constexpr (!OUT_COMPLEX) tma_out = prm.out_tma != 0;
         if (tma_out) {
           int c1 = 0, c2 = 0, c3 = 0;
-          const bool wv = warp_box_origin<FLAT>(prm, half, quarter, c1, c2, c3) && ok && !flags[1];
+          const bool wv = warp_box_origin<FLAT>(prm, half, quarter * 32, c1, c2, c3) && ok && !flags[1];
           store_accumulator_tma<KT, FLAT>(prm, t_acc, n_tile * KT, wv, c1, c2, c3,
                                           smem + C::kOutStageOffset + quarter * (kOutStageBytes / 4),
                                           lane);

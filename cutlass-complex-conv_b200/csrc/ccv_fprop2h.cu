@@ -41,21 +41,25 @@ static_assert(8 * (32 + 4 * kStageBufs) <= kBarBytes, "barrier block overflow");
 constexpr int kSmemDataBudget = 232448 - kBarBytes - 1024;  // minus alignment slack
 constexpr int kTimeoutH = CCV_ERR_DEVICE_TIMEOUT;
 
-template <int KT>
+// NSUB: 128-row sub-boxes per CTA tile (2 for KT <= 64: two accumulators
+// share every weight stage, halving weight bytes per MMA).
+template <int KT, int NSUB>
 struct CfgH {
-  static constexpr int kAccCols = 2 * KT;
-  static constexpr int kTmemCols = 2 * kAccCols < 32 ? 32 : 2 * kAccCols;
+  static constexpr int kAccCols = 2 * KT;            // one sub-box: [re | im]
+  static constexpr int kTileCols = NSUB * kAccCols;  // one tile buffer
+  static constexpr int kTmemCols = 2 * kTileCols < 32 ? 32 : 2 * kTileCols;
   static constexpr int kWStageBytes = 2 * KT * kRowH;
+  static_assert(2 * kTileCols <= 512, "TMEM");
 };
 
 constexpr int kConvWarps = 8;
 constexpr int kConvUnits = 5;   // (32-row block, channel quad) units per converter lane
 
-template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX>
+template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX, int NSUB>
 __global__ void __cluster_dims__(2, 1, 1)
     __launch_bounds__(IN_COMPLEX ? kThreadsH + 32 * kConvWarps : kThreadsH, 1)
     ccv_fprop2h_tf32_kernel(const __grid_constant__ FpropParams prm) {
-  using C = CfgH<KT>;
+  using C = CfgH<KT, NSUB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -239,7 +243,7 @@ __global__ void __cluster_dims__(2, 1, 1)
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * C::kAccCols);
+        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * C::kTileCols);
         bool first = true;
         for (int j = wu.jbeg; j < wu.jend && !abort; ++j, ++ga) {
           const int slot = static_cast<int>(ga % SA);
@@ -265,11 +269,18 @@ __global__ void __cluster_dims__(2, 1, 1)
 #pragma unroll
             for (int kk = 0; kk < kCH / 8; ++kk) {
               const uint32_t koff = kk * 32;
-              ptx::mma_tf32_pair(d, ptx::desc_kmajor_sw128(a_r + koff),
-                                 ptx::desc_kmajor_sw128(w_x + koff), idesc, first ? 0u : 1u);
+#pragma unroll
+              for (int sb = 0; sb < NSUB; ++sb) {
+                // Sub-box sb: slot rows from 128*sb on, accumulator columns
+                // from sb * 2*KT on.
+                const uint32_t aoff = koff + static_cast<uint32_t>(sb) * kBlockM * kRowH;
+                const uint32_t dsb = d + static_cast<uint32_t>(sb * C::kAccCols);
+                ptx::mma_tf32_pair(dsb, ptx::desc_kmajor_sw128(a_r + aoff),
+                                   ptx::desc_kmajor_sw128(w_x + koff), idesc, first ? 0u : 1u);
+                ptx::mma_tf32_pair(dsb, ptx::desc_kmajor_sw128(a_i + aoff),
+                                   ptx::desc_kmajor_sw128(w_y + koff), idesc, 1u);
+              }
               first = false;
-              ptx::mma_tf32_pair(d, ptx::desc_kmajor_sw128(a_i + koff),
-                                 ptx::desc_kmajor_sw128(w_y + koff), idesc, 1u);
             }
             ptx::mma_commit_pair(wempty(st));
           }
@@ -302,11 +313,11 @@ __global__ void __cluster_dims__(2, 1, 1)
       const int t = wu.tile;
       const int n_tile = t % prm.tiles_n;
       const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
-      int img = 0, op = 0, oq = 0;
-      const bool in_tile = tile_row_pixel<false>(prm, half, row, img, op, oq);
-      const uint32_t t_acc = t_row + static_cast<uint32_t>(buf * C::kAccCols);
       const uint32_t t_free = buf == 0 ? tempty_leader0 : tempty_leader1;
-      if (wu.split && ok && !flags[1]) {
+      if (NSUB == 1 && wu.split && ok && !flags[1]) {
+        int img = 0, op = 0, oq = 0;
+        const bool in_tile = tile_row_pixel<false>(prm, half, row, img, op, oq);
+        const uint32_t t_acc = t_row + static_cast<uint32_t>(buf * C::kTileCols);
         // After the cluster's last unit the operand buffers are idle: they
         // stage the split tile's partial sums.
         const bool final_unit = cursor_done(prm, cur);
@@ -317,17 +328,27 @@ __global__ void __cluster_dims__(2, 1, 1)
             op, oq, t_free, final_unit ? data + quarter * stage_per_warp : nullptr, stage_per_warp,
             stage_bar0 + 8u * kStageBufs * static_cast<uint32_t>(quarter));
       } else {
-        bool tma_out = false;
-        if constexpr (!OUT_COMPLEX) tma_out = prm.out_tma != 0;
-        if (tma_out) {
-          int c1 = 0, c2 = 0, c3 = 0;
-          const bool wv = warp_box_origin<false>(prm, half, quarter, c1, c2, c3) && ok && !flags[1];
-          store_accumulator_tma<KT, false>(prm, t_acc, n_tile * KT, wv, c1, c2, c3,
-                                           out_stage + quarter * (kOutStageBytes / 4), lane);
-        } else {
-          // The fused variant runs 448 threads (128 registers each): 16-column chunks.
-          store_accumulator<KT, OUT_COMPLEX, IN_COMPLEX ? 16 : 32>(
-              prm, t_acc, n_tile * KT, in_tile && ok && !flags[1], img, op, oq);
+#pragma unroll 1
+        for (int sb = 0; sb < NSUB; ++sb) {
+          const int row_sb = sb * kBlockM + row;
+          const uint32_t t_acc =
+              t_row + static_cast<uint32_t>(buf * C::kTileCols + sb * C::kAccCols);
+          bool tma_out = false;
+          if constexpr (!OUT_COMPLEX) tma_out = prm.out_tma != 0;
+          if (tma_out) {
+            int c1 = 0, c2 = 0, c3 = 0;
+            const bool wv = warp_box_origin<false>(prm, half, sb * kBlockM + quarter * 32, c1, c2,
+                                                   c3) &&
+                            ok && !flags[1];
+            store_accumulator_tma<KT, false>(prm, t_acc, n_tile * KT, wv, c1, c2, c3,
+                                             out_stage + quarter * (kOutStageBytes / 4), lane);
+          } else {
+            int img = 0, op = 0, oq = 0;
+            const bool in_tile = tile_row_pixel<false>(prm, half, row_sb, img, op, oq);
+            // The fused variant runs 448 threads (128 registers each): 16-column chunks.
+            store_accumulator<KT, OUT_COMPLEX, IN_COMPLEX ? 16 : 32>(
+                prm, t_acc, n_tile * KT, in_tile && ok && !flags[1], img, op, oq);
+          }
         }
         // This warp is done with the accumulator buffer: release it to the MMA.
         ptx::tc_fence_before();
@@ -414,10 +435,10 @@ __global__ void __cluster_dims__(2, 1, 1)
   }
 }
 
-template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX>
+template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX, int NSUB = 1>
 int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
                     cudaStream_t stream) {
-  auto kern = ccv_fprop2h_tf32_kernel<KT, OUT_COMPLEX, IN_COMPLEX>;
+  auto kern = ccv_fprop2h_tf32_kernel<KT, OUT_COMPLEX, IN_COMPLEX, NSUB>;
   constexpr int threads = IN_COMPLEX ? kThreadsH + 32 * kConvWarps : kThreadsH;
   static std::once_flag once[64];
   static int max_clusters[64] = {};
@@ -474,7 +495,9 @@ bool halo_fused_supported(const Problem& pb, const Tiling& th) {
   return ((rows + 31) / 32) * 8 <= kConvUnits * kConvWarps;
 }
 
-Tiling choose_halo_tiling(const Problem& pb) {
+Tiling choose_halo_tiling(const Problem& pb) { return choose_halo_tiling_px(pb, kBlockM); }
+
+Tiling choose_halo_tiling_px(const Problem& pb, int px) {
   Tiling t;
   t.kt = pb.k > 64 ? 128 : (pb.k > 32 ? 64 : 32);
   t.tiles_n = (pb.k + t.kt - 1) / t.kt;
@@ -482,7 +505,7 @@ Tiling choose_halo_tiling(const Problem& pb) {
   t.total_boxes = 0;
   long long best = -1;
   for (int bq = 8; bq <= 128; bq *= 2) {
-    const int bp = kBlockM / bq;
+    const int bp = px / bq;
     if (bp + pb.r - 1 > 256) continue;
     Tiling cand = t;
     cand.box_p = bp;
@@ -492,7 +515,7 @@ Tiling choose_halo_tiling(const Problem& pb) {
     const long long tbp = (pb.p + bp - 1) / bp;
     const long long boxes = static_cast<long long>(pb.n) * tbq * tbp;
     // Rows computed, then halo rows loaded per box (fewer is better).
-    const long long cost = boxes * kBlockM * 1024 + (bp + pb.r - 1) * bq;
+    const long long cost = boxes * px * 1024 + (bp + pb.r - 1) * bq;
     if (best < 0 || cost < best) {
       best = cost;
       t.box_p = bp;
@@ -509,8 +532,25 @@ Tiling choose_halo_tiling(const Problem& pb) {
 int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
                            const float* xi_lo, const float* xc, bool split,
                            const float* w_packed, float* y0, float* y1, const Problem& pb,
-                           const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
+                           const Tiling& t_in, OutLayout out_layout, void* ws, size_t ws_bytes,
                            cudaStream_t stream) {
+  // KT <= 64: two 128-pixel sub-boxes per CTA tile when the taller halo slot
+  // fits (CCV_SUBBOX=0 turns it off; testing knob).  No stream-K split then.
+  Tiling t = t_in;
+  int nsub = 1;
+  {
+    const char* env = getenv("CCV_SUBBOX");
+    const bool allow = env == nullptr || atoi(env) != 0;
+    if (allow && xc == nullptr && t.kt <= 64) {
+      const Tiling t2 = choose_halo_tiling_px(pb, 2 * kBlockM);
+      if (t2.total_boxes > 0 && halo_fits(t2, pb.r)) {
+        t = t2;
+        nsub = 2;
+        ws = nullptr;
+        ws_bytes = 0;
+      }
+    }
+  }
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;
@@ -592,6 +632,14 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
       case 64: return launchh_variant<64, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
       default: return launchh_variant<32, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
     }
+  }
+  if (nsub == 2) {
+    if (t.kt == 64) {
+      return cplx ? launchh_variant<64, true, false, 2>(prm, smem_bytes, ws, ws_bytes, stream)
+                  : launchh_variant<64, false, false, 2>(prm, smem_bytes, ws, ws_bytes, stream);
+    }
+    return cplx ? launchh_variant<32, true, false, 2>(prm, smem_bytes, ws, ws_bytes, stream)
+                : launchh_variant<32, false, false, 2>(prm, smem_bytes, ws, ws_bytes, stream);
   }
   switch (t.kt) {
     case 128:

@@ -230,6 +230,8 @@ int cluster_cap(int max_clusters);
 int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
                     cudaStream_t stream, int* rc);
 Tiling choose_halo_tiling(const Problem& pb);
+// Same for tiles of `px` output pixels per CTA (128 or 256).
+Tiling choose_halo_tiling_px(const Problem& pb, int px);
 // xc non-null: fused complex path (converter warps read complex64 NCHW; the
 // planar pointers are ignored and `split` selects 3xTF32).
 // Complex-direct kernel (ccv_fprop_cd.cu): forward() with the activations

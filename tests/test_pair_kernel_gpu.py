@@ -24,7 +24,7 @@ def force_kernel():
     with halo reuse, 'halo_fused' = the same reading complex64 input through
     its converter warps, 'tap' = CTA pair without halo reuse) through the
     library's env knobs."""
-    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_CD", "CCV_FUSED")
+    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_CD", "CCV_FUSED", "CCV_SUBBOX")
     old = {k: os.environ.get(k) for k in keys}
     # These tests pin the planar-operand kernels; the complex-direct kernel
     # has its own tests.
@@ -32,8 +32,12 @@ def force_kernel():
 
     def set_(v):
         os.environ.pop("CCV_FUSED", None)
+        os.environ.pop("CCV_SUBBOX", None)
         if v == "halo_fused":
+            # The converter-warp kernel has one 128-pixel box per CTA; pin the
+            # planar reference to the same tiling (same summation order).
             os.environ["CCV_FUSED"] = "1"
+            os.environ["CCV_SUBBOX"] = "0"
             v = "halo"
         if v == "halo":
             os.environ["CCV_FORCE_KERNEL"] = "2"
@@ -96,6 +100,7 @@ def test_converter_warps_3xtf32(force_kernel, name, case, x, wr, wi, y32, y64):
     packed = abi_prepack(case, torch.from_numpy(wr), torch.from_numpy(wi), precision=p3)
     xt = torch.from_numpy(x)
     force_kernel("halo")
+    os.environ["CCV_SUBBOX"] = "0"
     y = abi_fprop_complex(case, xt, packed, precision=p3, poison=True)
     force_kernel("halo_fused")
     yf = abi_fprop_complex(case, xt, packed, precision=p3, poison=True)
@@ -111,3 +116,21 @@ def test_converter_warps_kernel_name(force_kernel):
     assert lib.ccv_fprop_complex_kernel(ctypes.byref(shp), 0).decode() == "halo_pair_converter_warps"
     force_kernel("halo")
     assert lib.ccv_fprop_complex_kernel(ctypes.byref(shp), 0).decode() == "layout_pass+halo_pair"
+
+
+@pytest.mark.parametrize("name,case,x,wr,wi,y32,y64", GOLDEN_CASES, ids=[c[0] for c in GOLDEN_CASES])
+def test_two_subbox_tiles(force_kernel, name, case, x, wr, wi, y32, y64):
+    """Halo kernel with two 128-pixel sub-boxes per CTA (KT <= 64) against the
+    one-box kernel without stream-K: identical summation order."""
+    force_kernel("halo")
+    packed = abi_prepack(case, torch.from_numpy(wr), torch.from_numpy(wi))
+    xt = torch.from_numpy(x)
+    os.environ["CCV_STREAMK"] = "0"
+    try:
+        y2 = abi_fprop_planar(case, xt, packed, poison=True)
+        assert oracle.rel_frobenius(y2, y64) <= TF32_TOL
+        os.environ["CCV_SUBBOX"] = "0"
+        y1 = abi_fprop_planar(case, xt, packed, poison=True)
+    finally:
+        os.environ.pop("CCV_STREAMK", None)
+    assert torch.equal(y1, y2)
