@@ -480,6 +480,11 @@ int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_co
   char* ws = static_cast<char*>(workspace);
   float* xr = reinterpret_cast<float*>(ws);
   float* xi = reinterpret_cast<float*>(ws + pl);
+  if (use_in_kernel_conversion(pb, precision)) {
+    return launch_fprop_complex_cvt(static_cast<const float*>(x), xr, xi,
+                                    static_cast<const float*>(w_packed), static_cast<float*>(y),
+                                    pb, st);
+  }
   const bool split = precision == CCV_PRECISION_3XTF32;
   float* lr = split ? reinterpret_cast<float*>(ws + 2 * pl) : nullptr;
   float* li = split ? reinterpret_cast<float*>(ws + 3 * pl) : nullptr;
@@ -497,7 +502,8 @@ int ccv_fprop_kernel_launches(const ccv_conv_shape* shape, int precision, int co
   if (kernels == nullptr) return set_error(CCV_ERR_INVALID_ARGUMENT, "null output pointer");
   const bool split = precision == CCV_PRECISION_3XTF32;
   if (complex_input) {
-    *kernels = complex_required_bytes(pb, precision) == 0 ? 1 : 2;
+    const char* name = complex_kernel_name(pb, precision);
+    *kernels = strncmp(name, "layout_pass", 11) == 0 ? 2 : 1;
   } else {
     *kernels = split ? 2 : 1;
   }

@@ -35,6 +35,7 @@
 #include <mutex>
 
 #include "ccv_internal.h"
+#include "ccv_cvt_role.cuh"
 #include "ccv_fprop_common.cuh"
 #include "ccv_ptx.cuh"
 
@@ -584,8 +585,35 @@ bool fused_complex_available(const Problem& pb, int precision) {
          use_converter_warps(pb, precision, th);
 }
 
+bool use_in_kernel_conversion(const Problem& pb, int precision) {
+  if (precision != CCV_PRECISION_TF32) return false;
+  // Opt-in (CCV_CVT=1): a converter SM moves only ~20-25 GB/s through its
+  // TMA ring, so the converting clusters hold back the others; the separate
+  // layout pass runs at the HBM copy rate.
+  const char* env = getenv("CCV_CVT");
+  if (env == nullptr || atoi(env) != 1) return false;
+  if (use_complex_direct(pb, precision)) return false;
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  if (choose_family(pb, false, t, &th) != kPairHalo) return false;
+  if (use_converter_warps(pb, precision, th)) return false;
+  return (pb.w & 1) == 0 && pb.n <= kSkCounterWords - kCvtFlag0;
+}
+
+int launch_fprop_complex_cvt(const float* x, float* xr, float* xi, const float* w_packed, float* y,
+                             const Problem& pb, cudaStream_t stream) {
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  if (choose_family(pb, false, t, &th) != kPairHalo) {
+    return set_error(CCV_ERR_UNSUPPORTED, "no in-kernel conversion for this problem");
+  }
+  return launch_fprop_pair_halo(xr, xi, nullptr, nullptr, nullptr, false, w_packed, y, nullptr, pb,
+                                th, OUT_COMPLEX_NCHW, nullptr, 0, stream, x);
+}
+
 const char* complex_kernel_name(const Problem& pb, int precision) {
   if (use_complex_direct(pb, precision)) return "complex_direct_pair";
+  if (use_in_kernel_conversion(pb, precision)) return "halo_pair_converter_clusters";
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;

@@ -19,9 +19,11 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 
 #include "ccv_convert.cuh"
+#include "ccv_cvt_role.cuh"
 #include "ccv_epilogue.cuh"
 #include "ccv_fprop_common.cuh"
 #include "ccv_internal.h"
@@ -98,8 +100,9 @@ __global__ void __cluster_dims__(2, 1, 1)
 
   if (threadIdx.x == 0) {
     flags[1] = 0;
-    for (int i = 0; i < SA; ++i) {
+    for (int i = 0; i < kMaxASlots; ++i) {
       // Fused complex path: one arrival per converter warp of both CTAs.
+      // (Converter clusters use afull(0..2) for their input ring.)
       ptx::mbar_init(afull(i), IN_COMPLEX ? 2 * kConvWarps : 1);
       ptx::mbar_init(aempty(i), 1);
     }
@@ -144,14 +147,45 @@ __global__ void __cluster_dims__(2, 1, 1)
   const int per_img = prm.tiles_bp * prm.tiles_bq;
   const int sp_per_cb = prm.s * prm.passes;  // K slots per 32-channel block
 
-  if (warp == 0) {
+  // In-kernel layout conversion: the first prm.cvt_clusters clusters to get
+  // here convert images for the others (role by ticket, so a cluster only
+  // waits for clusters that are running).
+  int ucid = cid, uncl = ncl;
+  bool cvt_cta = false;
+  int cvt_me = 0;
+  if constexpr (!IN_COMPLEX) {
+    if (prm.cvt_clusters > 0) {
+      if (leader && threadIdx.x == 0) {
+        const int ticket =
+            skip ? cid : static_cast<int>(atomicAdd(prm.cvt_ctrs + kCvtTicket, 1u));
+        flags[2] = ticket;
+        ptx::st_shared_cluster_u32(
+            ptx::mapa_shared(ptx::smem_u32(const_cast<int*>(flags + 2)), 1),
+            static_cast<uint32_t>(ticket));
+      }
+      ptx::cluster_sync();
+      const int ticket = flags[2];
+      cvt_cta = ticket < prm.cvt_clusters;
+      cvt_me = 2 * ticket + static_cast<int>(rank);
+      ucid = ticket - prm.cvt_clusters;
+      uncl = ncl - prm.cvt_clusters;
+    }
+  }
+
+  if (cvt_cta) {
+    // ------------------------------------------------------------ converter cluster
+    if (!skip && !cvt_role(prm, cvt_me, 2 * prm.cvt_clusters, data, afull(0), blockDim.x)) {
+      flags[1] = 1;
+    }
+  } else if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && !skip) {
       uint32_t ga = 0, gw = 0;
+      int ready_img = -1;
       bool abort = false;
-      UnitCursor cur = unit_cursor(prm, cid);
+      UnitCursor cur = unit_cursor(prm, ucid);
       WorkUnit wu;
-      while (!abort && next_unit(prm, ncl, cur, wu)) {
+      while (!abort && next_unit(prm, uncl, cur, wu)) {
         const int t = wu.tile;
         const int n_tile = t % prm.tiles_n;
         const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
@@ -164,6 +198,17 @@ __global__ void __cluster_dims__(2, 1, 1)
         const int h0 = bp * prm.box_p - prm.ph;
         const int w0 = bq * prm.box_q - prm.pw;
         const int k0 = n_tile * KT;
+        if constexpr (!IN_COMPLEX) {
+          // Converted planes of this image (images arrive in order).
+          if (prm.cvt_clusters > 0 && img > ready_img) {
+            if (!cvt_wait_image(prm, img)) {
+              flags[1] = 1;
+              abort = true;
+              break;
+            }
+            ready_img = img;
+          }
+        }
         for (int j = wu.jbeg; j < wu.jend && !abort; ++j, ++ga) {
           // Slot j: channel block cb, filter column ss, precision pass
           // (3xTF32: hi*hi, hi*lo, lo*hi).
@@ -232,9 +277,9 @@ __global__ void __cluster_dims__(2, 1, 1)
       uint32_t ga = 0, gw = 0;
       int i = 0;
       bool abort = false;
-      UnitCursor cur = unit_cursor(prm, cid);
+      UnitCursor cur = unit_cursor(prm, ucid);
       WorkUnit wu;
-      while (!abort && next_unit(prm, ncl, cur, wu)) {
+      while (!abort && next_unit(prm, uncl, cur, wu)) {
         const int buf = i & 1;
         const uint32_t use = static_cast<uint32_t>(i >> 1);
         ++i;
@@ -301,9 +346,9 @@ __global__ void __cluster_dims__(2, 1, 1)
     const uint32_t tempty_leader0 = ptx::mapa_shared(tempty(0), 0);
     const uint32_t tempty_leader1 = ptx::mapa_shared(tempty(1), 0);
     int i = 0;
-    UnitCursor cur = unit_cursor(prm, cid);
+    UnitCursor cur = unit_cursor(prm, ucid);
     WorkUnit wu;
-    while (!skip && next_unit(prm, ncl, cur, wu)) {
+    while (!skip && next_unit(prm, uncl, cur, wu)) {
       const int buf = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);
       ++i;
@@ -324,7 +369,7 @@ __global__ void __cluster_dims__(2, 1, 1)
         const uint32_t stage_per_warp =
             (static_cast<uint32_t>(SA * prm.a_slot_bytes + SW * prm.w_stage_bytes) / 4u) & ~127u;
         split_piece_epilogue<KT, OUT_COMPLEX>(
-            prm, wu, cid, static_cast<int>(rank), quarter, lane, t_acc, n_tile * KT, in_tile, img,
+            prm, wu, ucid, static_cast<int>(rank), quarter, lane, t_acc, n_tile * KT, in_tile, img,
             op, oq, t_free, final_unit ? data + quarter * stage_per_warp : nullptr, stage_per_warp,
             stage_bar0 + 8u * kStageBufs * static_cast<uint32_t>(quarter));
       } else {
@@ -385,9 +430,9 @@ __global__ void __cluster_dims__(2, 1, 1)
         jb.c0 = cb * kCH;
         jb.mode = prm.passes == 1 ? kConvRaw : (pass == 2 ? kConvLo : kConvHi);
       };
-      UnitCursor cur = unit_cursor(prm, cid);
+      UnitCursor cur = unit_cursor(prm, ucid);
       WorkUnit wu;
-      bool have = next_unit(prm, ncl, cur, wu);
+      bool have = next_unit(prm, uncl, cur, wu);
       int j = have ? wu.jbeg : 0;
       SlotJob jb;
       float2 v[kConvUnits][4];
@@ -413,7 +458,7 @@ __global__ void __cluster_dims__(2, 1, 1)
         if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(afull(slot), 0));
         ++ga;
         if (++j == wu.jend) {
-          have = next_unit(prm, ncl, cur, wu);
+          have = next_unit(prm, uncl, cur, wu);
           j = have ? wu.jbeg : 0;
         }
         if (have) {
@@ -426,6 +471,22 @@ __global__ void __cluster_dims__(2, 1, 1)
   }
 
   __syncthreads();
+  if constexpr (!IN_COMPLEX) {
+    // The last CTA to finish leaves the conversion counters zero.
+    if (prm.cvt_clusters > 0 && threadIdx.x == 0) {
+      unsigned old;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                   : "=r"(old)
+                   : "l"(prm.cvt_ctrs + kCvtDone)
+                   : "memory");
+      if (old == 2u * static_cast<unsigned>(ncl) - 1u) {
+        for (int i = 0; i < prm.n; ++i) prm.cvt_ctrs[kCvtFlag0 + i] = 0u;
+        prm.cvt_ctrs[kCvtTicket] = 0u;
+        prm.cvt_ctrs[kCvtDone] = 0u;
+        __threadfence();
+      }
+    }
+  }
   if (flags[1]) ptx::nanosleep(100000);  // let stray copies of an aborted tile land
   ptx::tc_fence_before();
   ptx::cluster_sync();
@@ -433,6 +494,26 @@ __global__ void __cluster_dims__(2, 1, 1)
     ptx::tc_fence_after();
     ptx::tmem_dealloc_pair(tmem_base, C::kTmemCols);
   }
+}
+
+// Converter clusters for a G-cluster grid: the share of the SM time the
+// conversion takes at ~120 GB/s of traffic per SM against ~4.5 TFLOP/s of
+// convolution per SM (B200 measurements), at least 1, at most G/3.
+// CCV_CVT_CLUSTERS=n pins it (testing/benchmarking knob).
+int cvt_clusters_for(const FpropParams& prm, int G) {
+  const char* env = getenv("CCV_CVT_CLUSTERS");
+  int nc;
+  if (env != nullptr && atoi(env) > 0) {
+    nc = atoi(env);
+  } else {
+    const double elems = static_cast<double>(prm.n) * prm.c * prm.h * prm.w;
+    const double flops = 8.0 * prm.n * prm.p * prm.q * static_cast<double>(prm.k) * prm.c *
+                         prm.r * prm.s;
+    const double t_cvt = 16.0 * elems / 120e9;
+    const double t_conv = flops / 4.5e12;
+    nc = static_cast<int>(std::ceil(t_cvt / (t_cvt + t_conv) * G));
+  }
+  return std::max(1, std::min(nc, std::max(1, G / 3)));
 }
 
 template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX, int NSUB = 1>
@@ -464,8 +545,18 @@ int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
   const int clusters = cluster_cap(max_clusters[dev & 63]);
   const int slots = ((prm.c + kCH - 1) / kCH) * prm.s * prm.passes;
   int rc;
-  const int launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc);
-  if (rc != CCV_OK) return rc;
+  int launched = 0;
+  if (prm.cvt_clusters > 0) {
+    // In-kernel conversion: whole tiles only; converter clusters on top.
+    if (clusters < 2) return set_error(CCV_ERR_UNSUPPORTED, "too few clusters for conversion");
+    prm.cvt_clusters = cvt_clusters_for(prm, clusters);
+    launch_clusters(prm, clusters, slots, KT, nullptr, 0, stream, &rc);
+    if (rc != CCV_OK) return rc;
+    launched = std::min(clusters, prm.num_tiles + prm.cvt_clusters);
+  } else {
+    launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc);
+    if (rc != CCV_OK) return rc;
+  }
   cudaError_t e = launch_kernel(kern, dim3(2 * launched), dim3(threads), smem_bytes, stream, 0,
                                 prm);
   if (e == cudaSuccess) e = cudaGetLastError();
@@ -533,7 +624,7 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
                            const float* xi_lo, const float* xc, bool split,
                            const float* w_packed, float* y0, float* y1, const Problem& pb,
                            const Tiling& t_in, OutLayout out_layout, void* ws, size_t ws_bytes,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, const float* cvt_src) {
   // KT <= 64: two 128-pixel sub-boxes per CTA tile when the taller halo slot
   // fits (CCV_SUBBOX=0 turns it off; testing knob).  No stream-K split then.
   Tiling t = t_in;
@@ -598,8 +689,42 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
   if (sw < 3) return set_error(CCV_ERR_UNSUPPORTED, "halo tile does not fit in shared memory");
   prm.a_slots = sa;
   prm.w_stages = sw;
-  const int smem_bytes = 1024 + kBarBytes + sa * prm.a_slot_bytes + sw * prm.w_stage_bytes +
-                         (prm.out_tma ? kOutStageBytes : 0);
+  int smem_bytes = 1024 + kBarBytes + sa * prm.a_slot_bytes + sw * prm.w_stage_bytes +
+                   (prm.out_tma ? kOutStageBytes : 0);
+  if (cvt_src != nullptr) {
+    // In-kernel conversion of cvt_src (complex64 NCHW) into the planes xr/xi.
+    if (fused || split || (pb.w & 1) != 0 || pb.n > kSkCounterWords - kCvtFlag0) {
+      return set_error(CCV_ERR_UNSUPPORTED, "no in-kernel conversion for this problem");
+    }
+    prm.cvt_ctrs = stream_k_counters();
+    if (prm.cvt_ctrs == nullptr) return CCV_ERR_CUDA;
+    prm.cvt_clusters = 1;  // sized at launch
+    ws = nullptr;
+    ws_bytes = 0;
+    smem_bytes = std::max(smem_bytes, 1024 + kBarBytes + static_cast<int>(kCvtSmemBytes));
+    const uint64_t hw8 = static_cast<uint64_t>(pb.h) * pb.w * 8;
+    {
+      const uint64_t dims[4] = {static_cast<uint64_t>(pb.w), static_cast<uint64_t>(pb.c),
+                                static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
+      const uint64_t strides[3] = {hw8, static_cast<uint64_t>(pb.w) * 8, hw8 * pb.c};
+      const uint32_t box[4] = {kCvtPx, kCvtCh, kCvtRows, 1};
+      const uint32_t es[4] = {1, 1, 1, 1};
+      int rc1 = encode_tiled_ex(&prm.tm_cin, cvt_src, 4, dims, strides, box, es, kSwizzle128, true);
+      if (rc1 != CCV_OK) return rc1;
+    }
+    {
+      const uint64_t cb4 = static_cast<uint64_t>(pb.c) * 4;
+      const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.w),
+                                static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
+      const uint64_t strides[3] = {cb4, cb4 * pb.w, cb4 * pb.w * pb.h};
+      const uint32_t box[4] = {kCvtCh, kCvtPx, kCvtRows, 1};
+      const uint32_t es[4] = {1, 1, 1, 1};
+      int rc1 = encode_tiled_ex(&prm.tm_pr, xr, 4, dims, strides, box, es, kSwizzleNone, false);
+      if (rc1 != CCV_OK) return rc1;
+      rc1 = encode_tiled_ex(&prm.tm_pi, xi, 4, dims, strides, box, es, kSwizzleNone, false);
+      if (rc1 != CCV_OK) return rc1;
+    }
+  }
 
   int rc;
   const uint64_t cb = static_cast<uint64_t>(pb.c) * 4;

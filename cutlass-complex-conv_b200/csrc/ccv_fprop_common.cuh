@@ -21,6 +21,14 @@ struct alignas(64) FpropParams {
   // (K, N*P*Q) boxes of 16 channels x 32 pixels for flat tiles.
   CUtensorMap tm_y0;
   CUtensorMap tm_y1;
+  // In-kernel layout conversion (cvt_clusters > 0): complex64 NCHW input as
+  // 8-byte elements (W, C, H, N), and the fp32 NHWC planes it fills (C, W,
+  // H, N) - the planes tm_xr / tm_xi read.
+  CUtensorMap tm_cin;
+  CUtensorMap tm_pr;
+  CUtensorMap tm_pi;
+  int cvt_clusters;
+  unsigned* cvt_ctrs;
   const float* xc;    // fused complex path: complex64 NCHW input (interleaved)
   float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
   float* y1;          // planar: y_imag (NPQK); complex: unused
@@ -250,10 +258,12 @@ int launch_fprop_cd(const float* xc, const float* w_packed, float* y, const Prob
 
 // ws/ws_bytes: optional scratch for the tail split (see
 // halo_split_workspace_bytes); without it every tile runs whole.
+// cvt_src: complex64 NCHW input to convert inside the kernel into the
+// planes xr / xi (which the kernel then reads); see ccv_cvt_role.cuh.
 int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
                            const float* xi_lo, const float* xc, bool split,
                            const float* w_packed, float* y0, float* y1, const Problem& pb,
                            const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
-                           cudaStream_t stream);
+                           cudaStream_t stream, const float* cvt_src = nullptr);
 
 }  // namespace ccv

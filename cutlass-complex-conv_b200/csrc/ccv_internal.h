@@ -64,6 +64,11 @@ size_t split_workspace_bytes(const Problem& pb, int precision, bool complex_inpu
 // Fused complex path: complex64 NCHW in, complex64 NKPQ out, one launch, no
 // required workspace.  Available when the problem runs on the halo pair kernel.
 bool fused_complex_available(const Problem& pb, int precision);
+// forward() with the layout conversion done by converter clusters inside
+// the halo pair kernel (one launch; xr/xi: workspace planes it fills).
+bool use_in_kernel_conversion(const Problem& pb, int precision);
+int launch_fprop_complex_cvt(const float* x, float* xr, float* xi, const float* w_packed, float* y,
+                             const Problem& pb, cudaStream_t stream);
 // Name of the kernel path a complex (forward()) call takes.
 const char* complex_kernel_name(const Problem& pb, int precision);
 int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,

@@ -109,8 +109,11 @@ int ccv_fprop_kernel_launches(const ccv_conv_shape* shape, int precision, int co
 
 /* Name of the kernel path ccv_fprop_complex takes for this problem (static
  * string): "complex_direct_pair" (activations read from complex64 NCHW by
- * TMA, one launch), "halo_pair_converter_warps" (one launch), or
- * "layout_pass+<kernel>" (a complex64 -> planar pass, then the kernel). */
+ * TMA, one launch), "halo_pair_converter_warps" (one launch),
+ * "halo_pair_converter_clusters" (one launch; some clusters convert images
+ * into the workspace planes for the others), or "layout_pass+<kernel>" (a
+ * complex64 -> planar pass, then the kernel).  The first three are opt-in
+ * through the CCV_CD, CCV_FUSED and CCV_CVT environment switches. */
 const char* ccv_fprop_complex_kernel(const ccv_conv_shape* shape, int precision);
 
 /* Planar fprop: fp32 NHWC planes in, fp32 NPQK planes out, packed weights.

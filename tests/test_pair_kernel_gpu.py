@@ -24,11 +24,13 @@ def force_kernel():
     with halo reuse, 'halo_fused' = the same reading complex64 input through
     its converter warps, 'tap' = CTA pair without halo reuse) through the
     library's env knobs."""
-    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_CD", "CCV_FUSED", "CCV_SUBBOX")
+    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_CD", "CCV_FUSED", "CCV_SUBBOX", "CCV_STREAMK")
     old = {k: os.environ.get(k) for k in keys}
     # These tests pin the planar-operand kernels; the complex-direct kernel
-    # has its own tests.
+    # has its own tests.  Whole tiles only, so every complex64 path (layout
+    # pass, converter clusters, converter warps) sums like the planar one.
     os.environ["CCV_CD"] = "0"
+    os.environ["CCV_STREAMK"] = "0"
 
     def set_(v):
         os.environ.pop("CCV_FUSED", None)
@@ -125,12 +127,8 @@ def test_two_subbox_tiles(force_kernel, name, case, x, wr, wi, y32, y64):
     force_kernel("halo")
     packed = abi_prepack(case, torch.from_numpy(wr), torch.from_numpy(wi))
     xt = torch.from_numpy(x)
-    os.environ["CCV_STREAMK"] = "0"
-    try:
-        y2 = abi_fprop_planar(case, xt, packed, poison=True)
-        assert oracle.rel_frobenius(y2, y64) <= TF32_TOL
-        os.environ["CCV_SUBBOX"] = "0"
-        y1 = abi_fprop_planar(case, xt, packed, poison=True)
-    finally:
-        os.environ.pop("CCV_STREAMK", None)
+    y2 = abi_fprop_planar(case, xt, packed, poison=True)
+    assert oracle.rel_frobenius(y2, y64) <= TF32_TOL
+    os.environ["CCV_SUBBOX"] = "0"
+    y1 = abi_fprop_planar(case, xt, packed, poison=True)
     assert torch.equal(y1, y2)
