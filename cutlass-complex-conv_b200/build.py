@@ -27,7 +27,7 @@ INCLUDE = os.path.join(REPO, "include")
 
 CU_SOURCES = ["ccv_api.cu", "ccv_fprop.cu", "ccv_fprop2.cu", "ccv_fprop2h.cu", "ccv_fprop_cd.cu", "ccv_layout.cu", "ccv_noalloc.cu"]
 CU_HEADERS = ["ccv_internal.h", "ccv_ptx.cuh", "ccv_fprop_common.cuh", "ccv_epilogue.cuh", "ccv_convert.cuh",
-              "ccv_cvt_role.cuh"]
+              "ccv_cvt_role.cuh", "ccv_layout_role.cuh"]
 NVCC_ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -488,6 +488,11 @@ int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_co
   const bool split = precision == CCV_PRECISION_3XTF32;
   float* lr = split ? reinterpret_cast<float*>(ws + 2 * pl) : nullptr;
   float* li = split ? reinterpret_cast<float*>(ws + 3 * pl) : nullptr;
+  if (use_layout_warps(pb, precision)) {
+    return launch_fprop_complex_lw(static_cast<const float*>(x), xr, xi, lr, li,
+                                   static_cast<const float*>(w_packed), static_cast<float*>(y), pb,
+                                   precision, sk, sk_bytes, st);
+  }
   rc = launch_nchw_complex_to_planar(static_cast<const float*>(x), xr, xi, lr, li, pb, st);
   if (rc != CCV_OK) return rc;
   return launch_fprop(xr, xi, lr, li, static_cast<const float*>(w_packed), static_cast<float*>(y),

@@ -37,6 +37,7 @@
 #include "ccv_internal.h"
 #include "ccv_cvt_role.cuh"
 #include "ccv_fprop_common.cuh"
+#include "ccv_layout_role.cuh"
 #include "ccv_ptx.cuh"
 
 namespace ccv {
@@ -611,9 +612,45 @@ int launch_fprop_complex_cvt(const float* x, float* xr, float* xi, const float* 
                                 th, OUT_COMPLEX_NCHW, nullptr, 0, stream, x);
 }
 
+bool use_layout_warps(const Problem& pb, int precision) {
+  // CCV_LW=0: never; CCV_LW=1: wherever the halo kernel runs; unset: when
+  // the grid runs at least two waves of tiles.  Below that, most images are
+  // needed by the first wave, so converting them in the kernel only delays
+  // it, and the layout pass (at the HBM copy rate) is faster.
+  const char* env = getenv("CCV_LW");
+  const int mode = env != nullptr ? atoi(env) : -1;
+  if (mode == 0) return false;
+  if (use_complex_direct(pb, precision) || use_in_kernel_conversion(pb, precision)) return false;
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  if (choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th) != kPairHalo) return false;
+  if (use_converter_warps(pb, precision, th)) return false;
+  if (pb.n > kSkCounterWords - kLwFlag0) return false;
+  if (mode == 1) return true;
+  // Pixels per cluster tile: two CTAs of 128 (two sub-boxes each for KT <= 64).
+  const long long tile_px = 2LL * kBlockM * (th.kt <= 64 ? 2 : 1);
+  const long long tiles =
+      (static_cast<long long>(pb.n) * pb.p * pb.q + tile_px - 1) / tile_px * th.tiles_n;
+  return tiles >= 2LL * (device_sm_count() / 2);
+}
+
+int launch_fprop_complex_lw(const float* x, float* xr, float* xi, float* xr_lo, float* xi_lo,
+                            const float* w_packed, float* y, const Problem& pb, int precision,
+                            void* ws, size_t ws_bytes, cudaStream_t stream) {
+  const bool split = precision == CCV_PRECISION_3XTF32;
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  if (choose_family(pb, split, t, &th) != kPairHalo) {
+    return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
+  }
+  return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, nullptr, split, w_packed, y, nullptr, pb, th,
+                                OUT_COMPLEX_NCHW, ws, ws_bytes, stream, x, true);
+}
+
 const char* complex_kernel_name(const Problem& pb, int precision) {
   if (use_complex_direct(pb, precision)) return "complex_direct_pair";
   if (use_in_kernel_conversion(pb, precision)) return "halo_pair_converter_clusters";
+  if (use_layout_warps(pb, precision)) return "halo_pair_layout_warps";
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;

@@ -140,8 +140,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
         const int k0 = n_tile * KT;
         for (int v = wu.jbeg; v < wu.jend; ++v, ++g) {
-          const int ks = v / prm.passes;
-          const int pass = v - ks * prm.passes;
+          int ks;
+          const int pass = slot_pass(v, prm.ksteps, prm.passes, &ks);
           const CUtensorMap* mr = pass == 2 ? &prm.tm_xr_lo : &prm.tm_xr;
           const CUtensorMap* mi = pass == 2 ? &prm.tm_xi_lo : &prm.tm_xi;
           const int stage = static_cast<int>(g % C::kStages);

@@ -15,6 +15,11 @@
 // complex64 NCHW input (de-interleave + NCHW->K-major transpose in the
 // producer), so forward() needs no separate layout pass; they release each
 // slot to the even CTA's barrier with a cluster-scope release.
+//
+// LW (layout warps): two extra warps per CTA convert the whole complex64
+// NCHW batch into fp32 NHWC planes in the workspace, image by image, while
+// the pair MMA runs; the producer waits for an image's planes before its
+// first TMA load from them (ccv_layout_role.cuh).  One launch, TMA-fed MMA.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -27,6 +32,7 @@
 #include "ccv_epilogue.cuh"
 #include "ccv_fprop_common.cuh"
 #include "ccv_internal.h"
+#include "ccv_layout_role.cuh"
 #include "ccv_ptx.cuh"
 
 namespace ccv {
@@ -57,10 +63,15 @@ struct CfgH {
 constexpr int kConvWarps = 8;
 constexpr int kConvUnits = 5;   // (32-row block, channel quad) units per converter lane
 
-template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX, int NSUB>
-__global__ void __cluster_dims__(2, 1, 1)
-    __launch_bounds__(IN_COMPLEX ? kThreadsH + 32 * kConvWarps : kThreadsH, 1)
+template <bool IN_COMPLEX, bool LW>
+constexpr int halo_threads() {
+  return kThreadsH + (IN_COMPLEX ? 32 * kConvWarps : 0) + (LW ? 32 * kLwWarps : 0);
+}
+
+template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX, int NSUB, bool LW>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMPLEX, LW>(), 1)
     ccv_fprop2h_tf32_kernel(const __grid_constant__ FpropParams prm) {
+  static_assert(!(IN_COMPLEX && LW), "one conversion scheme per kernel");
   using C = CfgH<KT, NSUB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
@@ -145,7 +156,7 @@ __global__ void __cluster_dims__(2, 1, 1)
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
   const int per_img = prm.tiles_bp * prm.tiles_bq;
-  const int sp_per_cb = prm.s * prm.passes;  // K slots per 32-channel block
+  const int per_pass = ((prm.c + kCH - 1) / kCH) * prm.s;  // K slots per precision pass
 
   // In-kernel layout conversion: the first prm.cvt_clusters clusters to get
   // here convert images for the others (role by ticket, so a cluster only
@@ -153,7 +164,7 @@ __global__ void __cluster_dims__(2, 1, 1)
   int ucid = cid, uncl = ncl;
   bool cvt_cta = false;
   int cvt_me = 0;
-  if constexpr (!IN_COMPLEX) {
+  if constexpr (!IN_COMPLEX && !LW) {
     if (prm.cvt_clusters > 0) {
       if (leader && threadIdx.x == 0) {
         const int ticket =
@@ -198,7 +209,17 @@ __global__ void __cluster_dims__(2, 1, 1)
         const int h0 = bp * prm.box_p - prm.ph;
         const int w0 = bq * prm.box_q - prm.pw;
         const int k0 = n_tile * KT;
-        if constexpr (!IN_COMPLEX) {
+        if constexpr (LW) {
+          // This image's planes are written (tiles run in image order).
+          if (img != ready_img) {
+            if (!lw_wait_image(prm, img)) {
+              flags[1] = 1;
+              abort = true;
+              break;
+            }
+            ready_img = img;
+          }
+        } else if constexpr (!IN_COMPLEX) {
           // Converted planes of this image (images arrive in order).
           if (prm.cvt_clusters > 0 && img > ready_img) {
             if (!cvt_wait_image(prm, img)) {
@@ -210,13 +231,13 @@ __global__ void __cluster_dims__(2, 1, 1)
           }
         }
         for (int j = wu.jbeg; j < wu.jend && !abort; ++j, ++ga) {
-          // Slot j: channel block cb, filter column ss, precision pass
-          // (3xTF32: hi*hi, hi*lo, lo*hi).
-          const int cb = j / sp_per_cb;
-          const int sp = j - cb * sp_per_cb;
+          // Slot j: precision pass (slot_pass), channel block cb, filter
+          // column ss.
+          int rest;
+          const int pass = slot_pass(j, per_pass, prm.passes, &rest);
+          const int cb = rest / prm.s;
+          const int ss = rest - cb * prm.s;
           const int c0 = cb * kCH;
-          const int ss = sp / prm.passes;
-          const int pass = sp - ss * prm.passes;
           const CUtensorMap* mr = pass == 2 ? &prm.tm_xr_lo : &prm.tm_xr;
           const CUtensorMap* mi = pass == 2 ? &prm.tm_xi_lo : &prm.tm_xi;
           if (!IN_COMPLEX) {
@@ -420,10 +441,10 @@ __global__ void __cluster_dims__(2, 1, 1)
         const int rem = gb - img * per_img;
         const int bp = rem / prm.tiles_bq;
         const int bq = rem - bp * prm.tiles_bq;
-        const int cb = j / sp_per_cb;
-        const int sp = j - cb * sp_per_cb;
-        const int ss = sp / prm.passes;
-        const int pass = sp - ss * prm.passes;
+        int rest;
+        const int pass = slot_pass(j, per_pass, prm.passes, &rest);
+        const int cb = rest / prm.s;
+        const int ss = rest - cb * prm.s;
         jb.img = img;
         jb.h0 = bp * prm.box_p - prm.ph;
         jb.w0 = bq * prm.box_q - prm.pw + ss;
@@ -470,10 +491,19 @@ __global__ void __cluster_dims__(2, 1, 1)
     }
   }
 
+  if constexpr (LW) {
+    if (warp >= kThreadsH / 32 && !skip) {
+      // ---------------------------------------------------------- layout warps
+      layout_warp(prm, lane);
+    }
+  }
+
   __syncthreads();
   if constexpr (!IN_COMPLEX) {
-    // The last CTA to finish leaves the conversion counters zero.
-    if (prm.cvt_clusters > 0 && threadIdx.x == 0) {
+    // The last CTA to finish leaves the conversion counters zero (the
+    // converter-cluster and layout-warp sets share one layout).
+    static_assert(kLwTicket == kCvtTicket && kLwDone == kCvtDone && kLwFlag0 == kCvtFlag0, "");
+    if ((LW || prm.cvt_clusters > 0) && threadIdx.x == 0) {
       unsigned old;
       asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
                    : "=r"(old)
@@ -516,11 +546,11 @@ int cvt_clusters_for(const FpropParams& prm, int G) {
   return std::max(1, std::min(nc, std::max(1, G / 3)));
 }
 
-template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX, int NSUB = 1>
+template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX, int NSUB = 1, bool LW = false>
 int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
                     cudaStream_t stream) {
-  auto kern = ccv_fprop2h_tf32_kernel<KT, OUT_COMPLEX, IN_COMPLEX, NSUB>;
-  constexpr int threads = IN_COMPLEX ? kThreadsH + 32 * kConvWarps : kThreadsH;
+  auto kern = ccv_fprop2h_tf32_kernel<KT, OUT_COMPLEX, IN_COMPLEX, NSUB, LW>;
+  constexpr int threads = halo_threads<IN_COMPLEX, LW>();
   static std::once_flag once[64];
   static int max_clusters[64] = {};
   int dev = 0;
@@ -553,6 +583,16 @@ int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
     launch_clusters(prm, clusters, slots, KT, nullptr, 0, stream, &rc);
     if (rc != CCV_OK) return rc;
     launched = std::min(clusters, prm.num_tiles + prm.cvt_clusters);
+  } else if (LW) {
+    // Layout warps: the stream-K range runs first, so its first image is
+    // converted first.
+    launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc);
+    if (rc != CCV_OK) return rc;
+    prm.lw_first_img = 0;
+    if (prm.sk_slots > 0) {
+      const int half = 2 * (prm.sk_start / prm.tiles_n);
+      prm.lw_first_img = std::min(half, prm.total_boxes - 1) / (prm.tiles_bp * prm.tiles_bq);
+    }
   } else {
     launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc);
     if (rc != CCV_OK) return rc;
@@ -624,7 +664,7 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
                            const float* xi_lo, const float* xc, bool split,
                            const float* w_packed, float* y0, float* y1, const Problem& pb,
                            const Tiling& t_in, OutLayout out_layout, void* ws, size_t ws_bytes,
-                           cudaStream_t stream, const float* cvt_src) {
+                           cudaStream_t stream, const float* cvt_src, bool layout_warps) {
   // KT <= 64: two 128-pixel sub-boxes per CTA tile when the taller halo slot
   // fits (CCV_SUBBOX=0 turns it off; testing knob).  No stream-K split then.
   Tiling t = t_in;
@@ -678,7 +718,22 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
   // stages, then a third A slot.
   const bool cplx_out = out_layout == OUT_COMPLEX_NCHW;
   if (!cplx_out && (rc0 = encode_planar_out_maps(prm, y0, y1, false)) != CCV_OK) return rc0;
-  const int budget = kSmemDataBudget - (prm.out_tma ? kOutStageBytes : 0);
+  const bool lw = cvt_src != nullptr && layout_warps;
+  if (lw) {
+    // Layout warps write xr/xi (and the remainder planes) from cvt_src.
+    if (fused || !cplx_out || pb.n > kSkCounterWords - kLwFlag0) {
+      return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
+    }
+    prm.xc = cvt_src;
+    prm.lw_xr = const_cast<float*>(xr);
+    prm.lw_xi = const_cast<float*>(xi);
+    prm.lw_xr_lo = const_cast<float*>(xr_lo);
+    prm.lw_xi_lo = const_cast<float*>(xi_lo);
+    prm.cvt_ctrs = stream_k_counters();
+    if (prm.cvt_ctrs == nullptr) return CCV_ERR_CUDA;
+  }
+  const int budget =
+      kSmemDataBudget - (prm.out_tma ? kOutStageBytes : 0);
   int sa = 2;
   int sw = (budget - sa * prm.a_slot_bytes) / prm.w_stage_bytes;
   if (sw > 4 && budget - 3 * prm.a_slot_bytes >= 4 * prm.w_stage_bytes) {
@@ -691,7 +746,7 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
   prm.w_stages = sw;
   int smem_bytes = 1024 + kBarBytes + sa * prm.a_slot_bytes + sw * prm.w_stage_bytes +
                    (prm.out_tma ? kOutStageBytes : 0);
-  if (cvt_src != nullptr) {
+  if (cvt_src != nullptr && !lw) {
     // In-kernel conversion of cvt_src (complex64 NCHW) into the planes xr/xi.
     if (fused || split || (pb.w & 1) != 0 || pb.n > kSkCounterWords - kCvtFlag0) {
       return set_error(CCV_ERR_UNSUPPORTED, "no in-kernel conversion for this problem");
@@ -756,6 +811,17 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
       case 128: return launchh_variant<128, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
       case 64: return launchh_variant<64, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
       default: return launchh_variant<32, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
+    }
+  }
+  if (lw) {
+    if (nsub == 2) {
+      return t.kt == 64 ? launchh_variant<64, true, false, 2, true>(prm, smem_bytes, ws, ws_bytes, stream)
+                        : launchh_variant<32, true, false, 2, true>(prm, smem_bytes, ws, ws_bytes, stream);
+    }
+    switch (t.kt) {
+      case 128: return launchh_variant<128, true, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
+      case 64: return launchh_variant<64, true, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
+      default: return launchh_variant<32, true, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
     }
   }
   if (nsub == 2) {

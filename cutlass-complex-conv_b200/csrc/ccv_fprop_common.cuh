@@ -28,8 +28,15 @@ struct alignas(64) FpropParams {
   CUtensorMap tm_pr;
   CUtensorMap tm_pi;
   int cvt_clusters;
-  unsigned* cvt_ctrs;
+  unsigned* cvt_ctrs;  // conversion counters (converter clusters / layout warps)
   const float* xc;    // fused complex path: complex64 NCHW input (interleaved)
+  // Layout warps: the fp32 NHWC planes they write from xc (the planes tm_xr,
+  // tm_xi, tm_xr_lo, tm_xi_lo read).
+  float* lw_xr;
+  float* lw_xi;
+  float* lw_xr_lo;
+  float* lw_xi_lo;
+  int lw_first_img;  // image the layout warps convert first
   float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
   float* y1;          // planar: y_imag (NPQK); complex: unused
   int* status;        // device status word
@@ -43,7 +50,8 @@ struct alignas(64) FpropParams {
   int num_tiles;      // work units of the persistent kernel
   // halo kernel: rows of one shifted activation copy, ring depths and sizes
   int halo_rows, a_slots, w_stages, a_slot_bytes, w_stage_bytes;
-  // precision passes per K step: 1 (TF32) or 3 (3xTF32: hi*hi, hi*lo, lo*hi)
+  // precision passes per K step: 1 (TF32) or 3 (3xTF32: hi*hi, hi*lo, lo*hi;
+  // see slot_pass for their order)
   int passes;
   // single-CTA kernel: CTAs per output tile (a cluster splitting the K loop)
   int splits;
@@ -65,6 +73,19 @@ struct alignas(64) FpropParams {
 };
 
 // Work of one persistent cluster: its stream-K range, then whole tiles.
+// K slot order of the pair kernels: the precision pass is outermost, and
+// 3xTF32 runs its two correction passes (pass 1: hi(x)*lo(w), pass 2:
+// lo(x)*hi(w)) before the main pass 0 (hi*hi).  The tensor cores' fp32
+// accumulation loses a fraction of the accumulator's magnitude per MMA, so
+// the correction MMAs run while the accumulator is still small and only the
+// main pass's MMAs see the full magnitude.  Returns the pass of slot j;
+// *rest = the slot's index inside its pass (per_pass slots per pass).
+__device__ __forceinline__ int slot_pass(int j, int per_pass, int passes, int* rest) {
+  const int pidx = j / per_pass;
+  *rest = j - pidx * per_pass;
+  return passes == 1 ? 0 : (pidx == 2 ? 0 : pidx + 1);
+}
+
 struct UnitCursor {
   int dp;       // next whole tile
   int s, s1;    // remaining stream-K slot range
@@ -264,6 +285,7 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
                            const float* xi_lo, const float* xc, bool split,
                            const float* w_packed, float* y0, float* y1, const Problem& pb,
                            const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
-                           cudaStream_t stream, const float* cvt_src = nullptr);
+                           cudaStream_t stream, const float* cvt_src = nullptr,
+                           bool layout_warps = false);
 
 }  // namespace ccv

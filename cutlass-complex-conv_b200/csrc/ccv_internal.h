@@ -69,6 +69,13 @@ bool fused_complex_available(const Problem& pb, int precision);
 bool use_in_kernel_conversion(const Problem& pb, int precision);
 int launch_fprop_complex_cvt(const float* x, float* xr, float* xi, const float* w_packed, float* y,
                              const Problem& pb, cudaStream_t stream);
+// forward() with the layout conversion done by layout warps inside the halo
+// pair kernel (one launch; xr/xi and, for 3xTF32, xr_lo/xi_lo: workspace
+// planes it fills).  The default complex path where it applies.
+bool use_layout_warps(const Problem& pb, int precision);
+int launch_fprop_complex_lw(const float* x, float* xr, float* xi, float* xr_lo, float* xi_lo,
+                            const float* w_packed, float* y, const Problem& pb, int precision,
+                            void* ws, size_t ws_bytes, cudaStream_t stream);
 // Name of the kernel path a complex (forward()) call takes.
 const char* complex_kernel_name(const Problem& pb, int precision);
 int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,

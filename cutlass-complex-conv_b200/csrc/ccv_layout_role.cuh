@@ -1,0 +1,217 @@
+// Layout warps: forward()'s complex64 NCHW -> fp32 NHWC conversion done by
+// two extra warps in every CTA of a persistent pair kernel, ahead of (and
+// overlapping) the convolution, in the same launch.
+//
+// Work is handed out by a global counter in chunks of kLwChunk tickets (one
+// atomic per chunk, the next chunk's number fetched while the current one
+// is converted): one ticket = 32 channels x 32 consecutive pixels of one image (a pixel is h * W + w: both layouts keep an
+// image's H x W plane contiguous).  Tickets run image by image, starting at
+// image lw_first_img (the first image of a stream-K range, which the kernel
+// runs first) and wrapping around; warps count completed tickets per image
+// (release), and a producer may load an image's planes once the count
+// reaches the image's ticket count (acquire + async-proxy fence).
+// A ticket is taken only by a running warp and completed without waiting on
+// anything, so a producer waits only for work that is in progress or that any
+// running CTA - its own included - will take next: no CTA depends on another
+// CTA being resident.
+//
+// 3xTF32: the warps write tf32(x) into the hi planes and x - tf32(x) into the
+// lo planes (the activation split of three-pass TF32).
+#pragma once
+
+#include <cstdint>
+
+#include "ccv_fprop_common.cuh"
+#include "ccv_ptx.cuh"
+
+namespace ccv {
+
+constexpr int kLwWarps = 2;                 // layout warps per CTA
+constexpr int kLwPx = 32;                   // pixels per ticket
+constexpr int kLwCh = 32;                   // channels per ticket (lane = channel)
+constexpr int kLwChunk = 4;                 // tickets per counter increment
+// Counter set layout (a zeroed library-owned set; the last CTA resets it).
+constexpr int kLwTicket = 0;
+constexpr int kLwDone = 1;
+constexpr int kLwFlag0 = 8;                 // image i: tickets completed
+
+__device__ __forceinline__ int lw_tickets_per_image(const FpropParams& prm) {
+  return ((prm.h * prm.w + kLwPx - 1) / kLwPx) * ((prm.c + kLwCh - 1) / kLwCh);
+}
+
+__device__ __forceinline__ float lw_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+struct LwTicket {
+  long long tk;  // ticket index (>= total: none)
+  int img, px0, c0;
+};
+
+__device__ __forceinline__ LwTicket lw_decode(const FpropParams& prm, long long tk, int tpx,
+                                              int per_img) {
+  LwTicket t;
+  t.tk = tk;
+  const int order = static_cast<int>(tk / per_img);
+  const int rem = static_cast<int>(tk - static_cast<long long>(order) * per_img);
+  t.img = (order + prm.lw_first_img) % prm.n;
+  const int cb = rem / tpx;
+  t.px0 = (rem - cb * tpx) * kLwPx;
+  t.c0 = cb * kLwCh;
+  return t;
+}
+
+// Loads of one ticket.  Lane = channel: the lane reads its channel's 32
+// pixels (256 contiguous bytes) as 16-byte pieces, so one warp instruction
+// touches one 32-byte sector per channel and the next one finds the sector's
+// other half in L1.  v[j] = pixels 2j and 2j+1 (re, im, re, im).  `vec`:
+// 16-byte loads are aligned (H*W even and a 16-byte-aligned input).
+__device__ __forceinline__ void lw_load(const FpropParams& prm, const LwTicket& t, long long total,
+                                        int hw, int lane, bool vec, float4 (&v)[kLwPx / 2]) {
+  const int c = t.c0 + lane;
+  const bool ok = t.tk < total && c < prm.c;
+  const float2* src = reinterpret_cast<const float2*>(prm.xc) +
+                      (static_cast<long long>(t.img) * prm.c + c) * hw + t.px0;
+  const int np = min(kLwPx, hw - t.px0);
+  if (vec) {
+#pragma unroll
+    for (int j = 0; j < kLwPx / 2; ++j) {
+      v[j] = (ok && 2 * j < np) ? __ldg(reinterpret_cast<const float4*>(src + 2 * j))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kLwPx / 2; ++j) {
+      const float2 a = (ok && 2 * j < np) ? __ldg(src + 2 * j) : make_float2(0.f, 0.f);
+      const float2 b = (ok && 2 * j + 1 < np) ? __ldg(src + 2 * j + 1) : make_float2(0.f, 0.f);
+      v[j] = make_float4(a.x, a.y, b.x, b.y);
+    }
+  }
+}
+
+// Stores of one ticket: for each pixel, lane = channel gives one 128-byte
+// run per plane (fp32 NHWC).
+__device__ __forceinline__ void lw_store(const FpropParams& prm, const LwTicket& t, int hw,
+                                         int lane, const float4 (&v)[kLwPx / 2]) {
+  const int c = t.c0 + lane;
+  if (c >= prm.c) return;
+  const long long o0 = (static_cast<long long>(t.img) * hw + t.px0) * prm.c + c;
+  const int np = min(kLwPx, hw - t.px0);
+  const long long cs = prm.c;
+  if (prm.passes > 1) {
+#pragma unroll
+    for (int p = 0; p < kLwPx; ++p) {
+      if (p < np) {
+        const float a = (p & 1) ? v[p / 2].z : v[p / 2].x;
+        const float b = (p & 1) ? v[p / 2].w : v[p / 2].y;
+        const float ah = lw_tf32(a);
+        const float bh = lw_tf32(b);
+        prm.lw_xr[o0 + p * cs] = ah;
+        prm.lw_xi[o0 + p * cs] = bh;
+        prm.lw_xr_lo[o0 + p * cs] = a - ah;
+        prm.lw_xi_lo[o0 + p * cs] = b - bh;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int p = 0; p < kLwPx; ++p) {
+      if (p < np) {
+        prm.lw_xr[o0 + p * cs] = (p & 1) ? v[p / 2].z : v[p / 2].x;
+        prm.lw_xi[o0 + p * cs] = (p & 1) ? v[p / 2].w : v[p / 2].y;
+      }
+    }
+  }
+}
+
+// One layout warp: takes tickets until none are left, two in flight (the
+// loads of one overlap the stores of the other).
+// Completed tickets are counted per image and published in batches: after a
+// warp barrier, lane 0 fences (cumulative over the warp's stores) and adds
+// the count with release semantics.
+__device__ __forceinline__ void layout_warp(const FpropParams& prm, int lane) {
+  const int hw = prm.h * prm.w;
+  const int tpx = (hw + kLwPx - 1) / kLwPx;
+  const int per_img = tpx * ((prm.c + kLwCh - 1) / kLwCh);
+  const long long total = static_cast<long long>(per_img) * prm.n;
+  const bool vec = (hw & 1) == 0 && (reinterpret_cast<uintptr_t>(prm.xc) & 15) == 0;
+  unsigned* ctrs = prm.cvt_ctrs;
+  // Lane 0 holds the prefetched chunk number; it is read (shuffled) only
+  // when the current chunk is used up.
+  unsigned pre = lane == 0 ? atomicAdd(ctrs + kLwTicket, 1u) : 0u;
+  long long base = 0;
+  int idx = kLwChunk;
+  auto grab = [&]() -> long long {
+    if (idx == kLwChunk) {
+      base = static_cast<long long>(__shfl_sync(0xffffffffu, pre, 0)) * kLwChunk;
+      idx = 0;
+      pre = lane == 0 ? atomicAdd(ctrs + kLwTicket, 1u) : 0u;
+    }
+    return base + idx++;
+  };
+  int pend_img = -1;
+  unsigned pend = 0;
+  auto publish = [&]() {
+    if (pend == 0) return;
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence();
+      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(ctrs + kLwFlag0 + pend_img),
+                   "r"(pend)
+                   : "memory");
+    }
+    pend = 0;
+  };
+  auto done = [&](const LwTicket& t) {
+    if (t.img != pend_img || pend >= 8) {
+      publish();
+      pend_img = t.img;
+    }
+    ++pend;
+  };
+  float4 va[kLwPx / 2], vb[kLwPx / 2];
+  LwTicket ta = lw_decode(prm, grab(), tpx, per_img);
+  lw_load(prm, ta, total, hw, lane, vec, va);
+  LwTicket tb = lw_decode(prm, grab(), tpx, per_img);
+  lw_load(prm, tb, total, hw, lane, vec, vb);
+#pragma unroll 1
+  while (ta.tk < total) {
+    const long long na = grab();
+    lw_store(prm, ta, hw, lane, va);
+    done(ta);
+    ta = lw_decode(prm, na, tpx, per_img);
+    lw_load(prm, ta, total, hw, lane, vec, va);
+    if (tb.tk >= total) break;
+    const long long nb = grab();
+    lw_store(prm, tb, hw, lane, vb);
+    done(tb);
+    tb = lw_decode(prm, nb, tpx, per_img);
+    lw_load(prm, tb, total, hw, lane, vec, vb);
+  }
+  publish();
+}
+
+// Waits (bounded) until image `img`'s planes are written; then orders the
+// caller's later TMA (async-proxy) reads after those generic-proxy stores.
+__device__ __forceinline__ bool lw_wait_image(const FpropParams& prm, int img) {
+  const unsigned* f = prm.cvt_ctrs + kLwFlag0 + img;
+  const unsigned need = static_cast<unsigned>(lw_tickets_per_image(prm));
+  const uint64_t t0 = ptx::globaltimer();
+  uint32_t ns = 64;
+  while (true) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if (v >= need) break;
+    if (ptx::globaltimer() - t0 > CCV_WAIT_TIMEOUT_NS) {
+      atomicCAS(prm.status, 0, CCV_ERR_DEVICE_TIMEOUT);
+      return false;
+    }
+    ptx::nanosleep(ns);
+    if (ns < 512) ns <<= 1;
+  }
+  ptx::fence_proxy_async_all();
+  return true;
+}
+
+}  // namespace ccv

@@ -51,6 +51,21 @@ def test_mri_config_3xtf32_sampled_images():
         assert err <= TOL_3XTF32, (img, err)
 
 
+@pytest.mark.parametrize("c", [64, 128])
+def test_deep_k_3xtf32(c):
+    # K = 9*C terms per output: the correction passes run before the main
+    # pass (the accumulator is small while they run), which keeps C = 128
+    # under the bar on the tensor cores' fp32 accumulation.
+    case = oracle.ConvCase(3, c, 28, 28, 128, 3, 3, 1, 1, 1, 1)
+    x, wr, wi = oracle.make_inputs(case, input_seed=62)
+    packed = abi_prepack(case, wr, wi, precision=P3)
+    ref = oracle.oracle_fp64(case, x, wr, wi)
+    y = abi_fprop_planar(case, x, packed, precision=P3, poison=True)
+    assert oracle.rel_frobenius(y, ref) <= TOL_3XTF32
+    yc = abi_fprop_complex(case, x, packed, precision=P3, poison=True)
+    assert torch.equal(yc, y.to(torch.complex64))
+
+
 def test_tf32_is_measurably_less_accurate_than_3xtf32():
     case = oracle.ConvCase(2, 64, 16, 16, 64, 3, 3, 1, 1, 1, 1)
     x, wr, wi = oracle.make_inputs(case, input_seed=5)

@@ -32,11 +32,12 @@ CASES = [
 @pytest.fixture
 def knobs():
     keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_CVT", "CCV_CVT_CLUSTERS", "CCV_STREAMK",
-            "CCV_CD", "CCV_FUSED")
+            "CCV_CD", "CCV_FUSED", "CCV_LW")
     old = {k: os.environ.get(k) for k in keys}
     os.environ["CCV_FORCE_KERNEL"] = "2"
     os.environ["CCV_HALO"] = "1"
     os.environ["CCV_CVT"] = "1"
+    os.environ["CCV_LW"] = "0"  # the comparison path below is the layout pass
     for k in ("CCV_CVT_CLUSTERS", "CCV_CD", "CCV_FUSED"):
         os.environ.pop(k, None)
     yield

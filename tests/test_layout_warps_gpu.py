@@ -1,0 +1,163 @@
+"""forward() through layout warps (ccv_layout_role.cuh): two extra warps in
+every CTA of the halo pair kernel convert complex64 NCHW into the fp32 NHWC
+workspace planes while the MMA runs, in one launch.
+
+Checked against the fp64 oracle (TF32 and 3xTF32 bars) and bitwise against
+the two-launch path (layout pass + the same kernel), with the workspace
+filled with NaN before every call (a plane read before its image was written
+would show), repeated calls (the library-owned counters are left zero),
+ragged pixel counts (H*W not a multiple of 32), channel counts that are not
+multiples of 32, one image, and the two-sub-box tiles.
+"""
+
+import ctypes
+import os
+
+import pytest
+import torch
+
+import ccv_abi
+import oracle
+from test_parity_gpu import DEV, TF32_TOL, _ptr, _stream, abi_prepack, device_status
+
+pytestmark = pytest.mark.gpu
+
+C = oracle.ConvCase
+CASES = [
+    ("b8_128_56", C(8, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)),
+    ("k64_subbox", C(4, 64, 40, 40, 64, 3, 3, 1, 1, 1, 1)),
+    ("ragged_30x41_c36_k20", C(6, 36, 30, 41, 20, 3, 3, 1, 1, 1, 1)),
+    ("5x5_p2_k132", C(3, 48, 26, 34, 132, 5, 5, 1, 1, 2, 2)),
+    ("one_image_7x9_c8", C(1, 8, 7, 9, 40, 3, 3, 1, 1, 1, 1)),
+    ("k32_p0_3x1", C(5, 96, 23, 17, 32, 3, 1, 1, 1, 0, 0)),
+]
+
+
+@pytest.fixture
+def knobs():
+    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_LW", "CCV_CVT", "CCV_STREAMK", "CCV_CD",
+            "CCV_FUSED", "CCV_SUBBOX")
+    old = {k: os.environ.get(k) for k in keys}
+    os.environ["CCV_FORCE_KERNEL"] = "2"
+    os.environ["CCV_HALO"] = "1"
+    for k in ("CCV_CVT", "CCV_CD", "CCV_FUSED", "CCV_SUBBOX"):
+        os.environ.pop(k, None)
+    # Layout warps wherever they apply (by default only for grids of two or
+    # more waves of tiles).
+    os.environ["CCV_LW"] = "1"
+    # Whole tiles on the comparison path too (same summation order).
+    os.environ["CCV_STREAMK"] = "0"
+    yield
+    for k, v in old.items():
+        if v is None:
+            os.environ.pop(k, None)
+        else:
+            os.environ[k] = v
+    torch.cuda.synchronize()
+    assert device_status() == 0, "a bounded in-kernel wait ran out"
+
+
+def kernel_name(case, precision=ccv_abi.CCV_PRECISION_TF32):
+    lib = ccv_abi.load()
+    shp = ccv_abi.shape_of(case)
+    return lib.ccv_fprop_complex_kernel(ctypes.byref(shp), precision).decode()
+
+
+def fprop_complex_nan_ws(case, x, packed, precision):
+    """ccv_fprop_complex with a NaN-filled workspace and a NaN-filled output."""
+    lib = ccv_abi.load()
+    shp = ccv_abi.shape_of(case)
+    xd = x.to(DEV).contiguous()
+    y = torch.full((case.n, case.k, case.p, case.q), float("nan"), dtype=torch.complex64,
+                   device=DEV)
+    ws_bytes = lib.ccv_fprop_complex_workspace_bytes(ctypes.byref(shp), precision)
+    ws = torch.full((max(ws_bytes, 16),), 0xFF, dtype=torch.uint8, device=DEV)
+    ccv_abi.check(lib.ccv_fprop_complex(_ptr(xd), _ptr(packed), _ptr(y), ctypes.byref(shp),
+                                        precision, _ptr(ws), ws_bytes, _stream()),
+                  "fprop_complex")
+    torch.cuda.synchronize()
+    return y.cpu()
+
+
+def launches(case, precision):
+    lib = ccv_abi.load()
+    shp = ccv_abi.shape_of(case)
+    k = ctypes.c_int(0)
+    ccv_abi.check(lib.ccv_fprop_kernel_launches(ctypes.byref(shp), precision, 1, ctypes.byref(k)),
+                  "launches")
+    return k.value
+
+
+@pytest.mark.parametrize("name,case", CASES, ids=[c[0] for c in CASES])
+def test_layout_warps_tf32(knobs, name, case):
+    prec = ccv_abi.CCV_PRECISION_TF32
+    assert kernel_name(case) == "halo_pair_layout_warps"
+    assert launches(case, prec) == 1
+    x, wr, wi = oracle.make_inputs(case, input_seed=61)
+    packed = abi_prepack(case, wr, wi)
+    y = fprop_complex_nan_ws(case, x, packed, prec)
+    assert not torch.isnan(y.real).any() and not torch.isnan(y.imag).any()
+    sub = C(1, case.c, case.h, case.w, case.k, case.r, case.s, 1, 1, case.pad_h, case.pad_w)
+    for img in sorted({0, case.n - 1}):
+        ref = oracle.oracle_fp64(sub, x[img:img + 1], wr, wi)
+        assert oracle.rel_frobenius(y[img:img + 1], ref) <= TF32_TOL, img
+    # Repeated calls give the same bits (counters left zero by each call).
+    for _ in range(2):
+        assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
+    # The two-launch path: layout pass, then the same kernel.
+    os.environ["CCV_LW"] = "0"
+    assert kernel_name(case) == "layout_pass+halo_pair"
+    assert launches(case, prec) == 2
+    assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
+
+
+@pytest.mark.parametrize("name,case", [CASES[0], CASES[2]], ids=[CASES[0][0], CASES[2][0]])
+def test_layout_warps_3xtf32(knobs, name, case):
+    prec = ccv_abi.CCV_PRECISION_3XTF32
+    assert kernel_name(case, prec) == "halo_pair_layout_warps"
+    x, wr, wi = oracle.make_inputs(case, input_seed=62)
+    packed = abi_prepack(case, wr, wi, precision=prec)
+    y = fprop_complex_nan_ws(case, x, packed, prec)
+    os.environ["CCV_LW"] = "0"
+    assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
+    sub = C(1, case.c, case.h, case.w, case.k, case.r, case.s, 1, 1, case.pad_h, case.pad_w)
+    for img in (0, case.n - 1):
+        ref = oracle.oracle_fp64(sub, x[img:img + 1], wr, wi)
+        assert oracle.rel_frobenius(y[img:img + 1], ref) <= 1e-5, img
+
+
+def test_layout_warps_not_taken(knobs):
+    # Stride 2 and 1x1 filters run the tap kernel: layout pass first.
+    assert kernel_name(C(2, 32, 20, 20, 64, 3, 3, 2, 2, 1, 1)) != "halo_pair_layout_warps"
+    os.environ.pop("CCV_FORCE_KERNEL")
+    os.environ.pop("CCV_HALO")
+    assert kernel_name(C(4, 64, 28, 28, 128, 1, 1, 1, 1, 0, 0)) != "halo_pair_layout_warps"
+    # Default: only grids of at least two waves of tiles.
+    os.environ.pop("CCV_LW")
+    assert kernel_name(C(8, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == "layout_pass+halo_pair"
+    assert kernel_name(C(64, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == "halo_pair_layout_warps"
+    assert kernel_name(C(32, 64, 56, 56, 64, 3, 3, 1, 1, 1, 1)) == "halo_pair_layout_warps"
+    # The opt-in converter clusters take precedence when asked for.
+    os.environ["CCV_CVT"] = "1"
+    assert kernel_name(C(8, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == \
+        "halo_pair_converter_clusters"
+
+
+@pytest.mark.parametrize("name,case", [CASES[0], ("b3_c64_ragged", C(3, 64, 45, 29, 96, 3, 3, 1, 1, 1, 1))],
+                         ids=[CASES[0][0], "b3_c64_ragged"])
+def test_layout_warps_with_stream_k(knobs, name, case):
+    # Default stream-K policy (a partial last wave is split): the split range
+    # runs first, so the layout warps convert its images first.  Same plan,
+    # same sums as the layout pass + kernel.
+    os.environ.pop("CCV_STREAMK")
+    prec = ccv_abi.CCV_PRECISION_TF32
+    x, wr, wi = oracle.make_inputs(case, input_seed=63)
+    packed = abi_prepack(case, wr, wi)
+    y = fprop_complex_nan_ws(case, x, packed, prec)
+    assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
+    sub = C(1, case.c, case.h, case.w, case.k, case.r, case.s, 1, 1, case.pad_h, case.pad_w)
+    for img in (0, case.n - 1):
+        ref = oracle.oracle_fp64(sub, x[img:img + 1], wr, wi)
+        assert oracle.rel_frobenius(y[img:img + 1], ref) <= TF32_TOL, img
+    os.environ["CCV_LW"] = "0"
+    assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))

@@ -44,13 +44,14 @@ GRIDS = [3, 7]
 @pytest.fixture
 def knobs():
     keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_STREAMK", "CCV_MAX_CLUSTERS", "CCV_CD",
-            "CCV_FUSED", "CCV_SUBBOX", "CCV_CVT")
+            "CCV_FUSED", "CCV_SUBBOX", "CCV_CVT", "CCV_LW")
     old = {k: os.environ.get(k) for k in keys}
     # The split lives in the planar-operand pair kernels with one box per CTA
-    # (not with converter clusters).
+    # (not with converter clusters or layout warps).
     os.environ["CCV_CD"] = "0"
     os.environ["CCV_SUBBOX"] = "0"
     os.environ["CCV_CVT"] = "0"
+    os.environ["CCV_LW"] = "0"  # complex calls: layout pass + the split kernel
 
     def set_(family=None, streamk=None, clusters=None):
         if family is not None:
