@@ -613,24 +613,38 @@ int launch_fprop_complex_cvt(const float* x, float* xr, float* xi, const float* 
 }
 
 bool use_layout_warps(const Problem& pb, int precision) {
-  // CCV_LW=0: never; CCV_LW=1: wherever the halo kernel runs; unset: when
-  // the grid runs at least two waves of tiles.  Below that, most images are
-  // needed by the first wave, so converting them in the kernel only delays
-  // it, and the layout pass (at the HBM copy rate) is faster.
+  // CCV_LW=0: never; CCV_LW=1: wherever a pair kernel runs; unset: when
+  //   * the grid runs at least two waves of tiles (below that the first
+  //     wave needs most images at once),
+  //   * the input is at least 32 MB (small problems: the first wave's wait
+  //     dominates), and
+  //   * there are at least 500 flops per input byte, K*R*S*(P*Q)/(H*W) per
+  //     pass (the layout warps convert ~1 TB/s; below that - stride 2 at
+  //     C = 64 - they hold the MMAs back and a pass at the copy rate wins).
+  // Measured on B200 over the BASELINE layers and the batch sweep.
   const char* env = getenv("CCV_LW");
   const int mode = env != nullptr ? atoi(env) : -1;
   if (mode == 0) return false;
   if (use_complex_direct(pb, precision) || use_in_kernel_conversion(pb, precision)) return false;
   const Tiling t = choose_tiling(pb);
   Tiling th;
-  if (choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th) != kPairHalo) return false;
-  if (use_converter_warps(pb, precision, th)) return false;
+  const int fam = choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th);
+  if (fam != kPairHalo && fam != kPairTap) return false;
+  if (fam == kPairHalo && use_converter_warps(pb, precision, th)) return false;
   if (pb.n > kSkCounterWords - kLwFlag0) return false;
   if (mode == 1) return true;
-  // Pixels per cluster tile: two CTAs of 128 (two sub-boxes each for KT <= 64).
-  const long long tile_px = 2LL * kBlockM * (th.kt <= 64 ? 2 : 1);
+  const double in_bytes = 8.0 * pb.n * pb.h * pb.w * pb.c;
+  const double flops_per_byte = static_cast<double>(pb.k) * pb.r * pb.s * pb.p * pb.q /
+                                (static_cast<double>(pb.h) * pb.w) *
+                                (precision == CCV_PRECISION_3XTF32 ? 3 : 1);
+  if (in_bytes < 32.0 * 1024 * 1024 || flops_per_byte < 500.0) return false;
+  // Pixels per cluster tile: two CTAs of 128 (halo: two sub-boxes each for
+  // KT <= 64).
+  const int kt = fam == kPairHalo ? th.kt : t.kt;
+  const int tiles_n = fam == kPairHalo ? th.tiles_n : t.tiles_n;
+  const long long tile_px = 2LL * kBlockM * (fam == kPairHalo && kt <= 64 ? 2 : 1);
   const long long tiles =
-      (static_cast<long long>(pb.n) * pb.p * pb.q + tile_px - 1) / tile_px * th.tiles_n;
+      (static_cast<long long>(pb.n) * pb.p * pb.q + tile_px - 1) / tile_px * tiles_n;
   return tiles >= 2LL * (device_sm_count() / 2);
 }
 
@@ -640,17 +654,28 @@ int launch_fprop_complex_lw(const float* x, float* xr, float* xi, float* xr_lo, 
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;
-  if (choose_family(pb, split, t, &th) != kPairHalo) {
-    return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
+  switch (choose_family(pb, split, t, &th)) {
+    case kPairHalo:
+      return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, nullptr, split, w_packed, y, nullptr,
+                                    pb, th, OUT_COMPLEX_NCHW, ws, ws_bytes, stream, x, true);
+    case kPairTap:
+      return launch_fprop_pair(xr, xi, split ? xr_lo : nullptr, split ? xi_lo : nullptr, w_packed,
+                               y, nullptr, pb, t, OUT_COMPLEX_NCHW, ws, ws_bytes, stream, x);
+    default:
+      return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
   }
-  return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, nullptr, split, w_packed, y, nullptr, pb, th,
-                                OUT_COMPLEX_NCHW, ws, ws_bytes, stream, x, true);
 }
 
 const char* complex_kernel_name(const Problem& pb, int precision) {
   if (use_complex_direct(pb, precision)) return "complex_direct_pair";
   if (use_in_kernel_conversion(pb, precision)) return "halo_pair_converter_clusters";
-  if (use_layout_warps(pb, precision)) return "halo_pair_layout_warps";
+  if (use_layout_warps(pb, precision)) {
+    const Tiling t = choose_tiling(pb);
+    Tiling th;
+    return choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th) == kPairHalo
+               ? "halo_pair_layout_warps"
+               : "tap_pair_layout_warps";
+  }
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;

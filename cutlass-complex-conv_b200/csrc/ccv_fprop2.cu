@@ -19,7 +19,9 @@
 // transaction bytes of both CTAs complete on the even CTA's "full" barrier.
 //
 // Warp roles per CTA (192 threads): warp 0 TMA producer, warp 1 TMEM
-// allocation (both CTAs) and MMA issue (even CTA only), warps 2..5 epilogue.
+// allocation (both CTAs) and MMA issue (even CTA only), warps 2..5 epilogue;
+// LW: warps 6..7 are layout warps (ccv_layout_role.cuh) converting forward()'s
+// complex64 input into the planes the producer reads, in the same launch.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -28,6 +30,7 @@
 #include "ccv_epilogue.cuh"
 #include "ccv_fprop_common.cuh"
 #include "ccv_internal.h"
+#include "ccv_layout_role.cuh"
 #include "ccv_ptx.cuh"
 
 namespace ccv {
@@ -56,8 +59,8 @@ struct Cfg2 {
   static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
-template <int KT, bool FLAT, bool OUT_COMPLEX>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
+template <int KT, bool FLAT, bool OUT_COMPLEX, bool LW>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32 * kLwWarps : 0), 1)
     ccv_fprop2_tf32_kernel(const __grid_constant__ FpropParams prm) {
   using C = Cfg2<KT>;
   extern __shared__ uint8_t smem_raw[];
@@ -132,6 +135,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     if (lane == 0 && !skip) {
       uint32_t g = 0;
       bool abort = false;
+      int ready_lo = 0, ready_hi = -1;  // images known converted (layout warps)
       UnitCursor cur = unit_cursor(prm, cid);
       WorkUnit wu;
       while (!abort && next_unit(prm, ncl, cur, wu)) {
@@ -139,6 +143,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
         const int n_tile = t % prm.tiles_n;
         const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
         const int k0 = n_tile * KT;
+        if constexpr (LW) {
+          // Images this CTA's rows read: the planes of each are written
+          // before the first load.
+          int lo, hi;
+          if constexpr (FLAT) {
+            // Rows m0 .. m0+127 of N*P*Q (1x1, stride 1: input pixel = output
+            // pixel); rows past the end read the fill value.
+            const long long pq = static_cast<long long>(prm.p) * prm.q;
+            const long long m0 = min(static_cast<long long>(half) * kBlockM, prm.m_total - 1);
+            const long long m1 = min(static_cast<long long>(half) * kBlockM + kBlockM, prm.m_total) - 1;
+            lo = static_cast<int>(m0 / pq);
+            hi = static_cast<int>(max(m0, m1) / pq);
+          } else {
+            lo = min(half * prm.nb, prm.total_boxes - 1) / per_img;
+            hi = min(half * prm.nb + prm.nb - 1, prm.total_boxes - 1) / per_img;
+          }
+          if (lo < ready_lo || hi > ready_hi) {
+            for (int im = lo; im <= hi && !abort; ++im) {
+              if (im >= ready_lo && im <= ready_hi) continue;
+              if (!lw_wait_image(prm, im)) {
+                flags[1] = 1;
+                abort = true;
+              }
+            }
+            if (abort) break;
+            if (lo > ready_hi + 1 || hi < ready_lo - 1) {
+              ready_lo = lo;
+              ready_hi = hi;
+            } else {
+              ready_lo = min(ready_lo, lo);
+              ready_hi = max(ready_hi, hi);
+            }
+          }
+        }
         for (int v = wu.jbeg; v < wu.jend; ++v, ++g) {
           int ks;
           const int pass = slot_pass(v, prm.ksteps, prm.passes, &ks);
@@ -248,7 +286,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
       ptx::mbar_wait_bounded(done_bar, 0, prm.status, kTimeout);
     }
     __syncwarp();
-  } else {
+  } else if (warp <= 5) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
@@ -304,8 +342,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
     // Output stores still in flight complete before the CTA exits.
     if (lane == 0) ptx::bulk_wait_all();
   }
+  if constexpr (LW) {
+    if (warp >= kThreads2 / 32 && !skip) {
+      // ---------------------------------------------------------- layout warps
+      layout_warp(prm, lane);
+    }
+  }
 
   __syncthreads();
+  if constexpr (LW) {
+    // The last CTA to finish leaves the conversion counters zero.
+    if (threadIdx.x == 0) {
+      unsigned old;
+      asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                   : "=r"(old)
+                   : "l"(prm.cvt_ctrs + kLwDone)
+                   : "memory");
+      if (old == 2u * static_cast<unsigned>(ncl) - 1u) {
+        for (int i = 0; i < prm.n; ++i) prm.cvt_ctrs[kLwFlag0 + i] = 0u;
+        prm.cvt_ctrs[kLwTicket] = 0u;
+        prm.cvt_ctrs[kLwDone] = 0u;
+        __threadfence();
+      }
+    }
+  }
   if (flags[1]) ptx::nanosleep(100000);  // let stray copies of an aborted tile land
   ptx::tc_fence_before();
   ptx::cluster_sync();
@@ -315,10 +375,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2, 1)
   }
 }
 
-template <int KT, bool FLAT, bool OUT_COMPLEX>
+template <int KT, bool FLAT, bool OUT_COMPLEX, bool LW>
 int launch2_variant(FpropParams& prm, void* ws, size_t ws_bytes, cudaStream_t stream) {
   using C = Cfg2<KT>;
-  auto kern = ccv_fprop2_tf32_kernel<KT, FLAT, OUT_COMPLEX>;
+  auto kern = ccv_fprop2_tf32_kernel<KT, FLAT, OUT_COMPLEX, LW>;
+  constexpr int threads = kThreads2 + (LW ? 32 * kLwWarps : 0);
   static std::once_flag once[64];
   static int max_clusters[64] = {};
   int dev = 0;
@@ -329,7 +390,7 @@ int launch2_variant(FpropParams& prm, void* ws, size_t ws_bytes, cudaStream_t st
     if (err != cudaSuccess) return;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 148, 1, 1);
-    cfg.blockDim = dim3(kThreads2, 1, 1);
+    cfg.blockDim = dim3(threads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) {
@@ -345,19 +406,34 @@ int launch2_variant(FpropParams& prm, void* ws, size_t ws_bytes, cudaStream_t st
   const int launched = launch_clusters(prm, clusters, prm.ksteps * prm.passes, KT, ws, ws_bytes,
                                        stream, &rc);
   if (rc != CCV_OK) return rc;
-  cudaError_t e = launch_kernel(kern, dim3(2 * launched), dim3(kThreads2), C::kSmemBytes, stream,
-                                0, prm);
+  if (LW) {
+    // The stream-K range runs first: the layout warps start at its first image.
+    prm.lw_first_img = 0;
+    if (prm.sk_slots > 0) {
+      const int half = 2 * (prm.sk_start / prm.tiles_n);
+      if (FLAT) {
+        prm.lw_first_img = static_cast<int>(
+            std::min(static_cast<long long>(half) * kBlockM, prm.m_total - 1) /
+            (static_cast<long long>(prm.p) * prm.q));
+      } else {
+        prm.lw_first_img =
+            std::min(half * prm.nb, prm.total_boxes - 1) / (prm.tiles_bp * prm.tiles_bq);
+      }
+    }
+  }
+  cudaError_t e = launch_kernel(kern, dim3(2 * launched), dim3(threads), C::kSmemBytes, stream, 0,
+                                prm);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "fprop2 kernel launch");
   return CCV_OK;
 }
 
-template <bool FLAT, bool OUT_COMPLEX>
+template <bool FLAT, bool OUT_COMPLEX, bool LW = false>
 int launch2_kt(int kt, FpropParams& prm, void* ws, size_t ws_bytes, cudaStream_t stream) {
   switch (kt) {
-    case 128: return launch2_variant<128, FLAT, OUT_COMPLEX>(prm, ws, ws_bytes, stream);
-    case 64: return launch2_variant<64, FLAT, OUT_COMPLEX>(prm, ws, ws_bytes, stream);
-    default: return launch2_variant<32, FLAT, OUT_COMPLEX>(prm, ws, ws_bytes, stream);
+    case 128: return launch2_variant<128, FLAT, OUT_COMPLEX, LW>(prm, ws, ws_bytes, stream);
+    case 64: return launch2_variant<64, FLAT, OUT_COMPLEX, LW>(prm, ws, ws_bytes, stream);
+    default: return launch2_variant<32, FLAT, OUT_COMPLEX, LW>(prm, ws, ws_bytes, stream);
   }
 }
 
@@ -486,7 +562,7 @@ int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws,
 int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                       const float* w_packed, float* y0, float* y1, const Problem& pb,
                       const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const float* lw_src) {
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;
@@ -546,6 +622,21 @@ int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, cons
   }
   const bool cplx = out_layout == OUT_COMPLEX_NCHW;
   if (!cplx && (rc = encode_planar_out_maps(prm, y0, y1, t.flat)) != CCV_OK) return rc;
+  if (lw_src != nullptr) {
+    // Layout warps write xr/xi (and the remainder planes) from lw_src.
+    if (!cplx || pb.n > kSkCounterWords - kLwFlag0) {
+      return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
+    }
+    prm.xc = lw_src;
+    prm.lw_xr = const_cast<float*>(xr);
+    prm.lw_xi = const_cast<float*>(xi);
+    prm.lw_xr_lo = const_cast<float*>(xr_lo);
+    prm.lw_xi_lo = const_cast<float*>(xi_lo);
+    prm.cvt_ctrs = stream_k_counters();
+    if (prm.cvt_ctrs == nullptr) return CCV_ERR_CUDA;
+    return t.flat ? launch2_kt<true, true, true>(t.kt, prm, ws, ws_bytes, stream)
+                  : launch2_kt<false, true, true>(t.kt, prm, ws, ws_bytes, stream);
+  }
   if (t.flat) {
     return cplx ? launch2_kt<true, true>(t.kt, prm, ws, ws_bytes, stream)
                 : launch2_kt<true, false>(t.kt, prm, ws, ws_bytes, stream);

@@ -233,7 +233,7 @@ int pair_tiles(const Tiling& t);
 int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                       const float* w_packed, float* y0, float* y1, const Problem& pb,
                       const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
-                      cudaStream_t stream);
+                      cudaStream_t stream, const float* lw_src = nullptr);
 
 // Halo variant of the pair kernel (ccv_fprop2h.cu): stride-1 problems with a
 // filter wider than 1x1.  Each CTA tile is one box of box_p x box_q pixels

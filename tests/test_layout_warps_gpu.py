@@ -1,6 +1,6 @@
 """forward() through layout warps (ccv_layout_role.cuh): two extra warps in
-every CTA of the halo pair kernel convert complex64 NCHW into the fp32 NHWC
-workspace planes while the MMA runs, in one launch.
+every CTA of the halo or tap pair kernel convert complex64 NCHW into the fp32
+NHWC workspace planes while the MMA runs, in one launch.
 
 Checked against the fp64 oracle (TF32 and 3xTF32 bars) and bitwise against
 the two-launch path (layout pass + the same kernel), with the workspace
@@ -126,17 +126,52 @@ def test_layout_warps_3xtf32(knobs, name, case):
         assert oracle.rel_frobenius(y[img:img + 1], ref) <= 1e-5, img
 
 
+TAP_CASES = [
+    ("s2_c64_k128", C(4, 64, 38, 38, 128, 3, 3, 2, 2, 1, 1)),
+    ("s2_ragged_c36_k20", C(3, 36, 21, 27, 20, 3, 3, 2, 2, 1, 1)),
+    ("1x1_flat_c96_k160", C(5, 96, 14, 14, 160, 1, 1, 1, 1, 0, 0)),
+    # 7x7 images: one 128-row tile spans three images.
+    ("1x1_flat_7x7", C(9, 64, 7, 7, 64, 1, 1, 1, 1, 0, 0)),
+    ("1x1_s2", C(4, 32, 20, 20, 48, 1, 1, 2, 2, 0, 0)),
+]
+
+
+@pytest.mark.parametrize("name,case", TAP_CASES, ids=[c[0] for c in TAP_CASES])
+@pytest.mark.parametrize("prec", [ccv_abi.CCV_PRECISION_TF32, ccv_abi.CCV_PRECISION_3XTF32],
+                         ids=["tf32", "3xtf32"])
+def test_layout_warps_tap_kernel(knobs, name, case, prec):
+    assert kernel_name(case, prec) == "tap_pair_layout_warps"
+    assert launches(case, prec) == 1
+    x, wr, wi = oracle.make_inputs(case, input_seed=64)
+    packed = abi_prepack(case, wr, wi, precision=prec)
+    y = fprop_complex_nan_ws(case, x, packed, prec)
+    assert not torch.isnan(y.real).any() and not torch.isnan(y.imag).any()
+    ref = oracle.oracle_fp64(case, x, wr, wi)
+    tol = TF32_TOL if prec == ccv_abi.CCV_PRECISION_TF32 else 1e-5
+    assert oracle.rel_frobenius(y, ref) <= tol
+    assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
+    os.environ["CCV_LW"] = "0"
+    assert kernel_name(case, prec) == "layout_pass+tap_pair"
+    assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
+
+
 def test_layout_warps_not_taken(knobs):
-    # Stride 2 and 1x1 filters run the tap kernel: layout pass first.
-    assert kernel_name(C(2, 32, 20, 20, 64, 3, 3, 2, 2, 1, 1)) != "halo_pair_layout_warps"
     os.environ.pop("CCV_FORCE_KERNEL")
     os.environ.pop("CCV_HALO")
-    assert kernel_name(C(4, 64, 28, 28, 128, 1, 1, 1, 1, 0, 0)) != "halo_pair_layout_warps"
+    # Batch-1 layers run the single-CTA kernel: layout pass first.
+    assert kernel_name(C(1, 64, 28, 28, 128, 3, 3, 1, 1, 1, 1)) == "layout_pass+single_cta"
     # Default: only grids of at least two waves of tiles.
     os.environ.pop("CCV_LW")
     assert kernel_name(C(8, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == "layout_pass+halo_pair"
     assert kernel_name(C(64, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == "halo_pair_layout_warps"
     assert kernel_name(C(32, 64, 56, 56, 64, 3, 3, 1, 1, 1, 1)) == "halo_pair_layout_warps"
+    assert kernel_name(C(32, 256, 28, 28, 1024, 1, 1, 1, 1, 0, 0)) == "tap_pair_layout_warps"
+    # Stride 2 at C = 64: too few flops per input byte (TF32), enough for 3xTF32.
+    s2 = C(32, 64, 112, 112, 128, 3, 3, 2, 2, 1, 1)
+    assert kernel_name(s2) == "layout_pass+tap_pair"
+    assert kernel_name(s2, ccv_abi.CCV_PRECISION_3XTF32) == "tap_pair_layout_warps"
+    # Small input (12.8 MB): layout pass.
+    assert kernel_name(C(8, 256, 28, 28, 1024, 1, 1, 1, 1, 0, 0)) == "layout_pass+tap_pair"
     # The opt-in converter clusters take precedence when asked for.
     os.environ["CCV_CVT"] = "1"
     assert kernel_name(C(8, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == \
