@@ -130,6 +130,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32
   const int rs = prm.r * prm.s;
   const int per_img = prm.tiles_bp * prm.tiles_bq;
 
+  if constexpr (LW) {
+    // Every warp converts the first wave's images first (nothing to do
+    // before they are there), then takes up its role.
+    if (!skip && prm.lw_prefix > 0) layout_warp(prm, lane, true);
+  }
+
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && !skip) {
@@ -345,7 +351,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32
   if constexpr (LW) {
     if (warp >= kThreads2 / 32 && !skip) {
       // ---------------------------------------------------------- layout warps
-      layout_warp(prm, lane);
+      layout_warp(prm, lane, false);
     }
   }
 
@@ -361,6 +367,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32
       if (old == 2u * static_cast<unsigned>(ncl) - 1u) {
         for (int i = 0; i < prm.n; ++i) prm.cvt_ctrs[kLwFlag0 + i] = 0u;
         prm.cvt_ctrs[kLwTicket] = 0u;
+        prm.cvt_ctrs[kLwPrefixTicket] = 0u;
         prm.cvt_ctrs[kLwDone] = 0u;
         __threadfence();
       }
@@ -420,6 +427,7 @@ int launch2_variant(FpropParams& prm, void* ws, size_t ws_bytes, cudaStream_t st
             std::min(half * prm.nb, prm.total_boxes - 1) / (prm.tiles_bp * prm.tiles_bq);
       }
     }
+    prm.lw_prefix = lw_prefix_tickets(prm, launched, 2LL * kBlockM);
   }
   cudaError_t e = launch_kernel(kern, dim3(2 * launched), dim3(threads), C::kSmemBytes, stream, 0,
                                 prm);

@@ -183,6 +183,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
     }
   }
 
+  if constexpr (LW) {
+    // Every warp converts the first wave's images first (nothing to do
+    // before they are there), then takes up its role.
+    if (!skip && prm.lw_prefix > 0) layout_warp(prm, lane, true);
+  }
+
   if (cvt_cta) {
     // ------------------------------------------------------------ converter cluster
     if (!skip && !cvt_role(prm, cvt_me, 2 * prm.cvt_clusters, data, afull(0), blockDim.x)) {
@@ -494,7 +500,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
   if constexpr (LW) {
     if (warp >= kThreadsH / 32 && !skip) {
       // ---------------------------------------------------------- layout warps
-      layout_warp(prm, lane);
+      layout_warp(prm, lane, false);
     }
   }
 
@@ -512,6 +518,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
       if (old == 2u * static_cast<unsigned>(ncl) - 1u) {
         for (int i = 0; i < prm.n; ++i) prm.cvt_ctrs[kCvtFlag0 + i] = 0u;
         prm.cvt_ctrs[kCvtTicket] = 0u;
+        prm.cvt_ctrs[kLwPrefixTicket] = 0u;
         prm.cvt_ctrs[kCvtDone] = 0u;
         __threadfence();
       }
@@ -593,6 +600,7 @@ int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
       const int half = 2 * (prm.sk_start / prm.tiles_n);
       prm.lw_first_img = std::min(half, prm.total_boxes - 1) / (prm.tiles_bp * prm.tiles_bq);
     }
+    prm.lw_prefix = lw_prefix_tickets(prm, launched, 2LL * kBlockM * NSUB);
   } else {
     launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc);
     if (rc != CCV_OK) return rc;

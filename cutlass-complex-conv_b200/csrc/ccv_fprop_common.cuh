@@ -37,6 +37,7 @@ struct alignas(64) FpropParams {
   float* lw_xr_lo;
   float* lw_xi_lo;
   int lw_first_img;  // image the layout warps convert first
+  long long lw_prefix;  // tickets every warp converts before its role (first wave's images)
   float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
   float* y1;          // planar: y_imag (NPQK); complex: unused
   int* status;        // device status word

@@ -20,6 +20,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cstdlib>
 
 #include "ccv_fprop_common.cuh"
 #include "ccv_ptx.cuh"
@@ -31,8 +32,9 @@ constexpr int kLwPx = 32;                   // pixels per ticket
 constexpr int kLwCh = 32;                   // channels per ticket (lane = channel)
 constexpr int kLwChunk = 4;                 // tickets per counter increment
 // Counter set layout (a zeroed library-owned set; the last CTA resets it).
-constexpr int kLwTicket = 0;
+constexpr int kLwTicket = 0;               // chunks taken past the prefix
 constexpr int kLwDone = 1;
+constexpr int kLwPrefixTicket = 2;         // chunks taken of the prefix
 constexpr int kLwFlag0 = 8;                 // image i: tickets completed
 
 __device__ __forceinline__ int lw_tickets_per_image(const FpropParams& prm) {
@@ -125,30 +127,42 @@ __device__ __forceinline__ void lw_store(const FpropParams& prm, const LwTicket&
   }
 }
 
-// One layout warp: takes tickets until none are left, two in flight (the
-// loads of one overlap the stores of the other).
+// One layout warp: takes chunks of tickets, two tickets in flight (the
+// loads of one overlap the stores of the other), until its range runs out.
+// prefix: the range is tickets [0, lw_prefix), counted by their own word, so
+// the phase ends exactly there; otherwise [lw_prefix, total).  Every chunk a
+// warp takes inside its range is converted by that warp.
 // Completed tickets are counted per image and published in batches: after a
 // warp barrier, lane 0 fences (cumulative over the warp's stores) and adds
 // the count with release semantics.
-__device__ __forceinline__ void layout_warp(const FpropParams& prm, int lane) {
+__device__ __forceinline__ void layout_warp(const FpropParams& prm, int lane, bool prefix) {
   const int hw = prm.h * prm.w;
   const int tpx = (hw + kLwPx - 1) / kLwPx;
   const int per_img = tpx * ((prm.c + kLwCh - 1) / kLwCh);
   const long long total = static_cast<long long>(per_img) * prm.n;
   const bool vec = (hw & 1) == 0 && (reinterpret_cast<uintptr_t>(prm.xc) & 15) == 0;
   unsigned* ctrs = prm.cvt_ctrs;
+  const long long first = prefix ? 0 : prm.lw_prefix;
+  const long long end = prefix ? (prm.lw_prefix < total ? prm.lw_prefix : total) : total;
+  unsigned* counter = ctrs + (prefix ? kLwPrefixTicket : kLwTicket);
   // Lane 0 holds the prefetched chunk number; it is read (shuffled) only
   // when the current chunk is used up.
-  unsigned pre = lane == 0 ? atomicAdd(ctrs + kLwTicket, 1u) : 0u;
+  unsigned pre = lane == 0 ? atomicAdd(counter, 1u) : 0u;
   long long base = 0;
   int idx = kLwChunk;
+  bool out = false;  // the range is used up
   auto grab = [&]() -> long long {
     if (idx == kLwChunk) {
-      base = static_cast<long long>(__shfl_sync(0xffffffffu, pre, 0)) * kLwChunk;
+      if (out) return total;
+      base = first + static_cast<long long>(__shfl_sync(0xffffffffu, pre, 0)) * kLwChunk;
       idx = 0;
-      pre = lane == 0 ? atomicAdd(ctrs + kLwTicket, 1u) : 0u;
+      if (base >= end) {
+        out = true;
+        return total;
+      }
+      pre = lane == 0 ? atomicAdd(counter, 1u) : 0u;
     }
-    return base + idx++;
+    return base + idx < end ? base + idx++ : total;
   };
   int pend_img = -1;
   unsigned pend = 0;
@@ -190,6 +204,25 @@ __device__ __forceinline__ void layout_warp(const FpropParams& prm, int lane) {
     lw_load(prm, tb, total, hw, lane, vec, vb);
   }
   publish();
+}
+
+// Tickets every warp of a CTA converts before taking up its role: the
+// images the first unit of every cluster reads (the stream-K range's images,
+// when there is one, then the first wave of whole tiles), which no MMA can
+// start without (a multiple of kLwChunk).  `tile_px`: output pixels per
+// cluster tile (one m-tile); CCV_LW_PREFIX=0 turns the phase off (timing
+// knob).
+inline long long lw_prefix_tickets(const FpropParams& prm, int launched, long long tile_px) {
+  const char* env = getenv("CCV_LW_PREFIX");
+  if (env != nullptr && atoi(env) == 0) return 0;
+  const long long pq = static_cast<long long>(prm.p) * prm.q;
+  const long long mtiles = (launched + prm.tiles_n - 1) / prm.tiles_n;
+  long long images = (mtiles * tile_px + pq - 1) / pq;
+  if (prm.sk_slots > 0) images += prm.n - prm.lw_first_img;
+  images = images < prm.n ? images : prm.n;
+  const long long per_img = ((static_cast<long long>(prm.h) * prm.w + kLwPx - 1) / kLwPx) *
+                            ((prm.c + kLwCh - 1) / kLwCh);
+  return (images * per_img + kLwChunk - 1) / kLwChunk * kLwChunk;
 }
 
 // Waits (bounded) until image `img`'s planes are written; then orders the

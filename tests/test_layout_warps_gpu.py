@@ -160,18 +160,19 @@ def test_layout_warps_not_taken(knobs):
     os.environ.pop("CCV_HALO")
     # Batch-1 layers run the single-CTA kernel: layout pass first.
     assert kernel_name(C(1, 64, 28, 28, 128, 3, 3, 1, 1, 1, 1)) == "layout_pass+single_cta"
-    # Default: only grids of at least two waves of tiles.
+    # Default: inputs of at least 128 MB, at least two waves of tiles and
+    # 500 flops per input byte.
     os.environ.pop("CCV_LW")
     assert kernel_name(C(8, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == "layout_pass+halo_pair"
     assert kernel_name(C(64, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == "halo_pair_layout_warps"
-    assert kernel_name(C(32, 64, 56, 56, 64, 3, 3, 1, 1, 1, 1)) == "halo_pair_layout_warps"
-    assert kernel_name(C(32, 256, 28, 28, 1024, 1, 1, 1, 1, 0, 0)) == "tap_pair_layout_warps"
+    assert kernel_name(C(8, 64, 320, 320, 64, 3, 3, 1, 1, 1, 1)) == "halo_pair_layout_warps"
+    assert kernel_name(C(32, 64, 56, 56, 64, 3, 3, 1, 1, 1, 1)) == "layout_pass+halo_pair"
+    assert kernel_name(C(128, 256, 28, 28, 1024, 1, 1, 1, 1, 0, 0)) == "tap_pair_layout_warps"
+    assert kernel_name(C(32, 256, 28, 28, 1024, 1, 1, 1, 1, 0, 0)) == "layout_pass+tap_pair"
     # Stride 2 at C = 64: too few flops per input byte (TF32), enough for 3xTF32.
     s2 = C(32, 64, 112, 112, 128, 3, 3, 2, 2, 1, 1)
     assert kernel_name(s2) == "layout_pass+tap_pair"
     assert kernel_name(s2, ccv_abi.CCV_PRECISION_3XTF32) == "tap_pair_layout_warps"
-    # Small input (12.8 MB): layout pass.
-    assert kernel_name(C(8, 256, 28, 28, 1024, 1, 1, 1, 1, 0, 0)) == "layout_pass+tap_pair"
     # The opt-in converter clusters take precedence when asked for.
     os.environ["CCV_CVT"] = "1"
     assert kernel_name(C(8, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == \
