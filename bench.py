@@ -400,7 +400,9 @@ def run_ours(args, wl):
         "roofline": {
             "bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": UNIT,
             "frac": achieved / tf32_peak,
-            "traffic": profiled_traffic("forward_conv", args.workload),
+            # The committed ncu summary covers the single-GPU launch of the
+            # workload (whole batch); a per-GPU shard runs a smaller launch.
+            "traffic": profiled_traffic("forward_conv", args.workload) if world == 1 else None,
             "kernel": (f"forward() path {kernel_path}: {launches} launch(es); roofline of the "
                        f"convolution launch ({t_dom * 1e3:.4f} ms of {t_fwd * 1e3:.4f} ms per "
                        "forward())"),
