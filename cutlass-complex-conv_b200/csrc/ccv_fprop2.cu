@@ -42,6 +42,7 @@ constexpr int kC2 = 32;                 // input channels per K step
 constexpr int kRow2 = kC2 * 4;          // 128-byte rows
 constexpr int kA2 = kBlockM * kRow2;    // one activation plane of one CTA: 16 KB
 constexpr int kTimeout = CCV_ERR_DEVICE_TIMEOUT;
+constexpr int kTapMinSplitGain = 25;    // stream-K policy threshold, % (plan_stream_k)
 
 template <int KT>
 struct Cfg2 {
@@ -411,7 +412,7 @@ int launch2_variant(FpropParams& prm, void* ws, size_t ws_bytes, cudaStream_t st
   const int clusters = cluster_cap(max_clusters[dev & 63]);
   int rc;
   const int launched = launch_clusters(prm, clusters, prm.ksteps * prm.passes, KT, ws, ws_bytes,
-                                       stream, &rc);
+                                       stream, &rc, kTapMinSplitGain);
   if (rc != CCV_OK) return rc;
   if (LW) {
     // The stream-K range runs first: the layout warps start at its first image.
@@ -516,7 +517,8 @@ int cluster_cap(int max_clusters) {
   return max_clusters;
 }
 
-int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes) {
+int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
+                  int min_gain_pct) {
   prm.slots_per_tile = slots;
   prm.sk_start = prm.num_tiles;
   prm.sk_slots = 0;
@@ -536,14 +538,17 @@ int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, s
   const int gs = static_cast<int>(std::min<long long>(clusters, X / kMinSkSlots));
   if (gs < 2) return 0;
   const long long per_range = (X + gs - 1) / gs;
-  // Default: split when the slot-count model saves at least 10% of the
-  // kernel (whole tiles: (q + 1) * L slot times on the busiest cluster;
-  // split: q * L + per_range).  Below that the partial sums' traffic and
-  // the unit switches eat the gain (measured on B200).
+  // Default: split when the slot-count model saves at least min_gain_pct %
+  // of the kernel (whole tiles: (q + 1) * L slot times on the busiest
+  // cluster; split: q * L + per_range).  The model leaves out the partial
+  // sums' traffic, the reduction and the unit switches, which cost B200
+  // measurements 10-30 us per launch: the halo kernel (3-tap slots) splits
+  // at >= 10 % (batch 8 and 16 of the 56x56 layer gain), the tap kernel
+  // (one-tap slots) at >= 25 % (stride 2, 11 % by the model, lost 14 %).
   const long long q = T / clusters;
   const long long dp_time = (q + 1) * slots;
   const long long sk_time = q * slots + per_range;
-  if (mode != 1 && (slots < 4 || (dp_time - sk_time) * 10 < dp_time)) return 0;
+  if (mode != 1 && (slots < 4 || (dp_time - sk_time) * 100 < dp_time * min_gain_pct)) return 0;
   const size_t pbytes = partial_bytes(gs, kt);
   if (ws_bytes < pbytes || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return 0;
   if (r * 8 > kSkCounterWords) return 0;
@@ -558,12 +563,12 @@ int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, s
 }
 
 int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
-                    cudaStream_t stream, int* rc) {
+                    cudaStream_t stream, int* rc, int min_gain_pct) {
   (void)stream;
   *rc = CCV_OK;
   clusters = std::max(1, clusters);
   // Stream-K counters come zeroed from the library's ring (no memset).
-  if (plan_stream_k(prm, clusters, slots, kt, ws, ws_bytes) > 0) return clusters;
+  if (plan_stream_k(prm, clusters, slots, kt, ws, ws_bytes, min_gain_pct) > 0) return clusters;
   return std::max(1, std::min(prm.num_tiles, clusters));
 }
 

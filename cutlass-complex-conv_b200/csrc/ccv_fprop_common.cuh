@@ -252,13 +252,14 @@ size_t pair_split_workspace_bytes(int kt, int tiles, int slots);
 // for `clusters` co-resident clusters and `slots` K slots per tile, using ws
 // (at least pair_split_workspace_bytes(kt)) when given and worthwhile.
 // Returns the number of counters to zero before the launch (0: no split).
-int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes);
+int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
+                  int min_gain_pct = 10);
 // Persistent-grid size after the CCV_MAX_CLUSTERS testing cap.
 int cluster_cap(int max_clusters);
 // Plans the stream-K split and returns the number of clusters to launch;
 // *rc receives the status.
 int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
-                    cudaStream_t stream, int* rc);
+                    cudaStream_t stream, int* rc, int min_gain_pct = 10);
 Tiling choose_halo_tiling(const Problem& pb);
 // Same for tiles of `px` output pixels per CTA (128 or 256).
 Tiling choose_halo_tiling_px(const Problem& pb, int px);
