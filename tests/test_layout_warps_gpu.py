@@ -197,3 +197,20 @@ def test_layout_warps_with_stream_k(knobs, name, case):
         assert oracle.rel_frobenius(y[img:img + 1], ref) <= TF32_TOL, img
     os.environ["CCV_LW"] = "0"
     assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
+
+
+@pytest.mark.parametrize("name,case", [CASES[0], TAP_CASES[3]], ids=[CASES[0][0], TAP_CASES[3][0]])
+def test_layout_warps_without_prefix(knobs, name, case):
+    # CCV_LW_PREFIX=0: only the two layout warps convert (no all-warp phase
+    # before the roles); same planes, same bits.
+    prec = ccv_abi.CCV_PRECISION_TF32
+    x, wr, wi = oracle.make_inputs(case, input_seed=65)
+    packed = abi_prepack(case, wr, wi)
+    y = fprop_complex_nan_ws(case, x, packed, prec)
+    os.environ["CCV_LW_PREFIX"] = "0"
+    try:
+        assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
+    finally:
+        os.environ.pop("CCV_LW_PREFIX", None)
+    os.environ["CCV_LW"] = "0"
+    assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
