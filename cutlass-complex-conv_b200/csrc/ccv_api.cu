@@ -392,6 +392,11 @@ int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_pac
     float* hi = reinterpret_cast<float*>(ws + pl);
     float* lr = reinterpret_cast<float*>(ws + 2 * pl);
     float* li = reinterpret_cast<float*>(ws + 3 * pl);
+    if (use_layout_warps_planar(pb, precision)) {
+      return launch_fprop_planar_lw(x_real, x_imag, hr, hi, lr, li,
+                                    static_cast<const float*>(w_packed), y_real, y_imag, pb, sk,
+                                    sk_bytes, st);
+    }
     rc = launch_split_planes(x_real, x_imag, hr, hi, lr, li,
                              static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c, st);
     if (rc != CCV_OK) return rc;
@@ -510,7 +515,7 @@ int ccv_fprop_kernel_launches(const ccv_conv_shape* shape, int precision, int co
     const char* name = complex_kernel_name(pb, precision);
     *kernels = strncmp(name, "layout_pass", 11) == 0 ? 2 : 1;
   } else {
-    *kernels = split ? 2 : 1;
+    *kernels = split && !use_layout_warps_planar(pb, precision) ? 2 : 1;
   }
   return CCV_OK;
 }

@@ -623,15 +623,22 @@ bool use_layout_warps(const Problem& pb, int precision) {
   //     pass (the layout warps convert ~1 TB/s; below that - stride 2 at
   //     C = 64 - they hold the MMAs back and a pass at the copy rate wins).
   // Measured on B200 over the BASELINE layers and the batch sweep.
-  const char* env = getenv("CCV_LW");
-  const int mode = env != nullptr ? atoi(env) : -1;
-  if (mode == 0) return false;
   if (use_complex_direct(pb, precision) || use_in_kernel_conversion(pb, precision)) return false;
   const Tiling t = choose_tiling(pb);
   Tiling th;
   const int fam = choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th);
-  if (fam != kPairHalo && fam != kPairTap) return false;
   if (fam == kPairHalo && use_converter_warps(pb, precision, th)) return false;
+  return layout_warps_pay(pb, precision);
+}
+
+bool layout_warps_pay(const Problem& pb, int precision) {
+  const char* env = getenv("CCV_LW");
+  const int mode = env != nullptr ? atoi(env) : -1;
+  if (mode == 0) return false;
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  const int fam = choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th);
+  if (fam != kPairHalo && fam != kPairTap) return false;
   if (pb.n > kSkCounterWords - kLwFlag0) return false;
   if (mode == 1) return true;
   const double in_bytes = 8.0 * pb.n * pb.h * pb.w * pb.c;
@@ -647,6 +654,29 @@ bool use_layout_warps(const Problem& pb, int precision) {
   const long long tiles =
       (static_cast<long long>(pb.n) * pb.p * pb.q + tile_px - 1) / tile_px * tiles_n;
   return tiles >= 2LL * (device_sm_count() / 2);
+}
+
+bool use_layout_warps_planar(const Problem& pb, int precision) {
+  return precision == CCV_PRECISION_3XTF32 && layout_warps_pay(pb, precision);
+}
+
+int launch_fprop_planar_lw(const float* x_real, const float* x_imag, float* hr, float* hi,
+                           float* lr, float* li, const float* w_packed, float* y_real,
+                           float* y_imag, const Problem& pb, void* ws, size_t ws_bytes,
+                           cudaStream_t stream) {
+  const Tiling t = choose_tiling(pb);
+  Tiling th;
+  switch (choose_family(pb, true, t, &th)) {
+    case kPairHalo:
+      return launch_fprop_pair_halo(hr, hi, lr, li, nullptr, true, w_packed, y_real, y_imag, pb,
+                                    th, OUT_PLANAR_NHWC, ws, ws_bytes, stream, nullptr, true,
+                                    x_real, x_imag);
+    case kPairTap:
+      return launch_fprop_pair(hr, hi, lr, li, w_packed, y_real, y_imag, pb, t, OUT_PLANAR_NHWC,
+                               ws, ws_bytes, stream, nullptr, x_real, x_imag);
+    default:
+      return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
+  }
 }
 
 int launch_fprop_complex_lw(const float* x, float* xr, float* xi, float* xr_lo, float* xi_lo,

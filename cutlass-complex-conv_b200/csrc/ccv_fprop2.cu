@@ -575,7 +575,8 @@ int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws,
 int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                       const float* w_packed, float* y0, float* y1, const Problem& pb,
                       const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
-                      cudaStream_t stream, const float* lw_src) {
+                      cudaStream_t stream, const float* lw_src, const float* lw_pr,
+                      const float* lw_pi) {
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;
@@ -635,20 +636,27 @@ int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, cons
   }
   const bool cplx = out_layout == OUT_COMPLEX_NCHW;
   if (!cplx && (rc = encode_planar_out_maps(prm, y0, y1, t.flat)) != CCV_OK) return rc;
-  if (lw_src != nullptr) {
-    // Layout warps write xr/xi (and the remainder planes) from lw_src.
-    if (!cplx || pb.n > kSkCounterWords - kLwFlag0) {
+  if (lw_src != nullptr || lw_pr != nullptr) {
+    // Layout warps write xr/xi (and the remainder planes) from lw_src
+    // (complex64 NCHW) or from the planes lw_pr/lw_pi (fp32 NHWC).
+    if ((lw_pr == nullptr && !cplx) || pb.n > kSkCounterWords - kLwFlag0) {
       return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
     }
     prm.xc = lw_src;
+    prm.lw_pr = lw_pr;
+    prm.lw_pi = lw_pi;
     prm.lw_xr = const_cast<float*>(xr);
     prm.lw_xi = const_cast<float*>(xi);
     prm.lw_xr_lo = const_cast<float*>(xr_lo);
     prm.lw_xi_lo = const_cast<float*>(xi_lo);
     prm.cvt_ctrs = stream_k_counters();
     if (prm.cvt_ctrs == nullptr) return CCV_ERR_CUDA;
-    return t.flat ? launch2_kt<true, true, true>(t.kt, prm, ws, ws_bytes, stream)
-                  : launch2_kt<false, true, true>(t.kt, prm, ws, ws_bytes, stream);
+    if (cplx) {
+      return t.flat ? launch2_kt<true, true, true>(t.kt, prm, ws, ws_bytes, stream)
+                    : launch2_kt<false, true, true>(t.kt, prm, ws, ws_bytes, stream);
+    }
+    return t.flat ? launch2_kt<true, false, true>(t.kt, prm, ws, ws_bytes, stream)
+                  : launch2_kt<false, false, true>(t.kt, prm, ws, ws_bytes, stream);
   }
   if (t.flat) {
     return cplx ? launch2_kt<true, true>(t.kt, prm, ws, ws_bytes, stream)

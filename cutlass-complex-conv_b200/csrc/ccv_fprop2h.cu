@@ -672,7 +672,8 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
                            const float* xi_lo, const float* xc, bool split,
                            const float* w_packed, float* y0, float* y1, const Problem& pb,
                            const Tiling& t_in, OutLayout out_layout, void* ws, size_t ws_bytes,
-                           cudaStream_t stream, const float* cvt_src, bool layout_warps) {
+                           cudaStream_t stream, const float* cvt_src, bool layout_warps,
+                           const float* lw_pr, const float* lw_pi) {
   // KT <= 64: two 128-pixel sub-boxes per CTA tile when the taller halo slot
   // fits (CCV_SUBBOX=0 turns it off; testing knob).  No stream-K split then.
   Tiling t = t_in;
@@ -726,13 +727,16 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
   // stages, then a third A slot.
   const bool cplx_out = out_layout == OUT_COMPLEX_NCHW;
   if (!cplx_out && (rc0 = encode_planar_out_maps(prm, y0, y1, false)) != CCV_OK) return rc0;
-  const bool lw = cvt_src != nullptr && layout_warps;
+  const bool lw = layout_warps && (cvt_src != nullptr || lw_pr != nullptr);
   if (lw) {
-    // Layout warps write xr/xi (and the remainder planes) from cvt_src.
-    if (fused || !cplx_out || pb.n > kSkCounterWords - kLwFlag0) {
+    // Layout warps write xr/xi (and the remainder planes) from cvt_src
+    // (complex64 NCHW) or from the planes lw_pr/lw_pi (fp32 NHWC).
+    if (fused || (lw_pr == nullptr && !cplx_out) || pb.n > kSkCounterWords - kLwFlag0) {
       return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
     }
     prm.xc = cvt_src;
+    prm.lw_pr = lw_pr;
+    prm.lw_pi = lw_pi;
     prm.lw_xr = const_cast<float*>(xr);
     prm.lw_xi = const_cast<float*>(xi);
     prm.lw_xr_lo = const_cast<float*>(xr_lo);
@@ -821,7 +825,7 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
       default: return launchh_variant<32, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
     }
   }
-  if (lw) {
+  if (lw && cplx) {
     if (nsub == 2) {
       return t.kt == 64 ? launchh_variant<64, true, false, 2, true>(prm, smem_bytes, ws, ws_bytes, stream)
                         : launchh_variant<32, true, false, 2, true>(prm, smem_bytes, ws, ws_bytes, stream);
@@ -830,6 +834,18 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
       case 128: return launchh_variant<128, true, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
       case 64: return launchh_variant<64, true, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
       default: return launchh_variant<32, true, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
+    }
+  }
+  if (lw) {
+    // Planar output: the 3xTF32 split of forward_planar()'s input planes.
+    if (nsub == 2) {
+      return t.kt == 64 ? launchh_variant<64, false, false, 2, true>(prm, smem_bytes, ws, ws_bytes, stream)
+                        : launchh_variant<32, false, false, 2, true>(prm, smem_bytes, ws, ws_bytes, stream);
+    }
+    switch (t.kt) {
+      case 128: return launchh_variant<128, false, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
+      case 64: return launchh_variant<64, false, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
+      default: return launchh_variant<32, false, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
     }
   }
   if (nsub == 2) {

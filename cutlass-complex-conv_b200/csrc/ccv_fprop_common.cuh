@@ -36,6 +36,10 @@ struct alignas(64) FpropParams {
   float* lw_xi;
   float* lw_xr_lo;
   float* lw_xi_lo;
+  // Planar source of the layout warps (3xTF32 forward_planar: fp32 NHWC
+  // planes split into hi/remainder planes); null: complex64 NCHW from xc.
+  const float* lw_pr;
+  const float* lw_pi;
   int lw_first_img;  // image the layout warps convert first
   long long lw_prefix;  // tickets every warp converts before its role (first wave's images)
   float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
@@ -234,7 +238,8 @@ int pair_tiles(const Tiling& t);
 int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                       const float* w_packed, float* y0, float* y1, const Problem& pb,
                       const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
-                      cudaStream_t stream, const float* lw_src = nullptr);
+                      cudaStream_t stream, const float* lw_src = nullptr,
+                      const float* lw_pr = nullptr, const float* lw_pi = nullptr);
 
 // Halo variant of the pair kernel (ccv_fprop2h.cu): stride-1 problems with a
 // filter wider than 1x1.  Each CTA tile is one box of box_p x box_q pixels
@@ -288,6 +293,7 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
                            const float* w_packed, float* y0, float* y1, const Problem& pb,
                            const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
                            cudaStream_t stream, const float* cvt_src = nullptr,
-                           bool layout_warps = false);
+                           bool layout_warps = false, const float* lw_pr = nullptr,
+                           const float* lw_pi = nullptr);
 
 }  // namespace ccv

@@ -76,6 +76,17 @@ bool use_layout_warps(const Problem& pb, int precision);
 int launch_fprop_complex_lw(const float* x, float* xr, float* xi, float* xr_lo, float* xi_lo,
                             const float* w_packed, float* y, const Problem& pb, int precision,
                             void* ws, size_t ws_bytes, cudaStream_t stream);
+// Whether the layout-warp variant pays for this problem (dispatch rule,
+// complex or planar source).
+bool layout_warps_pay(const Problem& pb, int precision);
+// 3xTF32 forward_planar() with the TF32 split of the input planes done by
+// layout warps inside the pair kernel (one launch; hr/hi/lr/li: workspace
+// planes it fills from x_real/x_imag).
+bool use_layout_warps_planar(const Problem& pb, int precision);
+int launch_fprop_planar_lw(const float* x_real, const float* x_imag, float* hr, float* hi,
+                           float* lr, float* li, const float* w_packed, float* y_real,
+                           float* y_imag, const Problem& pb, void* ws, size_t ws_bytes,
+                           cudaStream_t stream);
 // Name of the kernel path a complex (forward()) call takes.
 const char* complex_kernel_name(const Problem& pb, int precision);
 int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,

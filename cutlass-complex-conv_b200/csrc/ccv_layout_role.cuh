@@ -16,7 +16,9 @@
 // CTA being resident.
 //
 // 3xTF32: the warps write tf32(x) into the hi planes and x - tf32(x) into the
-// lo planes (the activation split of three-pass TF32).
+// lo planes (the activation split of three-pass TF32).  The same warps also
+// take fp32 NHWC planes as the source (lw_pr/lw_pi: forward_planar() at
+// 3xTF32, where only the split is needed).
 #pragma once
 
 #include <cstdint>
@@ -74,6 +76,22 @@ __device__ __forceinline__ void lw_load(const FpropParams& prm, const LwTicket& 
                                         int hw, int lane, bool vec, float4 (&v)[kLwPx / 2]) {
   const int c = t.c0 + lane;
   const bool ok = t.tk < total && c < prm.c;
+  if (prm.lw_pr != nullptr) {
+    // fp32 NHWC planes: for each pixel, lane = channel reads one 128-byte run
+    // per plane (already channel-contiguous: no transpose).
+    const long long o0 = (static_cast<long long>(t.img) * hw + t.px0) * prm.c + c;
+    const int np = min(kLwPx, hw - t.px0);
+    const long long cs = prm.c;
+#pragma unroll
+    for (int j = 0; j < kLwPx / 2; ++j) {
+      const bool a = ok && 2 * j < np;
+      const bool b = ok && 2 * j + 1 < np;
+      const long long o = o0 + 2 * j * cs;
+      v[j] = make_float4(a ? __ldg(prm.lw_pr + o) : 0.f, a ? __ldg(prm.lw_pi + o) : 0.f,
+                         b ? __ldg(prm.lw_pr + o + cs) : 0.f, b ? __ldg(prm.lw_pi + o + cs) : 0.f);
+    }
+    return;
+  }
   const float2* src = reinterpret_cast<const float2*>(prm.xc) +
                       (static_cast<long long>(t.img) * prm.c + c) * hw + t.px0;
   const int np = min(kLwPx, hw - t.px0);

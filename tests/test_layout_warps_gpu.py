@@ -214,3 +214,51 @@ def test_layout_warps_without_prefix(knobs, name, case):
         os.environ.pop("CCV_LW_PREFIX", None)
     os.environ["CCV_LW"] = "0"
     assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
+
+
+def fprop_planar_nan_ws(case, x, packed, precision):
+    """ccv_fprop_planar with a NaN-filled workspace; returns complex64 NCHW."""
+    lib = ccv_abi.load()
+    shp = ccv_abi.shape_of(case)
+    xr = x.real.permute(0, 2, 3, 1).contiguous().to(DEV)
+    xi = x.imag.permute(0, 2, 3, 1).contiguous().to(DEV)
+    yr = torch.full((case.n, case.p, case.q, case.k), float("nan"), device=DEV)
+    yi = torch.full((case.n, case.p, case.q, case.k), float("nan"), device=DEV)
+    ws_bytes = lib.ccv_fprop_planar_workspace_bytes(ctypes.byref(shp), precision)
+    ws = torch.full((max(ws_bytes, 16),), 0xFF, dtype=torch.uint8, device=DEV)
+    ccv_abi.check(lib.ccv_fprop_planar(_ptr(xr), _ptr(xi), _ptr(packed), _ptr(yr), _ptr(yi),
+                                       ctypes.byref(shp), precision, _ptr(ws), ws_bytes,
+                                       _stream()), "fprop_planar")
+    torch.cuda.synchronize()
+    return oracle.planar_nhwc_to_complex_nchw(yr, yi).cpu()
+
+
+def planar_launches(case, precision):
+    lib = ccv_abi.load()
+    shp = ccv_abi.shape_of(case)
+    k = ctypes.c_int(0)
+    ccv_abi.check(lib.ccv_fprop_kernel_launches(ctypes.byref(shp), precision, 0, ctypes.byref(k)),
+                  "launches")
+    return k.value
+
+
+PLANAR_3X_CASES = [CASES[0], CASES[1], CASES[2], TAP_CASES[0], TAP_CASES[3]]
+
+
+@pytest.mark.parametrize("name,case", PLANAR_3X_CASES, ids=[c[0] for c in PLANAR_3X_CASES])
+def test_layout_warps_planar_3xtf32(knobs, name, case):
+    # forward_planar() at 3xTF32: the layout warps split the caller's fp32
+    # planes into the hi/remainder workspace planes in the convolution
+    # launch (one launch); the same bits as the split pass + kernel.
+    prec = ccv_abi.CCV_PRECISION_3XTF32
+    assert planar_launches(case, prec) == 1
+    x, wr, wi = oracle.make_inputs(case, input_seed=66)
+    packed = abi_prepack(case, wr, wi, precision=prec)
+    y = fprop_planar_nan_ws(case, x, packed, prec)
+    assert not torch.isnan(y.real).any() and not torch.isnan(y.imag).any()
+    ref = oracle.oracle_fp64(case, x, wr, wi)
+    assert oracle.rel_frobenius(y, ref) <= 1e-5
+    assert torch.equal(y, fprop_planar_nan_ws(case, x, packed, prec))
+    os.environ["CCV_LW"] = "0"
+    assert planar_launches(case, prec) == 2
+    assert torch.equal(y, fprop_planar_nan_ws(case, x, packed, prec))
