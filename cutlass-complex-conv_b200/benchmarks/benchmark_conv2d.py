@@ -74,6 +74,11 @@ CASES = [
     BenchmarkCase("b32_1x1_256_1024_28", 32, 256, 28, 28, 1024, 1, 1, 1, 0),
     BenchmarkCase("b32_64_64_320", 32, 64, 320, 320, 64, 3, 3, 1, 1, 0.1),
 ]
+# Not in the default run: one GPU's share of the MRI config at 4 GPUs (a
+# profiling-sized case of the same kernel).
+EXTRA_CASES = [
+    BenchmarkCase("b8_64_64_320", 8, 64, 320, 320, 64, 3, 3, 1, 1, 0.1),
+]
 
 
 class FourConv(nn.Module):
@@ -185,7 +190,8 @@ def main():
     args = ap.parse_args()
     if not torch.cuda.is_available():
         raise RuntimeError("CUDA is required to run this benchmark")
-    cases = CASES if args.cases == "all" else [c for c in CASES if c.name in args.cases.split(",")]
+    cases = (CASES if args.cases == "all"
+             else [c for c in CASES + EXTRA_CASES if c.name in args.cases.split(",")])
     print("PyTorch :", torch.__version__, "| GPU:", torch.cuda.get_device_name(args.device),
           "| TF32 peak (measured bf16/2):", tf32_peak(), "TFLOP/s")
     for case in cases:
