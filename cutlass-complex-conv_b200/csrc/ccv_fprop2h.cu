@@ -45,6 +45,9 @@ constexpr int kRowH = kCH * 4;        // 128-byte rows
 constexpr int kMaxASlots = 4;
 constexpr int kMaxWStages = 8;
 constexpr int kBarBytes = 1024;       // barrier block at the start of the carve-out
+constexpr int kLwTmaBar = 100;        // TMA prefix: kCvtInBufs barriers, then 19 words
+static_assert(8 * (kLwTmaBar + kCvtInBufs) + 4 * (kCvtInBufs + kLwTmaMaxImages) <= kBarBytes,
+              "barrier block overflow");
 static_assert(8 * (32 + 4 * kStageBufs) <= kBarBytes, "barrier block overflow");
 constexpr int kSmemDataBudget = 232448 - kBarBytes - 1024;  // minus alignment slack
 constexpr int kTimeoutH = CCV_ERR_DEVICE_TIMEOUT;
@@ -126,6 +129,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
       ptx::mbar_init(tempty(b), 8);  // 4 epilogue warps x 2 CTAs
     }
     ptx::mbar_init(done_bar, 1);
+    if (LW) {
+      for (int i = 0; i < kCvtInBufs; ++i) ptx::mbar_init(bar_base + 8u * (kLwTmaBar + i), 1);
+    }
     for (int i = 0; i < 4 * kStageBufs; ++i) ptx::mbar_init(stage_bar0 + 8u * i, 1);
     ptx::fence_mbar_init();
   }
@@ -186,7 +192,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
   if constexpr (LW) {
     // Every warp converts the first wave's images first (nothing to do
     // before they are there), then takes up its role.
-    if (!skip && prm.lw_prefix > 0) layout_warp(prm, lane, true);
+    if (!skip && prm.lw_tma_images > 0) {
+      // The operand rings are idle until the producer starts: they hold the
+      // TMA prefix's boxes, handed back to TMA by the proxy fence and the
+      // barrier below.
+      if (!lw_tma_prefix(prm, data, bar_base + 8u * kLwTmaBar,
+                         reinterpret_cast<unsigned*>(bars + kLwTmaBar + kCvtInBufs))) {
+        flags[1] = 1;
+      }
+      ptx::fence_proxy_async_shared();
+      __syncthreads();
+    } else if (!skip && prm.lw_prefix > 0) {
+      layout_warp(prm, lane, true);
+    }
   }
 
   if (cvt_cta) {
@@ -519,6 +537,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
         for (int i = 0; i < prm.n; ++i) prm.cvt_ctrs[kCvtFlag0 + i] = 0u;
         prm.cvt_ctrs[kCvtTicket] = 0u;
         prm.cvt_ctrs[kLwPrefixTicket] = 0u;
+        prm.cvt_ctrs[kLwTmaTicket] = 0u;
         prm.cvt_ctrs[kCvtDone] = 0u;
         __threadfence();
       }
@@ -600,7 +619,7 @@ int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
       const int half = 2 * (prm.sk_start / prm.tiles_n);
       prm.lw_first_img = std::min(half, prm.total_boxes - 1) / (prm.tiles_bp * prm.tiles_bq);
     }
-    prm.lw_prefix = lw_prefix_tickets(prm, launched, 2LL * kBlockM * NSUB);
+    lw_plan_prefix(prm, launched, 2LL * kBlockM * NSUB);
   } else {
     launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc);
     if (rc != CCV_OK) return rc;
@@ -667,6 +686,35 @@ Tiling choose_halo_tiling_px(const Problem& pb, int px) {
   }
   return t;
 }
+
+namespace {
+// Tensor maps of the TMA conversion (converter clusters, TMA prefix of the
+// layout warps): complex64 NCHW input as 8-byte elements (W, C, H, N), boxes
+// of 16 pixels x 32 channels x 8 rows (128-byte rows, 128-byte swizzle), and
+// the fp32 NHWC planes (C, W, H, N), boxes of 32 channels x 16 pixels x 8 rows.
+int encode_conversion_maps(FpropParams& prm, const float* src, const float* xr, const float* xi,
+                           const Problem& pb) {
+  const uint64_t hw8 = static_cast<uint64_t>(pb.h) * pb.w * 8;
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(pb.w), static_cast<uint64_t>(pb.c),
+                              static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
+    const uint64_t strides[3] = {hw8, static_cast<uint64_t>(pb.w) * 8, hw8 * pb.c};
+    const uint32_t box[4] = {kCvtPx, kCvtCh, kCvtRows, 1};
+    const uint32_t es[4] = {1, 1, 1, 1};
+    const int rc = encode_tiled_ex(&prm.tm_cin, src, 4, dims, strides, box, es, kSwizzle128, true);
+    if (rc != CCV_OK) return rc;
+  }
+  const uint64_t cb4 = static_cast<uint64_t>(pb.c) * 4;
+  const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.w),
+                            static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
+  const uint64_t strides[3] = {cb4, cb4 * pb.w, cb4 * pb.w * pb.h};
+  const uint32_t box[4] = {kCvtCh, kCvtPx, kCvtRows, 1};
+  const uint32_t es[4] = {1, 1, 1, 1};
+  int rc = encode_tiled_ex(&prm.tm_pr, xr, 4, dims, strides, box, es, kSwizzleNone, false);
+  if (rc != CCV_OK) return rc;
+  return encode_tiled_ex(&prm.tm_pi, xi, 4, dims, strides, box, es, kSwizzleNone, false);
+}
+}  // namespace
 
 int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
                            const float* xi_lo, const float* xc, bool split,
@@ -769,28 +817,17 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
     ws = nullptr;
     ws_bytes = 0;
     smem_bytes = std::max(smem_bytes, 1024 + kBarBytes + static_cast<int>(kCvtSmemBytes));
-    const uint64_t hw8 = static_cast<uint64_t>(pb.h) * pb.w * 8;
-    {
-      const uint64_t dims[4] = {static_cast<uint64_t>(pb.w), static_cast<uint64_t>(pb.c),
-                                static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
-      const uint64_t strides[3] = {hw8, static_cast<uint64_t>(pb.w) * 8, hw8 * pb.c};
-      const uint32_t box[4] = {kCvtPx, kCvtCh, kCvtRows, 1};
-      const uint32_t es[4] = {1, 1, 1, 1};
-      int rc1 = encode_tiled_ex(&prm.tm_cin, cvt_src, 4, dims, strides, box, es, kSwizzle128, true);
-      if (rc1 != CCV_OK) return rc1;
-    }
-    {
-      const uint64_t cb4 = static_cast<uint64_t>(pb.c) * 4;
-      const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.w),
-                                static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
-      const uint64_t strides[3] = {cb4, cb4 * pb.w, cb4 * pb.w * pb.h};
-      const uint32_t box[4] = {kCvtCh, kCvtPx, kCvtRows, 1};
-      const uint32_t es[4] = {1, 1, 1, 1};
-      int rc1 = encode_tiled_ex(&prm.tm_pr, xr, 4, dims, strides, box, es, kSwizzleNone, false);
-      if (rc1 != CCV_OK) return rc1;
-      rc1 = encode_tiled_ex(&prm.tm_pi, xi, 4, dims, strides, box, es, kSwizzleNone, false);
-      if (rc1 != CCV_OK) return rc1;
-    }
+    const int rc1 = encode_conversion_maps(prm, cvt_src, xr, xi, pb);
+    if (rc1 != CCV_OK) return rc1;
+  }
+  if (lw && cvt_src != nullptr && lw_pr == nullptr && !split && (pb.w & 1) == 0 &&
+      (reinterpret_cast<uintptr_t>(cvt_src) & 15) == 0 &&
+      sa * prm.a_slot_bytes + sw * prm.w_stage_bytes >= static_cast<int>(kCvtSmemBytes)) {
+    // TMA prefix possible (sized at launch): TF32, even W (8-byte elements,
+    // 16-byte row strides), the operand rings can hold its boxes.
+    const int rc1 = encode_conversion_maps(prm, cvt_src, xr, xi, pb);
+    if (rc1 != CCV_OK) return rc1;
+    prm.lw_tma_images = -1;
   }
 
   int rc;

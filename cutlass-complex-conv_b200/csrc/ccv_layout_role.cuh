@@ -24,6 +24,7 @@
 #include <cstdint>
 #include <cstdlib>
 
+#include "ccv_cvt_role.cuh"
 #include "ccv_fprop_common.cuh"
 #include "ccv_ptx.cuh"
 
@@ -37,6 +38,8 @@ constexpr int kLwChunk = 4;                 // tickets per counter increment
 constexpr int kLwTicket = 0;               // chunks taken past the prefix
 constexpr int kLwDone = 1;
 constexpr int kLwPrefixTicket = 2;         // chunks taken of the prefix
+constexpr int kLwTmaTicket = 3;            // TMA prefix: tiles taken
+constexpr int kLwTmaMaxImages = 16;        // TMA prefix: images at most
 constexpr int kLwFlag0 = 8;                 // image i: tickets completed
 
 __device__ __forceinline__ int lw_tickets_per_image(const FpropParams& prm) {
@@ -230,24 +233,172 @@ __device__ __forceinline__ void layout_warp(const FpropParams& prm, int lane, bo
 // start without (a multiple of kLwChunk).  `tile_px`: output pixels per
 // cluster tile (one m-tile); CCV_LW_PREFIX=0 turns the phase off (timing
 // knob).
-inline long long lw_prefix_tickets(const FpropParams& prm, int launched, long long tile_px) {
+inline long long lw_prefix_images(const FpropParams& prm, int launched, long long tile_px) {
   const char* env = getenv("CCV_LW_PREFIX");
   if (env != nullptr && atoi(env) == 0) return 0;
   const long long pq = static_cast<long long>(prm.p) * prm.q;
   const long long mtiles = (launched + prm.tiles_n - 1) / prm.tiles_n;
   long long images = (mtiles * tile_px + pq - 1) / pq;
   if (prm.sk_slots > 0) images += prm.n - prm.lw_first_img;
-  images = images < prm.n ? images : prm.n;
+  return images < prm.n ? images : prm.n;
+}
+
+inline long long lw_prefix_tickets(const FpropParams& prm, int launched, long long tile_px) {
   const long long per_img = ((static_cast<long long>(prm.h) * prm.w + kLwPx - 1) / kLwPx) *
                             ((prm.c + kLwCh - 1) / kLwCh);
-  return (images * per_img + kLwChunk - 1) / kLwChunk * kLwChunk;
+  return (lw_prefix_images(prm, launched, tile_px) * per_img + kLwChunk - 1) / kLwChunk * kLwChunk;
+}
+
+// Sets the prefix of a layout-warp launch: the TMA prefix when the host
+// prepared it (lw_tma_images < 0: eligible) and the first wave's images
+// number 1..kLwTmaMaxImages, else the all-warp ticket prefix.
+inline void lw_plan_prefix(FpropParams& prm, int launched, long long tile_px) {
+  const long long images = lw_prefix_images(prm, launched, tile_px);
+  const char* env = getenv("CCV_LW_TMA");
+  const bool tma_on = env == nullptr || atoi(env) != 0;
+  if (prm.lw_tma_images < 0 && tma_on && images >= 1 && images <= kLwTmaMaxImages) {
+    const long long per_img = ((static_cast<long long>(prm.h) * prm.w + kLwPx - 1) / kLwPx) *
+                              ((prm.c + kLwCh - 1) / kLwCh);
+    prm.lw_tma_images = static_cast<int>(images);
+    prm.lw_prefix = images * per_img;
+    return;
+  }
+  prm.lw_tma_images = 0;
+  prm.lw_prefix = lw_prefix_tickets(prm, launched, tile_px);
+}
+
+// TMA prefix: before taking up their roles, every thread of the CTA converts
+// tiles of the first lw_tma_images images (conversion order) through the
+// idle operand rings: complex64 boxes of 8 rows x 16 pixels x 32 channels
+// loaded by TMA (kCvtInBufs in flight), transposed in shared memory, the
+// two fp32 planes stored by TMA.  Tiles are handed out by a counter, so any
+// running CTA can finish them; each CTA adds its tile count per image once
+// its stores have landed.  `buf`: kCvtSmemBytes at a 1024-byte boundary;
+// `full0`: kCvtInBufs mbarriers (count 1); `sm`: kCvtInBufs + kLwTmaMaxImages
+// words of shared memory.  Returns false if a wait ran out (status set).
+__device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* buf, uint32_t full0,
+                                              unsigned* sm) {
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int nwarps = blockDim.x >> 5;
+  const int th = (prm.h + kCvtRows - 1) / kCvtRows;
+  const int tw = (prm.w + kCvtPx - 1) / kCvtPx;
+  const int tc = (prm.c + kCvtCh - 1) / kCvtCh;
+  const int per_img = th * tw * tc;
+  const unsigned total = static_cast<unsigned>(per_img * prm.lw_tma_images);
+  unsigned* ctr = prm.cvt_ctrs + kLwTmaTicket;
+  volatile unsigned* tks = sm;                   // ticket of each input buffer
+  volatile unsigned* cnt = sm + kCvtInBufs;      // this CTA's tiles per image (order)
+  uint8_t* in = buf;
+  uint8_t* out = buf + kCvtInBufs * kCvtInBytes;
+  const uint32_t in_u = ptx::smem_u32(in);
+  const uint32_t out_u = ptx::smem_u32(out);
+  auto coords = [&](unsigned tk, int& order, int& img, int& c0, int& w0, int& h0) {
+    order = static_cast<int>(tk / per_img);
+    const int j = static_cast<int>(tk - static_cast<unsigned>(order) * per_img);
+    img = (order + prm.lw_first_img) % prm.n;
+    const int cb = j % tc;
+    const int rest = j / tc;
+    c0 = cb * kCvtCh;
+    w0 = (rest % tw) * kCvtPx;
+    h0 = (rest / tw) * kCvtRows;
+  };
+  auto grab_and_load = [&](int b) {  // thread 0
+    const unsigned tk = atomicAdd(ctr, 1u);
+    tks[b] = tk;
+    if (tk < total) {
+      int order, img, c0, w0, h0;
+      coords(tk, order, img, c0, w0, h0);
+      const uint32_t bar = full0 + 8u * static_cast<uint32_t>(b);
+      ptx::mbar_arrive_expect_tx(bar, kCvtInBytes);
+      ptx::tma_load_4d(in_u + static_cast<uint32_t>(b) * kCvtInBytes, &prm.tm_cin, bar, w0, c0, h0,
+                       img);
+    }
+  };
+  if (tid == 0) {
+    for (int i = 0; i < kLwTmaMaxImages; ++i) cnt[i] = 0u;
+    for (int b = 0; b < kCvtInBufs; ++b) grab_and_load(b);
+  }
+  __syncthreads();
+  bool ok = true;
+#pragma unroll 1
+  for (int k = 0;; ++k) {
+    const int b = k % kCvtInBufs;
+    const unsigned tk = tks[b];
+    if (tk >= total) break;  // tickets grow: the later buffers are past the end too
+    int order, img, c0, w0, h0;
+    coords(tk, order, img, c0, w0, h0);
+    const bool got = ptx::mbar_wait_bounded_backoff(full0 + 8u * static_cast<uint32_t>(b),
+                                                    static_cast<uint32_t>(k / kCvtInBufs) & 1u,
+                                                    prm.status, CCV_ERR_DEVICE_TIMEOUT);
+    const int ob = k & 1;
+    if (tid == 0 && k >= 2) ptx::bulk_wait_read_le1();  // the store of k-2 has read its buffer
+    if (__syncthreads_or(!got)) {
+      ok = false;
+      break;
+    }
+    // Transpose: lane = channel, (row, pixel pair) spread over the warps.
+    const uint8_t* src = in + static_cast<uint32_t>(b) * kCvtInBytes;
+    float* orr = reinterpret_cast<float*>(out + static_cast<uint32_t>(ob) * 2u * kCvtOutPlane);
+    float* oii = orr + kCvtOutPlane / 4;
+    for (int idx = warp; idx < kCvtRows * (kCvtPx / 2); idx += nwarps) {
+      const int r = idx / (kCvtPx / 2);
+      const int q = idx % (kCvtPx / 2);
+      const int line = r * kCvtCh + lane;
+      // 128-byte swizzle: 16-byte chunk q of line `line` is at chunk q ^ (line & 7).
+      const float4 v = *reinterpret_cast<const float4*>(
+          src + static_cast<uint32_t>(line) * 128u + (static_cast<uint32_t>(q ^ (line & 7)) << 4));
+      const int p0 = (r * kCvtPx + 2 * q) * kCvtCh + lane;
+      orr[p0] = v.x;
+      oii[p0] = v.y;
+      orr[p0 + kCvtCh] = v.z;
+      oii[p0 + kCvtCh] = v.w;
+    }
+    ptx::fence_proxy_async_shared();
+    __syncthreads();
+    if (tid == 0) {
+      const uint32_t o = out_u + static_cast<uint32_t>(ob) * 2u * kCvtOutPlane;
+      ptx::tma_store_4d(&prm.tm_pr, o, c0, w0, h0, img);
+      ptx::tma_store_4d(&prm.tm_pi, o + kCvtOutPlane, c0, w0, h0, img);
+      ptx::bulk_commit_group();
+      cnt[order] = cnt[order] + 1u;
+      grab_and_load(b);  // buffer b was read by the transpose above
+    }
+  }
+  if (tid == 0) {
+    // Every store has landed: publish this CTA's tiles per image.
+    ptx::bulk_wait_all();
+    ptx::fence_proxy_async_all();
+    __threadfence();
+    for (int o = 0; o < prm.lw_tma_images; ++o) {
+      const unsigned c = cnt[o];
+      if (c != 0u) {
+        const int img = (o + prm.lw_first_img) % prm.n;
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(prm.cvt_ctrs + kLwFlag0 + img),
+                     "r"(c)
+                     : "memory");
+      }
+    }
+  }
+  __syncthreads();
+  return ok;
 }
 
 // Waits (bounded) until image `img`'s planes are written; then orders the
 // caller's later TMA (async-proxy) reads after those generic-proxy stores.
+__device__ __forceinline__ int lw_tma_tiles_per_image(const FpropParams& prm) {
+  return ((prm.h + kCvtRows - 1) / kCvtRows) * ((prm.w + kCvtPx - 1) / kCvtPx) *
+         ((prm.c + kCvtCh - 1) / kCvtCh);
+}
+
 __device__ __forceinline__ bool lw_wait_image(const FpropParams& prm, int img) {
   const unsigned* f = prm.cvt_ctrs + kLwFlag0 + img;
-  const unsigned need = static_cast<unsigned>(lw_tickets_per_image(prm));
+  // Images the TMA prefix converted count tiles, the others tickets.
+  const int order = (img - prm.lw_first_img + prm.n) % prm.n;
+  const unsigned need = static_cast<unsigned>(order < prm.lw_tma_images
+                                                  ? lw_tma_tiles_per_image(prm)
+                                                  : lw_tickets_per_image(prm));
   const uint64_t t0 = ptx::globaltimer();
   uint32_t ns = 64;
   while (true) {

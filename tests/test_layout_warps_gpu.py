@@ -212,6 +212,12 @@ def test_layout_warps_without_prefix(knobs, name, case):
         assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
     finally:
         os.environ.pop("CCV_LW_PREFIX", None)
+    # The warp-run prefix instead of the TMA one (even W, TF32): same bits.
+    os.environ["CCV_LW_TMA"] = "0"
+    try:
+        assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
+    finally:
+        os.environ.pop("CCV_LW_TMA", None)
     os.environ["CCV_LW"] = "0"
     assert torch.equal(y, fprop_complex_nan_ws(case, x, packed, prec))
 
