@@ -253,9 +253,24 @@ inline long long lw_prefix_tickets(const FpropParams& prm, int launched, long lo
 // prepared it (lw_tma_images < 0: eligible) and the first wave's images
 // number 1..kLwTmaMaxImages, else the all-warp ticket prefix.
 inline void lw_plan_prefix(FpropParams& prm, int launched, long long tile_px) {
-  const long long images = lw_prefix_images(prm, launched, tile_px);
+  long long images = lw_prefix_images(prm, launched, tile_px);
   const char* env = getenv("CCV_LW_TMA");
   const bool tma_on = env == nullptr || atoi(env) != 0;
+  if (prm.lw_tma_images < 0 && tma_on && images >= 1) {
+    // The TMA prefix converts at ~3 TB/s with every warp, the layout warps
+    // at ~0.85 TB/s of input beside the MMAs (B200): take so many images
+    // into the prefix that the rest converts within the convolution's time
+    // (~600 TFLOP/s), when that is more than the first wave's.
+    const double img_bytes = 8.0 * prm.h * prm.w * prm.c;
+    const double t_conv = 8.0 * prm.n * prm.p * prm.q * static_cast<double>(prm.k) * prm.c *
+                          prm.r * prm.s / 600e12;
+    const long long fit = static_cast<long long>(t_conv * 0.85e12 / img_bytes);
+    const long long balance = prm.n - fit;
+    if (balance > images) images = balance;
+    const char* force = getenv("CCV_LW_TMA_IMAGES");
+    if (force != nullptr && atoi(force) > 0) images = atoi(force);
+    images = images < prm.n ? images : prm.n;
+  }
   if (prm.lw_tma_images < 0 && tma_on && images >= 1 && images <= kLwTmaMaxImages) {
     const long long per_img = ((static_cast<long long>(prm.h) * prm.w + kLwPx - 1) / kLwPx) *
                               ((prm.c + kLwCh - 1) / kLwCh);
