@@ -39,7 +39,7 @@ constexpr int kCvtPx = 16;
 constexpr int kCvtCh = 32;
 constexpr uint32_t kCvtInBytes = kCvtRows * kCvtCh * kCvtPx * 8u;
 constexpr uint32_t kCvtOutPlane = kCvtRows * kCvtPx * kCvtCh * 4u;
-constexpr int kCvtInBufs = 3;
+constexpr int kCvtInBufs = 4;
 // Shared memory the converter role needs (input ring + two output buffers).
 constexpr uint32_t kCvtSmemBytes = kCvtInBufs * kCvtInBytes + 2u * 2u * kCvtOutPlane;
 

@@ -43,6 +43,7 @@ struct alignas(64) FpropParams {
   int lw_first_img;  // image the layout warps convert first
   long long lw_prefix;  // tickets every warp converts before its role (first wave's images)
   int lw_tma_images;    // images the TMA prefix converts instead (0: warp prefix)
+  int lw_tma_bufs;      // TMA prefix: boxes in flight
   float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
   float* y1;          // planar: y_imag (NPQK); complex: unused
   int* status;        // device status word

@@ -274,6 +274,10 @@ inline void lw_plan_prefix(FpropParams& prm, int launched, long long tile_px) {
   if (prm.lw_tma_images < 0 && tma_on && images >= 1 && images <= kLwTmaMaxImages) {
     const long long per_img = ((static_cast<long long>(prm.h) * prm.w + kLwPx - 1) / kLwPx) *
                               ((prm.c + kLwCh - 1) / kLwCh);
+    const char* bufs = getenv("CCV_LW_TMA_BUFS");  // boxes in flight (timing knob)
+    prm.lw_tma_bufs = bufs != nullptr && atoi(bufs) >= 2 && atoi(bufs) <= kCvtInBufs
+                          ? atoi(bufs)
+                          : kCvtInBufs;
     prm.lw_tma_images = static_cast<int>(images);
     prm.lw_prefix = images * per_img;
     return;
@@ -302,11 +306,12 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
   const int tc = (prm.c + kCvtCh - 1) / kCvtCh;
   const int per_img = th * tw * tc;
   const unsigned total = static_cast<unsigned>(per_img * prm.lw_tma_images);
+  const int nbuf = prm.lw_tma_bufs;  // boxes in flight (<= kCvtInBufs)
   unsigned* ctr = prm.cvt_ctrs + kLwTmaTicket;
   volatile unsigned* tks = sm;                   // ticket of each input buffer
   volatile unsigned* cnt = sm + kCvtInBufs;      // this CTA's tiles per image (order)
   uint8_t* in = buf;
-  uint8_t* out = buf + kCvtInBufs * kCvtInBytes;
+  uint8_t* out = buf + nbuf * kCvtInBytes;
   const uint32_t in_u = ptx::smem_u32(in);
   const uint32_t out_u = ptx::smem_u32(out);
   auto coords = [&](unsigned tk, int& order, int& img, int& c0, int& w0, int& h0) {
@@ -333,19 +338,19 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
   };
   if (tid == 0) {
     for (int i = 0; i < kLwTmaMaxImages; ++i) cnt[i] = 0u;
-    for (int b = 0; b < kCvtInBufs; ++b) grab_and_load(b);
+    for (int b = 0; b < nbuf; ++b) grab_and_load(b);
   }
   __syncthreads();
   bool ok = true;
 #pragma unroll 1
   for (int k = 0;; ++k) {
-    const int b = k % kCvtInBufs;
+    const int b = k % nbuf;
     const unsigned tk = tks[b];
     if (tk >= total) break;  // tickets grow: the later buffers are past the end too
     int order, img, c0, w0, h0;
     coords(tk, order, img, c0, w0, h0);
     const bool got = ptx::mbar_wait_bounded_backoff(full0 + 8u * static_cast<uint32_t>(b),
-                                                    static_cast<uint32_t>(k / kCvtInBufs) & 1u,
+                                                    static_cast<uint32_t>(k / nbuf) & 1u,
                                                     prm.status, CCV_ERR_DEVICE_TIMEOUT);
     const int ob = k & 1;
     if (tid == 0 && k >= 2) ptx::bulk_wait_read_le1();  // the store of k-2 has read its buffer
