@@ -324,8 +324,7 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
     w0 = (rest % tw) * kCvtPx;
     h0 = (rest / tw) * kCvtRows;
   };
-  auto grab_and_load = [&](int b) {  // thread 0
-    const unsigned tk = atomicAdd(ctr, 1u);
+  auto load = [&](int b, unsigned tk) {  // thread 0
     tks[b] = tk;
     if (tk < total) {
       int order, img, c0, w0, h0;
@@ -338,7 +337,7 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
   };
   if (tid == 0) {
     for (int i = 0; i < kLwTmaMaxImages; ++i) cnt[i] = 0u;
-    for (int b = 0; b < nbuf; ++b) grab_and_load(b);
+    for (int b = 0; b < nbuf; ++b) load(b, atomicAdd(ctr, 1u));
   }
   __syncthreads();
   bool ok = true;
@@ -349,6 +348,10 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
     if (tk >= total) break;  // tickets grow: the later buffers are past the end too
     int order, img, c0, w0, h0;
     coords(tk, order, img, c0, w0, h0);
+    // The ticket for this buffer's next box: taken now, used after the
+    // transpose, so the atomic's round trip overlaps the wait and the copy.
+    unsigned nxt = 0;
+    if (tid == 0) nxt = atomicAdd(ctr, 1u);
     const bool got = ptx::mbar_wait_bounded_backoff(full0 + 8u * static_cast<uint32_t>(b),
                                                     static_cast<uint32_t>(k / nbuf) & 1u,
                                                     prm.status, CCV_ERR_DEVICE_TIMEOUT);
@@ -383,7 +386,7 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
       ptx::tma_store_4d(&prm.tm_pi, o + kCvtOutPlane, c0, w0, h0, img);
       ptx::bulk_commit_group();
       cnt[order] = cnt[order] + 1u;
-      grab_and_load(b);  // buffer b was read by the transpose above
+      load(b, nxt);  // buffer b was read by the transpose above
     }
   }
   if (tid == 0) {
