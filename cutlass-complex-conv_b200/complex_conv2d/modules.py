@@ -277,3 +277,97 @@ class ComplexConv2d(nn.Module):
             self.padding[1],
             _PRECISIONS[self.precision],
         )
+
+    def _copy_streams(self, device):
+        """Host->device and device->host copy streams of ``device`` (made once)."""
+        streams = self.__dict__.setdefault("_host_copy_streams", {})
+        if device not in streams:
+            streams[device] = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+        return streams[device]
+
+    def output_shape(self, n, h, w):
+        """``(N, K, P, Q)`` of ``forward`` for an ``(N, C, H, W)`` input."""
+        p = (h + 2 * self.padding[0] - self.kernel_size[0]) // self.stride[0] + 1
+        q = (w + 2 * self.padding[1] - self.kernel_size[1]) // self.stride[1] + 1
+        if p <= 0 or q <= 0:
+            raise ValueError(f"input {h}x{w} is smaller than the kernel")
+        return (n, self.out_channels, p, q)
+
+    def forward_host(self, x, out=None, images_per_chunk=None):
+        """``forward`` for a complex64 NCHW batch in pinned host memory.
+
+        The batch is cut into chunks of whole images.  Chunk i's host->device
+        copy, its convolution (``forward`` on the chunk, on the current
+        stream) and its device->host copy run on three streams, so copies in
+        the two PCIe directions overlap each other and the kernels; a
+        serial copy-in, forward, copy-out pays both directions one after the
+        other.  Each chunk's output is identical to ``forward`` of that chunk.
+
+        Args:
+            x: pinned (``pin_memory()``) CPU complex64 tensor, NCHW, contiguous.
+            out: optional pinned CPU complex64 tensor of ``output_shape``;
+                allocated (pinned) when None.
+            images_per_chunk: images per chunk; None picks ~16 MB of input.
+
+        Returns:
+            ``out``.  Like ``Tensor.copy_(..., non_blocking=True)``, the call
+            returns before the copies end: ``out`` holds the result once the
+            current CUDA stream has reached this point (e.g. after
+            ``torch.cuda.current_stream().synchronize()``).
+        """
+        if x.is_cuda:
+            raise ValueError("forward_host takes a host tensor; use forward for CUDA input")
+        if x.dtype != torch.complex64:
+            raise ValueError(f"ComplexConv2d expects torch.complex64 input, got {x.dtype}")
+        if x.dim() != 4:
+            raise ValueError(f"ComplexConv2d expects a 4D NCHW tensor, got {x.dim()}D")
+        if x.size(1) != self.in_channels:
+            raise ValueError(f"expected {self.in_channels} input channels, got {x.size(1)}")
+        # An empty tensor has no storage to pin.
+        if not x.is_contiguous() or (x.numel() > 0 and not x.is_pinned()):
+            raise ValueError("forward_host input must be contiguous pinned host memory")
+        dev = self.weight_real.device
+        if not self.weight_real.is_cuda:
+            raise RuntimeError("ComplexConv2d weights must be on CUDA")
+        n, _, h, w = x.shape
+        shape = self.output_shape(n, h, w)
+        if out is None:
+            out = torch.empty(shape, dtype=torch.complex64, pin_memory=True)
+        elif (out.is_cuda or out.dtype != torch.complex64 or tuple(out.shape) != shape
+              or not out.is_contiguous() or (out.numel() > 0 and not out.is_pinned())):
+            raise ValueError(
+                f"out must be a contiguous pinned host complex64 tensor of shape {shape}")
+        if n == 0:
+            return out
+        if images_per_chunk is None:
+            images_per_chunk = max(1, (16 << 20) // max(1, x[0].numel() * 8))
+        if images_per_chunk < 1:
+            raise ValueError("images_per_chunk must be >= 1")
+
+        cur = torch.cuda.current_stream(dev)
+        h2d, d2h = self._copy_streams(dev)
+        xd = torch.empty(x.shape, dtype=x.dtype, device=dev)
+        # The side streams may touch xd (allocated on cur) only after cur's
+        # earlier work on that memory; cur waits for them again at the end.
+        h2d.wait_stream(cur)
+        d2h.wait_stream(cur)
+        for i0 in range(0, n, images_per_chunk):
+            i1 = min(n, i0 + images_per_chunk)
+            with torch.cuda.stream(h2d):
+                xd[i0:i1].copy_(x[i0:i1], non_blocking=True)
+            copied = torch.cuda.Event()
+            copied.record(h2d)
+            cur.wait_event(copied)
+            y = self.forward(xd[i0:i1])
+            done = torch.cuda.Event()
+            done.record(cur)
+            d2h.wait_event(done)
+            with torch.cuda.stream(d2h):
+                out[i0:i1].copy_(y, non_blocking=True)
+            # y's memory returns to the allocator at the next iteration; keep
+            # it from being reused before d2h has read it.
+            y.record_stream(d2h)
+        xd.record_stream(h2d)
+        cur.wait_stream(h2d)
+        cur.wait_stream(d2h)
+        return out

@@ -71,6 +71,20 @@ def test_forward_validation_before_any_cuda_use():
         m(torch.zeros(1, 4, 5, 5, dtype=torch.complex64))
 
 
+def test_forward_host_validation_and_output_shape():
+    m = ComplexConv2d(4, 8, 3, stride=2, padding=1)
+    assert m.output_shape(3, 9, 10) == (3, 8, 5, 5)
+    with pytest.raises(ValueError, match="smaller than the kernel"):
+        ComplexConv2d(4, 8, 5).output_shape(1, 3, 3)
+    with pytest.raises(ValueError, match="complex64"):
+        m.forward_host(torch.zeros(1, 4, 5, 5))
+    with pytest.raises(ValueError, match="input channels"):
+        m.forward_host(torch.zeros(1, 3, 5, 5, dtype=torch.complex64))
+    # Pageable (not pinned) host memory is refused before any CUDA use.
+    with pytest.raises(ValueError, match="pinned"):
+        m.forward_host(torch.zeros(1, 4, 5, 5, dtype=torch.complex64))
+
+
 def test_prepack_requires_cuda_weights():
     m = ComplexConv2d(4, 4, 3)
     with pytest.raises(RuntimeError, match="weights must be on CUDA"):
