@@ -67,14 +67,23 @@ def test_3xtf32_chunks():
 
 
 def test_default_chunking_several_chunks():
-    # 2 MiB per image -> 8 images per default chunk -> chunks of 8 and 4.
+    # 2 MiB per image: 16 MB gives 8 images, at least 3 chunks gives 4 -> chunks of 4.
     layer = _layer(64, 64, 3, 1, 1, seed=3)
     x = _host_batch((12, 64, 64, 64), seed=4)
     out = torch.empty(layer.output_shape(12, 64, 64), dtype=torch.complex64, pin_memory=True)
     y = layer.forward_host(x, out=out)
     assert y is out
     torch.cuda.current_stream().synchronize()
-    assert torch.equal(out, _chunk_reference(layer, x, 8))
+    assert torch.equal(out, _chunk_reference(layer, x, 4))
+
+
+def test_default_chunking_small_batch():
+    # 3.2 MB per image, batch 8: 16 MB gives 5 images, at least 3 chunks gives 3.
+    layer = _layer(128, 128, 3, 1, 1, seed=13)
+    x = _host_batch((8, 128, 56, 56), seed=14)
+    y = layer.forward_host(x)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(y, _chunk_reference(layer, x, 3))
 
 
 def test_back_to_back_calls_reuse_out():
