@@ -16,8 +16,13 @@ copied in from pinned host memory and its output copied back, chunks of images
 pipelined over the two copy directions); ``e2e.serial_ms_per_step`` is the
 plain copy-in, ``forward``, copy-out sequence for comparison.
 
+Besides the headline, the line's ``per_config`` map measures every BASELINE
+config through ``forward()`` and ``forward_planar()`` (batched layers sharded
+like the headline, batch-1 layers whole on every GPU, warm and cold-L2), with
+a CPU baseline per config at one GPU; configs[0] is CPU only.
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload NAME] [--precision tf32|3xtf32]
+                    [--workload NAME] [--precision tf32|3xtf32] [--no-per-config]
 
 ``--impl reference`` times the reference's four-real-Conv2d path
 (benchmarks/baseline.py:5-45) on the host CPU, restated in oracle/, on a
@@ -97,7 +102,7 @@ def profiled_traffic(kernel, workload):
 class ClockSampler:
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+              "clocks_event_reasons.sw_power_cap,utilization.gpu")
 
     def __init__(self, device_index):
         self.idx = device_index
@@ -126,7 +131,7 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.out.close()
-        sm, smax, reasons = [], [], set()
+        sm, smax, busy, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         with open(self.path) as f:
             for line in f:
@@ -138,13 +143,22 @@ class ClockSampler:
                     smax.append(float(parts[2]))
                 except ValueError:
                     continue
+                try:
+                    util = float(parts[8]) if len(parts) > 8 else 100.0
+                except ValueError:
+                    util = 100.0
+                if util >= 50.0:
+                    busy.append(sm[-1])
                 for nm, v in zip(names, parts[4:8]):
                     if v.lower().startswith("active"):
                         reasons.add(nm)
         os.unlink(self.path)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
+        under_load = busy if busy else sm
+        return {"sm_mhz": statistics.median(under_load) if under_load else None,
                 "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm),
+                "samples_under_load": len(busy),
+                "note": "median over samples with GPU utilization >= 50 % (all samples if none)"}
 
 
 # ------------------------------------------------------------------ distributed
@@ -186,20 +200,28 @@ def barrier(world):
 
 
 # ------------------------------------------------------------------ CPU baseline
+def use_all_host_threads():
+    """torchrun starts each rank with one intra-op thread; the CPU baseline
+    and the reference arm run on all of the host's cores."""
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return n
+
+
 def cpu_baseline(wl, budget_s=12.0):
     """The reference's four-conv path (restated in oracle/) on host cores, fp32,
     on a bounded sample: single images of the workload's layer."""
     import oracle
+    use_all_host_threads()
     n, c, h, w, k, r, s, st, pd, std = wl
     case = oracle.ConvCase(1, c, h, w, k, r, s, st, st, pd, pd)
-    threads = torch.get_num_threads()
     t1, _ = oracle.time_cpu_four_conv(case, iters=1, warmup=1)
     iters = max(1, min(200, int(budget_s / max(t1, 1e-4))))
     dt, threads = oracle.time_cpu_four_conv(case, iters=iters, warmup=0)
     tflops = case.flops / dt / 1e12
     return {"value": tflops, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{iters} single-image calls (batch 1 of the workload layer), fp32, "
-                      f"{dt * 1e3:.2f} ms/call, os.cpu_count()={os.cpu_count()}"}, dt
+                      f"{dt * 1e3:.3f} ms/call, os.cpu_count()={os.cpu_count()}"}, dt
 
 
 def run_reference(args, wl):
@@ -207,6 +229,7 @@ def run_reference(args, wl):
     if rank != 0:
         return 0
     import oracle
+    threads = use_all_host_threads()
     n, c, h, w, k, r, s, st, pd, std = wl
     case = oracle.ConvCase(1, c, h, w, k, r, s, st, st, pd, pd)
     x, wr, wi = oracle.make_inputs(case, input_std=std)
@@ -223,16 +246,214 @@ def run_reference(args, wl):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "sample": "batch 1 of the workload layer per step",
+        "config": {"workload": args.workload,
+                   "sample": "one image of the workload layer per step: the CPU path's rate "
+                             "(TFLOP/s) on the same layer, not the whole batch",
+                   "same_config": False,
                    "global_batch": n, "c": c, "h": h, "w": w, "k": k, "r": r, "s": s,
                    "stride": st, "pad": pd},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": torch.get_num_threads(),
-                         "kind": "port",
-                         "sample": f"{args.steps} single-image four-conv calls, fp32 CPU torch"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} single-image four-conv calls, fp32 CPU torch "
+                                   f"on {threads} threads (rank 0 only)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ------------------------------------------------------------------ timing
+def timed_blocks(step, steps, world, dev, min_total_s=0.02, max_blocks=64):
+    """Times blocks of exactly `steps` calls of step(), each bracketed by a
+    barrier and a device synchronize on both sides, with CUDA events on the
+    current stream.  A block's time is the max over ranks.  Blocks repeat
+    until together they cover min_total_s (so short per-rank steps at 8 GPUs
+    are not dominated by launch and barrier overhead); the decision uses the
+    max-over-ranks times, so every rank runs the same blocks.  Returns
+    (median seconds per step over the blocks, number of blocks)."""
+    stream = torch.cuda.current_stream()
+    per_step = []
+    total = 0.0
+    while True:
+        barrier(world)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        t = max_over_ranks(e0.elapsed_time(e1) / 1e3, world, dev)
+        per_step.append(t / steps)
+        total += t
+        if total >= min_total_s or len(per_step) >= max_blocks:
+            break
+    return statistics.median(per_step), len(per_step)
+
+
+# ------------------------------------------------------------------ per-config
+# BASELINE configs measured in every run besides the headline workload:
+# (entry, workload, precision).  configs[0] is CPU only.
+PER_CONFIG = [
+    ("b1_32_64_56", "b1_32_64_56", "tf32"),
+    ("b1_64_128_28", "b1_64_128_28", "tf32"),
+    ("b1_128_256_14", "b1_128_256_14", "tf32"),
+    ("b1_256_512_7", "b1_256_512_7", "tf32"),
+    ("b64_128_128_56", "b64_128_128_56", "tf32"),
+    ("b32_s2_64_128_112", "b32_s2_64_128_112", "tf32"),
+    ("b32_1x1_256_1024_28", "b32_1x1_256_1024_28", "tf32"),
+    ("b32_64_64_320", "b32_64_64_320", "tf32"),
+    ("b32_64_64_320_3xtf32", "b32_64_64_320", "3xtf32"),
+]
+CPU_CONFIG = (1, 32, 32, 32, 32, 3, 3, 1, 1, 1.0)  # configs[0]
+L2_BYTES = 126 * 2**20
+
+
+def make_layer(wl, precision, dev, seed=1):
+    from complex_conv2d import ComplexConv2d
+    n, c, h, w, k, r, s, st, pd, std = wl
+    g = torch.Generator().manual_seed(seed)
+    bound = 1.0 / (c * r * s) ** 0.5
+    wr = (torch.rand((k, c, r, s), generator=g) * 2 - 1) * bound
+    wi = (torch.rand((k, c, r, s), generator=g) * 2 - 1) * bound
+    layer = ComplexConv2d(c, k, (r, s), stride=st, padding=pd, device=dev, precision=precision)
+    with torch.no_grad():
+        layer.weight_real.copy_(wr)
+        layer.weight_imag.copy_(wi)
+        layer._ensure_prepacked()
+    return layer
+
+
+def make_inputs_dev(nb, wl, dev, seed, count=1):
+    n, c, h, w, k, r, s, st, pd, std = wl
+    gx = torch.Generator(device=dev).manual_seed(seed)
+    xs = []
+    for _ in range(count):
+        xr = torch.randn((nb, c, h, w), generator=gx, device=dev) * std
+        xi = torch.randn((nb, c, h, w), generator=gx, device=dev) * std
+        xs.append(torch.complex(xr, xi))
+    return xs
+
+
+def roofline_entry(flops, alg_bytes, t, precision, peaks):
+    tf32_peak = peaks["bf16_tflops"] / 2.0 / (3.0 if precision == "3xtf32" else 1.0)
+    tflops = flops / t / 1e12
+    gbs = alg_bytes / t / 1e9
+    return {"ms": t * 1e3, "tflops": tflops, "frac": tflops / tf32_peak,
+            "gbs": gbs, "hbm_frac": gbs / peaks["hbm_gbs"]}
+
+
+def measure_config(wname, precision, world, rank, dev, args, peaks):
+    """One BASELINE config: forward() and forward_planar() through the public
+    module.  Batched layers are batch-sharded over the ranks (weights
+    replicated); every step reads an input no earlier step left in L2 (the
+    steps rotate over buffers totalling > 2x L2).  Batch-1 layers run whole
+    on every rank (replicas); they are timed warm (one layer back to back,
+    the reference harness's method, benchmarks/benchmark_conv2d.py:36-53) and
+    cold (steps rotate over distinct layers and inputs totalling > 2x L2, so
+    weights and activations come from HBM)."""
+    from complex_conv2d import _C
+    from complex_conv2d.distributed import batch_shard
+    wl = WORKLOADS[wname]
+    n, c, h, w, k, r, s, st, pd, std = wl
+    p, q = out_hw(h, w, r, s, st, pd)
+    batch1 = n == 1
+    nb = 1 if batch1 else batch_shard(n, world, rank)[1]
+    prec_code = 1 if precision == "3xtf32" else 0
+    flops_rank = workload_flops(nb, c, h, w, k, r, s, st, pd)
+    w_bytes = 8 * k * r * s * c
+    in_bytes = 8 * nb * c * h * w
+    out_bytes = 8 * nb * k * p * q
+    alg_rank = in_bytes + w_bytes + out_bytes
+    res = {"precision": precision, "per_gpu_batch": nb,
+           "sharding": "replicas (whole layer on every GPU)" if batch1 else f"batch / {world}",
+           "forward_launches": _C.complex_forward_launches(nb, c, h, w, k, r, s, st, st, pd, pd,
+                                                           prec_code),
+           "forward_path": _C.complex_forward_kernel(nb, c, h, w, k, r, s, st, st, pd, pd,
+                                                     prec_code)}
+    nbuf = 1 if batch1 else max(1, -(-2 * L2_BYTES // in_bytes))
+    layer = make_layer(wl, precision, dev)
+    xs = make_inputs_dev(nb, wl, dev, 2000 + rank, nbuf)
+    planes = [(x.real.permute(0, 2, 3, 1).contiguous(), x.imag.permute(0, 2, 3, 1).contiguous())
+              for x in xs]
+    it = [0]
+
+    def fwd():
+        layer(xs[it[0] % nbuf])
+        it[0] += 1
+
+    def planar():
+        a, b = planes[it[0] % nbuf]
+        layer.forward_planar(a, b)
+        it[0] += 1
+
+    scale = 1 if batch1 else world
+    with torch.no_grad():
+        for name, fn in (("forward", fwd), ("forward_planar", planar)):
+            for _ in range(args.warmup):
+                fn()
+            t, blocks = timed_blocks(fn, args.steps, world, dev)
+            e = roofline_entry(flops_rank, alg_rank, t, precision, peaks)
+            e["tflops_all_gpus"] = e["tflops"] * scale
+            e["blocks"] = blocks
+            res[name + ("_warm" if batch1 else "")] = e
+        if batch1:
+            # Cold: distinct layers and inputs, > 2x L2 in total.
+            packed = layer._w_packed.numel() * 4
+            m = min(64, max(2, -(-2 * L2_BYTES // (packed + in_bytes + out_bytes))))
+            layers = [make_layer(wl, precision, dev, seed=100 + j) for j in range(m)]
+            cx = make_inputs_dev(1, wl, dev, 3000 + rank, m)
+            cp = [(x.real.permute(0, 2, 3, 1).contiguous(), x.imag.permute(0, 2, 3, 1).contiguous())
+                  for x in cx]
+
+            def fwd_cold():
+                j = it[0] % m
+                layers[j](cx[j])
+                it[0] += 1
+
+            def planar_cold():
+                j = it[0] % m
+                layers[j].forward_planar(*cp[j])
+                it[0] += 1
+
+            for name, fn in (("forward_cold", fwd_cold), ("forward_planar_cold", planar_cold)):
+                for _ in range(max(args.warmup, m)):
+                    fn()
+                t, blocks = timed_blocks(fn, max(args.steps, m), world, dev)
+                e = roofline_entry(flops_rank, alg_rank, t, precision, peaks)
+                e["blocks"] = blocks
+                e["rotation"] = f"{m} distinct layers + inputs"
+                res[name] = e
+            del layers, cx, cp
+    del layer, xs, planes
+    torch.cuda.empty_cache()
+    return res
+
+
+def shard_parity(layer, x, wl, dev):
+    """Relative Frobenius error of this rank's first and last image against
+    the reference's four-conv formula (benchmarks/baseline.py:5-9) run by
+    cuDNN in fp32 with TF32 off (max of the two)."""
+    import torch.nn.functional as F
+    n, c, h, w, k, r, s, st, pd, std = wl
+    old = torch.backends.cudnn.allow_tf32
+    torch.backends.cudnn.allow_tf32 = False
+    try:
+        worst = 0.0
+        for i in sorted({0, x.shape[0] - 1}):
+            xi = x[i:i + 1]
+            y = layer(xi)
+            wr, wim = layer.weight_real, layer.weight_imag
+            ref = torch.complex(
+                F.conv2d(xi.real, wr, stride=st, padding=pd) - F.conv2d(xi.imag, wim, stride=st, padding=pd),
+                F.conv2d(xi.imag, wr, stride=st, padding=pd) + F.conv2d(xi.real, wim, stride=st, padding=pd))
+            err = (torch.linalg.vector_norm((y - ref).to(torch.complex128))
+                   / torch.linalg.vector_norm(ref.to(torch.complex128))).item()
+            worst = max(worst, err)
+        return worst
+    finally:
+        torch.backends.cudnn.allow_tf32 = old
 
 
 # ------------------------------------------------------------------ our arm
@@ -241,8 +462,7 @@ def run_ours(args, wl):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     init_pg(world, "nccl", dev)
-    from complex_conv2d import ComplexConv2d
-
+    from complex_conv2d import _C
     from complex_conv2d.distributed import batch_shard
     n, c, h, w, k, r, s, st, pd, std = wl
     _, nb = batch_shard(n, world, rank)
@@ -251,91 +471,54 @@ def run_ours(args, wl):
     p, q = out_hw(h, w, r, s, st, pd)
     flops_rank = workload_flops(nb, c, h, w, k, r, s, st, pd)
     flops_total = workload_flops(n, c, h, w, k, r, s, st, pd)
+    peaks = load_peaks()
+    prec_code = 1 if args.precision == "3xtf32" else 0
 
     # Weights: identical seeded init on every rank (replicated, no broadcast).
-    g = torch.Generator().manual_seed(1)
-    bound = 1.0 / (c * r * s) ** 0.5
-    wr = (torch.rand((k, c, r, s), generator=g) * 2 - 1) * bound
-    wi = (torch.rand((k, c, r, s), generator=g) * 2 - 1) * bound
-    layer = ComplexConv2d(c, k, (r, s), stride=st, padding=pd, device=dev, precision=args.precision)
-    with torch.no_grad():
-        layer.weight_real.copy_(wr)
-        layer.weight_imag.copy_(wi)
-    # This rank's slice of the seeded global batch.  Steps rotate over enough
-    # distinct input buffers that their total exceeds twice the 126 MB L2, so
-    # no step reads an input left in L2 by an earlier step.
+    layer = make_layer(wl, args.precision, dev)
+    # This rank's slice of the batch.  Steps rotate over enough distinct input
+    # buffers that their total exceeds twice the 126 MB L2, so no step reads
+    # an input left in L2 by an earlier step.
     in_bytes = nb * c * h * w * 8
-    nbuf = max(1, -(-256 * 2**20 // in_bytes))
-    gx = torch.Generator(device=dev).manual_seed(1000 + rank)
-    xs = []
-    for _ in range(nbuf):
-        xr = torch.randn((nb, c, h, w), generator=gx, device=dev) * std
-        xi = torch.randn((nb, c, h, w), generator=gx, device=dev) * std
-        xs.append(torch.complex(xr, xi))
+    out_bytes = nb * k * p * q * 8
+    nbuf = max(1, -(-2 * L2_BYTES // in_bytes))
+    xs = make_inputs_dev(nb, wl, dev, 1000 + rank, nbuf)
     x = xs[0]
-    x_planar_r = xr.permute(0, 2, 3, 1).contiguous()
-    x_planar_i = xi.permute(0, 2, 3, 1).contiguous()
-    del xr, xi
-    stream = torch.cuda.current_stream()
 
     visible = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     phys = visible.split(",")[local] if visible else str(local)
     clocks = ClockSampler(phys)
+    it = [0]
+
+    def fwd():
+        layer(xs[it[0] % nbuf])
+        it[0] += 1
+
     with torch.no_grad():
         clocks.start()
         # ---- device-resident timing of the public forward()
-        for i in range(args.warmup):
-            y = layer(xs[i % nbuf])
-        barrier(world)
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for i in range(args.steps):
-            y = layer(xs[i % nbuf])
-        e1.record(stream)
-        torch.cuda.synchronize()
-        barrier(world)
-        t_fwd = e0.elapsed_time(e1) / 1e3 / args.steps
-        clk = clocks.stop()
-
-        # ---- the dominant kernel alone: forward_planar is one fprop launch
-        for _ in range(max(3, args.warmup // 2)):
-            yp = layer.forward_planar(x_planar_r, x_planar_i)
-        torch.cuda.synchronize()
-        e2 = torch.cuda.Event(enable_timing=True)
-        e3 = torch.cuda.Event(enable_timing=True)
-        e2.record(stream)
-        for _ in range(args.steps):
-            yp = layer.forward_planar(x_planar_r, x_planar_i)
-        e3.record(stream)
-        torch.cuda.synchronize()
-        t_kernel = e2.elapsed_time(e3) / 1e3 / args.steps
-        del yp
+        for _ in range(args.warmup):
+            fwd()
+        t_fwd, blocks = timed_blocks(fwd, args.steps, world, dev)
 
         # ---- forward()'s convolution launch alone (planar input, complex64
-        # output; forward() adds the complex64 -> planar layout pass)
-        from complex_conv2d import _C
-        layer._ensure_prepacked()
-        prec_code = 1 if args.precision == "3xtf32" else 0
+        # output; a forward() with a layout pass adds that pass in front)
+        xpr = x.real.permute(0, 2, 3, 1).contiguous()
+        xpi = x.imag.permute(0, 2, 3, 1).contiguous()
         conv = lambda: _C.forward_planar_to_complex_packed(
-            x_planar_r, x_planar_i, layer._w_packed, c, k, r, s, st, st, pd, pd, prec_code)
+            xpr, xpi, layer._w_packed, c, k, r, s, st, st, pd, pd, prec_code)
         for _ in range(max(3, args.warmup // 2)):
-            yc = conv()
-        torch.cuda.synchronize()
-        e6 = torch.cuda.Event(enable_timing=True)
-        e7 = torch.cuda.Event(enable_timing=True)
-        e6.record(stream)
-        for _ in range(args.steps):
-            yc = conv()
-        e7.record(stream)
-        torch.cuda.synchronize()
-        t_conv = e6.elapsed_time(e7) / 1e3 / args.steps
-        del yc
+            conv()
+        t_conv, _ = timed_blocks(conv, args.steps, world, dev)
+        del xpr, xpi
+
+        # ---- this rank's outputs against the four-conv formula
+        parity = max_over_ranks(shard_parity(layer, x, wl, dev), world, dev)
 
         # ---- end to end: pinned host input -> device -> forward -> pinned host output
         x_host = x.cpu().pin_memory()
         y_host = torch.empty((nb, k, p, q), dtype=torch.complex64).pin_memory()
+
         def serial_step():
             xd = x_host.to(dev, non_blocking=True)
             y_host.copy_(layer(xd), non_blocking=True)
@@ -343,57 +526,67 @@ def run_ours(args, wl):
         def host_step():
             layer.forward_host(x_host, out=y_host)
 
-        def timed(step):
+        for fn in (serial_step, host_step):
             for _ in range(max(3, min(args.warmup, 5))):
-                step()
-            barrier(world)
-            torch.cuda.synchronize()
-            e4 = torch.cuda.Event(enable_timing=True)
-            e5 = torch.cuda.Event(enable_timing=True)
-            e4.record(stream)
-            for _ in range(args.steps):
-                step()
-            e5.record(stream)
-            torch.cuda.synchronize()
-            barrier(world)
-            return e4.elapsed_time(e5) / 1e3 / args.steps
+                fn()
+        t_e2e_serial, _ = timed_blocks(serial_step, args.steps, world, dev)
+        t_e2e, e2e_blocks = timed_blocks(host_step, args.steps, world, dev)
+        del x_host, y_host, xs, x
+        torch.cuda.empty_cache()
 
-        t_e2e_serial = timed(serial_step)
-        t_e2e = timed(host_step)
-
-    t_fwd_max = max_over_ranks(t_fwd, world, dev)
-    t_e2e_max = max_over_ranks(t_e2e, world, dev)
-    t_e2e_serial_max = max_over_ranks(t_e2e_serial, world, dev)
-    t_kernel_max = max_over_ranks(t_kernel, world, dev)
+    # ---- every BASELINE config (the headline workload's entry included)
+    per_config = {}
+    if not args.no_per_config:
+        for entry, wname, prec in PER_CONFIG:
+            per_config[entry] = measure_config(wname, prec, world, rank, dev, args, peaks)
+    clk = clocks.stop()
+    # ---- CPU baselines (after the GPU work: the clock samples cover only that)
+    if not args.no_per_config and world == 1 and rank == 0 and not args.no_cpu_baseline:
+        for entry, wname, prec in PER_CONFIG:
+            per_config[entry]["cpu_baseline"], _ = cpu_baseline(WORKLOADS[wname], budget_s=1.5)
+        cbc, _ = cpu_baseline(CPU_CONFIG, budget_s=3.0)
+        per_config["cpu_b1_32_32_32"] = {"cpu_only": True, "cpu_baseline": cbc}
+    launches = _C.complex_forward_launches(nb, c, h, w, k, r, s, st, st, pd, pd, prec_code)
+    kernel_path = _C.complex_forward_kernel(nb, c, h, w, k, r, s, st, st, pd, pd, prec_code)
+    cb = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cb, _ = cpu_baseline(wl)
 
     if rank != 0:
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()
         return 0
+    emit_line(args, wl, world, nb, nbuf, in_bytes, out_bytes, flops_rank, flops_total, peaks,
+              t_fwd, blocks, t_conv, parity, t_e2e, t_e2e_serial, launches, kernel_path, clk,
+              per_config, cb)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
 
-    from complex_conv2d import _C
-    prec_code = 1 if args.precision == "3xtf32" else 0
-    launches = _C.complex_forward_launches(nb, c, h, w, k, r, s, st, st, pd, pd, prec_code)
-    kernel_path = _C.complex_forward_kernel(nb, c, h, w, k, r, s, st, st, pd, pd, prec_code)
-    peaks = load_peaks()
+
+def emit_line(args, wl, world, nb, nbuf, in_bytes, out_bytes, flops_rank, flops_total, peaks,
+              t_fwd, blocks, t_conv, parity, t_e2e, t_e2e_serial, launches, kernel_path, clk,
+              per_config, cb):
+    n, c, h, w, k, r, s, st, pd, std = wl
     tf32_peak = peaks["bf16_tflops"] / 2.0  # dense TF32 runs at half the bf16 rate
     if args.precision == "3xtf32":
         tf32_peak /= 3.0  # three TF32 products per fp32 product
-    # Roofline of the dominant kernel: forward()'s convolution launch, timed
-    # alone above (t_conv); the layout pass in front of it is HBM-bound.
+    # Roofline of the dominant kernel: forward()'s convolution launch.  With
+    # one launch per forward() that is the whole step; otherwise the
+    # convolution launch timed alone (the layout pass in front is HBM-bound).
     one_launch = launches == 1
     t_dom = t_fwd if one_launch else t_conv
     achieved = flops_rank / t_dom / 1e12
-    out_bytes = nb * k * p * q * 8
     line = {
         "metric": METRIC,
-        "value": flops_total / t_fwd_max / 1e12,
+        "value": flops_total / t_fwd / 1e12,
         "unit": UNIT,
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": t_fwd_max * 1e3,
+        "ms_per_step": t_fwd * 1e3,
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
@@ -406,10 +599,15 @@ def run_ours(args, wl):
             "l2": f"{in_bytes / 1e6:.0f} MB input + {out_bytes / 1e6:.0f} MB output per GPU per "
                   f"step; steps rotate over {nbuf} input buffers ({nbuf * in_bytes / 1e6:.0f} MB "
                   f"> 2x L2), so no step reads an L2-resident input",
+            "timing": f"blocks of exactly {args.steps} steps, each between barriers and device "
+                      f"syncs, max over ranks per block; {blocks} block(s) (repeated to cover "
+                      ">= 20 ms), median block reported",
             "api": "ComplexConv2d.forward (complex64 NCHW)",
         },
-        "forward_planar_ms": t_kernel_max * 1e3,
         "forward_conv_launch_ms": t_conv * 1e3,
+        "parity": {"max_rel_frobenius": parity, "bar": 1e-3,
+                   "check": "first and last image of every rank's shard vs the four-conv formula "
+                            "in fp32 (cuDNN, TF32 off); max over ranks"},
         "roofline": {
             "bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": UNIT,
             "frac": achieved / tf32_peak,
@@ -422,33 +620,37 @@ def run_ours(args, wl):
             "peak_source": (f"{peaks['source']} bf16 {peaks['bf16_tflops']} TFLOP/s / 2 (dense TF32)"
                             + (" / 3 (3xTF32)" if args.precision == "3xtf32" else "")),
         },
-        "e2e": {"value": flops_total / t_e2e_max / 1e12, "unit": UNIT,
+        "e2e": {"value": flops_total / t_e2e / 1e12, "unit": UNIT,
                 "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes,
-                "ms_per_step": t_e2e_max * 1e3,
+                "ms_per_step": t_e2e * 1e3,
                 "api": "ComplexConv2d.forward_host (pinned host in/out, chunked copy pipeline)",
-                "serial_ms_per_step": t_e2e_serial_max * 1e3},
+                "serial_ms_per_step": t_e2e_serial * 1e3},
         "gpu_launches": args.steps * launches,
+        "gpu_launches_note": "per timed block of --steps steps (one forward() each)",
         "clocks": clk,
+        "per_config": per_config,
+        "per_config_note": ("every BASELINE config through ComplexConv2d.forward / forward_planar; "
+                            "ms per call (max over ranks), tflops = this GPU's share (tflops_all_gpus "
+                            "= whole job), frac = of the dense TF32 peak (3xTF32: peak/3), gbs = "
+                            "algorithmic bytes 8*(NHWC+KRSC+NPQK) per call / time, hbm_frac = of the "
+                            "measured copy bandwidth; batch-1 layers: _warm = one layer back to "
+                            "back, _cold = rotating layers+inputs > 2x L2"),
     }
-    if world == 1 and not args.no_cpu_baseline:
-        cb, _ = cpu_baseline(wl)
+    if cb is not None:
         line["cpu_baseline"] = cb
     print(json.dumps(line), flush=True)
-    if world > 1:
-        import torch.distributed as dist
-        dist.destroy_process_group()
-    return 0
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default=DEFAULT_WORKLOAD)
     ap.add_argument("--precision", choices=["tf32", "3xtf32"], default="tf32")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -9,11 +9,13 @@ Produces, next to the Python sources in ``complex_conv2d/``:
     (csrc/bindings.cpp), linked against libccv_b200.so with an $ORIGIN rpath.
 
 Both are cross-compiled here without a GPU; nothing is JIT-built at import
-time.  Rebuilds happen only when a source is newer than its output.
+time.  Each CUDA translation unit compiles to an object under ``_build/`` in
+parallel; objects and libraries are rebuilt only when a source is newer.
 """
 
 from __future__ import annotations
 
+import concurrent.futures
 import os
 import subprocess
 import sys
@@ -24,10 +26,12 @@ REPO = os.path.dirname(HERE)
 PKG = os.path.join(HERE, "complex_conv2d")
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(REPO, "include")
+OBJ = os.path.join(HERE, "_build")
 
-CU_SOURCES = ["ccv_api.cu", "ccv_fprop.cu", "ccv_fprop2.cu", "ccv_fprop2h.cu", "ccv_fprop_cd.cu", "ccv_layout.cu", "ccv_noalloc.cu"]
-CU_HEADERS = ["ccv_internal.h", "ccv_ptx.cuh", "ccv_fprop_common.cuh", "ccv_epilogue.cuh", "ccv_convert.cuh",
-              "ccv_cvt_role.cuh", "ccv_layout_role.cuh"]
+CU_SOURCES = ["ccv_api.cu", "ccv_fprop.cu", "ccv_fprop2.cu", "ccv_fprop2h.cu", "ccv_layout.cu",
+              "ccv_noalloc.cu"]
+CU_HEADERS = ["ccv_internal.h", "ccv_ptx.cuh", "ccv_fprop_common.cuh", "ccv_epilogue.cuh",
+              "ccv_layout_role.cuh"]
 NVCC_ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -51,13 +55,23 @@ def _run(cmd, verbose):
 
 def build_lib(verbose: bool = False, force: bool = False) -> str:
     out = os.path.join(PKG, "libccv_b200.so")
-    deps = [os.path.join(CSRC, f) for f in CU_SOURCES + CU_HEADERS]
-    deps.append(os.path.join(INCLUDE, "ccv_b200.h"))
-    if force or _stale(out, deps):
-        cmd = [_nvcc(), "-O3", "-std=c++17", *NVCC_ARCH, "-lineinfo",
-               "-Xcompiler", "-fPIC", "-shared", "-I", INCLUDE, "-I", CSRC,
-               *[os.path.join(CSRC, f) for f in CU_SOURCES], "-o", out]
-        _run(cmd, verbose)
+    headers = [os.path.join(CSRC, f) for f in CU_HEADERS] + [os.path.join(INCLUDE, "ccv_b200.h")]
+    os.makedirs(OBJ, exist_ok=True)
+    jobs = []
+    objs = []
+    for f in CU_SOURCES:
+        src = os.path.join(CSRC, f)
+        obj = os.path.join(OBJ, f.replace(".cu", ".o"))
+        objs.append(obj)
+        if force or _stale(obj, [src] + headers):
+            jobs.append([_nvcc(), "-O3", "-std=c++17", *NVCC_ARCH, "-lineinfo",
+                         "-Xcompiler", "-fPIC", "-I", INCLUDE, "-I", CSRC, "-c", src, "-o", obj])
+    if jobs:
+        with concurrent.futures.ThreadPoolExecutor(max_workers=len(jobs)) as pool:
+            for fut in [pool.submit(_run, cmd, verbose) for cmd in jobs]:
+                fut.result()
+    if force or jobs or _stale(out, objs):
+        _run([_nvcc(), *NVCC_ARCH, "-shared", *objs, "-o", out], verbose)
     return out
 
 

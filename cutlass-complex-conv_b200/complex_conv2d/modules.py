@@ -12,6 +12,10 @@ initialisation and the cache-invalidation rules follow
 * ``forward`` hands the complex64 NCHW tensor to the native entry point,
   which does the NCHW->planar conversion and writes complex64 NCHW output
   itself, instead of the five ATen layout kernels of ``modules.py:198-207``.
+
+One capability is added: ``bias=True`` (rejected by the reference at
+``modules.py:73-74``) gives the layer a complex bias per output channel,
+``bias_real + 1j * bias_imag``, added in the kernels' epilogue.
 """
 
 import os
@@ -66,11 +70,15 @@ class ComplexConv2d(nn.Module):
     like the reference) or ``"3xtf32"`` (split-TF32, close to FP32 results).
     ``None`` reads ``COMPLEX_CONV2D_PRECISION`` from the environment.
 
+    ``bias=True`` adds a complex bias per output channel (parameters
+    ``bias_real`` and ``bias_imag``, fp32 ``[out_channels]``, initialised like
+    ``nn.Conv2d``'s bias: U(+-1/sqrt(in_channels * kernel_h * kernel_w))):
+    ``y[:, k] += bias_real[k] + 1j * bias_imag[k]``.
+
     Current limitations (as in the reference):
       - CUDA only (an sm_100 / B200 device)
       - torch.complex64 only
       - forward inference only (no autograd/backward)
-      - bias=False
       - dilation=1
       - groups=1
       - padding_mode="zeros"
@@ -113,8 +121,6 @@ class ComplexConv2d(nn.Module):
             raise NotImplementedError("dilation != 1 is not supported yet")
         if groups != 1:
             raise NotImplementedError("groups != 1 is not supported yet")
-        if bias:
-            raise NotImplementedError("bias=True is not supported yet")
         if padding_mode != "zeros":
             raise NotImplementedError(
                 'padding_mode other than "zeros" is not supported yet'
@@ -153,13 +159,41 @@ class ComplexConv2d(nn.Module):
         nn.init.kaiming_uniform_(self.weight_real)
         nn.init.kaiming_uniform_(self.weight_imag)
 
+        if bias:
+            fan_in = self.in_channels * self.kernel_size[0] * self.kernel_size[1]
+            bound = 1.0 / fan_in ** 0.5
+            self.bias_real = nn.Parameter(
+                torch.empty(self.out_channels, device=device, dtype=torch.float32)
+                .uniform_(-bound, bound),
+                requires_grad=False,
+            )
+            self.bias_imag = nn.Parameter(
+                torch.empty(self.out_channels, device=device, dtype=torch.float32)
+                .uniform_(-bound, bound),
+                requires_grad=False,
+            )
+        else:
+            self.register_parameter("bias_real", None)
+            self.register_parameter("bias_imag", None)
+
         self._clear_prepacked_weights()
 
     def extra_repr(self):
         return (
             f"{self.in_channels}, {self.out_channels}, kernel_size={self.kernel_size}, "
-            f"stride={self.stride}, padding={self.padding}, precision={self.precision!r}"
+            f"stride={self.stride}, padding={self.padding}, bias={self.bias_real is not None}, "
+            f"precision={self.precision!r}"
         )
+
+    def _bias_args(self):
+        """``(bias_real, bias_imag)`` as contiguous tensors, or ``(None, None)``."""
+        if self.bias_real is None:
+            return None, None
+        out = []
+        for b in (self.bias_real, self.bias_imag):
+            b = b.detach().contiguous()
+            out.append(b if _aligned16(b) else b.clone())
+        return out[0], out[1]
 
     def _clear_prepacked_weights(self):
         self._w_packed = None
@@ -223,6 +257,7 @@ class ComplexConv2d(nn.Module):
         if x_imag.is_cuda and x_imag.is_contiguous() and not _aligned16(x_imag):
             x_imag = x_imag.clone()
 
+        bias_real, bias_imag = self._bias_args()
         return cutlass_complex_conv.forward_planar_packed(
             x_real,
             x_imag,
@@ -236,6 +271,8 @@ class ComplexConv2d(nn.Module):
             self.padding[0],
             self.padding[1],
             _PRECISIONS[self.precision],
+            bias_real,
+            bias_imag,
         )
 
     def forward(self, x):
@@ -261,10 +298,13 @@ class ComplexConv2d(nn.Module):
 
         self._ensure_prepacked()
 
-        x = x.contiguous()
-        if not _aligned16(x):
-            x = x.clone()
+        # Any layout is read in place (strided layout pass; the reference
+        # makes a contiguous copy first, modules.py:198-199).  A dense input
+        # at an address the TMA path cannot use goes through the same
+        # strided pass instead of a copy.
+        strided = x.is_contiguous() and not _aligned16(x)
 
+        bias_real, bias_imag = self._bias_args()
         return cutlass_complex_conv.forward_complex_packed(
             x,
             self._w_packed,
@@ -276,6 +316,9 @@ class ComplexConv2d(nn.Module):
             self.padding[0],
             self.padding[1],
             _PRECISIONS[self.precision],
+            bias_real,
+            bias_imag,
+            strided,
         )
 
     def _copy_streams(self, device):

@@ -37,6 +37,24 @@ ccv_stream_t current_stream() {
   return reinterpret_cast<ccv_stream_t>(at::cuda::getCurrentCUDAStream().stream());
 }
 
+// Checks an optional complex bias (two K-element fp32 CUDA tensors) and
+// returns its device pointers (null, null without bias).
+std::pair<const float*, const float*> bias_ptrs(const c10::optional<torch::Tensor>& br,
+                                               const c10::optional<torch::Tensor>& bi,
+                                               int64_t K, const torch::Tensor& like) {
+  const bool has_r = br.has_value() && br->defined();
+  const bool has_i = bi.has_value() && bi->defined();
+  TORCH_CHECK(has_r == has_i, "bias_real and bias_imag must both be given or both be None");
+  if (!has_r) return {nullptr, nullptr};
+  for (const auto* b : {&*br, &*bi}) {
+    TORCH_CHECK(b->is_cuda() && b->scalar_type() == at::kFloat && b->is_contiguous(),
+                "bias must be a contiguous CUDA float32 tensor");
+    TORCH_CHECK(b->dim() == 1 && b->size(0) == K, "bias must have out_channels elements");
+    TORCH_CHECK(b->device() == like.device(), "bias must be on the input's CUDA device");
+  }
+  return {br->data_ptr<float>(), bi->data_ptr<float>()};
+}
+
 ccv_conv_shape make_shape(int64_t n, int64_t h, int64_t w, int64_t c, int64_t k, int64_t r,
                           int64_t s, int64_t sh, int64_t sw, int64_t ph, int64_t pw) {
   ccv_conv_shape shp;
@@ -119,8 +137,9 @@ std::vector<torch::Tensor> forward_planar_packed(torch::Tensor x_real, torch::Te
                                                  torch::Tensor w_packed, int64_t in_channels,
                                                  int64_t K, int64_t R, int64_t S,
                                                  int64_t stride_h, int64_t stride_w,
-                                                 int64_t pad_h, int64_t pad_w,
-                                                 int64_t precision) {
+                                                 int64_t pad_h, int64_t pad_w, int64_t precision,
+                                                 c10::optional<torch::Tensor> bias_real,
+                                                 c10::optional<torch::Tensor> bias_imag) {
   CHECK_CUDA(x_real); CHECK_CUDA(x_imag); CHECK_CUDA(w_packed);
   CHECK_FLOAT(x_real); CHECK_FLOAT(x_imag); CHECK_FLOAT(w_packed);
   CHECK_CONTIGUOUS(x_real); CHECK_CONTIGUOUS(x_imag); CHECK_CONTIGUOUS(w_packed);
@@ -144,6 +163,7 @@ std::vector<torch::Tensor> forward_planar_packed(torch::Tensor x_real, torch::Te
   TORCH_CHECK(static_cast<size_t>(w_packed.numel()) * 4 >=
                   ccv_packed_weight_bytes(&shp, static_cast<int>(precision)),
               "packed weights do not match the problem");
+  const auto bias = bias_ptrs(bias_real, bias_imag, K, x_real);
   auto y_real = torch::empty({N, P, Q, K}, x_real.options());
   auto y_imag = torch::empty({N, P, Q, K}, x_real.options());
   const size_t ws_bytes = ccv_fprop_planar_workspace_bytes(&shp, static_cast<int>(precision));
@@ -153,21 +173,23 @@ std::vector<torch::Tensor> forward_planar_packed(torch::Tensor x_real, torch::Te
     ws = torch::empty({static_cast<int64_t>(ws_bytes)}, x_real.options().dtype(torch::kUInt8));
     ws_ptr = ws.data_ptr();
   }
-  check_rc(ccv_fprop_planar(x_real.data_ptr<float>(), x_imag.data_ptr<float>(),
-                            w_packed.data_ptr(), y_real.data_ptr<float>(),
-                            y_imag.data_ptr<float>(), &shp, static_cast<int>(precision), ws_ptr,
-                            ws_bytes, current_stream()),
+  check_rc(ccv_fprop_planar_bias(x_real.data_ptr<float>(), x_imag.data_ptr<float>(),
+                                 w_packed.data_ptr(), bias.first, bias.second,
+                                 y_real.data_ptr<float>(), y_imag.data_ptr<float>(), &shp,
+                                 static_cast<int>(precision), ws_ptr, ws_bytes, current_stream()),
            "ccv_fprop_planar");
   return {y_real, y_imag};
 }
 
 torch::Tensor forward_complex_packed(torch::Tensor x, torch::Tensor w_packed, int64_t K,
                                      int64_t R, int64_t S, int64_t stride_h, int64_t stride_w,
-                                     int64_t pad_h, int64_t pad_w, int64_t precision) {
+                                     int64_t pad_h, int64_t pad_w, int64_t precision,
+                                     c10::optional<torch::Tensor> bias_real,
+                                     c10::optional<torch::Tensor> bias_imag, bool strided) {
   CHECK_CUDA(x); CHECK_CUDA(w_packed);
   TORCH_CHECK(x.scalar_type() == at::kComplexFloat, "x must be complex64");
   CHECK_FLOAT(w_packed);
-  CHECK_CONTIGUOUS(x); CHECK_CONTIGUOUS(w_packed);
+  CHECK_CONTIGUOUS(w_packed);
   TORCH_CHECK(x.dim() == 4, "x must be a 4D NCHW tensor");
   TORCH_CHECK(x.device() == w_packed.device(),
               "input and weights must be on the same CUDA device");
@@ -179,6 +201,7 @@ torch::Tensor forward_complex_packed(torch::Tensor x, torch::Tensor w_packed, in
   TORCH_CHECK(static_cast<size_t>(w_packed.numel()) * 4 >=
                   ccv_packed_weight_bytes(&shp, static_cast<int>(precision)),
               "packed weights do not match the problem");
+  const auto bias = bias_ptrs(bias_real, bias_imag, K, x);
   auto y = torch::empty({N, K, P, Q}, x.options());
   const size_t ws_bytes = ccv_fprop_complex_workspace_bytes(&shp, static_cast<int>(precision));
   torch::Tensor ws;
@@ -187,9 +210,21 @@ torch::Tensor forward_complex_packed(torch::Tensor x, torch::Tensor w_packed, in
     ws = torch::empty({static_cast<int64_t>(ws_bytes)}, x.options().dtype(torch::kUInt8));
     ws_ptr = ws.data_ptr();
   }
-  check_rc(ccv_fprop_complex(x.data_ptr(), w_packed.data_ptr(), y.data_ptr(), &shp,
-                             static_cast<int>(precision), ws_ptr, ws_bytes, current_stream()),
-           "ccv_fprop_complex");
+  if (x.is_contiguous() && !strided) {
+    check_rc(ccv_fprop_complex_bias(x.data_ptr(), w_packed.data_ptr(), bias.first, bias.second,
+                                    y.data_ptr(), &shp, static_cast<int>(precision), ws_ptr,
+                                    ws_bytes, current_stream()),
+             "ccv_fprop_complex");
+  } else {
+    // Any other layout (channels-last, slices, steps; or strided=true):
+    // the layout kernel reads the strides; no contiguous copy of the input.
+    const int64_t strides[4] = {x.stride(0), x.stride(1), x.stride(2), x.stride(3)};
+    check_rc(ccv_fprop_complex_strided(x.data_ptr(), strides, w_packed.data_ptr(), bias.first,
+                                       bias.second, y.data_ptr(), &shp,
+                                       static_cast<int>(precision), ws_ptr, ws_bytes,
+                                       current_stream()),
+             "ccv_fprop_complex");
+  }
   return y;
 }
 
@@ -263,8 +298,15 @@ void clear_device_status(int64_t device) {
   check_rc(ccv_clear_device_status(), "ccv_clear_device_status");
 }
 
-int64_t selftest_bounded_wait(int64_t device) {
+// Runs the bounded-wait self-test.  library=false: into a fresh device int,
+// returned; library=true: into the library's own status word, as a real
+// in-kernel timeout would (returns 0; read it with device_status).
+int64_t selftest_bounded_wait(int64_t device, bool library) {
   c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  if (library) {
+    check_rc(ccv_selftest_bounded_wait(nullptr, current_stream()), "ccv_selftest_bounded_wait");
+    return 0;
+  }
   auto st = torch::zeros({1}, torch::TensorOptions()
                                   .dtype(torch::kInt32)
                                   .device(torch::kCUDA, static_cast<c10::DeviceIndex>(device)));
@@ -286,12 +328,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("x_real"), pybind11::arg("x_imag"), pybind11::arg("w_packed"),
         pybind11::arg("in_channels"), pybind11::arg("out_channels"), pybind11::arg("kernel_h"), pybind11::arg("kernel_w"),
         pybind11::arg("stride_h"), pybind11::arg("stride_w"), pybind11::arg("pad_h"),
-        pybind11::arg("pad_w"), pybind11::arg("precision"));
+        pybind11::arg("pad_w"), pybind11::arg("precision"),
+        pybind11::arg("bias_real") = pybind11::none(), pybind11::arg("bias_imag") = pybind11::none());
   m.def("forward_complex_packed", &forward_complex_packed,
         "complex64 NCHW forward, packed weights", pybind11::arg("x"), pybind11::arg("w_packed"),
         pybind11::arg("out_channels"), pybind11::arg("kernel_h"), pybind11::arg("kernel_w"),
         pybind11::arg("stride_h"), pybind11::arg("stride_w"), pybind11::arg("pad_h"),
-        pybind11::arg("pad_w"), pybind11::arg("precision"));
+        pybind11::arg("pad_w"), pybind11::arg("precision"),
+        pybind11::arg("bias_real") = pybind11::none(), pybind11::arg("bias_imag") = pybind11::none(),
+        pybind11::arg("strided") = false);
   m.def("forward_planar_to_complex_packed", &forward_planar_to_complex_packed,
         "planar NHWC in, complex64 NCHW out, packed weights", pybind11::arg("x_real"),
         pybind11::arg("x_imag"), pybind11::arg("w_packed"), pybind11::arg("in_channels"),
@@ -310,6 +355,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("precision"));
   m.def("device_status", &device_status, pybind11::arg("device"));
   m.def("clear_device_status", &clear_device_status, pybind11::arg("device"));
-  m.def("selftest_bounded_wait", &selftest_bounded_wait, pybind11::arg("device"));
+  m.def("selftest_bounded_wait", &selftest_bounded_wait, pybind11::arg("device"),
+        pybind11::arg("library") = false);
+  m.def("reload_config", []() { check_rc(ccv_reload_config(), "ccv_reload_config"); },
+        "re-read the CCV_* environment switches");
   m.def("version", []() { return std::string(ccv_version()); });
 }

@@ -18,13 +18,14 @@
 
 namespace ccv {
 
-// Per-device status word.  Bounded in-kernel waits that run out write a
-// CCV_ERR_* code here; fprop kernels read it at start and exit without work
-// while it is set.
-__device__ int g_ccv_status = 0;
-// Stream-K counter sets (see stream_k_counters); zero-initialized.
-constexpr int kSkRing = 32;
-__device__ unsigned g_ccv_sk_counters[kSkRing * kSkCounterWords];
+// Per-device status block.  Word 0: bounded in-kernel waits that run out
+// write a CCV_ERR_* code here; fprop kernels read it at start and exit
+// without work while it is set.  Words 2-3: device address of the host-mapped
+// mirror of word 0 (null until the host sets it up), which the same waits
+// also write, so that host code sees a timeout without synchronizing.
+__device__ __align__(16) int g_ccv_status[4] = {0, 0, 0, 0};
+// Counter sets (see acquire_counter_set); zero-initialized.
+__device__ unsigned g_ccv_sk_counters[kCounterSets * kSkCounterWords];
 
 namespace {
 
@@ -33,6 +34,7 @@ thread_local std::string g_last_error;
 constexpr int kMaxDevices = 64;
 std::mutex g_dev_mutex;
 int* g_status_ptr[kMaxDevices] = {};
+volatile int* g_status_host[kMaxDevices] = {};  // host-mapped mirror of word 0
 int g_sm_count[kMaxDevices] = {};
 int g_arch_ok[kMaxDevices] = {};  // 0 unknown, 1 ok, -1 not sm_100
 
@@ -91,35 +93,148 @@ int cuda_error(cudaError_t e, const char* what) {
 }
 
 namespace {
-std::atomic<unsigned> g_sk_epoch[kMaxDevices];
-unsigned* g_sk_base[kMaxDevices] = {};
-}  // namespace
 
-unsigned* stream_k_counters() {
-  int dev = 0;
-  if (current_device(&dev) != CCV_OK) return nullptr;
-  {
-    std::lock_guard<std::mutex> lk(g_dev_mutex);
-    if (g_sk_base[dev] == nullptr) {
-      void* p = nullptr;
-      const cudaError_t e = cudaGetSymbolAddress(&p, g_ccv_sk_counters);
-      if (e != cudaSuccess) {
-        cuda_error(e, "cudaGetSymbolAddress(stream-K counters)");
-        return nullptr;
-      }
-      g_sk_base[dev] = static_cast<unsigned*>(p);
-    }
-  }
-  const unsigned slot = g_sk_epoch[dev].fetch_add(1u) % kSkRing;
-  return g_sk_base[dev] + static_cast<size_t>(slot) * kSkCounterWords;
+int env_int(const char* name, int dflt) {
+  const char* v = getenv(name);
+  return v != nullptr && *v != '\0' ? atoi(v) : dflt;
 }
 
-bool pdl_enabled() {
-  static const bool on = [] {
-    const char* env = getenv("CCV_PDL");
-    return env == nullptr || atoi(env) != 0;
-  }();
-  return on;
+Knobs parse_knobs() {
+  Knobs k;
+  k.pdl = env_int("CCV_PDL", 1);
+  k.kt = env_int("CCV_KT", 0);
+  k.force_kernel = env_int("CCV_FORCE_KERNEL", 0);
+  k.halo = env_int("CCV_HALO", -1);
+  k.splitk = env_int("CCV_SPLITK", 0);
+  k.lw = env_int("CCV_LW", -1);
+  k.lw_prefix = env_int("CCV_LW_PREFIX", -1);
+  k.lw_tma = env_int("CCV_LW_TMA", 1);
+  k.lw_tma_images = env_int("CCV_LW_TMA_IMAGES", 0);
+  k.lw_tma_bufs = env_int("CCV_LW_TMA_BUFS", 0);
+  k.subbox = env_int("CCV_SUBBOX", 1);
+  k.streamk = env_int("CCV_STREAMK", -1);
+  k.max_clusters = env_int("CCV_MAX_CLUSTERS", 0);
+  k.tma_store = env_int("CCV_TMA_STORE", 1);
+  return k;
+}
+
+// Readers may hold a reference across a reload, so replaced snapshots are
+// kept (a reload is a testing/benchmarking action, a few per process).
+std::atomic<const Knobs*> g_knobs{nullptr};
+std::mutex g_knobs_mutex;
+
+// Counter sets per device: the set's completion event (created on first
+// use), whether it has been handed out, and whether a captured graph owns
+// it for good.
+struct CounterSlot {
+  cudaEvent_t done = nullptr;
+  bool used = false;
+  bool reserved = false;
+};
+CounterSlot g_slots[kMaxDevices][kCounterSets];
+unsigned g_next_slot[kMaxDevices] = {};
+unsigned* g_sk_base[kMaxDevices] = {};
+
+// Sets this host thread took since its innermost CounterScope began.
+struct PendingSets {
+  int dev = -1;
+  int slots[8];
+  int count = 0;
+  int depth = 0;
+};
+thread_local PendingSets t_pending;
+
+}  // namespace
+
+const Knobs& knobs() {
+  const Knobs* k = g_knobs.load(std::memory_order_acquire);
+  if (k == nullptr) {
+    reload_knobs();
+    k = g_knobs.load(std::memory_order_acquire);
+  }
+  return *k;
+}
+
+void reload_knobs() {
+  std::lock_guard<std::mutex> lk(g_knobs_mutex);
+  g_knobs.store(new Knobs(parse_knobs()), std::memory_order_release);
+}
+
+unsigned* acquire_counter_set(cudaStream_t stream) {
+  int dev = 0;
+  if (current_device(&dev) != CCV_OK) return nullptr;
+  if (t_pending.depth == 0 || t_pending.count >= 8) return nullptr;
+  if (t_pending.count > 0 && t_pending.dev != dev) return nullptr;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  const bool capturing = cap != cudaStreamCaptureStatusNone;
+  std::lock_guard<std::mutex> lk(g_dev_mutex);
+  if (g_sk_base[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_ccv_sk_counters);
+    if (e != cudaSuccess) {
+      cuda_error(e, "cudaGetSymbolAddress(counter sets)");
+      return nullptr;
+    }
+    g_sk_base[dev] = static_cast<unsigned*>(p);
+  }
+  for (int i = 0; i < kCounterSets; ++i) {
+    const int slot = static_cast<int>((g_next_slot[dev] + i) % kCounterSets);
+    CounterSlot& cs = g_slots[dev][slot];
+    if (cs.reserved) continue;
+    bool pending_here = false;
+    for (int j = 0; j < t_pending.count; ++j) pending_here |= t_pending.slots[j] == slot;
+    if (pending_here) continue;
+    if (cs.used) {
+      // Querying events is not allowed while a stream captures; a set
+      // that has been used is then skipped.
+      if (capturing) continue;
+      const cudaError_t q = cudaEventQuery(cs.done);
+      if (q == cudaErrorNotReady) continue;
+      if (q != cudaSuccess) {
+        cudaGetLastError();
+        continue;
+      }
+    }
+    if (cs.done == nullptr && !capturing) {
+      if (cudaEventCreateWithFlags(&cs.done, cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        cs.done = nullptr;
+        return nullptr;
+      }
+    }
+    if (cs.done == nullptr && !capturing) return nullptr;
+    cs.used = true;
+    if (capturing) cs.reserved = true;
+    g_next_slot[dev] = static_cast<unsigned>(slot + 1);
+    t_pending.dev = dev;
+    t_pending.slots[t_pending.count++] = capturing ? -1 - slot : slot;
+    return g_sk_base[dev] + static_cast<size_t>(slot) * kSkCounterWords;
+  }
+  return nullptr;
+}
+
+CounterScope::CounterScope(cudaStream_t stream) : stream_(stream) {
+  if (t_pending.depth++ == 0) t_pending.count = 0;
+}
+
+CounterScope::~CounterScope() {
+  if (--t_pending.depth != 0) return;
+  std::lock_guard<std::mutex> lk(g_dev_mutex);
+  for (int j = 0; j < t_pending.count; ++j) {
+    const int slot = t_pending.slots[j];
+    if (slot < 0) continue;  // owned by a captured graph
+    CounterSlot& cs = g_slots[t_pending.dev][slot];
+    if (cudaEventRecord(cs.done, stream_) != cudaSuccess) {
+      // Without an event the set cannot be known free again: keep it out.
+      cudaGetLastError();
+      cs.reserved = true;
+    }
+  }
+  t_pending.count = 0;
 }
 
 int* device_status_ptr() {
@@ -137,6 +252,60 @@ int* device_status_ptr() {
   }
   return g_status_ptr[dev];
 }
+
+namespace {
+
+// Sets up the host-mapped mirror of the current device's status word (once
+// per device; a pinned host allocation, skipped while `stream` captures).
+void ensure_status_mirror(cudaStream_t stream) {
+  int dev = 0;
+  if (current_device(&dev) != CCV_OK) return;
+  {
+    std::lock_guard<std::mutex> lk(g_dev_mutex);
+    if (g_status_host[dev] != nullptr) return;
+  }
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return;
+  }
+  std::lock_guard<std::mutex> lk(g_dev_mutex);
+  if (g_status_host[dev] != nullptr) return;
+  int* h = nullptr;
+  if (cudaHostAlloc(reinterpret_cast<void**>(&h), sizeof(int),
+                    cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  *h = 0;
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess ||
+      cudaMemcpyToSymbol(g_ccv_status, &d, sizeof(d), 2 * sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFreeHost(h);
+    return;
+  }
+  g_status_host[dev] = h;
+}
+
+// CCV_ERR_DEVICE when a kernel on the current device has reported a timeout
+// that the host can see (the status mirror is set): the library's kernels
+// would skip their work, so nothing is launched.
+int check_status_clear() {
+  int dev = 0;
+  const int rc = current_device(&dev);
+  if (rc != CCV_OK) return rc;
+  const volatile int* h = g_status_host[dev];
+  if (h != nullptr && *h != 0) {
+    return set_error(CCV_ERR_DEVICE,
+                     "a library kernel on this device gave up a bounded wait (status " +
+                         std::to_string(*h) +
+                         "); outputs since then are invalid - call ccv_clear_device_status");
+  }
+  return CCV_OK;
+}
+
+}  // namespace
 
 int device_sm_count() {
   int dev = 0;
@@ -176,10 +345,9 @@ int encode_tiled_ex(CUtensorMap* map, const void* base, int rank, const uint64_t
     es[i] = elem_strides[i];
     if (i + 1 < rank) st[i] = strides_bytes[i];
   }
-  const CUtensorMapSwizzle sw = swizzle == kSwizzle128        ? CU_TENSOR_MAP_SWIZZLE_128B
-                                : swizzle == kSwizzle128Atom32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
-                                : swizzle == kSwizzleNone      ? CU_TENSOR_MAP_SWIZZLE_NONE
-                                                               : CU_TENSOR_MAP_SWIZZLE_64B;
+  const CUtensorMapSwizzle sw = swizzle == kSwizzle128   ? CU_TENSOR_MAP_SWIZZLE_128B
+                                : swizzle == kSwizzleNone ? CU_TENSOR_MAP_SWIZZLE_NONE
+                                                          : CU_TENSOR_MAP_SWIZZLE_64B;
   // 8-byte elements (complex64 moved as opaque 64-bit words) or fp32.
   const CUresult r = g_encode_tiled(
       map, elem8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT64 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank,
@@ -276,6 +444,18 @@ size_t ccv_packed_weight_bytes(const ccv_conv_shape* shape, int precision) {
 int ccv_prepack_weights(const float* w_real, const float* w_imag, int layout,
                         const ccv_conv_shape* shape, int precision, void* packed,
                         size_t packed_bytes, ccv_stream_t stream) {
+  ensure_status_mirror(reinterpret_cast<cudaStream_t>(stream));
+  return prepack_weights_impl(w_real, w_imag, layout, shape, precision, packed, packed_bytes,
+                              stream);
+}
+
+}  // extern "C"
+
+namespace ccv {
+
+int prepack_weights_impl(const float* w_real, const float* w_imag, int layout,
+                         const ccv_conv_shape* shape, int precision, void* packed,
+                         size_t packed_bytes, ccv_stream_t stream) {
   Problem pb;
   int rc = make_problem(shape, &pb);
   if (rc != CCV_OK) return rc;
@@ -293,6 +473,7 @@ int ccv_prepack_weights(const float* w_real, const float* w_imag, int layout,
     return set_error(CCV_ERR_WORKSPACE, "packed weight buffer too small");
   }
   if ((rc = check_device()) != CCV_OK) return rc;
+  if ((rc = check_status_clear()) != CCV_OK) return rc;
   return launch_prepack(w_real, w_imag, layout, pb, precision, static_cast<float*>(packed),
                         reinterpret_cast<cudaStream_t>(stream));
 }
@@ -307,11 +488,9 @@ size_t planar_required_bytes(const Problem& pb, int precision) {
   return precision == CCV_PRECISION_3XTF32 ? 4 * plane_bytes_aligned(pb) : 0;
 }
 
-// Workspace a complex call cannot run without: none for the fused kernel
-// (it reads complex64 directly); otherwise fp32 NHWC planes of the input
-// (real, imaginary; 3xTF32: also remainders).
+// Workspace a complex call cannot run without: fp32 NHWC planes of the
+// input (real, imaginary; 3xTF32: also remainders).
 size_t complex_required_bytes(const Problem& pb, int precision) {
-  if (fused_complex_available(pb, precision)) return 0;
   return (precision == CCV_PRECISION_3XTF32 ? 4 : 2) * plane_bytes_aligned(pb);
 }
 
@@ -330,7 +509,141 @@ void split_scratch(void* workspace, size_t workspace_bytes, size_t required, voi
   *ws_bytes = end - start;
 }
 
+int check_precision(int precision) {
+  if (precision != CCV_PRECISION_TF32 && precision != CCV_PRECISION_3XTF32) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "unknown precision");
+  }
+  return CCV_OK;
+}
+
+int make_epilogue(const float* bias_real, const float* bias_imag, Epilogue* ep) {
+  if ((bias_real == nullptr) != (bias_imag == nullptr)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "bias_real and bias_imag must both be set or both null");
+  }
+  if (bias_real != nullptr && (!aligned16(bias_real) || !aligned16(bias_imag))) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "bias pointers must be 16-byte aligned");
+  }
+  ep->bias_r = bias_real;
+  ep->bias_i = bias_imag;
+  return CCV_OK;
+}
+
 }  // namespace
+
+int fprop_planar_impl(const float* x_real, const float* x_imag, const void* w_packed,
+                      const float* bias_real, const float* bias_imag, float* y_real,
+                      float* y_imag, const ccv_conv_shape* shape, int precision, void* workspace,
+                      size_t workspace_bytes, ccv_stream_t stream) {
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if ((rc = check_precision(precision)) != CCV_OK) return rc;
+  if (!x_real || !x_imag || !w_packed || !y_real || !y_imag) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  }
+  if (!aligned16(x_real) || !aligned16(x_imag) || !aligned16(w_packed) || !aligned16(y_real) ||
+      !aligned16(y_imag)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  }
+  Epilogue ep;
+  if ((rc = make_epilogue(bias_real, bias_imag, &ep)) != CCV_OK) return rc;
+  const size_t need = planar_required_bytes(pb, precision);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
+  }
+  if ((rc = check_device()) != CCV_OK) return rc;
+  if ((rc = check_status_clear()) != CCV_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  CounterScope scope(st);
+  void* sk = nullptr;
+  size_t sk_bytes = 0;
+  split_scratch(workspace, workspace_bytes, need, &sk, &sk_bytes);
+  const float* wp = static_cast<const float*>(w_packed);
+  if (precision == CCV_PRECISION_3XTF32) {
+    const size_t pl = plane_bytes_aligned(pb);
+    char* ws = static_cast<char*>(workspace);
+    float* hr = reinterpret_cast<float*>(ws);
+    float* hi = reinterpret_cast<float*>(ws + pl);
+    float* lr = reinterpret_cast<float*>(ws + 2 * pl);
+    float* li = reinterpret_cast<float*>(ws + 3 * pl);
+    if (use_layout_warps_planar(pb, precision)) {
+      rc = launch_fprop_planar_lw(x_real, x_imag, hr, hi, lr, li, wp, y_real, y_imag, pb, ep, sk,
+                                  sk_bytes, st);
+      if (rc != kNoCounterSet) return rc;
+    }
+    rc = launch_split_planes(x_real, x_imag, hr, hi, lr, li,
+                             static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c, st);
+    if (rc != CCV_OK) return rc;
+    return launch_fprop(hr, hi, lr, li, wp, y_real, y_imag, pb, precision, OUT_PLANAR_NHWC, ep, sk,
+                        sk_bytes, st);
+  }
+  return launch_fprop(x_real, x_imag, nullptr, nullptr, wp, y_real, y_imag, pb, precision,
+                      OUT_PLANAR_NHWC, ep, sk, sk_bytes, st);
+}
+
+int fprop_complex_impl(const void* x, const int64_t* x_strides, const void* w_packed,
+                       const float* bias_real, const float* bias_imag, void* y,
+                       const ccv_conv_shape* shape, int precision, void* workspace,
+                       size_t workspace_bytes, ccv_stream_t stream) {
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if ((rc = check_precision(precision)) != CCV_OK) return rc;
+  if (!x || !w_packed || !y) return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  // Dense NCHW input, unless strides say otherwise.
+  bool dense = true;
+  if (x_strides != nullptr) {
+    const int64_t hw = static_cast<int64_t>(pb.h) * pb.w;
+    dense = x_strides[0] == hw * pb.c && x_strides[1] == hw && x_strides[2] == pb.w &&
+            x_strides[3] == 1;
+    for (int i = 0; i < 4; ++i) {
+      if (x_strides[i] < 0) return set_error(CCV_ERR_INVALID_ARGUMENT, "negative input stride");
+    }
+  }
+  if (dense ? !aligned16(x) : (reinterpret_cast<uintptr_t>(x) & 7u) != 0) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT,
+                     "complex input must be 16-byte aligned (dense) or 8-byte aligned (strided)");
+  }
+  if (!aligned16(w_packed) || !aligned16(y)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  }
+  Epilogue ep;
+  if ((rc = make_epilogue(bias_real, bias_imag, &ep)) != CCV_OK) return rc;
+  const size_t need = complex_required_bytes(pb, precision);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace)) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
+  }
+  if ((rc = check_device()) != CCV_OK) return rc;
+  if ((rc = check_status_clear()) != CCV_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  CounterScope scope(st);
+  void* sk = nullptr;
+  size_t sk_bytes = 0;
+  split_scratch(workspace, workspace_bytes, need, &sk, &sk_bytes);
+  const size_t pl = plane_bytes_aligned(pb);
+  char* ws = static_cast<char*>(workspace);
+  float* xr = reinterpret_cast<float*>(ws);
+  float* xi = reinterpret_cast<float*>(ws + pl);
+  const bool split = precision == CCV_PRECISION_3XTF32;
+  float* lr = split ? reinterpret_cast<float*>(ws + 2 * pl) : nullptr;
+  float* li = split ? reinterpret_cast<float*>(ws + 3 * pl) : nullptr;
+  const float* wp = static_cast<const float*>(w_packed);
+  if (dense && use_layout_warps(pb, precision)) {
+    rc = launch_fprop_complex_lw(static_cast<const float*>(x), xr, xi, lr, li, wp,
+                                 static_cast<float*>(y), pb, precision, ep, sk, sk_bytes, st);
+    if (rc != kNoCounterSet) return rc;
+  }
+  rc = dense ? launch_nchw_complex_to_planar(static_cast<const float*>(x), xr, xi, lr, li, pb, st)
+             : launch_strided_complex_to_planar(static_cast<const float*>(x), x_strides, xr, xi,
+                                                lr, li, pb, st);
+  if (rc != CCV_OK) return rc;
+  return launch_fprop(xr, xi, lr, li, wp, static_cast<float*>(y), nullptr, pb, precision,
+                      OUT_COMPLEX_NCHW, ep, sk, sk_bytes, st);
+}
+
+}  // namespace ccv
+
+extern "C" {
 
 size_t ccv_fprop_planar_workspace_bytes(const ccv_conv_shape* shape, int precision) {
   Problem pb;
@@ -363,48 +676,45 @@ size_t ccv_fprop_complex_min_workspace_bytes(const ccv_conv_shape* shape, int pr
 int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_packed,
                      float* y_real, float* y_imag, const ccv_conv_shape* shape, int precision,
                      void* workspace, size_t workspace_bytes, ccv_stream_t stream) {
-  Problem pb;
-  int rc = make_problem(shape, &pb);
-  if (rc != CCV_OK) return rc;
-  if (precision != CCV_PRECISION_TF32 && precision != CCV_PRECISION_3XTF32) {
-    return set_error(CCV_ERR_INVALID_ARGUMENT, "unknown precision");
-  }
-  if (!x_real || !x_imag || !w_packed || !y_real || !y_imag) {
-    return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
-  }
-  if (!aligned16(x_real) || !aligned16(x_imag) || !aligned16(w_packed) || !aligned16(y_real) ||
-      !aligned16(y_imag)) {
-    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
-  }
-  const size_t need = planar_required_bytes(pb, precision);
-  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) {
-    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
-  }
-  if ((rc = check_device()) != CCV_OK) return rc;
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  void* sk = nullptr;
-  size_t sk_bytes = 0;
-  split_scratch(workspace, workspace_bytes, need, &sk, &sk_bytes);
-  if (precision == CCV_PRECISION_3XTF32) {
-    const size_t pl = plane_bytes_aligned(pb);
-    char* ws = static_cast<char*>(workspace);
-    float* hr = reinterpret_cast<float*>(ws);
-    float* hi = reinterpret_cast<float*>(ws + pl);
-    float* lr = reinterpret_cast<float*>(ws + 2 * pl);
-    float* li = reinterpret_cast<float*>(ws + 3 * pl);
-    if (use_layout_warps_planar(pb, precision)) {
-      return launch_fprop_planar_lw(x_real, x_imag, hr, hi, lr, li,
-                                    static_cast<const float*>(w_packed), y_real, y_imag, pb, sk,
-                                    sk_bytes, st);
-    }
-    rc = launch_split_planes(x_real, x_imag, hr, hi, lr, li,
-                             static_cast<size_t>(pb.n) * pb.h * pb.w * pb.c, st);
-    if (rc != CCV_OK) return rc;
-    return launch_fprop(hr, hi, lr, li, static_cast<const float*>(w_packed), y_real, y_imag, pb,
-                        precision, OUT_PLANAR_NHWC, sk, sk_bytes, st);
-  }
-  return launch_fprop(x_real, x_imag, nullptr, nullptr, static_cast<const float*>(w_packed),
-                      y_real, y_imag, pb, precision, OUT_PLANAR_NHWC, sk, sk_bytes, st);
+  ensure_status_mirror(reinterpret_cast<cudaStream_t>(stream));
+  return fprop_planar_impl(x_real, x_imag, w_packed, nullptr, nullptr, y_real, y_imag, shape,
+                           precision, workspace, workspace_bytes, stream);
+}
+
+int ccv_fprop_planar_bias(const float* x_real, const float* x_imag, const void* w_packed,
+                          const float* bias_real, const float* bias_imag, float* y_real,
+                          float* y_imag, const ccv_conv_shape* shape, int precision,
+                          void* workspace, size_t workspace_bytes, ccv_stream_t stream) {
+  ensure_status_mirror(reinterpret_cast<cudaStream_t>(stream));
+  return fprop_planar_impl(x_real, x_imag, w_packed, bias_real, bias_imag, y_real, y_imag, shape,
+                           precision, workspace, workspace_bytes, stream);
+}
+
+int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_conv_shape* shape,
+                      int precision, void* workspace, size_t workspace_bytes,
+                      ccv_stream_t stream) {
+  ensure_status_mirror(reinterpret_cast<cudaStream_t>(stream));
+  return fprop_complex_impl(x, nullptr, w_packed, nullptr, nullptr, y, shape, precision,
+                            workspace, workspace_bytes, stream);
+}
+
+int ccv_fprop_complex_bias(const void* x, const void* w_packed, const float* bias_real,
+                           const float* bias_imag, void* y, const ccv_conv_shape* shape,
+                           int precision, void* workspace, size_t workspace_bytes,
+                           ccv_stream_t stream) {
+  ensure_status_mirror(reinterpret_cast<cudaStream_t>(stream));
+  return fprop_complex_impl(x, nullptr, w_packed, bias_real, bias_imag, y, shape, precision,
+                            workspace, workspace_bytes, stream);
+}
+
+int ccv_fprop_complex_strided(const void* x, const int64_t* x_strides, const void* w_packed,
+                              const float* bias_real, const float* bias_imag, void* y,
+                              const ccv_conv_shape* shape, int precision, void* workspace,
+                              size_t workspace_bytes, ccv_stream_t stream) {
+  if (x_strides == nullptr) return set_error(CCV_ERR_INVALID_ARGUMENT, "null strides");
+  ensure_status_mirror(reinterpret_cast<cudaStream_t>(stream));
+  return fprop_complex_impl(x, x_strides, w_packed, bias_real, bias_imag, y, shape, precision,
+                            workspace, workspace_bytes, stream);
 }
 
 int ccv_fprop_planar_to_complex(const float* x_real, const float* x_imag, const void* w_packed,
@@ -413,9 +723,7 @@ int ccv_fprop_planar_to_complex(const float* x_real, const float* x_imag, const 
   Problem pb;
   int rc = make_problem(shape, &pb);
   if (rc != CCV_OK) return rc;
-  if (precision != CCV_PRECISION_TF32 && precision != CCV_PRECISION_3XTF32) {
-    return set_error(CCV_ERR_INVALID_ARGUMENT, "unknown precision");
-  }
+  if ((rc = check_precision(precision)) != CCV_OK) return rc;
   if (!x_real || !x_imag || !w_packed || !y) {
     return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
   }
@@ -426,8 +734,11 @@ int ccv_fprop_planar_to_complex(const float* x_real, const float* x_imag, const 
   if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) {
     return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
   }
-  if ((rc = check_device()) != CCV_OK) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ensure_status_mirror(st);
+  if ((rc = check_device()) != CCV_OK) return rc;
+  if ((rc = check_status_clear()) != CCV_OK) return rc;
+  CounterScope scope(st);
   void* sk = nullptr;
   size_t sk_bytes = 0;
   split_scratch(workspace, workspace_bytes, need, &sk, &sk_bytes);
@@ -451,57 +762,7 @@ int ccv_fprop_planar_to_complex(const float* x_real, const float* x_imag, const 
     li = wli;
   }
   return launch_fprop(xr, xi, lr, li, static_cast<const float*>(w_packed), static_cast<float*>(y),
-                      nullptr, pb, precision, OUT_COMPLEX_NCHW, sk, sk_bytes, st);
-}
-
-int ccv_fprop_complex(const void* x, const void* w_packed, void* y, const ccv_conv_shape* shape,
-                      int precision, void* workspace, size_t workspace_bytes,
-                      ccv_stream_t stream) {
-  Problem pb;
-  int rc = make_problem(shape, &pb);
-  if (rc != CCV_OK) return rc;
-  if (precision != CCV_PRECISION_TF32 && precision != CCV_PRECISION_3XTF32) {
-    return set_error(CCV_ERR_INVALID_ARGUMENT, "unknown precision");
-  }
-  if (!x || !w_packed || !y) return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
-  if (!aligned16(x) || !aligned16(w_packed) || !aligned16(y)) {
-    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
-  }
-  const size_t need = complex_required_bytes(pb, precision);
-  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) {
-    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
-  }
-  if ((rc = check_device()) != CCV_OK) return rc;
-  void* sk = nullptr;
-  size_t sk_bytes = 0;
-  split_scratch(workspace, workspace_bytes, need, &sk, &sk_bytes);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (need == 0) {
-    return launch_fprop_fused_complex(static_cast<const float*>(x),
-                                      static_cast<const float*>(w_packed), static_cast<float*>(y),
-                                      pb, precision, sk, sk_bytes, st);
-  }
-  const size_t pl = plane_bytes_aligned(pb);
-  char* ws = static_cast<char*>(workspace);
-  float* xr = reinterpret_cast<float*>(ws);
-  float* xi = reinterpret_cast<float*>(ws + pl);
-  if (use_in_kernel_conversion(pb, precision)) {
-    return launch_fprop_complex_cvt(static_cast<const float*>(x), xr, xi,
-                                    static_cast<const float*>(w_packed), static_cast<float*>(y),
-                                    pb, st);
-  }
-  const bool split = precision == CCV_PRECISION_3XTF32;
-  float* lr = split ? reinterpret_cast<float*>(ws + 2 * pl) : nullptr;
-  float* li = split ? reinterpret_cast<float*>(ws + 3 * pl) : nullptr;
-  if (use_layout_warps(pb, precision)) {
-    return launch_fprop_complex_lw(static_cast<const float*>(x), xr, xi, lr, li,
-                                   static_cast<const float*>(w_packed), static_cast<float*>(y), pb,
-                                   precision, sk, sk_bytes, st);
-  }
-  rc = launch_nchw_complex_to_planar(static_cast<const float*>(x), xr, xi, lr, li, pb, st);
-  if (rc != CCV_OK) return rc;
-  return launch_fprop(xr, xi, lr, li, static_cast<const float*>(w_packed), static_cast<float*>(y),
-                      nullptr, pb, precision, OUT_COMPLEX_NCHW, sk, sk_bytes, st);
+                      nullptr, pb, precision, OUT_COMPLEX_NCHW, Epilogue(), sk, sk_bytes, st);
 }
 
 int ccv_fprop_kernel_launches(const ccv_conv_shape* shape, int precision, int complex_input,
@@ -566,18 +827,32 @@ int ccv_clear_device_status(void) {
   const int zero = 0;
   cudaError_t e = cudaMemcpyToSymbol(g_ccv_status, &zero, sizeof(int));
   if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyToSymbol(status)");
-  // A kernel that gave up may have left stream-K counters counted.
-  static const std::vector<unsigned> zeros(static_cast<size_t>(kSkRing) * kSkCounterWords, 0u);
+  // A kernel that gave up may have left counters counted.
+  static const std::vector<unsigned> zeros(static_cast<size_t>(kCounterSets) * kSkCounterWords,
+                                           0u);
   e = cudaMemcpyToSymbol(g_ccv_sk_counters, zeros.data(), zeros.size() * sizeof(unsigned));
-  if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyToSymbol(stream-K counters)");
+  if (e != cudaSuccess) return cuda_error(e, "cudaMemcpyToSymbol(counter sets)");
+  int dev = 0;
+  if (current_device(&dev) == CCV_OK && g_status_host[dev] != nullptr) *g_status_host[dev] = 0;
   return CCV_OK;
 }
 
 int ccv_selftest_bounded_wait(int* status_dev, ccv_stream_t stream) {
-  if (status_dev == nullptr) return set_error(CCV_ERR_INVALID_ARGUMENT, "status is null");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ensure_status_mirror(st);
   const int rc = check_device();
   if (rc != CCV_OK) return rc;
-  return launch_selftest_wait(status_dev, reinterpret_cast<cudaStream_t>(stream));
+  if (status_dev == nullptr) {
+    int* lib = device_status_ptr();
+    if (lib == nullptr) return CCV_ERR_CUDA;
+    return launch_selftest_wait(lib, true, st);
+  }
+  return launch_selftest_wait(status_dev, false, st);
+}
+
+int ccv_reload_config(void) {
+  reload_knobs();
+  return CCV_OK;
 }
 
 }  // extern "C"

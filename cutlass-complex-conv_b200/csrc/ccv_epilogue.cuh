@@ -42,11 +42,12 @@ __device__ __forceinline__ bool tile_row_pixel(const FpropParams& prm, int half,
 }
 
 // Stores channels [kb, kb + W) of pixel (img, op, oq) from vr (real) and
-// vi (imaginary) as fp32 NPQK planes or complex64 NKPQ (W % 4 == 0).
+// vi (imaginary), final sums, as fp32 NPQK planes or complex64 NKPQ
+// (W % 4 == 0), adding the launch's complex bias if it has one.
 template <bool OUT_COMPLEX, int W>
 __device__ __forceinline__ void store_chunk(const FpropParams& prm, int kb, int img, int op,
-                                            int oq, const uint32_t (&vr)[W],
-                                            const uint32_t (&vi)[W]) {
+                                            int oq, uint32_t (&vr)[W], uint32_t (&vi)[W]) {
+  add_bias<W>(prm, kb, vr, vi);
   if constexpr (!OUT_COMPLEX) {
     const long long pix = (static_cast<long long>(img) * prm.p + op) * prm.q + oq;
     float* dr = prm.y0 + pix * prm.k + kb;
@@ -119,6 +120,7 @@ __device__ __forceinline__ void store_accumulator_tma(const FpropParams& prm, ui
     ptx::tmem_wait_ld();
     const bool go = valid && k0 + ch < prm.k;
     if (!go) continue;
+    add_bias<16>(prm, k0 + ch, vr, vi);
     // The previous chunk's stores have read the buffer.
     if (lane == 0) ptx::bulk_wait_read_all();
     __syncwarp();

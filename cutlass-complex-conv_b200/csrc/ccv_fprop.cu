@@ -35,7 +35,6 @@
 #include <mutex>
 
 #include "ccv_internal.h"
-#include "ccv_cvt_role.cuh"
 #include "ccv_fprop_common.cuh"
 #include "ccv_layout_role.cuh"
 #include "ccv_ptx.cuh"
@@ -296,6 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tmem_wait_ld();
         const int kb = k0 + ch;
         if (valid && kb < prm.k) {
+          add_bias<32>(prm, kb, vr, vi);
           if constexpr (!OUT_COMPLEX) {
             float* dr = prm.y0 + pix * prm.k + kb;
             float* di = prm.y1 + pix * prm.k + kb;
@@ -394,6 +394,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int kb = k0 + 4 * q;
       if (!valid || kb >= prm.k) continue;
+      if (prm.bias_r != nullptr) {
+        const float4 br = __ldg(reinterpret_cast<const float4*>(prm.bias_r + kb));
+        const float4 bi = __ldg(reinterpret_cast<const float4*>(prm.bias_i + kb));
+        sr.x += br.x; sr.y += br.y; sr.z += br.z; sr.w += br.w;
+        si.x += bi.x; si.y += bi.y; si.z += bi.z; si.w += bi.w;
+      }
       const long long pix = (static_cast<long long>(img) * prm.p + op) * prm.q + oq;
       if constexpr (!OUT_COMPLEX) {
         *reinterpret_cast<float4*>(prm.y0 + pix * prm.k + kb) = sr;
@@ -494,11 +500,8 @@ enum KernelFamily { kSingleCta = 0, kPairTap = 1, kPairHalo = 2 };
 // 13.5 -> 10.9 us; deeper layers keep 128, e.g. 128->256 @ 14x14 14.5 us vs
 // 20.1 us with 64).
 int single_cta_kt(const Problem& pb, const Tiling& t) {
-  const char* env = getenv("CCV_KT");
-  if (env != nullptr) {
-    const int v = atoi(env);
-    if (v == 32 || v == 64 || v == 128) return v;
-  }
+  const int v = knobs().kt;
+  if (v == 32 || v == 64 || v == 128) return v;
   if (t.kt == 128 && pb.k <= 128 && t.tiles_m * 16 < device_sm_count()) return 64;
   return t.kt;
 }
@@ -511,13 +514,11 @@ int single_cta_kt(const Problem& pb, const Tiling& t) {
 // Testing/benchmarking knobs: CCV_FORCE_KERNEL=1|2 pins single-CTA / pair,
 // CCV_HALO=0|1 pins the pair variant.
 KernelFamily choose_family(const Problem& pb, bool split, const Tiling& t, Tiling* th) {
-  const char* force_env = getenv("CCV_FORCE_KERNEL");
-  const int forced = force_env ? atoi(force_env) : 0;
+  const int forced = knobs().force_kernel;
   const bool use_pair =
       split || forced == 2 || (forced != 1 && pair_tiles(t) * 2 >= device_sm_count());
   if (!use_pair) return kSingleCta;
-  const char* halo_env = getenv("CCV_HALO");
-  const int halo_forced = halo_env ? atoi(halo_env) : -1;
+  const int halo_forced = knobs().halo;
   if (halo_forced != 0 && halo_applicable(pb)) {
     *th = choose_halo_tiling(pb);
     const long long rows_tap = static_cast<long long>(t.tiles_m) * t.tiles_n;
@@ -529,25 +530,8 @@ KernelFamily choose_family(const Problem& pb, bool split, const Tiling& t, Tilin
 
 }  // namespace
 
-// forward() (complex64 in and out) on the complex-direct kernel: TF32,
-// problems the pair kernels serve, stride 1 with an odd filter width.  Opt
-// in with CCV_CD=1: measured on B200 it is slower than the converter-warp
-// halo kernel on every BASELINE layer (b64 128->128 56x56: 548 vs 441 us;
-// 1x1 256->1024 28x28: 217-303 vs 122 us), because all column slots of a
-// channel block must be resident (short weight ring) and the 4x16 box loads
-// 1.5x halo rows.
-bool use_complex_direct(const Problem& pb, int precision) {
-  if (precision != CCV_PRECISION_TF32) return false;
-  const char* env = getenv("CCV_CD");
-  if (env == nullptr || atoi(env) != 1) return false;
-  if (!cd_applicable(pb)) return false;
-  const Tiling t = choose_tiling(pb);
-  Tiling th;
-  return choose_family(pb, false, t, &th) != kSingleCta;
-}
-
 size_t split_workspace_bytes(const Problem& pb, int precision, bool complex_input) {
-  if (complex_input && use_complex_direct(pb, precision)) return 0;
+  (void)complex_input;
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;
@@ -564,55 +548,9 @@ size_t split_workspace_bytes(const Problem& pb, int precision, bool complex_inpu
   }
 }
 
-// The halo kernel with converter warps (one launch, no workspace) or a
-// layout pass plus the planar-input halo kernel.  Opt in with CCV_FUSED=1:
-// measured on B200 the layout pass (~7 TB/s) plus the TMA-fed kernel is
-// faster on every stride-1 layer (b64 128->128 56x56: 420 vs 440 us; b32
-// 64->64 320x320: 2.76 vs 2.88 ms TF32, 7.11 vs 8.24 ms 3xTF32): the
-// converter warps' scattered 8-byte loads (each input element read once per
-// filter column) cost more than one streaming pass.
-bool use_converter_warps(const Problem& pb, int precision, const Tiling& th) {
-  (void)precision;
-  if (!halo_fused_supported(pb, th)) return false;
-  const char* env = getenv("CCV_FUSED");
-  return env != nullptr && atoi(env) == 1;
-}
+bool use_layout_warps(const Problem& pb, int precision) { return layout_warps_pay(pb, precision); }
 
-bool fused_complex_available(const Problem& pb, int precision) {
-  if (use_complex_direct(pb, precision)) return true;
-  const Tiling t = choose_tiling(pb);
-  Tiling th;
-  return choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th) == kPairHalo &&
-         use_converter_warps(pb, precision, th);
-}
-
-bool use_in_kernel_conversion(const Problem& pb, int precision) {
-  if (precision != CCV_PRECISION_TF32) return false;
-  // Opt-in (CCV_CVT=1): a converter SM moves only ~20-25 GB/s through its
-  // TMA ring, so the converting clusters hold back the others; the separate
-  // layout pass runs at the HBM copy rate.
-  const char* env = getenv("CCV_CVT");
-  if (env == nullptr || atoi(env) != 1) return false;
-  if (use_complex_direct(pb, precision)) return false;
-  const Tiling t = choose_tiling(pb);
-  Tiling th;
-  if (choose_family(pb, false, t, &th) != kPairHalo) return false;
-  if (use_converter_warps(pb, precision, th)) return false;
-  return (pb.w & 1) == 0 && pb.n <= kSkCounterWords - kCvtFlag0;
-}
-
-int launch_fprop_complex_cvt(const float* x, float* xr, float* xi, const float* w_packed, float* y,
-                             const Problem& pb, cudaStream_t stream) {
-  const Tiling t = choose_tiling(pb);
-  Tiling th;
-  if (choose_family(pb, false, t, &th) != kPairHalo) {
-    return set_error(CCV_ERR_UNSUPPORTED, "no in-kernel conversion for this problem");
-  }
-  return launch_fprop_pair_halo(xr, xi, nullptr, nullptr, nullptr, false, w_packed, y, nullptr, pb,
-                                th, OUT_COMPLEX_NCHW, nullptr, 0, stream, x);
-}
-
-bool use_layout_warps(const Problem& pb, int precision) {
+bool layout_warps_pay(const Problem& pb, int precision) {
   // CCV_LW=0: never; CCV_LW=1: wherever a pair kernel runs; unset: when
   //   * the grid runs at least two waves of tiles (below that the first
   //     wave needs most images at once),
@@ -623,17 +561,7 @@ bool use_layout_warps(const Problem& pb, int precision) {
   //     pass (the layout warps convert ~1 TB/s; below that - stride 2 at
   //     C = 64 - they hold the MMAs back and a pass at the copy rate wins).
   // Measured on B200 over the BASELINE layers and the batch sweep.
-  if (use_complex_direct(pb, precision) || use_in_kernel_conversion(pb, precision)) return false;
-  const Tiling t = choose_tiling(pb);
-  Tiling th;
-  const int fam = choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th);
-  if (fam == kPairHalo && use_converter_warps(pb, precision, th)) return false;
-  return layout_warps_pay(pb, precision);
-}
-
-bool layout_warps_pay(const Problem& pb, int precision) {
-  const char* env = getenv("CCV_LW");
-  const int mode = env != nullptr ? atoi(env) : -1;
+  const int mode = knobs().lw;
   if (mode == 0) return false;
   const Tiling t = choose_tiling(pb);
   Tiling th;
@@ -662,18 +590,18 @@ bool use_layout_warps_planar(const Problem& pb, int precision) {
 
 int launch_fprop_planar_lw(const float* x_real, const float* x_imag, float* hr, float* hi,
                            float* lr, float* li, const float* w_packed, float* y_real,
-                           float* y_imag, const Problem& pb, void* ws, size_t ws_bytes,
-                           cudaStream_t stream) {
+                           float* y_imag, const Problem& pb, const Epilogue& ep, void* ws,
+                           size_t ws_bytes, cudaStream_t stream) {
   const Tiling t = choose_tiling(pb);
   Tiling th;
   switch (choose_family(pb, true, t, &th)) {
     case kPairHalo:
-      return launch_fprop_pair_halo(hr, hi, lr, li, nullptr, true, w_packed, y_real, y_imag, pb,
-                                    th, OUT_PLANAR_NHWC, ws, ws_bytes, stream, nullptr, true,
-                                    x_real, x_imag);
+      return launch_fprop_pair_halo(hr, hi, lr, li, true, w_packed, y_real, y_imag, pb, th,
+                                    OUT_PLANAR_NHWC, ep, ws, ws_bytes, stream, nullptr, x_real,
+                                    x_imag);
     case kPairTap:
       return launch_fprop_pair(hr, hi, lr, li, w_packed, y_real, y_imag, pb, t, OUT_PLANAR_NHWC,
-                               ws, ws_bytes, stream, nullptr, x_real, x_imag);
+                               ep, ws, ws_bytes, stream, nullptr, x_real, x_imag);
     default:
       return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
   }
@@ -681,39 +609,33 @@ int launch_fprop_planar_lw(const float* x_real, const float* x_imag, float* hr, 
 
 int launch_fprop_complex_lw(const float* x, float* xr, float* xi, float* xr_lo, float* xi_lo,
                             const float* w_packed, float* y, const Problem& pb, int precision,
-                            void* ws, size_t ws_bytes, cudaStream_t stream) {
+                            const Epilogue& ep, void* ws, size_t ws_bytes, cudaStream_t stream) {
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;
   switch (choose_family(pb, split, t, &th)) {
     case kPairHalo:
-      return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, nullptr, split, w_packed, y, nullptr,
-                                    pb, th, OUT_COMPLEX_NCHW, ws, ws_bytes, stream, x, true);
+      return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, split, w_packed, y, nullptr, pb, th,
+                                    OUT_COMPLEX_NCHW, ep, ws, ws_bytes, stream, x);
     case kPairTap:
       return launch_fprop_pair(xr, xi, split ? xr_lo : nullptr, split ? xi_lo : nullptr, w_packed,
-                               y, nullptr, pb, t, OUT_COMPLEX_NCHW, ws, ws_bytes, stream, x);
+                               y, nullptr, pb, t, OUT_COMPLEX_NCHW, ep, ws, ws_bytes, stream, x);
     default:
       return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
   }
 }
 
 const char* complex_kernel_name(const Problem& pb, int precision) {
-  if (use_complex_direct(pb, precision)) return "complex_direct_pair";
-  if (use_in_kernel_conversion(pb, precision)) return "halo_pair_converter_clusters";
-  if (use_layout_warps(pb, precision)) {
-    const Tiling t = choose_tiling(pb);
-    Tiling th;
-    return choose_family(pb, precision == CCV_PRECISION_3XTF32, t, &th) == kPairHalo
-               ? "halo_pair_layout_warps"
-               : "tap_pair_layout_warps";
-  }
   const bool split = precision == CCV_PRECISION_3XTF32;
   const Tiling t = choose_tiling(pb);
   Tiling th;
-  switch (choose_family(pb, split, t, &th)) {
+  const int fam = choose_family(pb, split, t, &th);
+  if (use_layout_warps(pb, precision)) {
+    return fam == kPairHalo ? "halo_pair_layout_warps" : "tap_pair_layout_warps";
+  }
+  switch (fam) {
     case kPairHalo:
-      return use_converter_warps(pb, precision, th) ? "halo_pair_converter_warps"
-                                                    : "layout_pass+halo_pair";
+      return "layout_pass+halo_pair";
     case kPairTap:
       return "layout_pass+tap_pair";
     default:
@@ -721,25 +643,10 @@ const char* complex_kernel_name(const Problem& pb, int precision) {
   }
 }
 
-int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
-                               const Problem& pb, int precision, void* ws, size_t ws_bytes,
-                               cudaStream_t stream) {
-  if (use_complex_direct(pb, precision)) {
-    return launch_fprop_cd(xc, w_packed, y, pb, ws, ws_bytes, stream);
-  }
-  const bool split = precision == CCV_PRECISION_3XTF32;
-  const Tiling t = choose_tiling(pb);
-  Tiling th;
-  if (choose_family(pb, split, t, &th) != kPairHalo || !use_converter_warps(pb, precision, th)) {
-    return set_error(CCV_ERR_UNSUPPORTED, "no fused complex kernel for this problem");
-  }
-  return launch_fprop_pair_halo(nullptr, nullptr, nullptr, nullptr, xc, split, w_packed, y,
-                                nullptr, pb, th, OUT_COMPLEX_NCHW, ws, ws_bytes, stream);
-}
-
 int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                  const float* w_packed, float* y0, float* y1, const Problem& pb, int precision,
-                 OutLayout out_layout, void* ws, size_t ws_bytes, cudaStream_t stream) {
+                 OutLayout out_layout, const Epilogue& ep, void* ws, size_t ws_bytes,
+                 cudaStream_t stream) {
   const bool split = precision == CCV_PRECISION_3XTF32;
   if (split && (xr_lo == nullptr || xi_lo == nullptr)) {
     return set_error(CCV_ERR_INVALID_ARGUMENT, "3xTF32 needs the activation remainder planes");
@@ -752,10 +659,10 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
   Tiling th;
   switch (choose_family(pb, split, t, &th)) {
     case kPairHalo:
-      return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, nullptr, split, w_packed, y0, y1, pb,
-                                    th, out_layout, ws, ws_bytes, stream);
+      return launch_fprop_pair_halo(xr, xi, xr_lo, xi_lo, split, w_packed, y0, y1, pb, th,
+                                    out_layout, ep, ws, ws_bytes, stream);
     case kPairTap:
-      return launch_fprop_pair(xr, xi, xr_lo, xi_lo, w_packed, y0, y1, pb, t, out_layout, ws,
+      return launch_fprop_pair(xr, xi, xr_lo, xi_lo, w_packed, y0, y1, pb, t, out_layout, ep, ws,
                                ws_bytes, stream);
     default:
       break;
@@ -766,6 +673,7 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;
   prm.y1 = y1;
+  set_epilogue(prm, ep);
   prm.status = device_status_ptr();
   if (prm.status == nullptr) return CCV_ERR_CUDA;
   prm.n = pb.n; prm.h = pb.h; prm.w = pb.w; prm.c = pb.c; prm.k = pb.k;
@@ -821,8 +729,7 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
     const long long per_tile = sms / std::max<long long>(grid, 1);
     want_split = static_cast<int>(std::min<long long>(std::min<long long>(per_tile, 16),
                                                       prm.ksteps));
-    const char* env = getenv("CCV_SPLITK");
-    if (env != nullptr) want_split = std::min(want_split, std::max(1, atoi(env)));
+    if (knobs().splitk > 0) want_split = std::min(want_split, knobs().splitk);
     if (want_split < 2) want_split = 1;
   }
   prm.splits = 1;
@@ -838,7 +745,7 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
 
 // ------------------------------------------------------------------ self-test
 namespace {
-__global__ void ccv_selftest_wait_kernel(int* status) {
+__global__ void ccv_selftest_wait_kernel(int* status, int mirror) {
   __shared__ uint64_t bar;
   const uint32_t b = ptx::smem_u32(&bar);
   if (threadIdx.x == 0) {
@@ -848,14 +755,15 @@ __global__ void ccv_selftest_wait_kernel(int* status) {
   __syncthreads();
   if (threadIdx.x == 0) {
     // Nothing ever arrives on `bar`: the bounded wait must give up.
-    const bool ok = ptx::mbar_wait_bounded(b, 0, status, CCV_ERR_DEVICE_TIMEOUT);
+    const bool ok = mirror ? ptx::mbar_wait_bounded<false, true>(b, 0, status, CCV_ERR_DEVICE_TIMEOUT)
+                           : ptx::mbar_wait_bounded<false, false>(b, 0, status, CCV_ERR_DEVICE_TIMEOUT);
     if (ok) atomicExch(status, -1);  // impossible completion is itself an error
   }
 }
 }  // namespace
 
-int launch_selftest_wait(int* status_dev, cudaStream_t stream) {
-  ccv_selftest_wait_kernel<<<1, 32, 0, stream>>>(status_dev);
+int launch_selftest_wait(int* status_dev, bool mirror, cudaStream_t stream) {
+  ccv_selftest_wait_kernel<<<1, 32, 0, stream>>>(status_dev, mirror ? 1 : 0);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "selftest kernel launch");
   return CCV_OK;

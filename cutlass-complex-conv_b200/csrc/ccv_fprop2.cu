@@ -363,13 +363,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32
       unsigned old;
       asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
                    : "=r"(old)
-                   : "l"(prm.cvt_ctrs + kLwDone)
+                   : "l"(prm.lw_ctrs + kLwDone)
                    : "memory");
       if (old == 2u * static_cast<unsigned>(ncl) - 1u) {
-        for (int i = 0; i < prm.n; ++i) prm.cvt_ctrs[kLwFlag0 + i] = 0u;
-        prm.cvt_ctrs[kLwTicket] = 0u;
-        prm.cvt_ctrs[kLwPrefixTicket] = 0u;
-        prm.cvt_ctrs[kLwDone] = 0u;
+        for (int i = 0; i < prm.n; ++i) prm.lw_ctrs[kLwFlag0 + i] = 0u;
+        prm.lw_ctrs[kLwTicket] = 0u;
+        prm.lw_ctrs[kLwPrefixTicket] = 0u;
+        prm.lw_ctrs[kLwDone] = 0u;
         __threadfence();
       }
     }
@@ -470,8 +470,7 @@ size_t pair_split_workspace_bytes(int kt, int tiles, int slots) {
 
 int encode_planar_out_maps(FpropParams& prm, float* y0, float* y1, bool flat) {
   prm.out_tma = 0;
-  const char* env = getenv("CCV_TMA_STORE");
-  if (env != nullptr && atoi(env) == 0) return CCV_OK;
+  if (knobs().tma_store == 0) return CCV_OK;
   const uint64_t kb = static_cast<uint64_t>(prm.k) * 4;
   int rc;
   if (flat) {
@@ -512,13 +511,12 @@ int encode_planar_out_maps(FpropParams& prm, float* y0, float* y1, bool flat) {
 int cluster_cap(int max_clusters) {
   // CCV_MAX_CLUSTERS=n caps the persistent grid (testing knob: exercises the
   // stream-K split on small problems).
-  const char* env = getenv("CCV_MAX_CLUSTERS");
-  if (env != nullptr && atoi(env) > 0) return std::min(max_clusters, atoi(env));
-  return max_clusters;
+  const int cap = knobs().max_clusters;
+  return cap > 0 ? std::min(max_clusters, cap) : max_clusters;
 }
 
 int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
-                  int min_gain_pct) {
+                  cudaStream_t stream, int min_gain_pct) {
   prm.slots_per_tile = slots;
   prm.sk_start = prm.num_tiles;
   prm.sk_slots = 0;
@@ -527,8 +525,7 @@ int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, s
   prm.split_count = nullptr;
   // CCV_STREAMK=0 disables the split, =1 takes it whenever it is possible
   // (testing knob); by default the model below decides.
-  const char* env = getenv("CCV_STREAMK");
-  const int mode = env ? atoi(env) : -1;
+  const int mode = knobs().streamk;
   if (mode == 0 || ws == nullptr || clusters < 2 || slots < kMinSkSlots) return 0;
   const int T = prm.num_tiles;
   const int r = T % clusters;
@@ -552,7 +549,7 @@ int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, s
   const size_t pbytes = partial_bytes(gs, kt);
   if (ws_bytes < pbytes || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return 0;
   if (r * 8 > kSkCounterWords) return 0;
-  unsigned* counters = stream_k_counters();
+  unsigned* counters = acquire_counter_set(stream);
   if (counters == nullptr) return 0;
   prm.sk_start = T - r;
   prm.sk_slots = X;
@@ -564,23 +561,25 @@ int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, s
 
 int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
                     cudaStream_t stream, int* rc, int min_gain_pct) {
-  (void)stream;
   *rc = CCV_OK;
   clusters = std::max(1, clusters);
-  // Stream-K counters come zeroed from the library's ring (no memset).
-  if (plan_stream_k(prm, clusters, slots, kt, ws, ws_bytes, min_gain_pct) > 0) return clusters;
+  // Stream-K counters come zeroed from the library's counter sets (no memset).
+  if (plan_stream_k(prm, clusters, slots, kt, ws, ws_bytes, stream, min_gain_pct) > 0) {
+    return clusters;
+  }
   return std::max(1, std::min(prm.num_tiles, clusters));
 }
 
 int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                       const float* w_packed, float* y0, float* y1, const Problem& pb,
-                      const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
-                      cudaStream_t stream, const float* lw_src, const float* lw_pr,
-                      const float* lw_pi) {
+                      const Tiling& t, OutLayout out_layout, const Epilogue& ep, void* ws,
+                      size_t ws_bytes, cudaStream_t stream, const float* lw_src,
+                      const float* lw_pr, const float* lw_pi) {
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;
   prm.y1 = y1;
+  set_epilogue(prm, ep);
   prm.status = device_status_ptr();
   if (prm.status == nullptr) return CCV_ERR_CUDA;
   prm.n = pb.n; prm.h = pb.h; prm.w = pb.w; prm.c = pb.c; prm.k = pb.k;
@@ -649,8 +648,8 @@ int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, cons
     prm.lw_xi = const_cast<float*>(xi);
     prm.lw_xr_lo = const_cast<float*>(xr_lo);
     prm.lw_xi_lo = const_cast<float*>(xi_lo);
-    prm.cvt_ctrs = stream_k_counters();
-    if (prm.cvt_ctrs == nullptr) return CCV_ERR_CUDA;
+    prm.lw_ctrs = acquire_counter_set(stream);
+    if (prm.lw_ctrs == nullptr) return kNoCounterSet;
     if (cplx) {
       return t.flat ? launch2_kt<true, true, true>(t.kt, prm, ws, ws_bytes, stream)
                     : launch2_kt<false, true, true>(t.kt, prm, ws, ws_bytes, stream);

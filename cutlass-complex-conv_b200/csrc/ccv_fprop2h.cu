@@ -11,11 +11,6 @@
 // to (box_p+R-1)*box_q/R.  Weights stream per tap as in the tap kernel.
 // Two rings: A slots (one per (cb, s)) and weight stages (one per tap).
 //
-// IN_COMPLEX: eight extra converter warps per CTA fill the A slots from the
-// complex64 NCHW input (de-interleave + NCHW->K-major transpose in the
-// producer), so forward() needs no separate layout pass; they release each
-// slot to the even CTA's barrier with a cluster-scope release.
-//
 // LW (layout warps): two extra warps per CTA convert the whole complex64
 // NCHW batch into fp32 NHWC planes in the workspace, image by image, while
 // the pair MMA runs; the producer waits for an image's planes before its
@@ -27,8 +22,6 @@
 #include <cmath>
 #include <mutex>
 
-#include "ccv_convert.cuh"
-#include "ccv_cvt_role.cuh"
 #include "ccv_epilogue.cuh"
 #include "ccv_fprop_common.cuh"
 #include "ccv_internal.h"
@@ -45,8 +38,8 @@ constexpr int kRowH = kCH * 4;        // 128-byte rows
 constexpr int kMaxASlots = 4;
 constexpr int kMaxWStages = 8;
 constexpr int kBarBytes = 1024;       // barrier block at the start of the carve-out
-constexpr int kLwTmaBar = 100;        // TMA prefix: kCvtInBufs barriers, then 19 words
-static_assert(8 * (kLwTmaBar + kCvtInBufs) + 4 * (kCvtInBufs + kLwTmaMaxImages) <= kBarBytes,
+constexpr int kLwTmaBar = 100;        // TMA prefix: kLwBoxBufs barriers, then 20 words
+static_assert(8 * (kLwTmaBar + kLwBoxBufs) + 4 * (kLwBoxBufs + kLwTmaMaxImages) <= kBarBytes,
               "barrier block overflow");
 static_assert(8 * (32 + 4 * kStageBufs) <= kBarBytes, "barrier block overflow");
 constexpr int kSmemDataBudget = 232448 - kBarBytes - 1024;  // minus alignment slack
@@ -63,18 +56,14 @@ struct CfgH {
   static_assert(2 * kTileCols <= 512, "TMEM");
 };
 
-constexpr int kConvWarps = 8;
-constexpr int kConvUnits = 5;   // (32-row block, channel quad) units per converter lane
-
-template <bool IN_COMPLEX, bool LW>
+template <bool LW>
 constexpr int halo_threads() {
-  return kThreadsH + (IN_COMPLEX ? 32 * kConvWarps : 0) + (LW ? 32 * kLwWarps : 0);
+  return kThreadsH + (LW ? 32 * kLwWarps : 0);
 }
 
-template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX, int NSUB, bool LW>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMPLEX, LW>(), 1)
+template <int KT, bool OUT_COMPLEX, int NSUB, bool LW>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<LW>(), 1)
     ccv_fprop2h_tf32_kernel(const __grid_constant__ FpropParams prm) {
-  static_assert(!(IN_COMPLEX && LW), "one conversion scheme per kernel");
   using C = CfgH<KT, NSUB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>(
@@ -115,9 +104,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
   if (threadIdx.x == 0) {
     flags[1] = 0;
     for (int i = 0; i < kMaxASlots; ++i) {
-      // Fused complex path: one arrival per converter warp of both CTAs.
-      // (Converter clusters use afull(0..2) for their input ring.)
-      ptx::mbar_init(afull(i), IN_COMPLEX ? 2 * kConvWarps : 1);
+      ptx::mbar_init(afull(i), 1);
       ptx::mbar_init(aempty(i), 1);
     }
     for (int i = 0; i < SW; ++i) {
@@ -130,18 +117,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
     }
     ptx::mbar_init(done_bar, 1);
     if (LW) {
-      for (int i = 0; i < kCvtInBufs; ++i) ptx::mbar_init(bar_base + 8u * (kLwTmaBar + i), 1);
+      for (int i = 0; i < kLwBoxBufs; ++i) ptx::mbar_init(bar_base + 8u * (kLwTmaBar + i), 1);
     }
     for (int i = 0; i < 4 * kStageBufs; ++i) ptx::mbar_init(stage_bar0 + 8u * i, 1);
     ptx::fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
-    if (!IN_COMPLEX) {
-      ptx::prefetch_tmap(&prm.tm_xr);
-      ptx::prefetch_tmap(&prm.tm_xi);
-    }
+    ptx::prefetch_tmap(&prm.tm_xr);
+    ptx::prefetch_tmap(&prm.tm_xi);
     ptx::prefetch_tmap(&prm.tm_w);
-    if (!IN_COMPLEX && prm.passes > 1) {
+    if (prm.passes > 1) {
       ptx::prefetch_tmap(&prm.tm_xr_lo);
       ptx::prefetch_tmap(&prm.tm_xi_lo);
     }
@@ -164,30 +149,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
   const int per_img = prm.tiles_bp * prm.tiles_bq;
   const int per_pass = ((prm.c + kCH - 1) / kCH) * prm.s;  // K slots per precision pass
 
-  // In-kernel layout conversion: the first prm.cvt_clusters clusters to get
-  // here convert images for the others (role by ticket, so a cluster only
-  // waits for clusters that are running).
-  int ucid = cid, uncl = ncl;
-  bool cvt_cta = false;
-  int cvt_me = 0;
-  if constexpr (!IN_COMPLEX && !LW) {
-    if (prm.cvt_clusters > 0) {
-      if (leader && threadIdx.x == 0) {
-        const int ticket =
-            skip ? cid : static_cast<int>(atomicAdd(prm.cvt_ctrs + kCvtTicket, 1u));
-        flags[2] = ticket;
-        ptx::st_shared_cluster_u32(
-            ptx::mapa_shared(ptx::smem_u32(const_cast<int*>(flags + 2)), 1),
-            static_cast<uint32_t>(ticket));
-      }
-      ptx::cluster_sync();
-      const int ticket = flags[2];
-      cvt_cta = ticket < prm.cvt_clusters;
-      cvt_me = 2 * ticket + static_cast<int>(rank);
-      ucid = ticket - prm.cvt_clusters;
-      uncl = ncl - prm.cvt_clusters;
-    }
-  }
+  const int ucid = cid, uncl = ncl;
 
   if constexpr (LW) {
     // Every warp converts the first wave's images first (nothing to do
@@ -197,7 +159,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
       // TMA prefix's boxes, handed back to TMA by the proxy fence and the
       // barrier below.
       if (!lw_tma_prefix(prm, data, bar_base + 8u * kLwTmaBar,
-                         reinterpret_cast<unsigned*>(bars + kLwTmaBar + kCvtInBufs))) {
+                         reinterpret_cast<unsigned*>(bars + kLwTmaBar + kLwBoxBufs))) {
         flags[1] = 1;
       }
       ptx::fence_proxy_async_shared();
@@ -207,12 +169,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
     }
   }
 
-  if (cvt_cta) {
-    // ------------------------------------------------------------ converter cluster
-    if (!skip && !cvt_role(prm, cvt_me, 2 * prm.cvt_clusters, data, afull(0), blockDim.x)) {
-      flags[1] = 1;
-    }
-  } else if (warp == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0 && !skip) {
       uint32_t ga = 0, gw = 0;
@@ -243,16 +200,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
             }
             ready_img = img;
           }
-        } else if constexpr (!IN_COMPLEX) {
-          // Converted planes of this image (images arrive in order).
-          if (prm.cvt_clusters > 0 && img > ready_img) {
-            if (!cvt_wait_image(prm, img)) {
-              flags[1] = 1;
-              abort = true;
-              break;
-            }
-            ready_img = img;
-          }
         }
         for (int j = wu.jbeg; j < wu.jend && !abort; ++j, ++ga) {
           // Slot j: precision pass (slot_pass), channel block cb, filter
@@ -264,7 +211,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
           const int c0 = cb * kCH;
           const CUtensorMap* mr = pass == 2 ? &prm.tm_xr_lo : &prm.tm_xr;
           const CUtensorMap* mi = pass == 2 ? &prm.tm_xi_lo : &prm.tm_xi;
-          if (!IN_COMPLEX) {
+          {
             const int slot = static_cast<int>(ga % SA);
             const uint32_t ph = (ga / SA) & 1u;
             if (!ptx::mbar_wait_bounded(aempty(slot), ph ^ 1u, prm.status, kTimeoutH) ||
@@ -302,7 +249,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
       }
       if (leader) {
         // Drain: every issued slot and stage (both CTAs) has landed.
-        for (uint32_t j = 0; !IN_COMPLEX && j < static_cast<uint32_t>(SA) && j < ga; ++j) {
+        for (uint32_t j = 0; j < static_cast<uint32_t>(SA) && j < ga; ++j) {
           const uint32_t g = ga - 1 - j;
           ptx::mbar_wait_bounded(afull(static_cast<int>(g % SA)), (g / SA) & 1u, prm.status,
                                  kTimeoutH);
@@ -337,8 +284,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
         bool first = true;
         for (int j = wu.jbeg; j < wu.jend && !abort; ++j, ++ga) {
           const int slot = static_cast<int>(ga % SA);
-          if (!ptx::mbar_wait_bounded<IN_COMPLEX>(afull(slot), (ga / SA) & 1u, prm.status,
-                                                  kTimeoutH)) {
+          if (!ptx::mbar_wait_bounded(afull(slot), (ga / SA) & 1u, prm.status, kTimeoutH)) {
             flags[1] = 1;
             abort = true;
             break;
@@ -435,8 +381,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
           } else {
             int img = 0, op = 0, oq = 0;
             const bool in_tile = tile_row_pixel<false>(prm, half, row_sb, img, op, oq);
-            // The fused variant runs 448 threads (128 registers each): 16-column chunks.
-            store_accumulator<KT, OUT_COMPLEX, IN_COMPLEX ? 16 : 32>(
+            store_accumulator<KT, OUT_COMPLEX>(
                 prm, t_acc, n_tile * KT, in_tile && ok && !flags[1], img, op, oq);
           }
         }
@@ -451,70 +396,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
     if (lane == 0) ptx::bulk_wait_all();
   }
 
-  if constexpr (IN_COMPLEX) {
-    if (warp > 5 && !skip) {
-      // ---------------------------------------------------------- converters
-      // Jobs in MMA order: (tile, channel block, filter column, pass).  The
-      // loads of job j+1 are issued before waiting for job j+1's slot.
-      const int wid = warp - 6;
-      const float2* xc = reinterpret_cast<const float2*>(prm.xc);
-      auto make_job = [&](int t, int j, SlotJob& jb) {
-        const int half = 2 * (t / prm.tiles_n) + static_cast<int>(rank);
-        const int gb = min(half, prm.total_boxes - 1);
-        const int img = gb / per_img;
-        const int rem = gb - img * per_img;
-        const int bp = rem / prm.tiles_bq;
-        const int bq = rem - bp * prm.tiles_bq;
-        int rest;
-        const int pass = slot_pass(j, per_pass, prm.passes, &rest);
-        const int cb = rest / prm.s;
-        const int ss = rest - cb * prm.s;
-        jb.img = img;
-        jb.h0 = bp * prm.box_p - prm.ph;
-        jb.w0 = bq * prm.box_q - prm.pw + ss;
-        jb.c0 = cb * kCH;
-        jb.mode = prm.passes == 1 ? kConvRaw : (pass == 2 ? kConvLo : kConvHi);
-      };
-      UnitCursor cur = unit_cursor(prm, ucid);
-      WorkUnit wu;
-      bool have = next_unit(prm, uncl, cur, wu);
-      int j = have ? wu.jbeg : 0;
-      SlotJob jb;
-      float2 v[kConvUnits][4];
-      if (have) {
-        make_job(wu.tile, j, jb);
-        slot_job_load(v, jb, xc, prm.c, prm.h, prm.w, prm.halo_rows, prm.box_q_log2, wid,
-                      kConvWarps, lane);
-      }
-      uint32_t ga = 0;
-      while (have) {
-        const int slot = static_cast<int>(ga % SA);
-        if (!ptx::mbar_wait_bounded_backoff(aempty(slot), ((ga / SA) & 1u) ^ 1u, prm.status,
-                                            kTimeoutH) ||
-            flags[1]) {
-          flags[1] = 1;
-          break;
-        }
-        uint8_t* pr = data + slot * prm.a_slot_bytes;
-        slot_job_store(v, jb.mode, prm.halo_rows, pr, pr + a_plane_bytes, wid, kConvWarps,
-                       lane);
-        ptx::fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(afull(slot), 0));
-        ++ga;
-        if (++j == wu.jend) {
-          have = next_unit(prm, uncl, cur, wu);
-          j = have ? wu.jbeg : 0;
-        }
-        if (have) {
-          make_job(wu.tile, j, jb);
-          slot_job_load(v, jb, xc, prm.c, prm.h, prm.w, prm.halo_rows, prm.box_q_log2, wid,
-                        kConvWarps, lane);
-        }
-      }
-    }
-  }
-
   if constexpr (LW) {
     if (warp >= kThreadsH / 32 && !skip) {
       // ---------------------------------------------------------- layout warps
@@ -523,22 +404,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
   }
 
   __syncthreads();
-  if constexpr (!IN_COMPLEX) {
-    // The last CTA to finish leaves the conversion counters zero (the
-    // converter-cluster and layout-warp sets share one layout).
-    static_assert(kLwTicket == kCvtTicket && kLwDone == kCvtDone && kLwFlag0 == kCvtFlag0, "");
-    if ((LW || prm.cvt_clusters > 0) && threadIdx.x == 0) {
+  if constexpr (LW) {
+    // The last CTA to finish leaves the conversion counters zero.
+    if (threadIdx.x == 0) {
       unsigned old;
       asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
                    : "=r"(old)
-                   : "l"(prm.cvt_ctrs + kCvtDone)
+                   : "l"(prm.lw_ctrs + kLwDone)
                    : "memory");
       if (old == 2u * static_cast<unsigned>(ncl) - 1u) {
-        for (int i = 0; i < prm.n; ++i) prm.cvt_ctrs[kCvtFlag0 + i] = 0u;
-        prm.cvt_ctrs[kCvtTicket] = 0u;
-        prm.cvt_ctrs[kLwPrefixTicket] = 0u;
-        prm.cvt_ctrs[kLwTmaTicket] = 0u;
-        prm.cvt_ctrs[kCvtDone] = 0u;
+        for (int i = 0; i < prm.n; ++i) prm.lw_ctrs[kLwFlag0 + i] = 0u;
+        prm.lw_ctrs[kLwTicket] = 0u;
+        prm.lw_ctrs[kLwPrefixTicket] = 0u;
+        prm.lw_ctrs[kLwTmaTicket] = 0u;
+        prm.lw_ctrs[kLwDone] = 0u;
         __threadfence();
       }
     }
@@ -552,31 +431,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<IN_COMP
   }
 }
 
-// Converter clusters for a G-cluster grid: the share of the SM time the
-// conversion takes at ~120 GB/s of traffic per SM against ~4.5 TFLOP/s of
-// convolution per SM (B200 measurements), at least 1, at most G/3.
-// CCV_CVT_CLUSTERS=n pins it (testing/benchmarking knob).
-int cvt_clusters_for(const FpropParams& prm, int G) {
-  const char* env = getenv("CCV_CVT_CLUSTERS");
-  int nc;
-  if (env != nullptr && atoi(env) > 0) {
-    nc = atoi(env);
-  } else {
-    const double elems = static_cast<double>(prm.n) * prm.c * prm.h * prm.w;
-    const double flops = 8.0 * prm.n * prm.p * prm.q * static_cast<double>(prm.k) * prm.c *
-                         prm.r * prm.s;
-    const double t_cvt = 16.0 * elems / 120e9;
-    const double t_conv = flops / 4.5e12;
-    nc = static_cast<int>(std::ceil(t_cvt / (t_cvt + t_conv) * G));
-  }
-  return std::max(1, std::min(nc, std::max(1, G / 3)));
-}
-
-template <int KT, bool OUT_COMPLEX, bool IN_COMPLEX, int NSUB = 1, bool LW = false>
+template <int KT, bool OUT_COMPLEX, int NSUB = 1, bool LW = false>
 int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
                     cudaStream_t stream) {
-  auto kern = ccv_fprop2h_tf32_kernel<KT, OUT_COMPLEX, IN_COMPLEX, NSUB, LW>;
-  constexpr int threads = halo_threads<IN_COMPLEX, LW>();
+  auto kern = ccv_fprop2h_tf32_kernel<KT, OUT_COMPLEX, NSUB, LW>;
+  constexpr int threads = halo_threads<LW>();
   static std::once_flag once[64];
   static int max_clusters[64] = {};
   int dev = 0;
@@ -602,14 +461,7 @@ int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
   const int slots = ((prm.c + kCH - 1) / kCH) * prm.s * prm.passes;
   int rc;
   int launched = 0;
-  if (prm.cvt_clusters > 0) {
-    // In-kernel conversion: whole tiles only; converter clusters on top.
-    if (clusters < 2) return set_error(CCV_ERR_UNSUPPORTED, "too few clusters for conversion");
-    prm.cvt_clusters = cvt_clusters_for(prm, clusters);
-    launch_clusters(prm, clusters, slots, KT, nullptr, 0, stream, &rc);
-    if (rc != CCV_OK) return rc;
-    launched = std::min(clusters, prm.num_tiles + prm.cvt_clusters);
-  } else if (LW) {
+  if (LW) {
     // Layout warps: the stream-K range runs first, so its first image is
     // converted first.
     launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc);
@@ -648,11 +500,6 @@ bool halo_applicable(const Problem& pb) {
   return t.total_boxes > 0 && halo_fits(t, pb.r);
 }
 
-bool halo_fused_supported(const Problem& pb, const Tiling& th) {
-  const int rows = (th.box_p + pb.r - 1) * th.box_q;
-  return ((rows + 31) / 32) * 8 <= kConvUnits * kConvWarps;
-}
-
 Tiling choose_halo_tiling(const Problem& pb) { return choose_halo_tiling_px(pb, kBlockM); }
 
 Tiling choose_halo_tiling_px(const Problem& pb, int px) {
@@ -688,8 +535,7 @@ Tiling choose_halo_tiling_px(const Problem& pb, int px) {
 }
 
 namespace {
-// Tensor maps of the TMA conversion (converter clusters, TMA prefix of the
-// layout warps): complex64 NCHW input as 8-byte elements (W, C, H, N), boxes
+// Tensor maps of the TMA prefix of the layout warps: complex64 NCHW input as 8-byte elements (W, C, H, N), boxes
 // of 16 pixels x 32 channels x 8 rows (128-byte rows, 128-byte swizzle), and
 // the fp32 NHWC planes (C, W, H, N), boxes of 32 channels x 16 pixels x 8 rows.
 int encode_conversion_maps(FpropParams& prm, const float* src, const float* xr, const float* xi,
@@ -699,7 +545,7 @@ int encode_conversion_maps(FpropParams& prm, const float* src, const float* xr, 
     const uint64_t dims[4] = {static_cast<uint64_t>(pb.w), static_cast<uint64_t>(pb.c),
                               static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
     const uint64_t strides[3] = {hw8, static_cast<uint64_t>(pb.w) * 8, hw8 * pb.c};
-    const uint32_t box[4] = {kCvtPx, kCvtCh, kCvtRows, 1};
+    const uint32_t box[4] = {kLwBoxPx, kLwBoxCh, kLwBoxRows, 1};
     const uint32_t es[4] = {1, 1, 1, 1};
     const int rc = encode_tiled_ex(&prm.tm_cin, src, 4, dims, strides, box, es, kSwizzle128, true);
     if (rc != CCV_OK) return rc;
@@ -708,7 +554,7 @@ int encode_conversion_maps(FpropParams& prm, const float* src, const float* xr, 
   const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.w),
                             static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
   const uint64_t strides[3] = {cb4, cb4 * pb.w, cb4 * pb.w * pb.h};
-  const uint32_t box[4] = {kCvtCh, kCvtPx, kCvtRows, 1};
+  const uint32_t box[4] = {kLwBoxCh, kLwBoxPx, kLwBoxRows, 1};
   const uint32_t es[4] = {1, 1, 1, 1};
   int rc = encode_tiled_ex(&prm.tm_pr, xr, 4, dims, strides, box, es, kSwizzleNone, false);
   if (rc != CCV_OK) return rc;
@@ -717,32 +563,28 @@ int encode_conversion_maps(FpropParams& prm, const float* src, const float* xr, 
 }  // namespace
 
 int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
-                           const float* xi_lo, const float* xc, bool split,
-                           const float* w_packed, float* y0, float* y1, const Problem& pb,
-                           const Tiling& t_in, OutLayout out_layout, void* ws, size_t ws_bytes,
-                           cudaStream_t stream, const float* cvt_src, bool layout_warps,
-                           const float* lw_pr, const float* lw_pi) {
+                           const float* xi_lo, bool split, const float* w_packed, float* y0,
+                           float* y1, const Problem& pb, const Tiling& t_in, OutLayout out_layout,
+                           const Epilogue& ep, void* ws, size_t ws_bytes, cudaStream_t stream,
+                           const float* lw_src, const float* lw_pr, const float* lw_pi) {
   // KT <= 64: two 128-pixel sub-boxes per CTA tile when the taller halo slot
   // fits (CCV_SUBBOX=0 turns it off; testing knob).  No stream-K split then.
   Tiling t = t_in;
   int nsub = 1;
-  {
-    const char* env = getenv("CCV_SUBBOX");
-    const bool allow = env == nullptr || atoi(env) != 0;
-    if (allow && xc == nullptr && t.kt <= 64) {
-      const Tiling t2 = choose_halo_tiling_px(pb, 2 * kBlockM);
-      if (t2.total_boxes > 0 && halo_fits(t2, pb.r)) {
-        t = t2;
-        nsub = 2;
-        ws = nullptr;
-        ws_bytes = 0;
-      }
+  if (knobs().subbox != 0 && t.kt <= 64) {
+    const Tiling t2 = choose_halo_tiling_px(pb, 2 * kBlockM);
+    if (t2.total_boxes > 0 && halo_fits(t2, pb.r)) {
+      t = t2;
+      nsub = 2;
+      ws = nullptr;
+      ws_bytes = 0;
     }
   }
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
   prm.y0 = y0;
   prm.y1 = y1;
+  set_epilogue(prm, ep);
   prm.status = device_status_ptr();
   if (prm.status == nullptr) return CCV_ERR_CUDA;
   prm.n = pb.n; prm.h = pb.h; prm.w = pb.w; prm.c = pb.c; prm.k = pb.k;
@@ -757,11 +599,6 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
   prm.ksteps = ((pb.c + kCH - 1) / kCH) * pb.r * pb.s;
   prm.m_total = static_cast<long long>(pb.n) * pb.p * pb.q;
   prm.num_tiles = pair_tiles(t);
-  const bool fused = xc != nullptr;
-  if (fused && !halo_fused_supported(pb, t)) {
-    return set_error(CCV_ERR_UNSUPPORTED, "halo slot too tall for the fused converters");
-  }
-  prm.xc = xc;
   prm.passes = split ? 3 : 1;
   if (!split) {
     xr_lo = xr;
@@ -771,29 +608,28 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
   prm.halo_rows = (t.box_p + pb.r - 1) * t.box_q;
   prm.a_slot_bytes = 2 * prm.halo_rows * kRowH;
   prm.w_stage_bytes = 2 * t.kt * kRowH;
-  // Ring depths: at least 2 A slots and 3 weight stages; prefer 4+ weight
-  // stages, then a third A slot.
-  const bool cplx_out = out_layout == OUT_COMPLEX_NCHW;
-  if (!cplx_out && (rc0 = encode_planar_out_maps(prm, y0, y1, false)) != CCV_OK) return rc0;
-  const bool lw = layout_warps && (cvt_src != nullptr || lw_pr != nullptr);
+  const bool cplx = out_layout == OUT_COMPLEX_NCHW;
+  if (!cplx && (rc0 = encode_planar_out_maps(prm, y0, y1, false)) != CCV_OK) return rc0;
+  const bool lw = lw_src != nullptr || lw_pr != nullptr;
   if (lw) {
-    // Layout warps write xr/xi (and the remainder planes) from cvt_src
+    // Layout warps write xr/xi (and the remainder planes) from lw_src
     // (complex64 NCHW) or from the planes lw_pr/lw_pi (fp32 NHWC).
-    if (fused || (lw_pr == nullptr && !cplx_out) || pb.n > kSkCounterWords - kLwFlag0) {
+    if ((lw_pr == nullptr && !cplx) || pb.n > kSkCounterWords - kLwFlag0) {
       return set_error(CCV_ERR_UNSUPPORTED, "no layout warps for this problem");
     }
-    prm.xc = cvt_src;
+    prm.xc = lw_src;
     prm.lw_pr = lw_pr;
     prm.lw_pi = lw_pi;
     prm.lw_xr = const_cast<float*>(xr);
     prm.lw_xi = const_cast<float*>(xi);
     prm.lw_xr_lo = const_cast<float*>(xr_lo);
     prm.lw_xi_lo = const_cast<float*>(xi_lo);
-    prm.cvt_ctrs = stream_k_counters();
-    if (prm.cvt_ctrs == nullptr) return CCV_ERR_CUDA;
+    prm.lw_ctrs = acquire_counter_set(stream);
+    if (prm.lw_ctrs == nullptr) return kNoCounterSet;
   }
-  const int budget =
-      kSmemDataBudget - (prm.out_tma ? kOutStageBytes : 0);
+  // Ring depths: at least 2 A slots and 3 weight stages; prefer 4+ weight
+  // stages, then a third A slot.
+  const int budget = kSmemDataBudget - (prm.out_tma ? kOutStageBytes : 0);
   int sa = 2;
   int sw = (budget - sa * prm.a_slot_bytes) / prm.w_stage_bytes;
   if (sw > 4 && budget - 3 * prm.a_slot_bytes >= 4 * prm.w_stage_bytes) {
@@ -804,35 +640,21 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
   if (sw < 3) return set_error(CCV_ERR_UNSUPPORTED, "halo tile does not fit in shared memory");
   prm.a_slots = sa;
   prm.w_stages = sw;
-  int smem_bytes = 1024 + kBarBytes + sa * prm.a_slot_bytes + sw * prm.w_stage_bytes +
-                   (prm.out_tma ? kOutStageBytes : 0);
-  if (cvt_src != nullptr && !lw) {
-    // In-kernel conversion of cvt_src (complex64 NCHW) into the planes xr/xi.
-    if (fused || split || (pb.w & 1) != 0 || pb.n > kSkCounterWords - kCvtFlag0) {
-      return set_error(CCV_ERR_UNSUPPORTED, "no in-kernel conversion for this problem");
-    }
-    prm.cvt_ctrs = stream_k_counters();
-    if (prm.cvt_ctrs == nullptr) return CCV_ERR_CUDA;
-    prm.cvt_clusters = 1;  // sized at launch
-    ws = nullptr;
-    ws_bytes = 0;
-    smem_bytes = std::max(smem_bytes, 1024 + kBarBytes + static_cast<int>(kCvtSmemBytes));
-    const int rc1 = encode_conversion_maps(prm, cvt_src, xr, xi, pb);
-    if (rc1 != CCV_OK) return rc1;
-  }
-  if (lw && cvt_src != nullptr && lw_pr == nullptr && !split && (pb.w & 1) == 0 &&
-      (reinterpret_cast<uintptr_t>(cvt_src) & 15) == 0 &&
-      sa * prm.a_slot_bytes + sw * prm.w_stage_bytes >= static_cast<int>(kCvtSmemBytes)) {
+  const int smem_bytes = 1024 + kBarBytes + sa * prm.a_slot_bytes + sw * prm.w_stage_bytes +
+                         (prm.out_tma ? kOutStageBytes : 0);
+  if (lw && lw_src != nullptr && lw_pr == nullptr && !split && (pb.w & 1) == 0 &&
+      (reinterpret_cast<uintptr_t>(lw_src) & 15) == 0 &&
+      sa * prm.a_slot_bytes + sw * prm.w_stage_bytes >= static_cast<int>(kLwBoxSmemBytes)) {
     // TMA prefix possible (sized at launch): TF32, even W (8-byte elements,
     // 16-byte row strides), the operand rings can hold its boxes.
-    const int rc1 = encode_conversion_maps(prm, cvt_src, xr, xi, pb);
+    const int rc1 = encode_conversion_maps(prm, lw_src, xr, xi, pb);
     if (rc1 != CCV_OK) return rc1;
     prm.lw_tma_images = -1;
   }
 
   int rc;
   const uint64_t cb = static_cast<uint64_t>(pb.c) * 4;
-  if (!fused) {
+  {
     const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.w),
                               static_cast<uint64_t>(pb.h), static_cast<uint64_t>(pb.n)};
     const uint64_t strides[3] = {cb, cb * pb.w, cb * pb.w * pb.h};
@@ -852,58 +674,28 @@ int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
     const uint32_t es[4] = {1, 1, 1, 1};
     if ((rc = encode_tiled(&prm.tm_w, w_packed, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
   }
-  const bool cplx = out_layout == OUT_COMPLEX_NCHW;
-  if (fused) {
-    // The fused path always writes complex64 NCHW.
-    if (!cplx) return set_error(CCV_ERR_INVALID_ARGUMENT, "fused complex input needs complex output");
-    switch (t.kt) {
-      case 128: return launchh_variant<128, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
-      case 64: return launchh_variant<64, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
-      default: return launchh_variant<32, true, true>(prm, smem_bytes, ws, ws_bytes, stream);
-    }
-  }
-  if (lw && cplx) {
-    if (nsub == 2) {
-      return t.kt == 64 ? launchh_variant<64, true, false, 2, true>(prm, smem_bytes, ws, ws_bytes, stream)
-                        : launchh_variant<32, true, false, 2, true>(prm, smem_bytes, ws, ws_bytes, stream);
-    }
-    switch (t.kt) {
-      case 128: return launchh_variant<128, true, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
-      case 64: return launchh_variant<64, true, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
-      default: return launchh_variant<32, true, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
-    }
-  }
-  if (lw) {
-    // Planar output: the 3xTF32 split of forward_planar()'s input planes.
-    if (nsub == 2) {
-      return t.kt == 64 ? launchh_variant<64, false, false, 2, true>(prm, smem_bytes, ws, ws_bytes, stream)
-                        : launchh_variant<32, false, false, 2, true>(prm, smem_bytes, ws, ws_bytes, stream);
-    }
-    switch (t.kt) {
-      case 128: return launchh_variant<128, false, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
-      case 64: return launchh_variant<64, false, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
-      default: return launchh_variant<32, false, false, 1, true>(prm, smem_bytes, ws, ws_bytes, stream);
-    }
-  }
-  if (nsub == 2) {
-    if (t.kt == 64) {
-      return cplx ? launchh_variant<64, true, false, 2>(prm, smem_bytes, ws, ws_bytes, stream)
-                  : launchh_variant<64, false, false, 2>(prm, smem_bytes, ws, ws_bytes, stream);
-    }
-    return cplx ? launchh_variant<32, true, false, 2>(prm, smem_bytes, ws, ws_bytes, stream)
-                : launchh_variant<32, false, false, 2>(prm, smem_bytes, ws, ws_bytes, stream);
-  }
-  switch (t.kt) {
-    case 128:
-      return cplx ? launchh_variant<128, true, false>(prm, smem_bytes, ws, ws_bytes, stream)
-                  : launchh_variant<128, false, false>(prm, smem_bytes, ws, ws_bytes, stream);
-    case 64:
-      return cplx ? launchh_variant<64, true, false>(prm, smem_bytes, ws, ws_bytes, stream)
-                  : launchh_variant<64, false, false>(prm, smem_bytes, ws, ws_bytes, stream);
-    default:
-      return cplx ? launchh_variant<32, true, false>(prm, smem_bytes, ws, ws_bytes, stream)
-                  : launchh_variant<32, false, false>(prm, smem_bytes, ws, ws_bytes, stream);
-  }
+#define CCV_HALO_LAUNCH(KT_, CPLX_, NSUB_, LW_) \
+  launchh_variant<KT_, CPLX_, NSUB_, LW_>(prm, smem_bytes, ws, ws_bytes, stream)
+#define CCV_HALO_BY_KT(CPLX_, LW_)                                                   \
+  do {                                                                               \
+    if (nsub == 2) {                                                                 \
+      return t.kt == 64 ? CCV_HALO_LAUNCH(64, CPLX_, 2, LW_)                         \
+                        : CCV_HALO_LAUNCH(32, CPLX_, 2, LW_);                        \
+    }                                                                                \
+    switch (t.kt) {                                                                  \
+      case 128: return CCV_HALO_LAUNCH(128, CPLX_, 1, LW_);                          \
+      case 64: return CCV_HALO_LAUNCH(64, CPLX_, 1, LW_);                            \
+      default: return CCV_HALO_LAUNCH(32, CPLX_, 1, LW_);                            \
+    }                                                                                \
+  } while (0)
+  // Layout warps with planar output: the 3xTF32 split of forward_planar()'s
+  // input planes.
+  if (lw && cplx) CCV_HALO_BY_KT(true, true);
+  if (lw) CCV_HALO_BY_KT(false, true);
+  if (cplx) CCV_HALO_BY_KT(true, false);
+  CCV_HALO_BY_KT(false, false);
+#undef CCV_HALO_BY_KT
+#undef CCV_HALO_LAUNCH
 }
 
 }  // namespace ccv

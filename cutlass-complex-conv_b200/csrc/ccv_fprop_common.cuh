@@ -21,15 +21,14 @@ struct alignas(64) FpropParams {
   // (K, N*P*Q) boxes of 16 channels x 32 pixels for flat tiles.
   CUtensorMap tm_y0;
   CUtensorMap tm_y1;
-  // In-kernel layout conversion (cvt_clusters > 0): complex64 NCHW input as
-  // 8-byte elements (W, C, H, N), and the fp32 NHWC planes it fills (C, W,
-  // H, N) - the planes tm_xr / tm_xi read.
+  // TMA prefix of the layout warps: complex64 NCHW input as 8-byte elements
+  // (W, C, H, N), and the fp32 NHWC planes it fills (C, W, H, N) - the
+  // planes tm_xr / tm_xi read.
   CUtensorMap tm_cin;
   CUtensorMap tm_pr;
   CUtensorMap tm_pi;
-  int cvt_clusters;
-  unsigned* cvt_ctrs;  // conversion counters (converter clusters / layout warps)
-  const float* xc;    // fused complex path: complex64 NCHW input (interleaved)
+  unsigned* lw_ctrs;  // layout-warp counter set
+  const float* xc;    // layout warps: complex64 NCHW input (interleaved)
   // Layout warps: the fp32 NHWC planes they write from xc (the planes tm_xr,
   // tm_xi, tm_xr_lo, tm_xi_lo read).
   float* lw_xr;
@@ -46,6 +45,10 @@ struct alignas(64) FpropParams {
   int lw_tma_bufs;      // TMA prefix: boxes in flight
   float* y0;          // planar: y_real (NPQK); complex: interleaved NKPQ
   float* y1;          // planar: y_imag (NPQK); complex: unused
+  // Complex bias per output channel (K fp32 each), added in the epilogue;
+  // null: none.  Either both are set or neither.
+  const float* bias_r;
+  const float* bias_i;
   int* status;        // device status word
   int n, h, w, c, k, r, s, p, q;
   int sh, sw, ph, pw;
@@ -78,6 +81,38 @@ struct alignas(64) FpropParams {
   float* split_ws;
   unsigned* split_count;
 };
+
+inline void set_epilogue(FpropParams& prm, const Epilogue& ep) {
+  prm.bias_r = ep.bias_r;
+  prm.bias_i = ep.bias_i;
+}
+
+#ifdef __CUDACC__
+// Adds the complex bias of output channels [kb, kb + W) to a row's real and
+// imaginary accumulator values (fp32 bits), once per output element: callers
+// apply it to final sums only, never to split-K partials.  K % 4 == 0, so a
+// group of four channels is either wholly inside K or wholly outside.
+template <int W>
+__device__ __forceinline__ void add_bias(const FpropParams& prm, int kb, uint32_t (&vr)[W],
+                                         uint32_t (&vi)[W]) {
+  if (prm.bias_r == nullptr) return;
+#pragma unroll
+  for (int j = 0; j < W; j += 4) {
+    if (kb + j < prm.k) {
+      const float4 br = __ldg(reinterpret_cast<const float4*>(prm.bias_r + kb + j));
+      const float4 bi = __ldg(reinterpret_cast<const float4*>(prm.bias_i + kb + j));
+      vr[j] = __float_as_uint(__uint_as_float(vr[j]) + br.x);
+      vr[j + 1] = __float_as_uint(__uint_as_float(vr[j + 1]) + br.y);
+      vr[j + 2] = __float_as_uint(__uint_as_float(vr[j + 2]) + br.z);
+      vr[j + 3] = __float_as_uint(__uint_as_float(vr[j + 3]) + br.w);
+      vi[j] = __float_as_uint(__uint_as_float(vi[j]) + bi.x);
+      vi[j + 1] = __float_as_uint(__uint_as_float(vi[j + 1]) + bi.y);
+      vi[j + 2] = __float_as_uint(__uint_as_float(vi[j + 2]) + bi.z);
+      vi[j + 3] = __float_as_uint(__uint_as_float(vi[j + 3]) + bi.w);
+    }
+  }
+}
+#endif
 
 // Work of one persistent cluster: its stream-K range, then whole tiles.
 // K slot order of the pair kernels: the precision pass is outermost, and
@@ -237,10 +272,12 @@ inline Tiling choose_tiling(const Problem& pb) {
 int pair_tiles(const Tiling& t);
 // xr_lo/xi_lo: 3xTF32 remainder planes (nullptr for TF32); xr/xi then hold
 // the TF32-rounded parts.
+// lw_src (complex64 NCHW) or lw_pr/lw_pi (fp32 NHWC planes): layout warps
+// fill xr/xi (and the remainder planes) from that source in the same launch.
 int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                       const float* w_packed, float* y0, float* y1, const Problem& pb,
-                      const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
-                      cudaStream_t stream, const float* lw_src = nullptr,
+                      const Tiling& t, OutLayout out_layout, const Epilogue& ep, void* ws,
+                      size_t ws_bytes, cudaStream_t stream, const float* lw_src = nullptr,
                       const float* lw_pr = nullptr, const float* lw_pi = nullptr);
 
 // Halo variant of the pair kernel (ccv_fprop2h.cu): stride-1 problems with a
@@ -248,9 +285,6 @@ int launch_fprop_pair(const float* xr, const float* xi, const float* xr_lo, cons
 // (box_q a multiple of 8); per 32-channel block the S column-shifted halo
 // copies of the box are loaded once and reused by the R filter rows.
 bool halo_applicable(const Problem& pb);
-// Whether the converter warps of the fused complex path cover one A slot of
-// this halo tiling (their register batch bounds the slot's rows).
-bool halo_fused_supported(const Problem& pb, const Tiling& th);
 // Scratch bytes that let a pair kernel with KT-wide tiles, `tiles` pair
 // tiles and `slots` K slots per tile split its last partial wave stream-K
 // style (partials and counters; an upper bound for the current device).
@@ -260,7 +294,7 @@ size_t pair_split_workspace_bytes(int kt, int tiles, int slots);
 // (at least pair_split_workspace_bytes(kt)) when given and worthwhile.
 // Returns the number of counters to zero before the launch (0: no split).
 int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, size_t ws_bytes,
-                  int min_gain_pct = 10);
+                  cudaStream_t stream, int min_gain_pct = 10);
 // Persistent-grid size after the CCV_MAX_CLUSTERS testing cap.
 int cluster_cap(int max_clusters);
 // Plans the stream-K split and returns the number of clusters to launch;
@@ -270,32 +304,21 @@ int launch_clusters(FpropParams& prm, int clusters, int slots, int kt, void* ws,
 Tiling choose_halo_tiling(const Problem& pb);
 // Same for tiles of `px` output pixels per CTA (128 or 256).
 Tiling choose_halo_tiling_px(const Problem& pb, int px);
-// xc non-null: fused complex path (converter warps read complex64 NCHW; the
-// planar pointers are ignored and `split` selects 3xTF32).
-// Complex-direct kernel (ccv_fprop_cd.cu): forward() with the activations
-// read from complex64 NCHW by TMA as an MN-major operand.  Stride 1, odd
-// filter width, even image width.
-bool cd_applicable(const Problem& pb);
-
 // Bytes of shared memory a pair kernel sets aside for the TMA-store epilogue
 // (4 warps x 32 rows x 16 channels x 2 planes).
 constexpr int kOutStageBytes = 4 * 32 * 16 * 4 * 2;
 // Encodes prm.tm_y0 / tm_y1 for planar output and sets prm.out_tma when the
 // tiling lets each epilogue warp's 32 rows form one TMA box.
 int encode_planar_out_maps(FpropParams& prm, float* y0, float* y1, bool flat);
-int launch_fprop_cd(const float* xc, const float* w_packed, float* y, const Problem& pb,
-                    void* ws, size_t ws_bytes, cudaStream_t stream);
 
-// ws/ws_bytes: optional scratch for the tail split (see
-// halo_split_workspace_bytes); without it every tile runs whole.
-// cvt_src: complex64 NCHW input to convert inside the kernel into the
-// planes xr / xi (which the kernel then reads); see ccv_cvt_role.cuh.
+// ws/ws_bytes: optional scratch for the tail split (pair_split_workspace_bytes);
+// without it every tile runs whole.  lw_src / lw_pr, lw_pi: as for
+// launch_fprop_pair (layout warps in the same launch).
 int launch_fprop_pair_halo(const float* xr, const float* xi, const float* xr_lo,
-                           const float* xi_lo, const float* xc, bool split,
-                           const float* w_packed, float* y0, float* y1, const Problem& pb,
-                           const Tiling& t, OutLayout out_layout, void* ws, size_t ws_bytes,
-                           cudaStream_t stream, const float* cvt_src = nullptr,
-                           bool layout_warps = false, const float* lw_pr = nullptr,
+                           const float* xi_lo, bool split, const float* w_packed, float* y0,
+                           float* y1, const Problem& pb, const Tiling& t, OutLayout out_layout,
+                           const Epilogue& ep, void* ws, size_t ws_bytes, cudaStream_t stream,
+                           const float* lw_src = nullptr, const float* lw_pr = nullptr,
                            const float* lw_pi = nullptr);
 
 }  // namespace ccv

@@ -23,6 +23,35 @@ int* device_status_ptr();
 // Number of SMs of the current device (cached per device).
 int device_sm_count();
 
+// Testing/benchmarking switches read from CCV_* environment variables: read
+// once, on first use (ccv_reload_config re-reads them).  Each field's
+// default is the tuned behaviour.
+struct Knobs {
+  int pdl = 1;            // CCV_PDL: programmatic dependent launch
+  int kt = 0;             // CCV_KT=32|64|128: single-CTA channel tile (0 auto)
+  int force_kernel = 0;   // CCV_FORCE_KERNEL=1|2: single-CTA / pair family (0 auto)
+  int halo = -1;          // CCV_HALO=0|1: pair variant (-1 auto)
+  int splitk = 0;         // CCV_SPLITK=n: cap of the single-CTA split (0 none)
+  int lw = -1;            // CCV_LW=0|1: layout warps off / wherever possible (-1 auto)
+  int lw_prefix = -1;     // CCV_LW_PREFIX=0: no prefix phase
+  int lw_tma = 1;         // CCV_LW_TMA=0: warp prefix instead of the TMA prefix
+  int lw_tma_images = 0;  // CCV_LW_TMA_IMAGES=n: images of the TMA prefix (0 auto)
+  int lw_tma_bufs = 0;    // CCV_LW_TMA_BUFS=2..4: TMA prefix boxes in flight (0 default)
+  int subbox = 1;         // CCV_SUBBOX=0: no two-sub-box halo tiles
+  int streamk = -1;       // CCV_STREAMK=0|1: never / whenever possible (-1 model)
+  int max_clusters = 0;   // CCV_MAX_CLUSTERS=n: persistent grid cap (0 none)
+  int tma_store = 1;      // CCV_TMA_STORE=0: planar epilogue without TMA stores
+};
+const Knobs& knobs();
+void reload_knobs();
+
+// Epilogue options of an fprop launch: complex bias per output channel
+// (K fp32 real parts and K imaginary parts), or none.
+struct Epilogue {
+  const float* bias_r = nullptr;
+  const float* bias_i = nullptr;
+};
+
 // Validated problem with derived sizes.
 struct Problem {
   int n, h, w, c, k, r, s, p, q;
@@ -43,6 +72,12 @@ int launch_prepack(const float* w_real, const float* w_imag, int layout, const P
 // xr/xi receive tf32(x) and xr_lo/xi_lo the remainders x - tf32(x).
 int launch_nchw_complex_to_planar(const float* x, float* xr, float* xi, float* xr_lo,
                                   float* xi_lo, const Problem& pb, cudaStream_t stream);
+// Same from complex64 input with element strides (n, c, h, w): any layout,
+// including slices and channels-last; the dense NCHW case takes the kernel
+// above.  x must be 8-byte aligned.
+int launch_strided_complex_to_planar(const float* x, const int64_t* strides, float* xr,
+                                     float* xi, float* xr_lo, float* xi_lo, const Problem& pb,
+                                     cudaStream_t stream);
 // fp32 planes -> (tf32(x), x - tf32(x)) planes, for 3xTF32 on planar inputs.
 int launch_split_planes(const float* xr, const float* xi, float* hr, float* hi, float* lr,
                         float* li, size_t count, cudaStream_t stream);
@@ -55,27 +90,20 @@ enum OutLayout { OUT_PLANAR_NHWC = 0, OUT_COMPLEX_NCHW = 1 };
 // the pair kernels' last partial wave; null runs every tile whole.
 int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const float* xi_lo,
                  const float* w_packed, float* y0, float* y1, const Problem& pb, int precision,
-                 OutLayout out_layout, void* ws, size_t ws_bytes, cudaStream_t stream);
+                 OutLayout out_layout, const Epilogue& ep, void* ws, size_t ws_bytes,
+                 cudaStream_t stream);
 
 // Scratch bytes the stream-K split of this problem's kernel can use (0 when
 // the problem runs on a kernel without the split).
 size_t split_workspace_bytes(const Problem& pb, int precision, bool complex_input);
 
-// Fused complex path: complex64 NCHW in, complex64 NKPQ out, one launch, no
-// required workspace.  Available when the problem runs on the halo pair kernel.
-bool fused_complex_available(const Problem& pb, int precision);
-// forward() with the layout conversion done by converter clusters inside
-// the halo pair kernel (one launch; xr/xi: workspace planes it fills).
-bool use_in_kernel_conversion(const Problem& pb, int precision);
-int launch_fprop_complex_cvt(const float* x, float* xr, float* xi, const float* w_packed, float* y,
-                             const Problem& pb, cudaStream_t stream);
-// forward() with the layout conversion done by layout warps inside the halo
+// forward() with the layout conversion done by layout warps inside the
 // pair kernel (one launch; xr/xi and, for 3xTF32, xr_lo/xi_lo: workspace
 // planes it fills).  The default complex path where it applies.
 bool use_layout_warps(const Problem& pb, int precision);
 int launch_fprop_complex_lw(const float* x, float* xr, float* xi, float* xr_lo, float* xi_lo,
                             const float* w_packed, float* y, const Problem& pb, int precision,
-                            void* ws, size_t ws_bytes, cudaStream_t stream);
+                            const Epilogue& ep, void* ws, size_t ws_bytes, cudaStream_t stream);
 // Whether the layout-warp variant pays for this problem (dispatch rule,
 // complex or planar source).
 bool layout_warps_pay(const Problem& pb, int precision);
@@ -85,13 +113,10 @@ bool layout_warps_pay(const Problem& pb, int precision);
 bool use_layout_warps_planar(const Problem& pb, int precision);
 int launch_fprop_planar_lw(const float* x_real, const float* x_imag, float* hr, float* hi,
                            float* lr, float* li, const float* w_packed, float* y_real,
-                           float* y_imag, const Problem& pb, void* ws, size_t ws_bytes,
-                           cudaStream_t stream);
+                           float* y_imag, const Problem& pb, const Epilogue& ep, void* ws,
+                           size_t ws_bytes, cudaStream_t stream);
 // Name of the kernel path a complex (forward()) call takes.
 const char* complex_kernel_name(const Problem& pb, int precision);
-int launch_fprop_fused_complex(const float* xc, const float* w_packed, float* y,
-                               const Problem& pb, int precision, void* ws, size_t ws_bytes,
-                               cudaStream_t stream);
 
 // Encodes a tiled tensor map through the driver entry point.
 // `swizzle_bytes` is 64 or 128 (the box's inner extent in bytes).
@@ -99,27 +124,70 @@ int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* d
                  const uint64_t* strides_bytes, const uint32_t* box, const uint32_t* elem_strides,
                  int swizzle_bytes = 64);
 // Same, with the swizzle mode named and optionally 8-byte elements.
-// kSwizzle128Atom32 swizzles 32-byte chunks within 128-byte rows (the
-// shared-memory layout of MN-major 32-bit tensor-core operands).
-enum TmaSwizzle { kSwizzle64 = 0, kSwizzle128 = 1, kSwizzle128Atom32 = 2, kSwizzleNone = 3 };
+enum TmaSwizzle { kSwizzle64 = 0, kSwizzle128 = 1, kSwizzleNone = 3 };
 int encode_tiled_ex(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                     const uint64_t* strides_bytes, const uint32_t* box,
                     const uint32_t* elem_strides, TmaSwizzle swizzle, bool elem8);
 
-int launch_selftest_wait(int* status_dev, cudaStream_t stream);
+// One CTA waits on an mbarrier nothing arrives on; the bounded wait writes
+// CCV_ERR_DEVICE_TIMEOUT into *status_dev (and, with `mirror`, into the
+// host-mapped mirror of the library's status block that status_dev points to).
+int launch_selftest_wait(int* status_dev, bool mirror, cudaStream_t stream);
 
-// Stream-K tile counters for one launch: a zeroed set of kSkCounterWords
-// words in library-owned device memory (a ring of sets, so launches in
-// flight at the same time use different sets).  Each split tile's counter is
-// reset by the piece that completes it, so a set is zero again when its
-// kernel ends; ccv_clear_device_status re-zeroes the ring after an abort.
+// Entry-point bodies without the one-time set-up of the host-mapped status
+// mirror (a pinned host allocation): the public functions add that set-up;
+// the no-allocation entry point calls these directly.
+int prepack_weights_impl(const float* w_real, const float* w_imag, int layout,
+                         const ccv_conv_shape* shape, int precision, void* packed,
+                         size_t packed_bytes, ccv_stream_t stream);
+int fprop_planar_impl(const float* x_real, const float* x_imag, const void* w_packed,
+                      const float* bias_real, const float* bias_imag, float* y_real,
+                      float* y_imag, const ccv_conv_shape* shape, int precision, void* workspace,
+                      size_t workspace_bytes, ccv_stream_t stream);
+// x_strides: element strides (n, c, h, w) of the complex64 input, or null
+// for dense NCHW.
+int fprop_complex_impl(const void* x, const int64_t* x_strides, const void* w_packed,
+                       const float* bias_real, const float* bias_imag, void* y,
+                       const ccv_conv_shape* shape, int precision, void* workspace,
+                       size_t workspace_bytes, ccv_stream_t stream);
+
+// Counter sets (stream-K tile counters, layout-warp tickets) for one launch:
+// kSkCounterWords zeroed words in library-owned device memory.  A kernel
+// leaves its set zero when it ends (each split tile's counter is reset by
+// the piece that completes it; the last layout-warp CTA resets the rest), so
+// no memset precedes a launch.  A set is handed to one launch at a time:
+// sets taken by an entry point are marked in flight by a CUDA event
+// recorded on the launch's stream when the entry point returns (see
+// CounterScope), and a set is reused only once its event has completed.
+// Sets taken during stream capture stay with the captured graph for good.
+// When every set is in flight acquire_counter_set returns nullptr and the
+// caller runs a path without counters (no split, layout pass).
+// ccv_clear_device_status re-zeroes every set after an abort.
 constexpr int kSkCounterWords = 1024;
-unsigned* stream_k_counters();
+constexpr int kCounterSets = 64;
+unsigned* acquire_counter_set(cudaStream_t stream);
+// Internal return code of the pair launchers: no counter set was free for
+// the layout warps (nothing was launched; the caller takes another path).
+constexpr int kNoCounterSet = -100;
+
+// Marks the counter sets this host thread acquired since the scope began as
+// in flight on `stream` when the scope ends (records their events).  Every
+// C-ABI entry point that may launch with counters opens one.
+class CounterScope {
+ public:
+  explicit CounterScope(cudaStream_t stream);
+  ~CounterScope();
+  CounterScope(const CounterScope&) = delete;
+  CounterScope& operator=(const CounterScope&) = delete;
+
+ private:
+  cudaStream_t stream_;
+};
 
 // Programmatic dependent launch for the library's kernels (each calls
 // griddepcontrol.wait before its first global-memory access, so its prologue
 // may overlap the previous kernel's tail).  CCV_PDL=0 turns it off.
-bool pdl_enabled();
+inline bool pdl_enabled() { return knobs().pdl != 0; }
 
 // cudaLaunchKernelEx with PDL (when enabled) and, for cluster_x > 1, a
 // runtime cluster size.

@@ -143,7 +143,99 @@ __global__ void __launch_bounds__(256) ccv_nchw_to_planar_kernel(
   }
 }
 
+// Strided complex64 input (element strides sn, sc, sh, sw; any layout, e.g.
+// a slice or a channels-last tensor) -> fp32 NHWC planes.  One thread per
+// output element pair (two consecutive channels of one pixel): the stores
+// are coalesced along C; the loads follow the input's layout.
+__global__ void __launch_bounds__(256) ccv_strided_to_planar_kernel(
+    const float2* __restrict__ x, float* __restrict__ xr, float* __restrict__ xi,
+    float* __restrict__ xr_lo, float* __restrict__ xi_lo, int C, int H, int W, long long sn,
+    long long sc, long long sh, long long sw, long long total2) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total2;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long o = 2 * i;  // NHWC element index of channel pair (c, c + 1)
+    const int c = static_cast<int>(o % C);
+    long long t = o / C;
+    const int w = static_cast<int>(t % W);
+    t /= W;
+    const int h = static_cast<int>(t % H);
+    const long long n = t / H;
+    const long long a = n * sn + static_cast<long long>(c) * sc + h * sh + w * sw;
+    const float2 v0 = __ldg(x + a);
+    const float2 v1 = __ldg(x + a + sc);
+    if (xr_lo != nullptr) {
+      const float r0 = to_tf32(v0.x), r1 = to_tf32(v1.x), i0 = to_tf32(v0.y), i1 = to_tf32(v1.y);
+      *reinterpret_cast<float2*>(xr + o) = make_float2(r0, r1);
+      *reinterpret_cast<float2*>(xi + o) = make_float2(i0, i1);
+      *reinterpret_cast<float2*>(xr_lo + o) = make_float2(v0.x - r0, v1.x - r1);
+      *reinterpret_cast<float2*>(xi_lo + o) = make_float2(v0.y - i0, v1.y - i1);
+    } else {
+      *reinterpret_cast<float2*>(xr + o) = make_float2(v0.x, v1.x);
+      *reinterpret_cast<float2*>(xi + o) = make_float2(v0.y, v1.y);
+    }
+  }
+}
+
+// Channels-last complex64 input (C innermost, dense NHWC): the planes are a
+// plain de-interleave, four complex values per thread and step.
+__global__ void __launch_bounds__(256) ccv_nhwc_complex_to_planar_kernel(
+    const float4* __restrict__ x, float4* __restrict__ xr, float4* __restrict__ xi,
+    float4* __restrict__ xr_lo, float4* __restrict__ xi_lo, long long count4) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < count4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 a = __ldg(x + 2 * i);      // (re0, im0, re1, im1)
+    const float4 b = __ldg(x + 2 * i + 1);  // (re2, im2, re3, im3)
+    float4 r = make_float4(a.x, a.z, b.x, b.z);
+    float4 m = make_float4(a.y, a.w, b.y, b.w);
+    if (xr_lo != nullptr) {
+      const float4 rh = make_float4(to_tf32(r.x), to_tf32(r.y), to_tf32(r.z), to_tf32(r.w));
+      const float4 mh = make_float4(to_tf32(m.x), to_tf32(m.y), to_tf32(m.z), to_tf32(m.w));
+      xr_lo[i] = make_float4(r.x - rh.x, r.y - rh.y, r.z - rh.z, r.w - rh.w);
+      xi_lo[i] = make_float4(m.x - mh.x, m.y - mh.y, m.z - mh.z, m.w - mh.w);
+      r = rh;
+      m = mh;
+    }
+    xr[i] = r;
+    xi[i] = m;
+  }
+}
+
 }  // namespace
+
+int launch_strided_complex_to_planar(const float* x, const int64_t* strides, float* xr,
+                                     float* xi, float* xr_lo, float* xi_lo, const Problem& pb,
+                                     cudaStream_t stream) {
+  const long long C = pb.c, H = pb.h, W = pb.w;
+  const long long sn = strides[0], sc = strides[1], sh = strides[2], sw = strides[3];
+  if (sn == C * H * W && sc == H * W && sh == W && sw == 1) {
+    return launch_nchw_complex_to_planar(x, xr, xi, xr_lo, xi_lo, pb, stream);
+  }
+  const long long total = static_cast<long long>(pb.n) * H * W * C;
+  const int threads = 256;
+  cudaError_t e;
+  if (sc == 1 && sw == C && sh == W * C && sn == H * W * C &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    const long long c4 = total / 4;  // C % 4 == 0
+    const long long blocks = std::min<long long>((c4 + threads - 1) / threads, 148LL * 16);
+    e = launch_kernel(ccv_nhwc_complex_to_planar_kernel, dim3(static_cast<unsigned>(blocks)),
+                      dim3(threads), 0, stream, 0, reinterpret_cast<const float4*>(x),
+                      reinterpret_cast<float4*>(xr), reinterpret_cast<float4*>(xi),
+                      reinterpret_cast<float4*>(xr_lo), reinterpret_cast<float4*>(xi_lo), c4);
+  } else {
+    const long long t2 = total / 2;  // C % 4 == 0: channel pairs never straddle pixels
+    const long long blocks = std::min<long long>((t2 + threads - 1) / threads, 148LL * 16);
+    e = launch_kernel(ccv_strided_to_planar_kernel, dim3(static_cast<unsigned>(blocks)),
+                      dim3(threads), 0, stream, 0, reinterpret_cast<const float2*>(x), xr, xi,
+                      xr_lo, xi_lo, pb.c, pb.h, pb.w, sn, sc, sh, sw, t2);
+  }
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_error(e, "strided layout kernel launch");
+  return CCV_OK;
+}
 
 int launch_prepack(const float* w_real, const float* w_imag, int layout, const Problem& pb,
                    int precision, float* packed, cudaStream_t stream) {

@@ -22,9 +22,7 @@
 #pragma once
 
 #include <cstdint>
-#include <cstdlib>
 
-#include "ccv_cvt_role.cuh"
 #include "ccv_fprop_common.cuh"
 #include "ccv_ptx.cuh"
 
@@ -41,6 +39,16 @@ constexpr int kLwPrefixTicket = 2;         // chunks taken of the prefix
 constexpr int kLwTmaTicket = 3;            // TMA prefix: tiles taken
 constexpr int kLwTmaMaxImages = 16;        // TMA prefix: images at most
 constexpr int kLwFlag0 = 8;                 // image i: tickets completed
+// TMA prefix box: 8 rows x 16 pixels x 32 channels (32 KB of complex64 in,
+// two 16 KB fp32 planes out), kLwBoxBufs boxes in flight.
+constexpr int kLwBoxRows = 8;
+constexpr int kLwBoxPx = 16;
+constexpr int kLwBoxCh = 32;
+constexpr uint32_t kLwBoxInBytes = kLwBoxRows * kLwBoxCh * kLwBoxPx * 8u;
+constexpr uint32_t kLwBoxOutPlane = kLwBoxRows * kLwBoxPx * kLwBoxCh * 4u;
+constexpr int kLwBoxBufs = 4;
+// Shared memory the TMA prefix needs (input ring + two output buffers).
+constexpr uint32_t kLwBoxSmemBytes = kLwBoxBufs * kLwBoxInBytes + 2u * 2u * kLwBoxOutPlane;
 
 __device__ __forceinline__ int lw_tickets_per_image(const FpropParams& prm) {
   return ((prm.h * prm.w + kLwPx - 1) / kLwPx) * ((prm.c + kLwCh - 1) / kLwCh);
@@ -162,7 +170,7 @@ __device__ __forceinline__ void layout_warp(const FpropParams& prm, int lane, bo
   const int per_img = tpx * ((prm.c + kLwCh - 1) / kLwCh);
   const long long total = static_cast<long long>(per_img) * prm.n;
   const bool vec = (hw & 1) == 0 && (reinterpret_cast<uintptr_t>(prm.xc) & 15) == 0;
-  unsigned* ctrs = prm.cvt_ctrs;
+  unsigned* ctrs = prm.lw_ctrs;
   const long long first = prefix ? 0 : prm.lw_prefix;
   const long long end = prefix ? (prm.lw_prefix < total ? prm.lw_prefix : total) : total;
   unsigned* counter = ctrs + (prefix ? kLwPrefixTicket : kLwTicket);
@@ -234,8 +242,7 @@ __device__ __forceinline__ void layout_warp(const FpropParams& prm, int lane, bo
 // cluster tile (one m-tile); CCV_LW_PREFIX=0 turns the phase off (timing
 // knob).
 inline long long lw_prefix_images(const FpropParams& prm, int launched, long long tile_px) {
-  const char* env = getenv("CCV_LW_PREFIX");
-  if (env != nullptr && atoi(env) == 0) return 0;
+  if (knobs().lw_prefix == 0) return 0;
   const long long pq = static_cast<long long>(prm.p) * prm.q;
   const long long mtiles = (launched + prm.tiles_n - 1) / prm.tiles_n;
   long long images = (mtiles * tile_px + pq - 1) / pq;
@@ -254,8 +261,7 @@ inline long long lw_prefix_tickets(const FpropParams& prm, int launched, long lo
 // number 1..kLwTmaMaxImages, else the all-warp ticket prefix.
 inline void lw_plan_prefix(FpropParams& prm, int launched, long long tile_px) {
   long long images = lw_prefix_images(prm, launched, tile_px);
-  const char* env = getenv("CCV_LW_TMA");
-  const bool tma_on = env == nullptr || atoi(env) != 0;
+  const bool tma_on = knobs().lw_tma != 0;
   if (prm.lw_tma_images < 0 && tma_on && images >= 1) {
     // The TMA prefix converts at ~3 TB/s with every warp, the layout warps
     // at ~0.85 TB/s of input beside the MMAs (B200): take so many images
@@ -267,17 +273,14 @@ inline void lw_plan_prefix(FpropParams& prm, int launched, long long tile_px) {
     const long long fit = static_cast<long long>(t_conv * 0.85e12 / img_bytes);
     const long long balance = prm.n - fit;
     if (balance > images) images = balance;
-    const char* force = getenv("CCV_LW_TMA_IMAGES");
-    if (force != nullptr && atoi(force) > 0) images = atoi(force);
+    if (knobs().lw_tma_images > 0) images = knobs().lw_tma_images;
     images = images < prm.n ? images : prm.n;
   }
   if (prm.lw_tma_images < 0 && tma_on && images >= 1 && images <= kLwTmaMaxImages) {
     const long long per_img = ((static_cast<long long>(prm.h) * prm.w + kLwPx - 1) / kLwPx) *
                               ((prm.c + kLwCh - 1) / kLwCh);
-    const char* bufs = getenv("CCV_LW_TMA_BUFS");  // boxes in flight (timing knob)
-    prm.lw_tma_bufs = bufs != nullptr && atoi(bufs) >= 2 && atoi(bufs) <= kCvtInBufs
-                          ? atoi(bufs)
-                          : kCvtInBufs;
+    const int bufs = knobs().lw_tma_bufs;  // boxes in flight (timing knob)
+    prm.lw_tma_bufs = bufs >= 2 && bufs <= kLwBoxBufs ? bufs : kLwBoxBufs;
     prm.lw_tma_images = static_cast<int>(images);
     prm.lw_prefix = images * per_img;
     return;
@@ -289,11 +292,11 @@ inline void lw_plan_prefix(FpropParams& prm, int launched, long long tile_px) {
 // TMA prefix: before taking up their roles, every thread of the CTA converts
 // tiles of the first lw_tma_images images (conversion order) through the
 // idle operand rings: complex64 boxes of 8 rows x 16 pixels x 32 channels
-// loaded by TMA (kCvtInBufs in flight), transposed in shared memory, the
+// loaded by TMA (kLwBoxBufs in flight), transposed in shared memory, the
 // two fp32 planes stored by TMA.  Tiles are handed out by a counter, so any
 // running CTA can finish them; each CTA adds its tile count per image once
-// its stores have landed.  `buf`: kCvtSmemBytes at a 1024-byte boundary;
-// `full0`: kCvtInBufs mbarriers (count 1); `sm`: kCvtInBufs + kLwTmaMaxImages
+// its stores have landed.  `buf`: kLwBoxSmemBytes at a 1024-byte boundary;
+// `full0`: kLwBoxBufs mbarriers (count 1); `sm`: kLwBoxBufs + kLwTmaMaxImages
 // words of shared memory.  Returns false if a wait ran out (status set).
 __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* buf, uint32_t full0,
                                               unsigned* sm) {
@@ -301,17 +304,17 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int nwarps = blockDim.x >> 5;
-  const int th = (prm.h + kCvtRows - 1) / kCvtRows;
-  const int tw = (prm.w + kCvtPx - 1) / kCvtPx;
-  const int tc = (prm.c + kCvtCh - 1) / kCvtCh;
+  const int th = (prm.h + kLwBoxRows - 1) / kLwBoxRows;
+  const int tw = (prm.w + kLwBoxPx - 1) / kLwBoxPx;
+  const int tc = (prm.c + kLwBoxCh - 1) / kLwBoxCh;
   const int per_img = th * tw * tc;
   const unsigned total = static_cast<unsigned>(per_img * prm.lw_tma_images);
-  const int nbuf = prm.lw_tma_bufs;  // boxes in flight (<= kCvtInBufs)
-  unsigned* ctr = prm.cvt_ctrs + kLwTmaTicket;
+  const int nbuf = prm.lw_tma_bufs;  // boxes in flight (<= kLwBoxBufs)
+  unsigned* ctr = prm.lw_ctrs + kLwTmaTicket;
   volatile unsigned* tks = sm;                   // ticket of each input buffer
-  volatile unsigned* cnt = sm + kCvtInBufs;      // this CTA's tiles per image (order)
+  volatile unsigned* cnt = sm + kLwBoxBufs;      // this CTA's tiles per image (order)
   uint8_t* in = buf;
-  uint8_t* out = buf + nbuf * kCvtInBytes;
+  uint8_t* out = buf + nbuf * kLwBoxInBytes;
   const uint32_t in_u = ptx::smem_u32(in);
   const uint32_t out_u = ptx::smem_u32(out);
   auto coords = [&](unsigned tk, int& order, int& img, int& c0, int& w0, int& h0) {
@@ -320,9 +323,9 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
     img = (order + prm.lw_first_img) % prm.n;
     const int cb = j % tc;
     const int rest = j / tc;
-    c0 = cb * kCvtCh;
-    w0 = (rest % tw) * kCvtPx;
-    h0 = (rest / tw) * kCvtRows;
+    c0 = cb * kLwBoxCh;
+    w0 = (rest % tw) * kLwBoxPx;
+    h0 = (rest / tw) * kLwBoxRows;
   };
   auto load = [&](int b, unsigned tk) {  // thread 0
     tks[b] = tk;
@@ -330,8 +333,8 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
       int order, img, c0, w0, h0;
       coords(tk, order, img, c0, w0, h0);
       const uint32_t bar = full0 + 8u * static_cast<uint32_t>(b);
-      ptx::mbar_arrive_expect_tx(bar, kCvtInBytes);
-      ptx::tma_load_4d(in_u + static_cast<uint32_t>(b) * kCvtInBytes, &prm.tm_cin, bar, w0, c0, h0,
+      ptx::mbar_arrive_expect_tx(bar, kLwBoxInBytes);
+      ptx::tma_load_4d(in_u + static_cast<uint32_t>(b) * kLwBoxInBytes, &prm.tm_cin, bar, w0, c0, h0,
                        img);
     }
   };
@@ -362,28 +365,28 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
       break;
     }
     // Transpose: lane = channel, (row, pixel pair) spread over the warps.
-    const uint8_t* src = in + static_cast<uint32_t>(b) * kCvtInBytes;
-    float* orr = reinterpret_cast<float*>(out + static_cast<uint32_t>(ob) * 2u * kCvtOutPlane);
-    float* oii = orr + kCvtOutPlane / 4;
-    for (int idx = warp; idx < kCvtRows * (kCvtPx / 2); idx += nwarps) {
-      const int r = idx / (kCvtPx / 2);
-      const int q = idx % (kCvtPx / 2);
-      const int line = r * kCvtCh + lane;
+    const uint8_t* src = in + static_cast<uint32_t>(b) * kLwBoxInBytes;
+    float* orr = reinterpret_cast<float*>(out + static_cast<uint32_t>(ob) * 2u * kLwBoxOutPlane);
+    float* oii = orr + kLwBoxOutPlane / 4;
+    for (int idx = warp; idx < kLwBoxRows * (kLwBoxPx / 2); idx += nwarps) {
+      const int r = idx / (kLwBoxPx / 2);
+      const int q = idx % (kLwBoxPx / 2);
+      const int line = r * kLwBoxCh + lane;
       // 128-byte swizzle: 16-byte chunk q of line `line` is at chunk q ^ (line & 7).
       const float4 v = *reinterpret_cast<const float4*>(
           src + static_cast<uint32_t>(line) * 128u + (static_cast<uint32_t>(q ^ (line & 7)) << 4));
-      const int p0 = (r * kCvtPx + 2 * q) * kCvtCh + lane;
+      const int p0 = (r * kLwBoxPx + 2 * q) * kLwBoxCh + lane;
       orr[p0] = v.x;
       oii[p0] = v.y;
-      orr[p0 + kCvtCh] = v.z;
-      oii[p0 + kCvtCh] = v.w;
+      orr[p0 + kLwBoxCh] = v.z;
+      oii[p0 + kLwBoxCh] = v.w;
     }
     ptx::fence_proxy_async_shared();
     __syncthreads();
     if (tid == 0) {
-      const uint32_t o = out_u + static_cast<uint32_t>(ob) * 2u * kCvtOutPlane;
+      const uint32_t o = out_u + static_cast<uint32_t>(ob) * 2u * kLwBoxOutPlane;
       ptx::tma_store_4d(&prm.tm_pr, o, c0, w0, h0, img);
-      ptx::tma_store_4d(&prm.tm_pi, o + kCvtOutPlane, c0, w0, h0, img);
+      ptx::tma_store_4d(&prm.tm_pi, o + kLwBoxOutPlane, c0, w0, h0, img);
       ptx::bulk_commit_group();
       cnt[order] = cnt[order] + 1u;
       load(b, nxt);  // buffer b was read by the transpose above
@@ -398,7 +401,7 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
       const unsigned c = cnt[o];
       if (c != 0u) {
         const int img = (o + prm.lw_first_img) % prm.n;
-        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(prm.cvt_ctrs + kLwFlag0 + img),
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(prm.lw_ctrs + kLwFlag0 + img),
                      "r"(c)
                      : "memory");
       }
@@ -411,12 +414,12 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
 // Waits (bounded) until image `img`'s planes are written; then orders the
 // caller's later TMA (async-proxy) reads after those generic-proxy stores.
 __device__ __forceinline__ int lw_tma_tiles_per_image(const FpropParams& prm) {
-  return ((prm.h + kCvtRows - 1) / kCvtRows) * ((prm.w + kCvtPx - 1) / kCvtPx) *
-         ((prm.c + kCvtCh - 1) / kCvtCh);
+  return ((prm.h + kLwBoxRows - 1) / kLwBoxRows) * ((prm.w + kLwBoxPx - 1) / kLwBoxPx) *
+         ((prm.c + kLwBoxCh - 1) / kLwBoxCh);
 }
 
 __device__ __forceinline__ bool lw_wait_image(const FpropParams& prm, int img) {
-  const unsigned* f = prm.cvt_ctrs + kLwFlag0 + img;
+  const unsigned* f = prm.lw_ctrs + kLwFlag0 + img;
   // Images the TMA prefix converted count tiles, the others tickets.
   const int order = (img - prm.lw_first_img + prm.n) % prm.n;
   const unsigned need = static_cast<unsigned>(order < prm.lw_tma_images
@@ -429,7 +432,7 @@ __device__ __forceinline__ bool lw_wait_image(const FpropParams& prm, int img) {
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
     if (v >= need) break;
     if (ptx::globaltimer() - t0 > CCV_WAIT_TIMEOUT_NS) {
-      atomicCAS(prm.status, 0, CCV_ERR_DEVICE_TIMEOUT);
+      ptx::report_status(prm.status, CCV_ERR_DEVICE_TIMEOUT);
       return false;
     }
     ptx::nanosleep(ns);

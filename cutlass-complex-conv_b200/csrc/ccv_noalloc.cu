@@ -83,9 +83,11 @@ extern "C" int ccv_forward_noalloc(const float* x_real, const float* x_imag,
   void* scratch = nullptr;
   rc = noalloc_scratch(&scratch);
   if (rc != CCV_OK) return rc;
-  rc = ccv_prepack_weights(w_real_krsc, w_imag_krsc, CCV_WEIGHT_KRSC, shape, CCV_PRECISION_TF32,
-                           scratch, kNoAllocMaxWeightBytes, stream);
+  // The entry-point bodies without the public functions' one-time pinned
+  // allocation of the host-visible status mirror.
+  rc = prepack_weights_impl(w_real_krsc, w_imag_krsc, CCV_WEIGHT_KRSC, shape, CCV_PRECISION_TF32,
+                            scratch, kNoAllocMaxWeightBytes, stream);
   if (rc != CCV_OK) return rc;
-  return ccv_fprop_planar(x_real, x_imag, scratch, y_real, y_imag, shape, CCV_PRECISION_TF32,
-                          nullptr, 0, stream);
+  return fprop_planar_impl(x_real, x_imag, scratch, nullptr, nullptr, y_real, y_imag, shape,
+                           CCV_PRECISION_TF32, nullptr, 0, stream);
 }

@@ -87,10 +87,27 @@ __device__ __forceinline__ void fence_proxy_async_shared() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Records a failed wait: `code` into *status (first error wins) and, with
+// MIRROR, into the host-mapped mirror whose device address the library's
+// status block keeps in its words 2-3 (status points at word 0 of that
+// block), so host code sees the timeout without synchronizing.
+template <bool MIRROR = true>
+__device__ __forceinline__ void report_status(int* status, int code) {
+  if (status == nullptr) return;
+  atomicCAS(status, 0, code);
+  if constexpr (MIRROR) {
+    int* host = *reinterpret_cast<int* const volatile*>(status + 2);
+    if (host != nullptr) {
+      *reinterpret_cast<volatile int*>(host) = code;
+      __threadfence_system();
+    }
+  }
+}
+
 // Wait for the phase with the given parity to complete, for at most
-// CCV_WAIT_TIMEOUT_NS.  On timeout, writes `code` into *status (first error
-// wins) and returns false.
-template <bool CLUSTER_ACQUIRE = false>
+// CCV_WAIT_TIMEOUT_NS.  On timeout, reports `code` (report_status) and
+// returns false.
+template <bool CLUSTER_ACQUIRE = false, bool MIRROR = true>
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int* status,
                                                   int code) {
   auto test = [&]() {
@@ -105,7 +122,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
   while (true) {
     if (test()) return true;
     if (globaltimer() - t0 > CCV_WAIT_TIMEOUT_NS) {
-      if (status != nullptr) atomicCAS(status, 0, code);
+      report_status<MIRROR>(status, code);
       return false;
     }
   }
@@ -130,7 +147,7 @@ __device__ __forceinline__ bool mbar_wait_bounded_backoff(uint32_t bar, uint32_t
   while (true) {
     if (test()) return true;
     if (globaltimer() - t0 > CCV_WAIT_TIMEOUT_NS) {
-      if (status != nullptr) atomicCAS(status, 0, code);
+      report_status(status, code);
       return false;
     }
     asm volatile("nanosleep.u32 %0;" ::"r"(ns));

@@ -5,10 +5,13 @@
  * extension `complex_conv2d._C` (pybind module defined in
  * csrc/bindings.cpp:16-29 of jaeeunHwang/cutlass-complex-conv, whose body is
  * `complex_conv2d_cuda` in csrc/complex_conv2d.cu:84-309).  All entry points
- * take plain device pointers and sizes; none allocates memory.  Scratch
- * memory comes from the caller: the *_workspace_bytes queries give the size
- * that enables every optimisation, *_min_workspace_bytes the size a call
- * cannot run without.  Every launch is asynchronous on the given stream.
+ * take plain device pointers and sizes and allocate no device memory.
+ * Scratch memory comes from the caller: the *_workspace_bytes queries give
+ * the size that enables every optimisation, *_min_workspace_bytes the size a
+ * call cannot run without.  The first launching call on a device makes one
+ * 4-byte pinned host allocation (the host copy of the device status word,
+ * see ccv_get_device_status); ccv_forward_noalloc makes none.  Every launch
+ * is asynchronous on the given stream.
  *
  * Conventions
  *   - Activation planes x_real/x_imag: fp32 NHWC, contiguous
@@ -93,8 +96,7 @@ int ccv_prepack_weights(const float* w_real, const float* w_imag, int layout,
  * of the last partial wave of output tiles (partial sums and counters; an
  * upper bound for the current device).  *_min_workspace_bytes: the required
  * part alone; a call given only that runs every tile whole.  The required
- * part is 0 for TF32 planar calls and for complex calls served by the fused
- * complex-input kernel. */
+ * part is 0 for TF32 planar calls. */
 size_t ccv_fprop_planar_workspace_bytes(const ccv_conv_shape* shape, int precision);
 size_t ccv_fprop_complex_workspace_bytes(const ccv_conv_shape* shape, int precision);
 size_t ccv_fprop_planar_min_workspace_bytes(const ccv_conv_shape* shape, int precision);
@@ -102,18 +104,15 @@ size_t ccv_fprop_complex_min_workspace_bytes(const ccv_conv_shape* shape, int pr
 
 /* Number of library kernels one ccv_fprop_planar (complex_input = 0) or
  * ccv_fprop_complex (complex_input = 1) call launches: the conv kernel plus
- * any layout/split pass (a stream-K counter reset, when taken, is one
- * cudaMemsetAsync on top). */
+ * any layout/split pass. */
 int ccv_fprop_kernel_launches(const ccv_conv_shape* shape, int precision, int complex_input,
                               int* kernels);
 
 /* Name of the kernel path ccv_fprop_complex takes for this problem (static
- * string): "complex_direct_pair" (activations read from complex64 NCHW by
- * TMA, one launch), "halo_pair_converter_warps" (one launch),
- * "halo_pair_converter_clusters" (one launch; some clusters convert images
- * into the workspace planes for the others), or "layout_pass+<kernel>" (a
- * complex64 -> planar pass, then the kernel).  The first three are opt-in
- * through the CCV_CD, CCV_FUSED and CCV_CVT environment switches. */
+ * string): "halo_pair_layout_warps" / "tap_pair_layout_warps" (one launch:
+ * warps of the convolution kernel convert the complex64 input into the
+ * workspace planes it reads) or "layout_pass+<kernel>" (a complex64 ->
+ * planar pass, then the kernel). */
 const char* ccv_fprop_complex_kernel(const ccv_conv_shape* shape, int precision);
 
 /* Planar fprop: fp32 NHWC planes in, fp32 NPQK planes out, packed weights.
@@ -131,10 +130,39 @@ int ccv_fprop_planar(const float* x_real, const float* x_imag, const void* w_pac
 
 /* Complex fprop: complex64 NCHW in, complex64 NKPQ out, packed weights.
  * Replaces the layout conversions plus kernel of ComplexConv2d.forward
- * (modules.py:176-207). */
+ * (modules.py:176-207).  Needs ccv_fprop_complex_min_workspace_bytes() of
+ * workspace (fp32 planes of the input). */
 int ccv_fprop_complex(const void* x, const void* w_packed, void* y,
                       const ccv_conv_shape* shape, int precision, void* workspace,
                       size_t workspace_bytes, ccv_stream_t stream);
+
+/* ccv_fprop_planar / ccv_fprop_complex with a complex bias per output
+ * channel: y[n, k, p, q] += bias_real[k] + i * bias_imag[k], added once to
+ * the final sums in the kernels' epilogue.  bias_real and bias_imag are K
+ * fp32 values each on the device, 16-byte aligned; both null is the call
+ * without bias.  The reference rejects bias=True (modules.py:73-74), so
+ * these have no reference counterpart; the bias is the one of
+ * torch.nn.Conv2d on complex64 tensors. */
+int ccv_fprop_planar_bias(const float* x_real, const float* x_imag, const void* w_packed,
+                          const float* bias_real, const float* bias_imag, float* y_real,
+                          float* y_imag, const ccv_conv_shape* shape, int precision,
+                          void* workspace, size_t workspace_bytes, ccv_stream_t stream);
+int ccv_fprop_complex_bias(const void* x, const void* w_packed, const float* bias_real,
+                           const float* bias_imag, void* y, const ccv_conv_shape* shape,
+                           int precision, void* workspace, size_t workspace_bytes,
+                           ccv_stream_t stream);
+
+/* ccv_fprop_complex_bias on a complex64 input of any layout: x_strides[4]
+ * are the element strides of dimensions (n, c, h, w) - a channels-last
+ * tensor, a slice, a view with a step.  Replaces the .contiguous() copy that
+ * ComplexConv2d.forward makes of such inputs (modules.py:198-199): the
+ * layout kernel reads the strides directly.  x 8-byte aligned; strides >= 0.
+ * Dense NCHW strides take the ccv_fprop_complex path.  Output, workspace
+ * and bias as ccv_fprop_complex_bias (bias pointers may be null). */
+int ccv_fprop_complex_strided(const void* x, const int64_t* x_strides, const void* w_packed,
+                              const float* bias_real, const float* bias_imag, void* y,
+                              const ccv_conv_shape* shape, int precision, void* workspace,
+                              size_t workspace_bytes, ccv_stream_t stream);
 
 /* Planar fp32 NHWC in, complex64 NKPQ out: the convolution launch of
  * ccv_fprop_complex without its layout pass (for callers that hold planar
@@ -172,16 +200,27 @@ int ccv_forward_noalloc(const float* x_real, const float* x_imag,
 
 /* Device status word of the current device: nonzero after an in-kernel
  * bounded wait ran out (a CCV_ERR_* code).  While it is set, fprop kernels
- * on that device exit without work.  get copies it to the host
- * (synchronizes the device); clear resets it. */
+ * on that device exit without work.  The kernel that gives up also writes a
+ * host-mapped copy of the word (set up by the first allocating call on the
+ * device), and every entry point that launches work reads that copy first:
+ * once a timeout has reached it, they return CCV_ERR_DEVICE and launch
+ * nothing until ccv_clear_device_status.  (A call enqueued before the
+ * timeout happened returns CCV_OK and its kernels exit without work.)
+ * get copies the device word to the host (synchronizes the device); clear
+ * resets the word, its host copy and the library's counter sets. */
 int ccv_get_device_status(int* status);
 int ccv_clear_device_status(void);
 
 /* Self-test of the bounded wait: launches one CTA that waits on an mbarrier
  * nothing arrives on.  The wait gives up after its time limit and the
  * kernel writes CCV_ERR_DEVICE_TIMEOUT into *status_dev (a device int the
- * caller zeroed), leaving the context usable. */
+ * caller zeroed), leaving the context usable.  status_dev == NULL: into the
+ * library's own status word (and its host copy), as a real timeout would. */
 int ccv_selftest_bounded_wait(int* status_dev, ccv_stream_t stream);
+
+/* Re-reads the CCV_* environment switches (testing and benchmarking knobs,
+ * read once on first use otherwise). */
+int ccv_reload_config(void);
 
 /* Text of the last error raised on the calling host thread. */
 const char* ccv_last_error_message(void);

@@ -255,11 +255,24 @@ def planar_nhwc_to_complex_nchw(y_real: torch.Tensor, y_imag: torch.Tensor) -> t
 
 
 def oracle_fp64(case: ConvCase, x: torch.Tensor, w_real: torch.Tensor,
-                w_imag: torch.Tensor) -> torch.Tensor:
-    """The parity oracle used by the GPU tests: fp64 four-conv on CPU."""
-    return four_conv(x.cpu(), w_real.cpu(), w_imag.cpu(),
-                     (case.stride_h, case.stride_w), (case.pad_h, case.pad_w),
-                     dtype=torch.float64)
+                w_imag: torch.Tensor, bias_real: Optional[torch.Tensor] = None,
+                bias_imag: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The parity oracle used by the GPU tests: fp64 four-conv on CPU.
+
+    With ``bias_real``/``bias_imag`` (K values each), the complex bias
+    ``bias_real[k] + 1j * bias_imag[k]`` is added to output channel k - the
+    bias of ``torch.nn.Conv2d`` on complex tensors.  The reference has no
+    bias (``modules.py:73-74`` rejects it; ``benchmarks/baseline.py:27-42``
+    builds its convolutions with ``bias=False``), so this extension is
+    restated here from that definition.
+    """
+    y = four_conv(x.cpu(), w_real.cpu(), w_imag.cpu(),
+                  (case.stride_h, case.stride_w), (case.pad_h, case.pad_w),
+                  dtype=torch.float64)
+    if bias_real is not None:
+        b = torch.complex(bias_real.cpu().double(), bias_imag.cpu().double())
+        y = y + b.view(1, -1, 1, 1)
+    return y
 
 
 def time_cpu_four_conv(case: ConvCase, iters: int, warmup: int = 1,

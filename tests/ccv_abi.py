@@ -64,6 +64,12 @@ def load():
                                                      ctypes.POINTER(ctypes.c_int)]),
         "ccv_fprop_planar": (ctypes.c_int, [vp, vp, vp, vp, vp, sp, ctypes.c_int, vp, sz, vp]),
         "ccv_fprop_complex": (ctypes.c_int, [vp, vp, vp, sp, ctypes.c_int, vp, sz, vp]),
+        "ccv_fprop_planar_bias": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, vp, sp, ctypes.c_int, vp,
+                                                 sz, vp]),
+        "ccv_fprop_complex_bias": (ctypes.c_int, [vp, vp, vp, vp, vp, sp, ctypes.c_int, vp, sz,
+                                                  vp]),
+        "ccv_fprop_complex_strided": (ctypes.c_int, [vp, i64p, vp, vp, vp, vp, sp, ctypes.c_int,
+                                                     vp, sz, vp]),
         "ccv_fprop_planar_to_complex": (ctypes.c_int, [vp, vp, vp, vp, sp, ctypes.c_int, vp, sz,
                                                        vp]),
         "ccv_fprop_complex_kernel": (ctypes.c_char_p, [sp, ctypes.c_int]),
@@ -75,13 +81,40 @@ def load():
         "ccv_selftest_bounded_wait": (ctypes.c_int, [vp, vp]),
         "ccv_last_error_message": (ctypes.c_char_p, []),
         "ccv_version": (ctypes.c_char_p, []),
+        "ccv_reload_config": (ctypes.c_int, []),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)
         f.restype = res
         f.argtypes = args
-    _lib = lib
-    return lib
+    _lib = _ConfigTracking(lib)
+    return _lib
+
+
+class _ConfigTracking:
+    """The library handle, re-reading the library's CCV_* switches (which it
+    reads once) before any call made after the test changed one of them."""
+
+    def __init__(self, lib):
+        self._lib = lib
+        self._env = None
+
+    def _sync(self):
+        snap = tuple(sorted((k, v) for k, v in os.environ.items() if k.startswith("CCV_")))
+        if snap != self._env:
+            self._lib.ccv_reload_config()
+            self._env = snap
+
+    def __getattr__(self, name):
+        f = getattr(self._lib, name)
+        if not name.startswith("ccv_") or name == "ccv_reload_config":
+            return f
+
+        def call(*args):
+            self._sync()
+            return f(*args)
+
+        return call
 
 
 def last_error():

@@ -32,3 +32,14 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+@pytest.fixture(autouse=True)
+def _library_switches_follow_env():
+    """Tests pin kernels through CCV_* environment switches, which the library
+    reads once; after each test the switches are re-read, so a test that
+    restored the environment leaves the library as it found it."""
+    yield
+    import ccv_abi
+    if ccv_abi._lib is not None:
+        ccv_abi._lib._sync()

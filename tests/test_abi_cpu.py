@@ -21,7 +21,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_binding_covers_header():
-    lib = ccv_abi.load()
+    lib = ccv_abi.load()._lib
     for n in ccv_abi.declared_functions():
         assert getattr(lib, n).restype is not None, n
 

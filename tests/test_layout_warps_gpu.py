@@ -35,13 +35,11 @@ CASES = [
 
 @pytest.fixture
 def knobs():
-    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_LW", "CCV_CVT", "CCV_STREAMK", "CCV_CD",
-            "CCV_FUSED", "CCV_SUBBOX")
+    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_LW", "CCV_STREAMK", "CCV_SUBBOX")
     old = {k: os.environ.get(k) for k in keys}
     os.environ["CCV_FORCE_KERNEL"] = "2"
     os.environ["CCV_HALO"] = "1"
-    for k in ("CCV_CVT", "CCV_CD", "CCV_FUSED", "CCV_SUBBOX"):
-        os.environ.pop(k, None)
+    os.environ.pop("CCV_SUBBOX", None)
     # Layout warps wherever they apply (by default only for grids of two or
     # more waves of tiles).
     os.environ["CCV_LW"] = "1"
@@ -173,10 +171,6 @@ def test_layout_warps_not_taken(knobs):
     s2 = C(32, 64, 112, 112, 128, 3, 3, 2, 2, 1, 1)
     assert kernel_name(s2) == "layout_pass+tap_pair"
     assert kernel_name(s2, ccv_abi.CCV_PRECISION_3XTF32) == "tap_pair_layout_warps"
-    # The opt-in converter clusters take precedence when asked for.
-    os.environ["CCV_CVT"] = "1"
-    assert kernel_name(C(8, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == \
-        "halo_pair_converter_clusters"
 
 
 @pytest.mark.parametrize("name,case", [CASES[0], ("b3_c64_ragged", C(3, 64, 45, 29, 96, 3, 3, 1, 1, 1, 1))],

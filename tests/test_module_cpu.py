@@ -11,8 +11,6 @@ from complex_conv2d.modules import _pair
 
 
 def test_rejects_unsupported_options():
-    with pytest.raises(NotImplementedError, match="bias"):
-        ComplexConv2d(32, 64, 3, bias=True)
     with pytest.raises(NotImplementedError, match="groups"):
         ComplexConv2d(32, 64, 3, groups=2)
     with pytest.raises(NotImplementedError, match="dilation"):
@@ -21,6 +19,25 @@ def test_rejects_unsupported_options():
         ComplexConv2d(32, 64, 3, padding_mode="reflect")
     with pytest.raises(NotImplementedError, match="complex64"):
         ComplexConv2d(32, 64, 3, dtype=torch.complex128)
+
+
+def test_complex_bias_parameters():
+    """bias=True (rejected by the reference, modules.py:73-74) adds a complex
+    bias per output channel: two fp32 [K] parameters in the state_dict,
+    initialised like nn.Conv2d's bias."""
+    m = ComplexConv2d(8, 12, (3, 5), bias=True)
+    assert m.bias_real.shape == (12,) and m.bias_imag.shape == (12,)
+    assert m.bias_real.dtype == torch.float32
+    assert not m.bias_real.requires_grad and not m.bias_imag.requires_grad
+    assert set(m.state_dict()) == {"weight_real", "weight_imag", "bias_real", "bias_imag"}
+    bound = 1.0 / (8 * 15) ** 0.5
+    assert m.bias_real.abs().max().item() <= bound and m.bias_imag.abs().max().item() <= bound
+    m2 = ComplexConv2d(8, 12, (3, 5), bias=True)
+    m2.load_state_dict(m.state_dict())
+    assert torch.equal(m2.bias_imag, m.bias_imag)
+    assert "bias=True" in repr(m)
+    plain = ComplexConv2d(8, 12, 3)
+    assert plain.bias_real is None and plain.bias_imag is None
 
 
 def test_rejects_bad_sizes():

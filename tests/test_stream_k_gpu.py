@@ -43,14 +43,11 @@ GRIDS = [3, 7]
 
 @pytest.fixture
 def knobs():
-    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_STREAMK", "CCV_MAX_CLUSTERS", "CCV_CD",
-            "CCV_FUSED", "CCV_SUBBOX", "CCV_CVT", "CCV_LW")
+    keys = ("CCV_FORCE_KERNEL", "CCV_HALO", "CCV_STREAMK", "CCV_MAX_CLUSTERS", "CCV_SUBBOX",
+            "CCV_LW")
     old = {k: os.environ.get(k) for k in keys}
-    # The split lives in the planar-operand pair kernels with one box per CTA
-    # (not with converter clusters or layout warps).
-    os.environ["CCV_CD"] = "0"
+    # The split lives in the pair kernels with one box per CTA.
     os.environ["CCV_SUBBOX"] = "0"
-    os.environ["CCV_CVT"] = "0"
     os.environ["CCV_LW"] = "0"  # complex calls: layout pass + the split kernel
 
     def set_(family=None, streamk=None, clusters=None):
@@ -129,12 +126,6 @@ def test_stream_k_split(knobs, name, case, family, precision):
         reassociated |= not torch.equal(y1, whole)
         yc = complex_(case, x, packed, precision)
         assert torch.equal(yc, y1.to(torch.complex64)), grid
-        if family == "halo":
-            # The converter-warp variant reads complex64 and splits the same way.
-            os.environ["CCV_FUSED"] = "1"
-            yf = complex_(case, x, packed, precision)
-            os.environ.pop("CCV_FUSED", None)
-            assert torch.equal(yf, yc), grid
         # Without stream-K room in the workspace every tile runs whole.
         y0 = planar(case, x, packed, precision, full_workspace=False)
         if precision == TF32:

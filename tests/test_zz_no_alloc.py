@@ -87,6 +87,33 @@ def test_noalloc_matches_workspace_entry_on_two_calls():
     assert st.value == 0
 
 
+@pytest.mark.gpu
+def test_noalloc_back_to_back_on_one_stream_without_sync():
+    """Two calls with different weights enqueued on one stream with no host
+    sync between them: the second call's weight prepack rewrites the shared
+    array only after the first call's convolution has finished reading it
+    (stream order; with programmatic dependent launch the prepack kernel
+    waits for the previous kernel to complete before its first global
+    access), so each output matches ccv_forward on its own weights."""
+    torch.cuda.set_device(0)
+    lib = ccv_abi.load()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    case = oracle.ConvCase(2, 64, 24, 24, 128, 3, 3, 1, 1, 1, 1)
+    xr, xi, wr1, wi1 = _inputs(case, seed=21)
+    _, _, wr2, wi2 = _inputs(case, seed=23)
+    ya = _run_noalloc(lib, case, xr, xi, wr1, wi1, stream)
+    yb = _run_noalloc(lib, case, xr, xi, wr2, wi2, stream)
+    ra = _run_with_workspace(lib, case, xr, xi, wr1, wi1, stream)
+    rb = _run_with_workspace(lib, case, xr, xi, wr2, wi2, stream)
+    torch.cuda.synchronize()
+    for got, want in ((ya, ra), (yb, rb)):
+        g, w = _as_complex(*got), _as_complex(*want)
+        assert not torch.isnan(g.real).any() and not torch.isnan(g.imag).any()
+        assert oracle.rel_frobenius(g, w) <= TF32_TOL
+    # The two weight sets give different outputs (the test can tell them apart).
+    assert oracle.rel_frobenius(_as_complex(*ya), _as_complex(*yb)) > 0.1
+
+
 def test_noalloc_rejects_weights_above_fixed_scratch():
     """Rejected on the host, before any device work: 3x3, K*C above 155,344."""
     lib = ccv_abi.load()
