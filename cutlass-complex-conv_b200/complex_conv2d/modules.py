@@ -357,7 +357,10 @@ class ComplexConv2d(nn.Module):
             ``out``.  Like ``Tensor.copy_(..., non_blocking=True)``, the call
             returns before the copies end: ``out`` holds the result once the
             current CUDA stream has reached this point (e.g. after
-            ``torch.cuda.current_stream().synchronize()``).
+            ``torch.cuda.current_stream().synchronize()``).  Until then the
+            copy-in stream may still be reading ``x``: a caller that reuses
+            a pinned staging buffer must not refill ``x`` before that point
+            either.
         """
         if x.is_cuda:
             raise ValueError("forward_host takes a host tensor; use forward for CUDA input")

@@ -600,10 +600,15 @@ int fprop_complex_impl(const void* x, const int64_t* x_strides, const void* w_pa
       if (x_strides[i] < 0) return set_error(CCV_ERR_INVALID_ARGUMENT, "negative input stride");
     }
   }
-  if (dense ? !aligned16(x) : (reinterpret_cast<uintptr_t>(x) & 7u) != 0) {
-    return set_error(CCV_ERR_INVALID_ARGUMENT,
-                     "complex input must be 16-byte aligned (dense) or 8-byte aligned (strided)");
+  if ((reinterpret_cast<uintptr_t>(x) & 7u) != 0) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "complex input must be 8-byte aligned");
   }
+  // The layout-warp path reads dense input in 16-byte pieces; a dense input
+  // at an 8-byte boundary goes through the layout kernels (8-byte loads).
+  if (x_strides == nullptr && !aligned16(x)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  }
+  dense = dense && aligned16(x);
   if (!aligned16(w_packed) || !aligned16(y)) {
     return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
   }

@@ -110,15 +110,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tmem_alloc(ptx::smem_u32(tmem_holder), C::kTmemCols);
     ptx::tmem_relinquish();
   }
+  // The status word is read before the wait below, so its latency overlaps
+  // the previous kernel's tail (programmatic dependent launch).  No kernel
+  // writes it except on a timeout, which the host also sees through the
+  // word's host copy before it launches again.
+  if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   // Everything above may overlap the previous kernel on the stream
-  // (programmatic dependent launch); global memory is touched only below.
+  // (programmatic dependent launch); the operands and outputs are touched
+  // only below.
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
-  if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
-  __syncthreads();
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
 
@@ -267,7 +271,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       valid = valid && (op < prm.p) && (oq < prm.q);
     }
     if (flags[1]) valid = false;
-    if (!skip && splits > 1) {
+    if (!skip && splits > 1 && prm.split_ws != nullptr) {
+      // Split-K through L2: this warp's 32 rows, when one of them holds an
+      // output pixel, go to this CTA's partial block in the workspace as
+      // 2 KB granules - granule g holds channels 8g..8g+7, its float4 j
+      // (re 0-3, re 4-7, im 0-3, im 4-7) of row `lane` at g*128 + j*32 +
+      // lane - so a warp stores 512 contiguous bytes at a time.
+      if (__any_sync(0xffffffffu, valid)) {
+        const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+        float4* dst = reinterpret_cast<float4*>(prm.split_ws) +
+                      ((static_cast<long long>(tile) * splits + split) * 4 + quarter) * (16 * KT) +
+                      lane;
+#pragma unroll 1
+        for (int ch = 0; ch < KT; ch += 16) {
+          uint32_t vr[16], vi[16];
+          ptx::tmem_ld_32x32b_x16(t_row + ch, vr);
+          ptx::tmem_ld_32x32b_x16(t_row + KT + ch, vi);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float4* gd = dst + (ch / 8 + h) * 128;
+            __stcg(gd, u4f(vr[8 * h], vr[8 * h + 1], vr[8 * h + 2], vr[8 * h + 3]));
+            __stcg(gd + 32, u4f(vr[8 * h + 4], vr[8 * h + 5], vr[8 * h + 6], vr[8 * h + 7]));
+            __stcg(gd + 64, u4f(vi[8 * h], vi[8 * h + 1], vi[8 * h + 2], vi[8 * h + 3]));
+            __stcg(gd + 96, u4f(vi[8 * h + 4], vi[8 * h + 5], vi[8 * h + 6], vi[8 * h + 7]));
+          }
+        }
+        __threadfence();
+      }
+    } else if (!skip && splits > 1) {
       // Split-K: park this CTA's partial accumulator row in shared memory
       // (the pipeline buffers are idle now) for the cluster reduction;
       // 16-byte columns XOR-swizzled by row to spread banks.
@@ -337,43 +369,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (splits > 1) {
     // ---------------------------------------------------------- cluster reduce
-    // Every partial is parked; CTA `split` sums rows [split*128/S, ...) over
-    // the S partials in rank order (deterministic) and writes them out.
+    // Every partial is parked.  Only the tile rows that hold an output pixel
+    // are summed (a 7x7 image fills 49 of a 128-row tile): the CTAs list
+    // them in the same order, and CTA `split` sums an equal share of the
+    // (row, 4-channel group) items over the S partials in rank order
+    // (deterministic), reading the other CTAs' partials through distributed
+    // shared memory, and writes them out.
+    __shared__ int vrows[kBlockM];
+    __shared__ unsigned vmask[kBlockM / 32];
+    bool v = false;
+    unsigned vm = 0;
+    if (threadIdx.x < kBlockM) {
+      const int row = threadIdx.x;
+      if constexpr (FLAT) {
+        v = static_cast<long long>(m_tile) * kBlockM + row < prm.m_total;
+      } else {
+        const int b = row >> prm.box_px_log2;
+        const int local = row & ((1 << prm.box_px_log2) - 1);
+        const int gb = m_tile * prm.nb + b;
+        const int per_img = prm.tiles_bp * prm.tiles_bq;
+        const int rem = gb - (gb / per_img) * per_img;
+        const int bp = rem / prm.tiles_bq;
+        const int bq = rem - bp * prm.tiles_bq;
+        v = gb < prm.total_boxes && bp * prm.box_p + (local >> prm.box_q_log2) < prm.p &&
+            bq * prm.box_q + (local & ((1 << prm.box_q_log2) - 1)) < prm.q;
+      }
+      vm = __ballot_sync(0xffffffffu, v);
+      if (lane == 0) vmask[warp] = vm;
+    }
+    __syncthreads();
+    if (v) {
+      int idx = __popc(vm & ((1u << lane) - 1u));
+      for (int w2 = 0; w2 < warp; ++w2) idx += __popc(vmask[w2]);
+      vrows[idx] = threadIdx.x;
+    }
     ptx::cluster_sync();
-    const int rows_per = kBlockM / splits;
-    const int r0 = split * rows_per;
-    const int quads = KT / 4;
-    const uint32_t part_base = smem_base;
+    int nvalid = 0;
+#pragma unroll
+    for (int w2 = 0; w2 < kBlockM / 32; ++w2) nvalid += __popc(vmask[w2]);
     const bool do_store = !skip && !flags[1];
-    for (int it = threadIdx.x; it < rows_per * quads; it += kThreads) {
-      const int row = r0 + it / quads;
-      const int q = it - (it / quads) * quads;
-      const uint32_t off_r =
-          static_cast<uint32_t>(row * (KT / 2) + (q ^ (row & 7))) * 16u;
-      const uint32_t off_i =
-          static_cast<uint32_t>(row * (KT / 2) + ((quads + q) ^ (row & 7))) * 16u;
-      // All remote loads first (they overlap), then the sums in rank order.
-      float4 pa[16], pb[16];
-#pragma unroll
-      for (int s2 = 0; s2 < 16; ++s2) {
-        if (s2 < splits) {
-          pa[s2] = ptx::ld_shared_cluster_v4(ptx::mapa_shared(part_base + off_r, s2));
-          pb[s2] = ptx::ld_shared_cluster_v4(ptx::mapa_shared(part_base + off_i, s2));
-        }
-      }
-      float4 sr = make_float4(0.f, 0.f, 0.f, 0.f), si = sr;
-#pragma unroll
-      for (int s2 = 0; s2 < 16; ++s2) {
-        if (s2 < splits) {
-          sr.x += pa[s2].x; sr.y += pa[s2].y; sr.z += pa[s2].z; sr.w += pa[s2].w;
-          si.x += pb[s2].x; si.y += pb[s2].y; si.z += pb[s2].z; si.w += pb[s2].w;
-        }
-      }
+    // Stores the sums (sr, si) of channels kb..kb+3 of tile row `row`.
+    auto store4 = [&](int row, int kb, float4 sr, float4 si) {
       int img = 0, op = 0, oq = 0;
-      bool valid = do_store;
       if constexpr (FLAT) {
         const long long m = static_cast<long long>(m_tile) * kBlockM + row;
-        valid = valid && (m < prm.m_total);
         const long long pq = static_cast<long long>(prm.p) * prm.q;
         img = static_cast<int>(m / pq);
         const long long rem = m - static_cast<long long>(img) * pq;
@@ -390,10 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int bq = rem - bp * prm.tiles_bq;
         op = bp * prm.box_p + (local >> prm.box_q_log2);
         oq = bq * prm.box_q + (local & ((1 << prm.box_q_log2) - 1));
-        valid = valid && (gb < prm.total_boxes) && (op < prm.p) && (oq < prm.q);
       }
-      const int kb = k0 + 4 * q;
-      if (!valid || kb >= prm.k) continue;
       if (prm.bias_r != nullptr) {
         const float4 br = __ldg(reinterpret_cast<const float4*>(prm.bias_r + kb));
         const float4 bi = __ldg(reinterpret_cast<const float4*>(prm.bias_i + kb));
@@ -413,9 +449,88 @@ __global__ void __launch_bounds__(kThreads, 1)
         y[static_cast<long long>(kb + 2) * pq] = make_float2(sr.z, si.z);
         y[static_cast<long long>(kb + 3) * pq] = make_float2(sr.w, si.w);
       }
+    };
+    if (prm.split_ws != nullptr) {
+      // L2 partials: items are (32-row block with outputs, granule, half,
+      // lane), lane fastest, so a warp loads 512 contiguous bytes from each
+      // partial; the S partials are summed in rank order.
+      int qlist[kBlockM / 32];
+      int nq = 0;
+#pragma unroll
+      for (int w2 = 0; w2 < kBlockM / 32; ++w2) {
+        if (vmask[w2] != 0u) qlist[nq++] = w2;
+      }
+      constexpr int kGran = KT / 8;
+      const int items = nq * kGran * 64;
+      const int i0 = items * split / splits;
+      const int i1 = items * (split + 1) / splits;
+      const float4* ws4 = reinterpret_cast<const float4*>(prm.split_ws);
+      for (int it = i0 + threadIdx.x; it < i1; it += kThreads) {
+        const int ln = it & 31;
+        const int h = (it >> 5) & 1;
+        const int rest = it >> 6;
+        const int g = rest % kGran;
+        const int qb = qlist[rest / kGran];
+        const int row = qb * 32 + ln;
+        if (!((vmask[qb] >> ln) & 1u)) continue;
+        const long long base =
+            ((static_cast<long long>(tile) * splits) * 4 + qb) * (16 * KT) + g * 128 + ln;
+        float4 pa[16], pb[16];
+#pragma unroll
+        for (int s2 = 0; s2 < 16; ++s2) {
+          if (s2 < splits) {
+            const float4* src = ws4 + base + static_cast<long long>(s2) * 4 * (16 * KT);
+            pa[s2] = __ldcg(src + h * 32);
+            pb[s2] = __ldcg(src + (2 + h) * 32);
+          }
+        }
+        float4 sr = make_float4(0.f, 0.f, 0.f, 0.f), si = sr;
+#pragma unroll
+        for (int s2 = 0; s2 < 16; ++s2) {
+          if (s2 < splits) {
+            sr.x += pa[s2].x; sr.y += pa[s2].y; sr.z += pa[s2].z; sr.w += pa[s2].w;
+            si.x += pb[s2].x; si.y += pb[s2].y; si.z += pb[s2].z; si.w += pb[s2].w;
+          }
+        }
+        const int kb = k0 + 8 * g + 4 * h;
+        if (do_store && kb < prm.k) store4(row, kb, sr, si);
+      }
+    } else {
+      const int quads = KT / 4;
+      const long long items = static_cast<long long>(nvalid) * quads;
+      const int i0 = static_cast<int>(items * split / splits);
+      const int i1 = static_cast<int>(items * (split + 1) / splits);
+      const uint32_t part_base = smem_base;
+      for (int it = i0 + threadIdx.x; it < i1; it += kThreads) {
+        const int row = vrows[it / quads];
+        const int q = it - (it / quads) * quads;
+        const uint32_t off_r =
+            static_cast<uint32_t>(row * (KT / 2) + (q ^ (row & 7))) * 16u;
+        const uint32_t off_i =
+            static_cast<uint32_t>(row * (KT / 2) + ((quads + q) ^ (row & 7))) * 16u;
+        // All remote loads first (they overlap), then the sums in rank order.
+        float4 pa[16], pb[16];
+#pragma unroll
+        for (int s2 = 0; s2 < 16; ++s2) {
+          if (s2 < splits) {
+            pa[s2] = ptx::ld_shared_cluster_v4(ptx::mapa_shared(part_base + off_r, s2));
+            pb[s2] = ptx::ld_shared_cluster_v4(ptx::mapa_shared(part_base + off_i, s2));
+          }
+        }
+        float4 sr = make_float4(0.f, 0.f, 0.f, 0.f), si = sr;
+#pragma unroll
+        for (int s2 = 0; s2 < 16; ++s2) {
+          if (s2 < splits) {
+            sr.x += pa[s2].x; sr.y += pa[s2].y; sr.z += pa[s2].z; sr.w += pa[s2].w;
+            si.x += pb[s2].x; si.y += pb[s2].y; si.z += pb[s2].z; si.w += pb[s2].w;
+          }
+        }
+        const int kb = k0 + 4 * q;
+        if (do_store && kb < prm.k) store4(row, kb, sr, si);
+      }
+      // Keep every partial alive until all CTAs finished reading.
+      ptx::cluster_sync();
     }
-    // Keep every partial alive until all CTAs finished reading.
-    ptx::cluster_sync();
   }
   if (warp == 1) {
     ptx::tc_fence_after();
@@ -424,49 +539,69 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ------------------------------------------------------------------ host side
-// Largest power-of-two cluster (<= want) the device can co-schedule for this
-// kernel; 1 if clusters are unavailable.
-template <class K>
-int max_split(K kern, int smem, int want) {
-  for (int s = want; s >= 2; s >>= 1) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(s, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = s;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) return s;
-    cudaGetLastError();
-  }
-  return 1;
-}
-
+// Function attributes of one single-CTA kernel variant (once per device).
 template <int KT, bool FLAT, bool OUT_COMPLEX>
-int launch_variant(FpropParams& prm, int tiles, int want_split, cudaStream_t stream) {
+cudaError_t prepare_variant() {
   using C = Cfg<KT>;
   auto kern = ccv_fprop_tf32_kernel<KT, FLAT, OUT_COMPLEX>;
   static std::once_flag once[64];
-  static int split_cap[64] = {};
+  static cudaError_t err[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  cudaError_t attr_err = cudaSuccess;
   std::call_once(once[dev & 63], [&]() {
-    attr_err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    C::kSmemBytes);
-    if (attr_err != cudaSuccess) return;
+    err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         C::kSmemBytes);
+    if (err[dev & 63] != cudaSuccess) return;
     cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     cudaGetLastError();
-    split_cap[dev & 63] = max_split(kern, C::kSmemBytes, 16);
   });
+  return err[dev & 63];
+}
+
+// Clusters of 1, 2, 4, 8 and 16 CTAs of the KT-wide single-CTA kernel the
+// device can hold at once (0: that size cannot be launched), queried once
+// per device.  Clusters of 16 take 16 SMs of one GPC, so B200 holds only
+// about 7 of them - fewer than it has SMs for.
+template <int KT>
+const int* cluster_capacity() {
+  using C = Cfg<KT>;
+  auto kern = ccv_fprop_tf32_kernel<KT, false, false>;
+  static std::once_flag once[64];
+  static int caps[64][5] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&]() {
+    if (prepare_variant<KT, false, false>() != cudaSuccess) return;
+    for (int l = 0; l < 5; ++l) {
+      const int size = 1 << l;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(size), 1, 1);
+      cfg.blockDim = dim3(kThreads, 1, 1);
+      cfg.dynamicSmemBytes = C::kSmemBytes;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = static_cast<unsigned>(size);
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) {
+        caps[dev & 63][l] = n;
+      } else {
+        cudaGetLastError();
+      }
+    }
+  });
+  return caps[dev & 63];
+}
+
+template <int KT, bool FLAT, bool OUT_COMPLEX>
+int launch_variant(FpropParams& prm, int tiles, int splits, cudaStream_t stream) {
+  using C = Cfg<KT>;
+  auto kern = ccv_fprop_tf32_kernel<KT, FLAT, OUT_COMPLEX>;
+  const cudaError_t attr_err = prepare_variant<KT, FLAT, OUT_COMPLEX>();
   if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(fprop)");
-  int splits = 1;
-  while (splits * 2 <= want_split && splits * 2 <= split_cap[dev & 63]) splits *= 2;
   prm.splits = splits;
   const long long grid = static_cast<long long>(tiles) * splits;
   if (grid > 0x7fffffffLL) return set_error(CCV_ERR_UNSUPPORTED, "problem too large for the grid");
@@ -479,12 +614,79 @@ int launch_variant(FpropParams& prm, int tiles, int want_split, cudaStream_t str
 }
 
 template <bool FLAT, bool OUT_COMPLEX>
-int launch_kt(int kt, FpropParams& prm, int tiles, int want_split, cudaStream_t stream) {
+int launch_kt(int kt, FpropParams& prm, int tiles, int splits, cudaStream_t stream) {
   switch (kt) {
-    case 128: return launch_variant<128, FLAT, OUT_COMPLEX>(prm, tiles, want_split, stream);
-    case 64: return launch_variant<64, FLAT, OUT_COMPLEX>(prm, tiles, want_split, stream);
-    default: return launch_variant<32, FLAT, OUT_COMPLEX>(prm, tiles, want_split, stream);
+    case 128: return launch_variant<128, FLAT, OUT_COMPLEX>(prm, tiles, splits, stream);
+    case 64: return launch_variant<64, FLAT, OUT_COMPLEX>(prm, tiles, splits, stream);
+    default: return launch_variant<32, FLAT, OUT_COMPLEX>(prm, tiles, splits, stream);
   }
+}
+
+const int* cluster_capacity_kt(int kt) {
+  switch (kt) {
+    case 128: return cluster_capacity<128>();
+    case 64: return cluster_capacity<64>();
+    default: return cluster_capacity<32>();
+  }
+}
+
+// Plan of the single-CTA kernel: output-channel tile, CTAs per tile (a
+// cluster splitting the K loop) and where the split's partial sums meet.
+struct SinglePlan {
+  int kt = 128;
+  int splits = 1;
+  bool l2 = false;       // partial sums through L2 (workspace) rather than DSMEM
+  size_t ws_bytes = 0;   // workspace the L2 reduction needs
+};
+
+size_t single_l2_bytes(int tiles, int splits, int kt) {
+  return static_cast<size_t>(tiles) * splits * kBlockM * 2 * kt * sizeof(float);
+}
+
+// Picks the channel tile (32, 64 or 128) and the split (1, 2, 4 or 8 CTAs
+// per tile) that put the most CTAs to work - at most one per SM, and only
+// as many clusters as the device holds at once (a second wave of clusters
+// doubles the time) - preferring the wider tile on a tie (fewer activation
+// re-reads).  Measured on B200 over the batch-1 layers (graph replay, every
+// tile x split): clusters of 16 were slower than clusters of 8 with the same
+// CTA count (256->512 @ 7x7: 12.7 vs 12.4 us; 128->256 @ 14x14: 14.4 vs
+// 11.2 us), and a split too wide for one wave of clusters ran 2x slower.
+// With workspace room (`ws_bytes`; SIZE_MAX: unbounded) the split's partial
+// sums meet in L2, else over distributed shared memory (~1 us slower on the
+// deep layers).  CCV_KT pins the tile; CCV_SPLITK caps the split.
+SinglePlan plan_single_cta(const Problem& pb, const Tiling& t, size_t ws_bytes) {
+  SinglePlan best;
+  long long best_ctas = -1;
+  const int sms = device_sm_count();
+  const int ksteps = ((pb.c + kBlockC - 1) / kBlockC) * pb.r * pb.s;
+  const int pin = knobs().kt;
+  const int cap = knobs().splitk > 0 ? std::min(knobs().splitk, 8) : 8;
+  for (int kt = 128; kt >= 32; kt /= 2) {
+    if (pin == 32 || pin == 64 || pin == 128) {
+      if (kt != pin) continue;
+    } else if (kt > t.kt) {
+      continue;
+    }
+    const int tiles_n = (pb.k + kt - 1) / kt;
+    const long long tiles = static_cast<long long>(t.tiles_m) * tiles_n;
+    const int* caps = cluster_capacity_kt(kt);
+    int s = 1;
+    for (int l = 1; l < 4; ++l) {
+      const int c = 1 << l;
+      if (c > cap || c > ksteps || tiles * c > sms || caps[l] < tiles) break;
+      s = c;
+    }
+    const long long ctas = tiles * s;
+    if (ctas > best_ctas) {  // ties keep the wider tile (visited first)
+      best_ctas = ctas;
+      best.kt = kt;
+      best.splits = s;
+      const size_t need = s > 1 ? single_l2_bytes(static_cast<int>(tiles), s, kt) : 0;
+      best.l2 = s > 1 && ws_bytes >= need;
+      best.ws_bytes = best.l2 ? need : 0;
+    }
+  }
+  return best;
 }
 
 }  // namespace
@@ -492,19 +694,6 @@ int launch_kt(int kt, FpropParams& prm, int tiles, int want_split, cudaStream_t 
 namespace {
 
 enum KernelFamily { kSingleCta = 0, kPairTap = 1, kPairHalo = 2 };
-
-// Output-channel tile of the single-CTA kernel.  CCV_KT=32|64|128 pins it
-// (testing knob).  Otherwise the widest tile, except that 65..128 output
-// channels over fewer than SMs/16 pixel tiles take two 64-wide tiles: more
-// CTAs to spread the split-K over (measured on B200, batch-1 64->128 @ 28x28:
-// 13.5 -> 10.9 us; deeper layers keep 128, e.g. 128->256 @ 14x14 14.5 us vs
-// 20.1 us with 64).
-int single_cta_kt(const Problem& pb, const Tiling& t) {
-  const int v = knobs().kt;
-  if (v == 32 || v == 64 || v == 128) return v;
-  if (t.kt == 128 && pb.k <= 128 && t.tiles_m * 16 < device_sm_count()) return 64;
-  return t.kt;
-}
 
 // Kernel family for a problem.  Large problems go to the persistent CTA-pair
 // kernels; small ones (fewer pair tiles than half the SMs) to the single-CTA
@@ -544,7 +733,8 @@ size_t split_workspace_bytes(const Problem& pb, int precision, bool complex_inpu
       return pair_split_workspace_bytes(t.kt, pair_tiles(t),
                                         ((pb.c + kBlockC - 1) / kBlockC) * pb.r * pb.s * passes);
     default:
-      return 0;
+      // Single-CTA kernel: room for its split-K partial sums in L2.
+      return plan_single_cta(pb, t, SIZE_MAX).ws_bytes;
   }
 }
 
@@ -667,7 +857,8 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
     default:
       break;
   }
-  t.kt = single_cta_kt(pb, t);
+  const SinglePlan plan = plan_single_cta(pb, t, ws != nullptr ? ws_bytes : 0);
+  t.kt = plan.kt;
   t.tiles_n = (pb.k + t.kt - 1) / t.kt;
   FpropParams prm;
   memset(&prm, 0, sizeof(prm));
@@ -720,27 +911,18 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
   if (grid <= 0 || grid > 0x7fffffffLL) {
     return set_error(CCV_ERR_UNSUPPORTED, "problem too large for the grid");
   }
-  // Split-K across a cluster when the tiles alone leave most SMs idle: aim
-  // for about one CTA per SM, at most 16 CTAs per tile and one K step each.
-  // CCV_SPLITK=n caps the split (testing/benchmarking knob; 1 disables).
-  int want_split = 1;
-  {
-    const int sms = device_sm_count();
-    const long long per_tile = sms / std::max<long long>(grid, 1);
-    want_split = static_cast<int>(std::min<long long>(std::min<long long>(per_tile, 16),
-                                                      prm.ksteps));
-    if (knobs().splitk > 0) want_split = std::min(want_split, knobs().splitk);
-    if (want_split < 2) want_split = 1;
-  }
+  // Split-K across a cluster of plan.splits CTAs per tile (plan_single_cta);
+  // with workspace room the partial sums meet in L2, else over DSMEM.
   prm.splits = 1;
+  prm.split_ws = plan.l2 ? static_cast<float*>(ws) : nullptr;
   const bool cplx = out_layout == OUT_COMPLEX_NCHW;
   const int tiles = static_cast<int>(grid);
   if (t.flat) {
-    return cplx ? launch_kt<true, true>(t.kt, prm, tiles, want_split, stream)
-                : launch_kt<true, false>(t.kt, prm, tiles, want_split, stream);
+    return cplx ? launch_kt<true, true>(t.kt, prm, tiles, plan.splits, stream)
+                : launch_kt<true, false>(t.kt, prm, tiles, plan.splits, stream);
   }
-  return cplx ? launch_kt<false, true>(t.kt, prm, tiles, want_split, stream)
-              : launch_kt<false, false>(t.kt, prm, tiles, want_split, stream);
+  return cplx ? launch_kt<false, true>(t.kt, prm, tiles, plan.splits, stream)
+              : launch_kt<false, false>(t.kt, prm, tiles, plan.splits, stream);
 }
 
 // ------------------------------------------------------------------ self-test

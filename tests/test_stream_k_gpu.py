@@ -166,3 +166,24 @@ def test_stream_k_default_policy_batched(knobs):
     for img in (0, 7):
         ref = oracle.oracle_fp64(sub, x[img:img + 1], wr, wi)
         assert oracle.rel_frobenius(split[img:img + 1], ref) <= TF32_TOL
+
+
+@pytest.mark.parametrize("case", [C(1, 32, 56, 56, 64, 3, 3, 1, 1, 1, 1),
+                                  C(1, 64, 28, 28, 128, 3, 3, 1, 1, 1, 1),
+                                  C(1, 128, 14, 14, 256, 3, 3, 1, 1, 1, 1),
+                                  C(1, 256, 7, 7, 512, 3, 3, 1, 1, 1, 1),
+                                  C(2, 36, 9, 11, 20, 1, 1, 1, 1, 0, 0)],
+                         ids=["b1_32_64_56", "b1_64_128_28", "b1_128_256_14", "b1_256_512_7",
+                              "flat_small"])
+def test_single_cta_split_through_l2_matches_dsmem(case):
+    """The batch-1 kernel's cluster split sums its partials in rank order
+    either way: through L2 when the workspace has room (recommended size),
+    over distributed shared memory without workspace - bitwise equal, and
+    within the TF32 bar of the fp64 oracle."""
+    x, wr, wi = oracle.make_inputs(case, input_seed=81)
+    packed = abi_prepack(case, wr, wi)
+    y_l2 = planar(case, x, packed, TF32, full_workspace=True)
+    y_dsmem = planar(case, x, packed, TF32, full_workspace=False)
+    assert not torch.isnan(y_l2.real).any() and not torch.isnan(y_l2.imag).any()
+    assert torch.equal(y_l2, y_dsmem)
+    assert oracle.rel_frobenius(y_l2, oracle.oracle_fp64(case, x, wr, wi)) <= TOL[TF32]
