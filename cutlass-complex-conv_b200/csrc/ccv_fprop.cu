@@ -55,13 +55,20 @@ constexpr int kTimeoutEpilogue = CCV_ERR_DEVICE_TIMEOUT;
 
 
 
+// The weight stage holds two planes, [W_re; W_im] (KT rows each), which
+// both MMAs of a K slice share: D1 += A_re * [W_re; W_im]^T and
+// D2 += A_im * [W_re; W_im]^T, two TMEM accumulators of 2*KT columns; the
+// epilogue forms re = D1[:, :KT] - D2[:, KT:] and im = D1[:, KT:] + D2[:, :KT]
+// (each thread holds its whole row).  Two planes instead of the three of the
+// one-accumulator form (-W_im, W_re, W_im) cut this kernel's weight bytes by
+// a third; its batch-1 layers stream the weights from HBM.
 template <int KT>
 struct Cfg {
-  static constexpr int kWBytes = 3 * KT * kRowBytes;
+  static constexpr int kWBytes = 2 * KT * kRowBytes;
   static constexpr int kStageBytes = 2 * kABytes + kWBytes;
-  static constexpr int kStages = (200 * 1024) / kStageBytes;  // 2 / 3 / 4 for KT 128 / 64 / 32
+  static constexpr int kStages = (200 * 1024) / kStageBytes;  // 3 / 4 / 5 for KT 128 / 64 / 32
   static_assert(kStages >= 2, "pipeline too shallow");
-  static constexpr int kTmemCols = 2 * KT < 32 ? 32 : 2 * KT;
+  static constexpr int kTmemCols = 4 * KT;  // D1 | D2, 2*KT columns each
   static constexpr int kBarOffset = kStages * kStageBytes;
   static constexpr int kSmemBytes = kBarOffset + 256 + 1024;  // + barriers + alignment slack
 };
@@ -69,6 +76,25 @@ struct Cfg {
 __device__ __forceinline__ float4 u4f(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return make_float4(__uint_as_float(a), __uint_as_float(b), __uint_as_float(c),
                      __uint_as_float(d));
+}
+
+// Output channels [ch, ch + 16) of this thread's accumulator row (TMEM
+// address t_row: its lane, column 0) as fp32 bits: re = D1 - D2 (imag
+// weights), im = D1 (imag weights) + D2 (real weights).  Warp-collective.
+template <int KT>
+__device__ __forceinline__ void load_complex16(uint32_t t_row, int ch, uint32_t (&re)[16],
+                                               uint32_t (&im)[16]) {
+  uint32_t a[16], b[16];
+  ptx::tmem_ld_32x32b_x16(t_row + ch, re);           // sum x_re * W_re
+  ptx::tmem_ld_32x32b_x16(t_row + KT + ch, im);      // sum x_re * W_im
+  ptx::tmem_ld_32x32b_x16(t_row + 2 * KT + ch, a);   // sum x_im * W_re
+  ptx::tmem_ld_32x32b_x16(t_row + 3 * KT + ch, b);   // sum x_im * W_im
+  ptx::tmem_wait_ld();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    re[j] = __float_as_uint(__uint_as_float(re[j]) - __uint_as_float(b[j]));
+    im[j] = __float_as_uint(__uint_as_float(im[j]) + __uint_as_float(a[j]));
+  }
 }
 
 template <int KT, bool FLAT, bool OUT_COMPLEX>
@@ -180,7 +206,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::tma_load_4d(a_i + b * box_bytes, &prm.tm_xi, fb, c0, wc, hc, img);
           }
         }
-        ptx::tma_load_4d(w_s, &prm.tm_w, fb, c0, k0, 0, tap);
+        // Planes 1 and 2 of the packed tap: [W_re; W_im].
+        ptx::tma_load_4d(w_s, &prm.tm_w, fb, c0, k0, 1, tap);
         ++issued;
         if (++stage == C::kStages) {
           stage = 0;
@@ -217,10 +244,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t koff = kk * 32;
           const uint64_t da_r = ptx::desc_kmajor_sw128(a_r + koff);
           const uint64_t da_i = ptx::desc_kmajor_sw128(a_i + koff);
-          const uint64_t db_top = ptx::desc_kmajor_sw128(w_s + KT * kRowBytes + koff);  // [Wr; Wi]
-          const uint64_t db_bot = ptx::desc_kmajor_sw128(w_s + koff);                   // [-Wi; Wr]
-          ptx::mma_tf32_ss(tmem_base, da_r, db_top, idesc, (t != kbeg || kk != 0) ? 1u : 0u);
-          ptx::mma_tf32_ss(tmem_base, da_i, db_bot, idesc, 1u);
+          const uint64_t db = ptx::desc_kmajor_sw128(w_s + koff);  // [Wr; Wi]
+          const uint32_t acc = (t != kbeg || kk != 0) ? 1u : 0u;
+          ptx::mma_tf32_ss(tmem_base, da_r, db, idesc, acc);           // D1
+          ptx::mma_tf32_ss(tmem_base + 2 * KT, da_i, db, idesc, acc);  // D2
         }
         ptx::mma_commit(empty_bar(stage));
         if (++stage == C::kStages) {
@@ -285,9 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
         for (int ch = 0; ch < KT; ch += 16) {
           uint32_t vr[16], vi[16];
-          ptx::tmem_ld_32x32b_x16(t_row + ch, vr);
-          ptx::tmem_ld_32x32b_x16(t_row + KT + ch, vi);
-          ptx::tmem_wait_ld();
+          load_complex16<KT>(t_row, ch, vr, vi);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             float4* gd = dst + (ch / 8 + h) * 128;
@@ -306,40 +331,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
       float4* part = reinterpret_cast<float4*>(smem) + static_cast<size_t>(row) * (KT / 2);
 #pragma unroll 1
-      for (int ch = 0; ch < 2 * KT; ch += 32) {
-        uint32_t v[32];
-        ptx::tmem_ld_32x32b_x32(t_row + ch, v);
-        ptx::tmem_wait_ld();
+      for (int ch = 0; ch < KT; ch += 16) {
+        uint32_t vr[16], vi[16];
+        load_complex16<KT>(t_row, ch, vr, vi);
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          const int c4 = (ch + j) >> 2;
-          part[c4 ^ (row & 7)] = u4f(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        for (int j = 0; j < 16; j += 4) {
+          part[((ch + j) >> 2) ^ (row & 7)] = u4f(vr[j], vr[j + 1], vr[j + 2], vr[j + 3]);
+          part[((KT + ch + j) >> 2) ^ (row & 7)] = u4f(vi[j], vi[j + 1], vi[j + 2], vi[j + 3]);
         }
       }
     } else if (!skip) {
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
       const long long pix = (static_cast<long long>(img) * prm.p + op) * prm.q + oq;
 #pragma unroll 1
-      for (int ch = 0; ch < KT; ch += 32) {
-        uint32_t vr[32], vi[32];
-        ptx::tmem_ld_32x32b_x32(t_row + ch, vr);
-        ptx::tmem_ld_32x32b_x32(t_row + KT + ch, vi);
-        ptx::tmem_wait_ld();
+      for (int ch = 0; ch < KT; ch += 16) {
+        uint32_t vr[16], vi[16];
+        load_complex16<KT>(t_row, ch, vr, vi);
         const int kb = k0 + ch;
         if (valid && kb < prm.k) {
-          add_bias<32>(prm, kb, vr, vi);
+          add_bias<16>(prm, kb, vr, vi);
           if constexpr (!OUT_COMPLEX) {
             float* dr = prm.y0 + pix * prm.k + kb;
             float* di = prm.y1 + pix * prm.k + kb;
-            if (kb + 32 <= prm.k) {
+            if (kb + 16 <= prm.k) {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4) {
+              for (int j = 0; j < 16; j += 4) {
                 *reinterpret_cast<float4*>(dr + j) = u4f(vr[j], vr[j + 1], vr[j + 2], vr[j + 3]);
                 *reinterpret_cast<float4*>(di + j) = u4f(vi[j], vi[j + 1], vi[j + 2], vi[j + 3]);
               }
             } else {
 #pragma unroll
-              for (int j = 0; j < 32; j += 4) {
+              for (int j = 0; j < 16; j += 4) {
                 if (kb + j < prm.k) {
                   *reinterpret_cast<float4*>(dr + j) = u4f(vr[j], vr[j + 1], vr[j + 2], vr[j + 3]);
                   *reinterpret_cast<float4*>(di + j) = u4f(vi[j], vi[j + 1], vi[j + 2], vi[j + 3]);
@@ -353,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const long long base = static_cast<long long>(img) * prm.k * pq +
                                    static_cast<long long>(op) * prm.q + oq;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
+            for (int j = 0; j < 16; ++j) {
               if (kb + j < prm.k) {
                 y[base + static_cast<long long>(kb + j) * pq] =
                     make_float2(__uint_as_float(vr[j]), __uint_as_float(vi[j]));
@@ -903,7 +925,8 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
     const uint64_t dims[4] = {static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.k), 3,
                               static_cast<uint64_t>(pb.r) * pb.s};
     const uint64_t strides[3] = {cb, cb * pb.k, cb * pb.k * 3};
-    const uint32_t box[4] = {kBlockC, static_cast<uint32_t>(t.kt), 3, 1};
+    // Two planes (W_re, W_im) of the packed tap per box (Cfg).
+    const uint32_t box[4] = {kBlockC, static_cast<uint32_t>(t.kt), 2, 1};
     const uint32_t es[4] = {1, 1, 1, 1};
     if ((rc = encode_tiled(&prm.tm_w, w_packed, 4, dims, strides, box, es, 128)) != CCV_OK) return rc;
   }
