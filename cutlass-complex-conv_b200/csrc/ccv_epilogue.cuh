@@ -99,19 +99,19 @@ __device__ __forceinline__ void store_accumulator(const FpropParams& prm, uint32
 }
 
 // Planar output through TMA stores.  The warp's 32 rows (TMEM lanes) are one
-// box of the output: `stage` (this warp's 4 KB: 32 rows x 16 channels for
-// each plane) is filled from TMEM 16 channels at a time and lane 0 issues the
-// two tensor stores; the next chunk waits until those have read the buffer.
-// (c1, c2, c3) are the box's pixel coordinates in the output tensor map
-// (q, p, n; or m, -, - for flat tiles).  `valid`: the box holds real pixels.
-template <int KT, bool FLAT>
+// box of the output: a 4 KB buffer of `stage` (32 rows x 16 channels for each
+// plane) is filled from TMEM 16 channels at a time and lane 0 issues the two
+// tensor stores.  With NBUF = 2 the warp's chunks alternate between two
+// buffers, so filling one overlaps the stores still reading the other;
+// `seq` counts this warp's committed chunks across calls (the buffer of the
+// next one) and must start at 0.  (c1, c2, c3) are the box's pixel
+// coordinates in the output tensor map (q, p, n; or m, -, - for flat tiles).
+// `valid`: the box holds real pixels.
+template <int KT, bool FLAT, int NBUF = 1>
 __device__ __forceinline__ void store_accumulator_tma(const FpropParams& prm, uint32_t t_acc,
                                                       int k0, bool valid, int c1, int c2, int c3,
-                                                      uint8_t* stage, int lane) {
-  float* sr = reinterpret_cast<float*>(stage);
-  float* si = sr + 32 * 16;
-  const uint32_t ur = ptx::smem_u32(sr);
-  const uint32_t ui = ptx::smem_u32(si);
+                                                      uint8_t* stage, int lane, uint32_t& seq) {
+  static_assert(NBUF == 1 || NBUF == 2, "one or two staging buffers");
 #pragma unroll 1
   for (int ch = 0; ch < KT; ch += 16) {
     uint32_t vr[16], vi[16];
@@ -121,8 +121,18 @@ __device__ __forceinline__ void store_accumulator_tma(const FpropParams& prm, ui
     const bool go = valid && k0 + ch < prm.k;
     if (!go) continue;
     add_bias<16>(prm, k0 + ch, vr, vi);
-    // The previous chunk's stores have read the buffer.
-    if (lane == 0) ptx::bulk_wait_read_all();
+    float* sr = reinterpret_cast<float*>(stage + (NBUF == 2 ? (seq & 1u) * 4096u : 0u));
+    float* si = sr + 32 * 16;
+    ++seq;
+    // The stores that last read this buffer are done with it: with two
+    // buffers that is every group but the most recent one.
+    if (lane == 0) {
+      if constexpr (NBUF == 2) {
+        ptx::bulk_wait_read_le1();
+      } else {
+        ptx::bulk_wait_read_all();
+      }
+    }
     __syncwarp();
     // Row `lane`: 16 channels (64 B).  Rotating the float4 order spreads a
     // warp's writes over all banks.
@@ -147,6 +157,8 @@ __device__ __forceinline__ void store_accumulator_tma(const FpropParams& prm, ui
     ptx::fence_proxy_async_shared();
     __syncwarp();
     if (lane == 0) {
+      const uint32_t ur = ptx::smem_u32(sr);
+      const uint32_t ui = ptx::smem_u32(si);
       if constexpr (FLAT) {
         ptx::tma_store_2d(&prm.tm_y0, ur, k0 + ch, c1);
         ptx::tma_store_2d(&prm.tm_y1, ui, k0 + ch, c1);

@@ -7,12 +7,12 @@
 // four real products per fragment:
 //     re += Ar*Br,  re += Ai*(-Bi),  im += Ar*Bi,  im += Ai*Br.
 // Here the same four products are two tcgen05 MMAs per 8-deep K step, each
-// M=128 x N=2*KT, accumulating [re | im] side by side in Tensor Memory:
-//     D[:, 0:2KT] += Ar * [Wr ; Wi]^T      (B rows KT..3KT of the packed tile)
-//     D[:, 0:2KT] += Ai * [-Wi ; Wr]^T     (B rows 0..2KT of the packed tile)
-// The packed weight tile per (tap, 16 input channels) is the three planes
-// (-Wi, Wr, Wi) stacked along N, so both B operands are windows of one TMA
-// box and every activation/weight byte is loaded into shared memory once.
+// M=128 x N=2*KT, sharing one weight operand and accumulating into two
+// Tensor Memory accumulators:
+//     D1 += Ar * [Wr ; Wi]^T,   D2 += Ai * [Wr ; Wi]^T
+// (planes 1 and 2 of the packed tap), and the epilogue forms
+// re = D1[:, :KT] - D2[:, KT:], im = D1[:, KT:] + D2[:, :KT].  Every
+// activation and weight byte is loaded into shared memory once.
 //
 // Warp roles (192 threads, one CTA per SM):
 //   warp 0      TMA producer: activation boxes (both planes) + weight box

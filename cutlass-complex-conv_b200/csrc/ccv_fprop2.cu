@@ -42,7 +42,12 @@ constexpr int kC2 = 32;                 // input channels per K step
 constexpr int kRow2 = kC2 * 4;          // 128-byte rows
 constexpr int kA2 = kBlockM * kRow2;    // one activation plane of one CTA: 16 KB
 constexpr int kTimeout = CCV_ERR_DEVICE_TIMEOUT;
-constexpr int kTapMinSplitGain = 25;    // stream-K policy threshold, % (plan_stream_k)
+// Stream-K policy threshold of the tap kernel, % (plan_stream_k): above 100,
+// i.e. never by default.  Its split lost wherever it was measured on B200:
+// stride 2 batch 32 (model gain 11 %) 121.2 -> 141.5 us, batch 8 (model gain
+// 34 %) 47.3 -> 61.7 us; one-tap slots make many short pieces whose partial
+// sums cost more than the tail they remove.  CCV_STREAMK=1 still forces it.
+constexpr int kTapMinSplitGain = 101;
 
 template <int KT>
 struct Cfg2 {
@@ -54,7 +59,10 @@ struct Cfg2 {
   static constexpr int kBarOffset = kStages * kStageBytes;
   static constexpr int kBarBytes = 1024;
   static constexpr int kOutStageOffset = kBarOffset + kBarBytes;  // TMA-store staging
-  static constexpr int kSmemBytes = kOutStageOffset + kOutStageBytes + 1024;
+  // Two staging buffers per epilogue warp where they fit beside the stages.
+  static constexpr int kOutBufs =
+      kOutStageOffset + 2 * kOutStageBytes + 1024 <= 232448 ? 2 : 1;
+  static constexpr int kSmemBytes = kOutStageOffset + kOutBufs * kOutStageBytes + 1024;
   static_assert(kStages >= 3, "pipeline too shallow");
   static_assert((2 * kStages + 8 + 4 * kStageBufs) * 8 <= kBarBytes, "barrier block overflow");
   static_assert(kSmemBytes <= 232448, "shared memory");
@@ -301,6 +309,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32
     const uint32_t tempty_leader0 = ptx::mapa_shared(tempty_bar(0), 0);
     const uint32_t tempty_leader1 = ptx::mapa_shared(tempty_bar(1), 0);
     int i = 0;
+    uint32_t stores = 0;  // TMA-store chunks this warp has committed
     UnitCursor cur = unit_cursor(prm, cid);
     WorkUnit wu;
     while (!skip && next_unit(prm, ncl, cur, wu)) {
@@ -332,9 +341,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32
         if (tma_out) {
           int c1 = 0, c2 = 0, c3 = 0;
           const bool wv = warp_box_origin<FLAT>(prm, half, quarter * 32, c1, c2, c3) && ok && !flags[1];
-          store_accumulator_tma<KT, FLAT>(prm, t_acc, n_tile * KT, wv, c1, c2, c3,
-                                          smem + C::kOutStageOffset + quarter * (kOutStageBytes / 4),
-                                          lane);
+          store_accumulator_tma<KT, FLAT, C::kOutBufs>(
+              prm, t_acc, n_tile * KT, wv, c1, c2, c3,
+              smem + C::kOutStageOffset + quarter * C::kOutBufs * (kOutStageBytes / 4), lane,
+              stores);
         } else {
           store_accumulator<KT, OUT_COMPLEX>(prm, t_acc, n_tile * KT, in_tile && ok && !flags[1],
                                              img, op, oq);
@@ -540,8 +550,8 @@ int plan_stream_k(FpropParams& prm, int clusters, int slots, int kt, void* ws, s
   // cluster; split: q * L + per_range).  The model leaves out the partial
   // sums' traffic, the reduction and the unit switches, which cost B200
   // measurements 10-30 us per launch: the halo kernel (3-tap slots) splits
-  // at >= 10 % (batch 8 and 16 of the 56x56 layer gain), the tap kernel
-  // (one-tap slots) at >= 25 % (stride 2, 11 % by the model, lost 14 %).
+  // at >= 10 % (batch 8 and 16 of the 56x56 layer gain); the tap kernel
+  // (one-tap slots) passes a threshold no model gain reaches.
   const long long q = T / clusters;
   const long long dp_time = (q + 1) * slots;
   const long long sk_time = q * slots + per_range;

@@ -337,6 +337,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<LW>(), 
     const uint32_t tempty_leader0 = ptx::mapa_shared(tempty(0), 0);
     const uint32_t tempty_leader1 = ptx::mapa_shared(tempty(1), 0);
     int i = 0;
+    uint32_t stores = 0;  // TMA-store chunks this warp has committed
     UnitCursor cur = unit_cursor(prm, ucid);
     WorkUnit wu;
     while (!skip && next_unit(prm, uncl, cur, wu)) {
@@ -377,7 +378,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<LW>(), 
                                                    c3) &&
                             ok && !flags[1];
             store_accumulator_tma<KT, false>(prm, t_acc, n_tile * KT, wv, c1, c2, c3,
-                                             out_stage + quarter * (kOutStageBytes / 4), lane);
+                                             out_stage + quarter * (kOutStageBytes / 4), lane,
+                                             stores);
           } else {
             int img = 0, op = 0, oq = 0;
             const bool in_tile = tile_row_pixel<false>(prm, half, row_sb, img, op, oq);
