@@ -134,25 +134,19 @@ __device__ __forceinline__ void store_accumulator_tma(const FpropParams& prm, ui
       }
     }
     __syncwarp();
-    // Row `lane`: 16 channels (64 B).  Rotating the float4 order spreads a
-    // warp's writes over all banks.
-    float4 fr[4], fi[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      fr[j] = make_float4(__uint_as_float(vr[4 * j]), __uint_as_float(vr[4 * j + 1]),
-                          __uint_as_float(vr[4 * j + 2]), __uint_as_float(vr[4 * j + 3]));
-      fi[j] = make_float4(__uint_as_float(vi[4 * j]), __uint_as_float(vi[4 * j + 1]),
-                          __uint_as_float(vi[4 * j + 2]), __uint_as_float(vi[4 * j + 3]));
-    }
+    // Row `lane`: 16 channels (64 B) in the 64-byte swizzle of the output
+    // tensor maps - 16-byte chunk j of row r sits at chunk j ^ ((r >> 1) & 3)
+    // (the buffers are 512-byte aligned) - so the lanes of each store below
+    // cover all banks with static register indices.
     const int rot = (lane >> 1) & 3;
+    float4* rr = reinterpret_cast<float4*>(sr + lane * 16);
+    float4* ri = reinterpret_cast<float4*>(si + lane * 16);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int qd = (j + rot) & 3;
-      // Register selects (a runtime index into fr/fi would go to local memory).
-      const float4 a = qd == 0 ? fr[0] : qd == 1 ? fr[1] : qd == 2 ? fr[2] : fr[3];
-      const float4 b = qd == 0 ? fi[0] : qd == 1 ? fi[1] : qd == 2 ? fi[2] : fi[3];
-      reinterpret_cast<float4*>(sr + lane * 16)[qd] = a;
-      reinterpret_cast<float4*>(si + lane * 16)[qd] = b;
+      rr[j ^ rot] = make_float4(__uint_as_float(vr[4 * j]), __uint_as_float(vr[4 * j + 1]),
+                                __uint_as_float(vr[4 * j + 2]), __uint_as_float(vr[4 * j + 3]));
+      ri[j ^ rot] = make_float4(__uint_as_float(vi[4 * j]), __uint_as_float(vi[4 * j + 1]),
+                                __uint_as_float(vi[4 * j + 2]), __uint_as_float(vi[4 * j + 3]));
     }
     ptx::fence_proxy_async_shared();
     __syncwarp();
@@ -424,7 +418,7 @@ __device__ __noinline__ bool split_piece_epilogue(const FpropParams& prm, WorkUn
   }
   ptx::tc_fence_before();
   __syncwarp();
-  if (lane == 0) ptx::mbar_arrive_cluster(tempty_remote);
+  if (lane == 0) ptx::mbar_arrive_cluster_relaxed(tempty_remote);
   return last;
 }
 

@@ -352,7 +352,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32
         // This warp is done with the accumulator buffer: release it to the MMA.
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive_cluster(t_free);
+        if (lane == 0) ptx::mbar_arrive_cluster_relaxed(t_free);
       }
       if (!ok) break;
     }
@@ -488,11 +488,11 @@ int encode_planar_out_maps(FpropParams& prm, float* y0, float* y1, bool flat) {
     const uint64_t strides[1] = {kb};
     const uint32_t box[2] = {16, 32};
     const uint32_t es[2] = {1, 1};
-    if ((rc = encode_tiled_ex(&prm.tm_y0, y0, 2, dims, strides, box, es, kSwizzleNone, false)) !=
+    if ((rc = encode_tiled_ex(&prm.tm_y0, y0, 2, dims, strides, box, es, kSwizzle64, false)) !=
         CCV_OK) {
       return rc;
     }
-    if ((rc = encode_tiled_ex(&prm.tm_y1, y1, 2, dims, strides, box, es, kSwizzleNone, false)) !=
+    if ((rc = encode_tiled_ex(&prm.tm_y1, y1, 2, dims, strides, box, es, kSwizzle64, false)) !=
         CCV_OK) {
       return rc;
     }
@@ -505,11 +505,11 @@ int encode_planar_out_maps(FpropParams& prm, float* y0, float* y1, bool flat) {
     const uint64_t strides[3] = {kb, kb * prm.q, kb * prm.q * prm.p};
     const uint32_t box[4] = {16, px, 32u / px, 1};
     const uint32_t es[4] = {1, 1, 1, 1};
-    if ((rc = encode_tiled_ex(&prm.tm_y0, y0, 4, dims, strides, box, es, kSwizzleNone, false)) !=
+    if ((rc = encode_tiled_ex(&prm.tm_y0, y0, 4, dims, strides, box, es, kSwizzle64, false)) !=
         CCV_OK) {
       return rc;
     }
-    if ((rc = encode_tiled_ex(&prm.tm_y1, y1, 4, dims, strides, box, es, kSwizzleNone, false)) !=
+    if ((rc = encode_tiled_ex(&prm.tm_y1, y1, 4, dims, strides, box, es, kSwizzle64, false)) !=
         CCV_OK) {
       return rc;
     }

@@ -390,7 +390,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<LW>(), 
         // This warp is done with the accumulator buffer: release it to the MMA.
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive_cluster(t_free);
+        if (lane == 0) ptx::mbar_arrive_cluster_relaxed(t_free);
       }
       if (!ok) break;
     }

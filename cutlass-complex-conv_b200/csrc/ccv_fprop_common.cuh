@@ -307,8 +307,9 @@ Tiling choose_halo_tiling_px(const Problem& pb, int px);
 // Bytes of shared memory a pair kernel sets aside for the TMA-store epilogue
 // (4 warps x 32 rows x 16 channels x 2 planes).
 constexpr int kOutStageBytes = 4 * 32 * 16 * 4 * 2;
-// Encodes prm.tm_y0 / tm_y1 for planar output and sets prm.out_tma when the
-// tiling lets each epilogue warp's 32 rows form one TMA box.
+// Encodes prm.tm_y0 / tm_y1 for planar output (16-channel x 32-pixel boxes,
+// 64-byte swizzle: the layout store_accumulator_tma stages) and sets
+// prm.out_tma when the tiling lets each epilogue warp's 32 rows form one box.
 int encode_planar_out_maps(FpropParams& prm, float* y0, float* y1, bool flat);
 
 // ws/ws_bytes: optional scratch for the tail split (pair_split_workspace_bytes);

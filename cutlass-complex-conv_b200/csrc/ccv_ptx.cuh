@@ -411,6 +411,16 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
                : "memory");
 }
+// Arrival without release semantics, for "accumulator buffer free" signals:
+// the epilogue's tcgen05.ld reads are complete once tcgen05.wait::ld returns,
+// and nothing else the arriving thread wrote is read by the waiter.  A
+// release arrival would first wait for the thread's earlier memory
+// operations - the TMA stores it just issued included - which measured
+// ~2.8k cycles per tile in the pair kernels' epilogue.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
 
 // 32-bit store to shared memory of a CTA of the cluster (cluster address).
 __device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
