@@ -376,43 +376,92 @@ __device__ __noinline__ bool split_piece_epilogue(const FpropParams& prm, WorkUn
         if (k + nbuf < nchunk) issue(k + nbuf);
       }
     } else {
-      // Register path: two granules (16 channels) per step.
-#pragma unroll 1
-      for (int ch = 0; ch < 8 * ngran; ch += 16) {
-        uint32_t vr[16], vi[16];
-#pragma unroll 1
-        for (int g = g0; g <= g1; ++g) {
-          uint32_t ar[16], ai[16];
-          if (g == cid) {
-            ptx::tmem_ld_32x32b_x16(t_acc + ch, ar);
-            ptx::tmem_ld_32x32b_x16(t_acc + KT + ch, ai);
-            ptx::tmem_wait_ld();
-          } else {
-            const float4* src = ws4 + block0(g) + lane + (ch / 8) * 128;
-            float4 v[8];
+      // Register path: two granules (16 channels) per step.  The other
+      // pieces' rows are "items" (step, piece) read in summation order; two
+      // items are in flight at a time, so the L2 round trip of the next item
+      // overlaps the sums of the current one instead of every step waiting
+      // for its own loads (this path runs while the cluster's MMAs stream
+      // operands, which makes each round trip long).
+      const int npo = ng - 1;                        // other pieces
+      const int nsteps = (8 * ngran + 15) / 16;
+      const int nitems = nsteps * npo;
+      auto load_item = [&](int it, float4 (&v)[8]) {
+        const int step = it / npo;
+        const int po = it - step * npo;
+        const int g = g0 + po + (g0 + po >= cid ? 1 : 0);  // po-th piece other than cid
+        const float4* src = ws4 + block0(g) + lane + (2 * step) * 128;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + j * 32);
+        for (int j = 0; j < 8; ++j) v[j] = __ldcg(src + j * 32);
+      };
+      float4 bufa[8], bufb[8];
+      if (nitems > 0) load_item(0, bufa);
+      if (nitems > 1) load_item(1, bufb);
+      uint32_t vr[16], vi[16];
+      bool first = true, own_done = false;
+      // Adds one piece's 16 channels (in cluster order) to the step's sums.
+      auto add16 = [&](const uint32_t (&ar)[16], const uint32_t (&ai)[16]) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const float4 a0 = v[4 * h], a1 = v[4 * h + 1], b0 = v[4 * h + 2], b1 = v[4 * h + 3];
-              const float fa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
-              const float fb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        for (int e = 0; e < 16; ++e) {
+          vr[e] = first ? ar[e] : __float_as_uint(__uint_as_float(vr[e]) + __uint_as_float(ar[e]));
+          vi[e] = first ? ai[e] : __float_as_uint(__uint_as_float(vi[e]) + __uint_as_float(ai[e]));
+        }
+        first = false;
+      };
+      // This CTA's own partial of the step, read from TMEM where it joins.
+      auto add_own = [&](int step) {
+        uint32_t ar[16], ai[16];
+        ptx::tmem_ld_32x32b_x16(t_acc + 16 * step, ar);
+        ptx::tmem_ld_32x32b_x16(t_acc + KT + 16 * step, ai);
+        ptx::tmem_wait_ld();
+        add16(ar, ai);
+        own_done = true;
+      };
+      auto begin_step = [&](int) {
+        first = true;
+        own_done = false;
+      };
+      auto end_step = [&](int step) {
+        if (!own_done) add_own(step);
+        if (valid) store_chunk<OUT_COMPLEX, 16>(prm, k0 + 16 * step, img, op, oq, vr, vi);
+      };
+      // Consumes item `it` from v: the piece's value joins the sums after
+      // this CTA's own partial when the piece comes later in cluster order.
+      auto consume = [&](int it, const float4 (&v)[8]) {
+        const int step = it / npo;
+        const int po = it - step * npo;
+        if (po == 0) begin_step(step);
+        const int g = g0 + po + (g0 + po >= cid ? 1 : 0);
+        if (!own_done && g > cid) add_own(step);
+        uint32_t ar[16], ai[16];
 #pragma unroll
-              for (int e = 0; e < 8; ++e) {
-                ar[8 * h + e] = __float_as_uint(fa[e]);
-                ai[8 * h + e] = __float_as_uint(fb[e]);
-              }
-            }
-          }
+        for (int h = 0; h < 2; ++h) {
+          const float4 a0 = v[4 * h], a1 = v[4 * h + 1], b0 = v[4 * h + 2], b1 = v[4 * h + 3];
+          const float fa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+          const float fb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            vr[e] = g == g0 ? ar[e]
-                            : __float_as_uint(__uint_as_float(vr[e]) + __uint_as_float(ar[e]));
-            vi[e] = g == g0 ? ai[e]
-                            : __float_as_uint(__uint_as_float(vi[e]) + __uint_as_float(ai[e]));
+          for (int e = 0; e < 8; ++e) {
+            ar[8 * h + e] = __float_as_uint(fa[e]);
+            ai[8 * h + e] = __float_as_uint(fb[e]);
           }
         }
-        if (valid) store_chunk<OUT_COMPLEX, 16>(prm, k0 + ch, img, op, oq, vr, vi);
+        add16(ar, ai);
+        if (po == npo - 1) end_step(step);
+      };
+      if (npo == 0) {
+#pragma unroll 1
+        for (int step = 0; step < nsteps; ++step) {
+          begin_step(step);
+          end_step(step);
+        }
+      }
+#pragma unroll 1
+      for (int it = 0; it < nitems; it += 2) {
+        consume(it, bufa);
+        if (it + 2 < nitems) load_item(it + 2, bufa);
+        if (it + 1 < nitems) {
+          consume(it + 1, bufb);
+          if (it + 3 < nitems) load_item(it + 3, bufb);
+        }
       }
     }
   }

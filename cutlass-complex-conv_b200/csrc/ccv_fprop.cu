@@ -118,6 +118,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto empty_bar = [&](int i) { return bar_base + 8u * (C::kStages + i); };
   const uint32_t acc_bar = bar_base + 8u * (2 * C::kStages);
 
+  // Split-K: a cluster of `splits` CTAs shares one output tile; CTA `split`
+  // runs K steps [kbeg, kend) and the partial sums are reduced after the
+  // mainloop (splits == 1: no cluster).
+  const int splits = prm.splits;
+  const int tile = blockIdx.x / splits;
+  const int split = blockIdx.x - tile * splits;
+  const int kbeg = static_cast<int>(static_cast<long long>(split) * prm.ksteps / splits);
+  const int kend = static_cast<int>(static_cast<long long>(split + 1) * prm.ksteps / splits);
+  const int n_tile = tile % prm.tiles_n;
+  const int m_tile = tile / prm.tiles_n;
+  const int k0 = n_tile * KT;
+  const int rs = prm.r * prm.s;
+
+  if (warp == 0 && lane == 0) {
+    // Every weight byte of this CTA's K range is read once, from HBM: ask
+    // for all of it now, before the prologue and the wait for the previous
+    // kernel, so the stream of the whole grid is in flight at once instead
+    // of `kStages` boxes per CTA at a time.  The loads below then hit L2.
+    for (int t = kbeg; t < kend; ++t) {
+      const int cb = t / rs;
+      ptx::tma_prefetch_l2_4d(&prm.tm_w, cb * kBlockC, k0, 1, t - cb * rs);
+    }
+  }
   if (threadIdx.x == 0) {
     flags[1] = 0;
     for (int i = 0; i < C::kStages; ++i) {
@@ -151,19 +174,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::griddep_launch_dependents();
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
-
-  // Split-K: a cluster of `splits` CTAs shares one output tile; CTA `split`
-  // runs K steps [kbeg, kend) and the partial sums are reduced through
-  // distributed shared memory after the mainloop (splits == 1: no cluster).
-  const int splits = prm.splits;
-  const int tile = blockIdx.x / splits;
-  const int split = blockIdx.x - tile * splits;
-  const int kbeg = static_cast<int>(static_cast<long long>(split) * prm.ksteps / splits);
-  const int kend = static_cast<int>(static_cast<long long>(split + 1) * prm.ksteps / splits);
-  const int n_tile = tile % prm.tiles_n;
-  const int m_tile = tile / prm.tiles_n;
-  const int k0 = n_tile * KT;
-  const int rs = prm.r * prm.s;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
