@@ -26,6 +26,31 @@ from torch import nn
 from ._extension import cutlass_complex_conv
 
 _PRECISIONS = {"tf32": 0, "3xtf32": 1}
+# Input bytes per chunk in the middle of forward_host's pipeline.
+_HOST_CHUNK_BYTES = 24 << 20
+
+
+def _host_chunks(n, middle):
+    """Chunk sizes (images) of forward_host's default schedule for n images.
+
+    The pipeline's two ends have only one PCIe direction busy: the first
+    chunk's copy-in runs before any copy-out and the last chunk's copy-out
+    after every copy-in.  So the chunks ramp up 1, 2, 4, ... to `middle`
+    images and back down at the end, which keeps both ends short while the
+    middle chunks stay large (few calls).  Small batches get >= 3 equal
+    chunks.
+    """
+    head = []
+    c = 1
+    while c < middle:
+        head.append(c)
+        c *= 2
+    if 2 * sum(head) + middle > n:
+        per = max(1, min(middle, -(-n // 3)))
+        return [min(per, n - i) for i in range(0, n, per)]
+    rest = n - 2 * sum(head)
+    mid = [middle] * (rest // middle) + ([rest % middle] if rest % middle else [])
+    return head + mid + head[::-1]
 _WEIGHT_KCRS = 0
 
 
@@ -350,8 +375,10 @@ class ComplexConv2d(nn.Module):
             x: pinned (``pin_memory()``) CPU complex64 tensor, NCHW, contiguous.
             out: optional pinned CPU complex64 tensor of ``output_shape``;
                 allocated (pinned) when None.
-            images_per_chunk: images per chunk; None picks ~16 MB of input,
-                capped so that there are at least 3 chunks.
+            images_per_chunk: images per chunk; None picks chunks of about
+                24 MB of input with smaller chunks at both ends (1, 2, 4, ...
+                images), so that the start and the end of the pipeline,
+                where only one copy direction is busy, stay short.
 
         Returns:
             ``out``.  Like ``Tensor.copy_(..., non_blocking=True)``, the call
@@ -387,13 +414,12 @@ class ComplexConv2d(nn.Module):
         if n == 0:
             return out
         if images_per_chunk is None:
-            # ~16 MB of input per chunk, and at least 3 chunks so that copies
-            # in both directions overlap (best of 1..32 images per chunk at
-            # batch 8, 32 and 64 of a 3.2 MB/image layer on B200).
-            images_per_chunk = max(1, min((16 << 20) // max(1, x[0].numel() * 8),
-                                          -(-n // 3)))
-        if images_per_chunk < 1:
-            raise ValueError("images_per_chunk must be >= 1")
+            middle = max(1, _HOST_CHUNK_BYTES // max(1, x[0].numel() * 8))
+            sizes = _host_chunks(n, middle)
+        else:
+            if images_per_chunk < 1:
+                raise ValueError("images_per_chunk must be >= 1")
+            sizes = [min(images_per_chunk, n - i) for i in range(0, n, images_per_chunk)]
 
         cur = torch.cuda.current_stream(dev)
         h2d, d2h = self._copy_streams(dev)
@@ -402,8 +428,9 @@ class ComplexConv2d(nn.Module):
         # earlier work on that memory; cur waits for them again at the end.
         h2d.wait_stream(cur)
         d2h.wait_stream(cur)
-        for i0 in range(0, n, images_per_chunk):
-            i1 = min(n, i0 + images_per_chunk)
+        i1 = 0
+        for size in sizes:
+            i0, i1 = i1, i1 + size
             with torch.cuda.stream(h2d):
                 xd[i0:i1].copy_(x[i0:i1], non_blocking=True)
             copied = torch.cuda.Event()

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from complex_conv2d import ComplexConv2d
-from complex_conv2d.modules import _pair
+from complex_conv2d.modules import _host_chunks, _pair
 
 
 def test_rejects_unsupported_options():
@@ -114,3 +114,15 @@ def test_apply_clears_cache():
     m._weight_version = (0, 0)
     m.float()
     assert m._w_packed is None and m._weight_version is None
+
+
+def test_forward_host_chunk_schedule():
+    # Ramp 1, 2, 4 up to the middle size and back down; every image once.
+    assert _host_chunks(64, 7) == [1, 2, 4] + [7] * 7 + [1] + [4, 2, 1]
+    for n in range(1, 130):
+        for middle in (1, 3, 7, 8, 16):
+            sizes = _host_chunks(n, middle)
+            assert sum(sizes) == n and min(sizes) >= 1 and max(sizes) <= max(middle, 1)
+    # Small batches: at least three equal chunks where there are 3 images.
+    assert _host_chunks(8, 7) == [3, 3, 2]
+    assert _host_chunks(1, 7) == [1]
