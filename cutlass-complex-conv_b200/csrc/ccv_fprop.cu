@@ -188,7 +188,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (flags[1]) break;
         const uint32_t fb = full_bar(stage);
-        ptx::mbar_arrive_expect_tx(fb, C::kStageBytes);
+        // Boxes of the tile past the last box of the problem are not loaded:
+        // their rows hold whatever the stage held before, and the MMA rows
+        // they feed are never stored or summed (a 7x7 image is one 8x8 box of
+        // a two-box tile).
+        int nload = 1;
+        if constexpr (!FLAT) nload = max(1, min(prm.nb, prm.total_boxes - m_tile * prm.nb));
+        const uint32_t a_bytes =
+            FLAT ? static_cast<uint32_t>(kABytes)
+                 : static_cast<uint32_t>(nload) * ((1u << prm.box_px_log2) * kRowBytes);
+        ptx::mbar_arrive_expect_tx(fb, 2u * a_bytes + static_cast<uint32_t>(C::kWBytes));
         const int cb = t / rs;
         const int tap = t - cb * rs;
         const int rr = tap / prm.s;
@@ -203,9 +212,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           const int per_img = prm.tiles_bp * prm.tiles_bq;
           const uint32_t box_bytes = (1u << prm.box_px_log2) * kRowBytes;
-          for (int b = 0; b < prm.nb; ++b) {
-            // Boxes past the end repeat the last box; their rows are not stored.
-            const int gb = min(m_tile * prm.nb + b, prm.total_boxes - 1);
+          for (int b = 0; b < nload; ++b) {
+            const int gb = m_tile * prm.nb + b;
             const int img = gb / per_img;
             const int rem = gb - img * per_img;
             const int bp = rem / prm.tiles_bq;
@@ -889,6 +897,7 @@ int launch_fprop(const float* xr, const float* xi, const float* xr_lo, const flo
     default:
       break;
   }
+  t = choose_tiling(pb, true);  // same tiles, fewer loaded rows (boxes past the end skipped)
   const SinglePlan plan = plan_single_cta(pb, t, ws != nullptr ? ws_bytes : 0);
   t.kt = plan.kt;
   t.tiles_n = (pb.k + t.kt - 1) / t.kt;

@@ -159,8 +159,10 @@ __host__ __device__ inline bool next_unit(const FpropParams& prm, int ncl, UnitC
                                           WorkUnit& w) {
   const int L = prm.slots_per_tile;
   // The stream-K range first: a split tile's sum is then finished by
-  // whichever piece ends last while its cluster goes on with whole tiles,
-  // off the kernel's critical path.
+  // whichever piece ends last while its cluster goes on with whole tiles.
+  // (Measured: whole tiles first, split pieces last, ran the batch-8 share
+  // of the 56x56 layer in 73 us instead of 56 us - the last pieces then
+  // wait for each other at the end of the launch.)
   if (c.s < c.s1) {
     const int a = c.s / L;
     const int end = c.s1 < (a + 1) * L ? c.s1 : (a + 1) * L;
@@ -229,7 +231,13 @@ inline int ilog2(int v) {
   return l;
 }
 
-inline Tiling choose_tiling(const Problem& pb) {
+// fewest_loaded: among tilings computing the same rows prefer the one that
+// loads the fewest activation rows when boxes past the problem's last box are
+// skipped (the single-CTA kernel skips them; the pair kernels repeat the last
+// box), then the fewest boxes per tile; boxes of at least 64 pixels (smaller
+// TMA boxes load slower).  A 7x7 image is then one 8x8 box of a two-box tile
+// (64 loaded rows) rather than one 8x16 box (128).
+inline Tiling choose_tiling(const Problem& pb, bool fewest_loaded = false) {
   Tiling t;
   t.kt = pb.k > 64 ? 128 : (pb.k > 32 ? 64 : 32);
   t.tiles_n = (pb.k + t.kt - 1) / t.kt;
@@ -242,7 +250,7 @@ inline Tiling choose_tiling(const Problem& pb) {
   // Spatial boxes: box_p x box_q (powers of two, product 8..128, at most 4
   // boxes per tile), chosen to cover P x Q with the fewest computed rows.
   long long best_cost = -1;
-  for (int px = 32; px <= 128; px *= 2) {
+  for (int px = fewest_loaded ? 64 : 32; px <= 128; px *= 2) {
     const int nb = kBlockM / px;
     for (int bq = 1; bq <= px; bq *= 2) {
       const int bp = px / bq;
@@ -251,7 +259,9 @@ inline Tiling choose_tiling(const Problem& pb) {
       const long long tbp = (pb.p + bp - 1) / bp;
       const long long boxes = static_cast<long long>(pb.n) * tbq * tbp;
       const long long tiles = (boxes + nb - 1) / nb;
-      const long long cost = tiles * kBlockM * 4 + nb;  // rows computed, then fewer boxes
+      // Rows computed, then (fewest_loaded) rows loaded, then fewer boxes.
+      const long long cost = fewest_loaded ? (tiles * kBlockM * 4096 + boxes * px * 4 + nb)
+                                           : (tiles * kBlockM * 4 + nb);
       if (best_cost < 0 || cost < best_cost) {
         best_cost = cost;
         t.box_p = bp;
