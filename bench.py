@@ -399,6 +399,29 @@ def measure_config(wname, precision, world, rank, dev, args, peaks):
             e["blocks"] = blocks
             res[name + ("_warm" if batch1 else "")] = e
         if batch1:
+            # Device time per call: the same module calls captured in one CUDA
+            # graph (a serving loop's form), replayed; what is left is the
+            # kernels and the gaps between them, not the host-side call.
+            for name, fn in (("forward", fwd), ("forward_planar", planar)):
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(side):
+                    for _ in range(3):
+                        fn()
+                torch.cuda.current_stream(dev).wait_stream(side)
+                torch.cuda.synchronize(dev)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for _ in range(args.steps):
+                        fn()
+                graph.replay()
+                torch.cuda.synchronize(dev)
+                t, blocks = timed_blocks(graph.replay, 1, world, dev)
+                e = roofline_entry(flops_rank, alg_rank, t / args.steps, precision, peaks)
+                e["blocks"] = blocks
+                e["method"] = f"CUDA graph of {args.steps} calls, replayed; device time per call"
+                res[name + "_graph"] = e
+                del graph
             # Cold: distinct layers and inputs, > 2x L2 in total.
             packed = layer._w_packed.numel() * 4
             m = min(64, max(2, -(-2 * L2_BYTES // (packed + in_bytes + out_bytes))))
@@ -634,7 +657,8 @@ def emit_line(args, wl, world, nb, nbuf, in_bytes, out_bytes, flops_rank, flops_
                             "= whole job), frac = of the dense TF32 peak (3xTF32: peak/3), gbs = "
                             "algorithmic bytes 8*(NHWC+KRSC+NPQK) per call / time, hbm_frac = of the "
                             "measured copy bandwidth; batch-1 layers: _warm = one layer back to "
-                            "back, _cold = rotating layers+inputs > 2x L2"),
+                            "back, _cold = rotating layers+inputs > 2x L2, _graph = device time "
+                            "per call in a replayed CUDA graph of the same calls"),
     }
     if cb is not None:
         line["cpu_baseline"] = cb
