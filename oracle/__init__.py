@@ -6,6 +6,8 @@ use this package, as the checker.  The product package never imports it.
 
 from .oracle import (  # noqa: F401
     ConvCase,
+    backward_autograd_fp64,
+    backward_formula_fp64,
     build_c_oracle,
     direct_c,
     four_conv,

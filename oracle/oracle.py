@@ -1,4 +1,4 @@
-"""CPU oracle for the complex Conv2d forward path.
+"""CPU oracle for the complex Conv2d forward path (and its gradients).
 
 TEST INFRASTRUCTURE ONLY. Nothing in the product package imports this file:
 only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline
@@ -273,6 +273,65 @@ def oracle_fp64(case: ConvCase, x: torch.Tensor, w_real: torch.Tensor,
         b = torch.complex(bias_real.cpu().double(), bias_imag.cpu().double())
         y = y + b.view(1, -1, 1, 1)
     return y
+
+
+# --------------------------------------------------------------------------
+# Backward (data and weight gradients)
+# --------------------------------------------------------------------------
+def backward_autograd_fp64(case: ConvCase, x: torch.Tensor, w_real: torch.Tensor,
+                           w_imag: torch.Tensor, dy: torch.Tensor):
+    """Vector-Jacobian product of the four-conv formula, by torch autograd in fp64.
+
+    The reference module is built from ``nn.Conv2d`` layers
+    (``benchmarks/baseline.py:12-45``), so autograd differentiates it; with
+    the upstream gradient ``dy`` (complex, shape of the output) this returns
+    what ``torch.autograd.grad(y, (x, conv_real.weight, conv_imag.weight),
+    grad_outputs=dy)`` gives for it: (dx complex128 NCHW, dw_real, dw_imag
+    fp64 KCRS).  PyTorch's complex convention (conjugate Wirtinger) makes
+    dx = conv_transpose(dy, conj(W)) and dW = sum dy * conj(x).
+    """
+    xx = x.cpu().to(torch.complex128).requires_grad_(True)
+    wr = w_real.cpu().double().requires_grad_(True)
+    wi = w_imag.cpu().double().requires_grad_(True)
+    y = four_conv(xx, wr, wi, (case.stride_h, case.stride_w), (case.pad_h, case.pad_w),
+                  dtype=torch.float64)
+    dx, dwr, dwi = torch.autograd.grad(y, (xx, wr, wi),
+                                       grad_outputs=dy.cpu().to(torch.complex128))
+    return dx.detach(), dwr.detach(), dwi.detach()
+
+
+def backward_formula_fp64(case: ConvCase, x: torch.Tensor, w_real: torch.Tensor,
+                          w_imag: torch.Tensor, dy: torch.Tensor):
+    """The same gradients from their closed forms, without autograd:
+
+        dx[n,c,h,w]  = sum_{k,r,s} conj(W[k,c,r,s]) dy[n,k,p,q]
+        dW[k,c,r,s]  = sum_{n,p,q} dy[n,k,p,q] conj(x[n,c,h,w])
+
+    over h = p*sh - ph + r, w = q*sw - pw + s (numpy fp64 loops over the
+    filter taps; zero padding outside the image).  Returns (dx, dw_real,
+    dw_imag) like ``backward_autograd_fp64``.
+    """
+    xn = x.cpu().to(torch.complex128).numpy()
+    g = dy.cpu().to(torch.complex128).numpy()
+    W = (w_real.cpu().double() + 1j * w_imag.cpu().double()).numpy()
+    n, c, h, w = xn.shape
+    k, _, r_, s_ = W.shape
+    p, q = case.p, case.q
+    sh, sw, ph, pw = case.stride_h, case.stride_w, case.pad_h, case.pad_w
+    xp = np.zeros((n, c, h + 2 * ph + sh * p, w + 2 * pw + sw * q), dtype=np.complex128)
+    xp[:, :, ph:ph + h, pw:pw + w] = xn
+    dxp = np.zeros_like(xp)
+    dW = np.zeros_like(W)
+    for r in range(r_):
+        for s in range(s_):
+            # Input pixels read by tap (r, s): rows r + sh*p', cols s + sw*q'.
+            patch = xp[:, :, r:r + sh * p:sh, s:s + sw * q:sw]          # n c p q
+            dW[:, :, r, s] = np.einsum("nkpq,ncpq->kc", g, np.conj(patch))
+            dxp[:, :, r:r + sh * p:sh, s:s + sw * q:sw] += np.einsum(
+                "kc,nkpq->ncpq", np.conj(W[:, :, r, s]), g)
+    dx = dxp[:, :, ph:ph + h, pw:pw + w]
+    return (torch.from_numpy(dx.copy()), torch.from_numpy(dW.real.copy()),
+            torch.from_numpy(dW.imag.copy()))
 
 
 def time_cpu_four_conv(case: ConvCase, iters: int, warmup: int = 1,
