@@ -29,7 +29,7 @@ INCLUDE = os.path.join(REPO, "include")
 OBJ = os.path.join(HERE, "_build")
 
 CU_SOURCES = ["ccv_api.cu", "ccv_fprop.cu", "ccv_fprop2.cu", "ccv_fprop2h.cu", "ccv_layout.cu",
-              "ccv_noalloc.cu"]
+              "ccv_noalloc.cu", "ccv_backward.cu"]
 CU_HEADERS = ["ccv_internal.h", "ccv_ptx.cuh", "ccv_fprop_common.cuh", "ccv_epilogue.cuh",
               "ccv_layout_role.cuh"]
 NVCC_ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -861,3 +861,146 @@ int ccv_reload_config(void) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ backward
+namespace ccv {
+namespace {
+
+// The forward problem's data gradient as a forward problem: dy (spread onto
+// the stride grid, hu x wu) convolved with the transposed filter, stride 1,
+// padding R-1-ph / S-1-pw; its output is H x W.
+int dgrad_problem(const Problem& pb, ccv_conv_shape* out, int* hu, int* wu) {
+  if (pb.ph > pb.r - 1 || pb.pw > pb.s - 1) {
+    return set_error(CCV_ERR_UNSUPPORTED,
+                     "cannot implement the data gradient: padding above kernel size - 1");
+  }
+  // Rows/columns the forward's floor division left out keep a zero gradient.
+  const int eh = (pb.h + 2 * pb.ph - pb.r) % pb.sh;
+  const int ew = (pb.w + 2 * pb.pw - pb.s) % pb.sw;
+  *hu = (pb.p - 1) * pb.sh + 1 + eh;
+  *wu = (pb.q - 1) * pb.sw + 1 + ew;
+  ccv_conv_shape d;
+  d.n = pb.n;
+  d.h = *hu;
+  d.w = *wu;
+  d.c = pb.k;
+  d.k = pb.c;
+  d.r = pb.r;
+  d.s = pb.s;
+  d.stride_h = 1;
+  d.stride_w = 1;
+  d.pad_h = pb.r - 1 - pb.ph;
+  d.pad_w = pb.s - 1 - pb.pw;
+  *out = d;
+  return CCV_OK;
+}
+
+size_t zero_insert_bytes(const Problem& pb, int hu, int wu) {
+  if (pb.sh == 1 && pb.sw == 1) return 0;
+  return align256(static_cast<size_t>(pb.n) * pb.k * hu * wu * 8);
+}
+
+}  // namespace
+}  // namespace ccv
+
+extern "C" {
+
+int ccv_prepack_weights_dgrad(const float* w_real, const float* w_imag, int layout,
+                              const ccv_conv_shape* shape, int precision, void* packed,
+                              size_t packed_bytes, ccv_stream_t stream) {
+  ensure_status_mirror(reinterpret_cast<cudaStream_t>(stream));
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if (layout != CCV_WEIGHT_KCRS && layout != CCV_WEIGHT_KRSC) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "unknown weight layout");
+  }
+  if ((rc = check_precision(precision)) != CCV_OK) return rc;
+  if (w_real == nullptr || w_imag == nullptr || packed == nullptr) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "null weight pointer");
+  }
+  if (!aligned16(packed)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "packed weights must be 16-byte aligned");
+  }
+  if (packed_bytes < ccv_packed_weight_bytes(shape, precision)) {
+    return set_error(CCV_ERR_WORKSPACE, "packed weight buffer too small");
+  }
+  if ((rc = check_device()) != CCV_OK) return rc;
+  if ((rc = check_status_clear()) != CCV_OK) return rc;
+  return launch_prepack_dgrad(w_real, w_imag, layout, pb, precision, static_cast<float*>(packed),
+                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t ccv_dgrad_complex_workspace_bytes(const ccv_conv_shape* shape, int precision) {
+  Problem pb;
+  if (make_problem(shape, &pb) != CCV_OK) return 0;
+  ccv_conv_shape d;
+  int hu = 0, wu = 0;
+  if (dgrad_problem(pb, &d, &hu, &wu) != CCV_OK) return 0;
+  return zero_insert_bytes(pb, hu, wu) + ccv_fprop_complex_workspace_bytes(&d, precision);
+}
+
+int ccv_dgrad_complex(const void* dy, const void* w_packed_dgrad, void* dx,
+                      const ccv_conv_shape* shape, int precision, void* workspace,
+                      size_t workspace_bytes, ccv_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ensure_status_mirror(st);
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if ((rc = check_precision(precision)) != CCV_OK) return rc;
+  if (!dy || !w_packed_dgrad || !dx) return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  if (!aligned16(dy) || !aligned16(w_packed_dgrad) || !aligned16(dx)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  }
+  ccv_conv_shape d;
+  int hu = 0, wu = 0;
+  if ((rc = dgrad_problem(pb, &d, &hu, &wu)) != CCV_OK) return rc;
+  Problem pd;
+  if ((rc = make_problem(&d, &pd)) != CCV_OK) return rc;
+  const size_t up = zero_insert_bytes(pb, hu, wu);
+  if (workspace == nullptr || !aligned16(workspace) ||
+      workspace_bytes < up + complex_required_bytes(pd, precision)) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
+  }
+  if ((rc = check_device()) != CCV_OK) return rc;
+  if ((rc = check_status_clear()) != CCV_OK) return rc;
+  const void* src = dy;
+  if (up > 0) {
+    if ((rc = launch_zero_insert(dy, workspace, pb, hu, wu, st)) != CCV_OK) return rc;
+    src = workspace;
+  }
+  return fprop_complex_impl(src, nullptr, w_packed_dgrad, nullptr, nullptr, dx, &d, precision,
+                            static_cast<char*>(workspace) + up, workspace_bytes - up, stream);
+}
+
+size_t ccv_wgrad_complex_workspace_bytes(const ccv_conv_shape* shape) {
+  Problem pb;
+  if (make_problem(shape, &pb) != CCV_OK) return 0;
+  return wgrad_workspace_bytes(pb);
+}
+
+int ccv_wgrad_complex(const void* x, const void* dy, float* dw_real, float* dw_imag,
+                      const ccv_conv_shape* shape, void* workspace, size_t workspace_bytes,
+                      ccv_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ensure_status_mirror(st);
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if (!x || !dy || !dw_real || !dw_imag) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  }
+  if (!aligned16(x) || !aligned16(dy) || !aligned16(dw_real) || !aligned16(dw_imag)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  }
+  if (workspace == nullptr || !aligned16(workspace) ||
+      workspace_bytes < wgrad_workspace_bytes(pb)) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
+  }
+  if ((rc = check_device()) != CCV_OK) return rc;
+  if ((rc = check_status_clear()) != CCV_OK) return rc;
+  return launch_wgrad(x, dy, dw_real, dw_imag, pb, workspace, st);
+}
+
+}  // extern "C"

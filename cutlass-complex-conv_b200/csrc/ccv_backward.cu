@@ -1,0 +1,633 @@
+// Backward of the complex Conv2d: data gradient (dgrad) and weight gradient
+// (wgrad).  The reference is forward-only (its README lists backward as
+// absent); the gradients here are those torch autograd gives for the
+// reference's own four-conv module (benchmarks/baseline.py:12-45), in
+// PyTorch's complex convention (conjugate Wirtinger):
+//
+//     dx[n,c,h,w] = sum_{k,r,s} conj(W[k,c,r,s]) * dy[n,k,p,q]
+//     dW[k,c,r,s] = sum_{n,p,q} dy[n,k,p,q] * conj(x[n,c,h,w])
+//
+// over h = p*sh - ph + r, w = q*sw - pw + s.
+//
+// dgrad is a forward convolution of dy with the filter transposed (K <-> C),
+// flipped (r -> R-1-r, s -> S-1-s) and conjugated, padding R-1-ph / S-1-pw;
+// for stride > 1, dy is first spread onto the stride grid with zeros between
+// (zero insertion), plus the rows/columns the forward's floor division left
+// out.  It runs on the forward kernels (ccv_fprop*.cu) with a packed image
+// of that filter (ccv_prepack_dgrad_kernel).
+//
+// wgrad is an implicit GEMM per filter tap (r, s): M = output channels k
+// (128-row tiles), N = input channels c, reduction over the output pixels
+// (n, p, q) in steps of 32 consecutive q.  Its operands come from two
+// layout kernels: dy as fp32 planes [N][K][P][Q] (q contiguous) and x as
+// fp32 planes [S][N][C][H][Q], the input column q*sw - pw + s that filter
+// column s reads for output column q (zero outside the image) - one copy
+// per filter column, so that every TMA box starts at a multiple of 32
+// pixels (a tiled TMA copy must start on a 16-byte boundary) - both
+// TF32-rounded.  Two
+// tcgen05 MMAs per 8-deep slice share the x operand [x_re; x_im]:
+//     D1 += dy_re * [x_re; x_im]^T,   D2 += dy_im * [x_re; x_im]^T
+// and the epilogue forms Re dW = D1[:, :CT] + D2[:, CT:],
+// Im dW = D2[:, :CT] - D1[:, CT:].  The reduction is split over CTAs; the
+// partial sums are added in split order by a second kernel (deterministic).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "ccv_internal.h"
+#include "ccv_ptx.cuh"
+
+namespace ccv {
+
+namespace {
+
+__device__ __forceinline__ float to_tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// ------------------------------------------------------------------ dgrad
+// Packed image of the dgrad filter W'[c][k][r'][s'] = conj(W[k][c][R-1-r'][S-1-s'])
+// in the forward's packed layout for the problem (K' = C, C' = K):
+// [tap'][plane][C][K], plane 0 = -W'_im = W_im, 1 = W'_re = W_re,
+// 2 = W'_im = -W_im (TF32-rounded; with `split`, the remainders follow as a
+// second image).
+__global__ void ccv_prepack_dgrad_kernel(const float* __restrict__ wr,
+                                         const float* __restrict__ wi, float* __restrict__ out,
+                                         int K, int C, int R, int S, int krsc, int split) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const long long total = static_cast<long long>(R) * S * K * C;
+  const long long image = total * 3;
+  const long long ck = static_cast<long long>(C) * K;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    // Output order: tap', c (row), k (innermost).
+    const int k = static_cast<int>(i % K);
+    long long t = i / K;
+    const int c = static_cast<int>(t % C);
+    const int tap = static_cast<int>(t / C);
+    const int r = R - 1 - tap / S;
+    const int s = S - 1 - tap % S;
+    const long long src = krsc ? ((static_cast<long long>(k) * R + r) * S + s) * C + c
+                               : ((static_cast<long long>(k) * C + c) * R + r) * S + s;
+    const float xr = wr[src];
+    const float xi = wi[src];
+    const float hr = to_tf32_rna(xr);
+    const float hi = to_tf32_rna(xi);
+    const long long o = static_cast<long long>(tap) * 3 * ck + static_cast<long long>(c) * K + k;
+    out[o] = hi;
+    out[o + ck] = hr;
+    out[o + 2 * ck] = -hi;
+    if (split) {
+      const float lr = to_tf32_rna(xr - hr);
+      const float li = to_tf32_rna(xi - hi);
+      out[image + o] = li;
+      out[image + o + ck] = lr;
+      out[image + o + 2 * ck] = -li;
+    }
+  }
+}
+
+// complex64 [N][K][P][Q] -> complex64 [N][K][Hu][Wu]: dy on the stride grid
+// (dy[.., p, q] at (p*sh, q*sw)), zeros elsewhere.
+__global__ void ccv_zero_insert_kernel(const float2* __restrict__ dy, float2* __restrict__ up,
+                                       long long planes, int P, int Q, int Hu, int Wu, int sh,
+                                       int sw) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const long long total = planes * Hu * Wu;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int wu = static_cast<int>(i % Wu);
+    long long t = i / Wu;
+    const int hu = static_cast<int>(t % Hu);
+    const long long pl = t / Hu;
+    float2 v = make_float2(0.f, 0.f);
+    if (hu % sh == 0 && wu % sw == 0 && hu / sh < P && wu / sw < Q) {
+      v = dy[(pl * P + hu / sh) * Q + wu / sw];
+    }
+    up[i] = v;
+  }
+}
+
+}  // namespace
+
+int launch_prepack_dgrad(const float* w_real, const float* w_imag, int layout, const Problem& pb,
+                         int precision, float* packed, cudaStream_t stream) {
+  const long long total = static_cast<long long>(pb.r) * pb.s * pb.k * pb.c;
+  const int block = 256;
+  const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, 4096));
+  const cudaError_t e = launch_kernel(ccv_prepack_dgrad_kernel, dim3(grid), dim3(block), 0, stream,
+                                      1, w_real, w_imag, packed, pb.k, pb.c, pb.r, pb.s,
+                                      layout == CCV_WEIGHT_KRSC ? 1 : 0,
+                                      precision == CCV_PRECISION_3XTF32 ? 1 : 0);
+  return e == cudaSuccess ? CCV_OK : cuda_error(e, "dgrad weight prepack launch");
+}
+
+int launch_zero_insert(const void* dy, void* up, const Problem& pb, int hu, int wu,
+                       cudaStream_t stream) {
+  const long long planes = static_cast<long long>(pb.n) * pb.k;
+  const long long total = planes * hu * wu;
+  const int block = 256;
+  const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, 148 * 16));
+  const cudaError_t e =
+      launch_kernel(ccv_zero_insert_kernel, dim3(grid), dim3(block), 0, stream, 1,
+                    static_cast<const float2*>(dy), static_cast<float2*>(up), planes, pb.p, pb.q,
+                    hu, wu, pb.sh, pb.sw);
+  return e == cudaSuccess ? CCV_OK : cuda_error(e, "dgrad zero-insertion launch");
+}
+
+// ------------------------------------------------------------------ wgrad
+namespace {
+
+constexpr int kWgThreads = 192;
+constexpr int kWgRowBytes = 128;  // one K-major operand row: 32 fp32 (32 pixels)
+constexpr int kWgM = 128;         // output channels per tile (MMA M)
+
+template <int CT>
+struct WgCfg {
+  static constexpr int kABytes = kWgM * kWgRowBytes;  // one dy plane per stage
+  static constexpr int kBBytes = CT * kWgRowBytes;    // one x plane per stage
+  static constexpr int kStageBytes = 2 * kABytes + 2 * kBBytes;
+  static constexpr int kStages = (192 * 1024) / kStageBytes;  // 3 / 4 / 5 for CT 128 / 64 / 32
+  static_assert(kStages >= 2, "pipeline too shallow");
+  static constexpr int kTmemCols = 4 * CT;  // D1 | D2, 2*CT columns each
+  static constexpr int kBarOffset = kStages * kStageBytes;
+  static constexpr int kSmemBytes = kBarOffset + 256 + 1024;
+};
+
+struct WgradParams {
+  CUtensorMap tm_dyr, tm_dyi;  // fp32 [N][K][P][Q] planes: dims (Q, P, K, N)
+  CUtensorMap tm_xr, tm_xi;    // fp32 [S][N][C][H][Q] planes: dims (Q, H, C, N, S)
+  float* partial;              // [tile][split][128][2*CT] or null (splits == 1)
+  float* dw_r;
+  float* dw_i;
+  int* status;
+  int k, c, r, s, sh, sw, ph, pw, p, q;
+  int tiles_c, splits, qblocks;
+  long long steps;  // reduction steps of a tile: N * P * qblocks
+};
+
+// Complex64 [planes][P][Q] -> TF32-rounded fp32 planes [planes][P][Qa].
+__global__ void ccv_wgrad_dy_planes_kernel(const float2* __restrict__ dy, float* __restrict__ yr,
+                                           float* __restrict__ yi, long long rows, int Q,
+                                           int Qa) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const long long total = rows * Q;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long row = i / Q;
+    const int q = static_cast<int>(i - row * Q);
+    const float2 v = dy[i];
+    yr[row * Qa + q] = to_tf32_rna(v.x);
+    yi[row * Qa + q] = to_tf32_rna(v.y);
+  }
+}
+
+// Complex64 NCHW -> TF32-rounded fp32 planes [S][N][C][H][Qa], element
+// (s, .., q) = x[.., w = q*sw - pw + s] (0 outside the image), for q < Q.
+__global__ void ccv_wgrad_x_planes_kernel(const float2* __restrict__ x, float* __restrict__ xr,
+                                          float* __restrict__ xi, long long rows, int W, int S,
+                                          int Q, int Qa, int sw, int pw) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const long long total = static_cast<long long>(S) * rows * Q;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int q = static_cast<int>(i % Q);
+    const long long t = i / Q;  // (s, n, c, h)
+    const int s = static_cast<int>(t / rows);
+    const long long row = t - static_cast<long long>(s) * rows;
+    const int w = q * sw - pw + s;
+    float2 v = make_float2(0.f, 0.f);
+    if (w >= 0 && w < W) v = x[row * W + w];
+    const long long o = t * Qa + q;
+    xr[o] = to_tf32_rna(v.x);
+    xi[o] = to_tf32_rna(v.y);
+  }
+}
+
+__device__ __forceinline__ float4 f4(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return make_float4(__uint_as_float(a), __uint_as_float(b), __uint_as_float(c),
+                     __uint_as_float(d));
+}
+
+// One CTA: tile (k block, c block, tap) x split (a contiguous range of its
+// reduction steps).  Warps: 0 TMA producer, 1 TMEM allocation + MMA issue,
+// 2..5 epilogue (one output channel k per thread).
+template <int CT>
+__global__ void __launch_bounds__(kWgThreads, 1)
+    ccv_wgrad_tf32_kernel(const __grid_constant__ WgradParams prm) {
+  using Cf = WgCfg<CT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cf::kBarOffset);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * Cf::kStages + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [0] skip, [1] abort
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t smem_base = ptx::smem_u32(smem);
+  const uint32_t bar_base = ptx::smem_u32(bars);
+  auto full_bar = [&](int i) { return bar_base + 8u * i; };
+  auto empty_bar = [&](int i) { return bar_base + 8u * (Cf::kStages + i); };
+  const uint32_t acc_bar = bar_base + 8u * (2 * Cf::kStages);
+
+  const int splits = prm.splits;
+  const int tile = blockIdx.x / splits;
+  const int split = blockIdx.x - tile * splits;
+  const int rs = prm.r * prm.s;
+  const int tap = tile % rs;
+  const int rest = tile / rs;
+  const int ct = rest % prm.tiles_c;
+  const int kt = rest / prm.tiles_c;
+  const int rr = tap / prm.s;
+  const int ss = tap - rr * prm.s;
+  const long long b0 = static_cast<long long>(split) * prm.steps / splits;
+  const long long b1 = static_cast<long long>(split + 1) * prm.steps / splits;
+
+  if (threadIdx.x == 0) {
+    flags[1] = 0;
+    for (int i = 0; i < Cf::kStages; ++i) {
+      ptx::mbar_init(full_bar(i), 1);
+      ptx::mbar_init(empty_bar(i), 1);
+    }
+    ptx::mbar_init(acc_bar, 1);
+    ptx::fence_mbar_init();
+    ptx::prefetch_tmap(&prm.tm_dyr);
+    ptx::prefetch_tmap(&prm.tm_dyi);
+    ptx::prefetch_tmap(&prm.tm_xr);
+    ptx::prefetch_tmap(&prm.tm_xi);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), Cf::kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const uint32_t tmem_base = *tmem_holder;
+  const bool skip = flags[0] != 0 || b1 <= b0;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0 && !skip) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long long issued = 0;
+      for (long long t = b0; t < b1; ++t) {
+        if (!ptx::mbar_wait_bounded(empty_bar(stage), phase ^ 1u, prm.status,
+                                    CCV_ERR_DEVICE_TIMEOUT)) {
+          flags[1] = 1;
+          break;
+        }
+        if (flags[1]) break;
+        const uint32_t fb = full_bar(stage);
+        ptx::mbar_arrive_expect_tx(fb, Cf::kStageBytes);
+        const int qb = static_cast<int>(t % prm.qblocks);
+        const long long pr = t / prm.qblocks;
+        const int pp = static_cast<int>(pr % prm.p);
+        const int nn = static_cast<int>(pr / prm.p);
+        const uint32_t a_r = smem_base + stage * Cf::kStageBytes;
+        const uint32_t a_i = a_r + Cf::kABytes;
+        const uint32_t b_r = a_i + Cf::kABytes;
+        const uint32_t b_i = b_r + Cf::kBBytes;
+        // dy rows k of output row pp, columns 32*qb.. (zero past Q and K).
+        ptx::tma_load_4d(a_r, &prm.tm_dyr, fb, qb * 32, pp, kt * kWgM, nn);
+        ptx::tma_load_4d(a_i, &prm.tm_dyi, fb, qb * 32, pp, kt * kWgM, nn);
+        // x rows c of input row pp*sh - ph + rr (zero outside the image:
+        // the padding), the columns filter column ss reads for output
+        // columns 32*qb..
+        const int hh = pp * prm.sh - prm.ph + rr;
+        ptx::tma_load_5d(b_r, &prm.tm_xr, fb, qb * 32, hh, ct * CT, nn, ss);
+        ptx::tma_load_5d(b_i, &prm.tm_xi, fb, qb * 32, hh, ct * CT, nn, ss);
+        ++issued;
+        if (++stage == Cf::kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      // No TMA write may be in flight into this CTA's shared memory when it
+      // exits (matters only after an abort).
+      for (int j = 0; j < Cf::kStages && j < issued; ++j) {
+        const long long u = issued - 1 - j;
+        ptx::mbar_wait_bounded(full_bar(static_cast<int>(u % Cf::kStages)),
+                               static_cast<uint32_t>((u / Cf::kStages) & 1), prm.status,
+                               CCV_ERR_DEVICE_TIMEOUT);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0 && !skip) {
+      constexpr uint32_t idesc = ptx::idesc_tf32(kWgM, 2 * CT, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (long long t = b0; t < b1; ++t) {
+        if (!ptx::mbar_wait_bounded(full_bar(stage), phase, prm.status, CCV_ERR_DEVICE_TIMEOUT)) {
+          flags[1] = 1;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t a_r = smem_base + stage * Cf::kStageBytes;
+        const uint32_t a_i = a_r + Cf::kABytes;
+        const uint32_t b_r = a_i + Cf::kABytes;  // [x_re; x_im]: 2*CT rows
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t koff = kk * 32;
+          const uint64_t da_r = ptx::desc_kmajor_sw128(a_r + koff);
+          const uint64_t da_i = ptx::desc_kmajor_sw128(a_i + koff);
+          const uint64_t db = ptx::desc_kmajor_sw128(b_r + koff);
+          const uint32_t acc = (t != b0 || kk != 0) ? 1u : 0u;
+          ptx::mma_tf32_ss(tmem_base, da_r, db, idesc, acc);           // D1
+          ptx::mma_tf32_ss(tmem_base + 2 * CT, da_i, db, idesc, acc);  // D2
+        }
+        ptx::mma_commit(empty_bar(stage));
+        if (++stage == Cf::kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      ptx::mma_commit(acc_bar);
+      ptx::mbar_wait_bounded(acc_bar, 0, prm.status, CCV_ERR_DEVICE_TIMEOUT);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int k = kt * kWgM + row;
+    bool ok = false;
+    if (!skip) {
+      ok = ptx::mbar_wait_bounded_backoff(acc_bar, 0, prm.status, CCV_ERR_DEVICE_TIMEOUT);
+      ptx::tc_fence_after();
+    }
+    if (flags[1]) ok = false;
+    const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16);
+    float* part = prm.partial != nullptr
+                      ? prm.partial + ((static_cast<long long>(tile) * splits + split) * kWgM +
+                                       row) * (2 * CT)
+                      : nullptr;
+#pragma unroll 1
+    for (int c16 = 0; c16 < CT; c16 += 16) {
+      uint32_t a[16], b[16], e[16], f[16];
+      if (ok) {
+        ptx::tmem_ld_32x32b_x16(t_row + c16, a);               // dy_re * x_re
+        ptx::tmem_ld_32x32b_x16(t_row + CT + c16, b);          // dy_re * x_im
+        ptx::tmem_ld_32x32b_x16(t_row + 2 * CT + c16, e);      // dy_im * x_re
+        ptx::tmem_ld_32x32b_x16(t_row + 3 * CT + c16, f);      // dy_im * x_im
+        ptx::tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) a[j] = b[j] = e[j] = f[j] = 0u;
+      }
+      uint32_t re[16], im[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        re[j] = __float_as_uint(__uint_as_float(a[j]) + __uint_as_float(f[j]));
+        im[j] = __float_as_uint(__uint_as_float(e[j]) - __uint_as_float(b[j]));
+      }
+      if (part != nullptr) {
+        // A split CTA writes its partial even when it has no steps (zeros),
+        // so the reduction reads defined values.
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) {
+          *reinterpret_cast<float4*>(part + c16 + j) = f4(re[j], re[j + 1], re[j + 2], re[j + 3]);
+          *reinterpret_cast<float4*>(part + CT + c16 + j) =
+              f4(im[j], im[j + 1], im[j + 2], im[j + 3]);
+        }
+      } else if (ok && k < prm.k) {
+        const long long base = static_cast<long long>(k) * prm.c;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int c = ct * CT + c16 + j;
+          if (c < prm.c) {
+            const long long o = (base + c) * rs + tap;
+            prm.dw_r[o] = __uint_as_float(re[j]);
+            prm.dw_i[o] = __uint_as_float(im[j]);
+          }
+        }
+      }
+    }
+    ptx::tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, Cf::kTmemCols);
+  }
+}
+
+// Sums the splits' partials of every tile in split order and scatters the
+// result to dW (KCRS planes).  One thread per (tile, row, 4 channels).
+__global__ void ccv_wgrad_reduce_kernel(const float* __restrict__ partial, float* __restrict__ dw_r,
+                                        float* __restrict__ dw_i, int tiles, int splits, int ct_w,
+                                        int tiles_c, int K, int C, int RS) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const int groups = ct_w / 4;
+  const long long total = static_cast<long long>(tiles) * kWgM * groups;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int g = static_cast<int>(i % groups);
+    long long t = i / groups;
+    const int row = static_cast<int>(t % kWgM);
+    const int tile = static_cast<int>(t / kWgM);
+    float4 sr = make_float4(0.f, 0.f, 0.f, 0.f), si = sr;
+    for (int sp = 0; sp < splits; ++sp) {
+      const float* p =
+          partial + ((static_cast<long long>(tile) * splits + sp) * kWgM + row) * (2 * ct_w);
+      const float4 a = *reinterpret_cast<const float4*>(p + 4 * g);
+      const float4 b = *reinterpret_cast<const float4*>(p + ct_w + 4 * g);
+      sr.x += a.x; sr.y += a.y; sr.z += a.z; sr.w += a.w;
+      si.x += b.x; si.y += b.y; si.z += b.z; si.w += b.w;
+    }
+    const int tap = tile % RS;
+    const int rest = tile / RS;
+    const int ct = rest % tiles_c;
+    const int kt = rest / tiles_c;
+    const int k = kt * kWgM + row;
+    if (k >= K) continue;
+    const float vr[4] = {sr.x, sr.y, sr.z, sr.w};
+    const float vi[4] = {si.x, si.y, si.z, si.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = ct * ct_w + 4 * g + j;
+      if (c < C) {
+        const long long o = (static_cast<long long>(k) * C + c) * RS + tap;
+        dw_r[o] = vr[j];
+        dw_i[o] = vi[j];
+      }
+    }
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------ wgrad host side
+namespace {
+
+size_t align256b(size_t b) { return (b + 255) & ~static_cast<size_t>(255); }
+
+struct WgradPlan {
+  int ct = 128;
+  int tiles_c = 1, tiles = 1, splits = 1, qblocks = 1, qa = 4;
+  long long steps = 1;
+  size_t dy_plane = 0, x_plane = 0, partial = 0;
+};
+
+// Channel tile CT (N = 2*CT), tiles (k block, c block, tap) and the split of
+// each tile's reduction: about one CTA per SM in total, each split a
+// contiguous range of (n, p, 32-column block) steps.
+WgradPlan plan_wgrad(const Problem& pb) {
+  WgradPlan w;
+  w.ct = pb.c > 64 ? 128 : (pb.c > 32 ? 64 : 32);
+  w.tiles_c = (pb.c + w.ct - 1) / w.ct;
+  const int tiles_k = (pb.k + kWgM - 1) / kWgM;
+  w.tiles = tiles_k * w.tiles_c * pb.r * pb.s;
+  w.qblocks = (pb.q + 31) / 32;
+  w.steps = static_cast<long long>(pb.n) * pb.p * w.qblocks;
+  const int sms = device_sm_count();
+  w.splits = static_cast<int>(std::max<long long>(1, std::min<long long>(w.steps, sms / w.tiles)));
+  w.qa = (pb.q + 3) & ~3;
+  w.dy_plane = align256b(static_cast<size_t>(pb.n) * pb.k * pb.p * w.qa * 4);
+  w.x_plane = align256b(static_cast<size_t>(pb.s) * pb.n * pb.c * pb.h * w.qa * 4);
+  w.partial = w.splits > 1
+                  ? align256b(static_cast<size_t>(w.tiles) * w.splits * kWgM * 2 * w.ct * 4)
+                  : 0;
+  return w;
+}
+
+template <int CT>
+cudaError_t prepare_wgrad_variant() {
+  static std::once_flag once[64];
+  static cudaError_t err[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int slot = dev & 63;
+  std::call_once(once[slot], [&]() {
+    err[slot] = cudaFuncSetAttribute(ccv_wgrad_tf32_kernel<CT>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     WgCfg<CT>::kSmemBytes);
+  });
+  return err[slot];
+}
+
+template <int CT>
+int launch_wgrad_kernel(const WgradParams& prm, int ctas, cudaStream_t stream) {
+  cudaError_t e = prepare_wgrad_variant<CT>();
+  if (e == cudaSuccess) {
+    e = launch_kernel(ccv_wgrad_tf32_kernel<CT>, dim3(ctas), dim3(kWgThreads),
+                      WgCfg<CT>::kSmemBytes, stream, 1, prm);
+  }
+  return e == cudaSuccess ? CCV_OK : cuda_error(e, "wgrad kernel launch");
+}
+
+}  // namespace
+
+size_t wgrad_workspace_bytes(const Problem& pb) {
+  const WgradPlan w = plan_wgrad(pb);
+  return 2 * w.dy_plane + 2 * w.x_plane + w.partial;
+}
+
+int launch_wgrad(const void* x, const void* dy, float* dw_r, float* dw_i, const Problem& pb,
+                 void* ws, cudaStream_t stream) {
+  const WgradPlan w = plan_wgrad(pb);
+  char* base = static_cast<char*>(ws);
+  float* dyr = reinterpret_cast<float*>(base);
+  float* dyi = reinterpret_cast<float*>(base + w.dy_plane);
+  float* xr = reinterpret_cast<float*>(base + 2 * w.dy_plane);
+  float* xi = reinterpret_cast<float*>(base + 2 * w.dy_plane + w.x_plane);
+  float* partial = w.splits > 1
+                       ? reinterpret_cast<float*>(base + 2 * w.dy_plane + 2 * w.x_plane)
+                       : nullptr;
+  const int block = 256;
+  const int sms = device_sm_count();
+  {
+    const long long rows = static_cast<long long>(pb.n) * pb.k * pb.p;
+    const long long total = rows * pb.q;
+    const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, sms * 16LL));
+    const cudaError_t e =
+        launch_kernel(ccv_wgrad_dy_planes_kernel, dim3(grid), dim3(block), 0, stream, 1,
+                      static_cast<const float2*>(dy), dyr, dyi, rows, pb.q, w.qa);
+    if (e != cudaSuccess) return cuda_error(e, "wgrad dy layout launch");
+  }
+  {
+    const long long rows = static_cast<long long>(pb.n) * pb.c * pb.h;
+    const long long total = rows * pb.s * pb.q;
+    const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, sms * 16LL));
+    const cudaError_t e =
+        launch_kernel(ccv_wgrad_x_planes_kernel, dim3(grid), dim3(block), 0, stream, 1,
+                      static_cast<const float2*>(x), xr, xi, rows, pb.w, pb.s, pb.q, w.qa, pb.sw,
+                      pb.pw);
+    if (e != cudaSuccess) return cuda_error(e, "wgrad x layout launch");
+  }
+  WgradParams prm;
+  memset(&prm, 0, sizeof(prm));
+  int rc;
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(pb.q), static_cast<uint64_t>(pb.p),
+                              static_cast<uint64_t>(pb.k), static_cast<uint64_t>(pb.n)};
+    const uint64_t row = static_cast<uint64_t>(w.qa) * 4;
+    const uint64_t strides[3] = {row, row * pb.p, row * pb.p * pb.k};
+    const uint32_t box[4] = {32, 1, kWgM, 1};
+    const uint32_t es[4] = {1, 1, 1, 1};
+    if ((rc = encode_tiled_ex(&prm.tm_dyr, dyr, 4, dims, strides, box, es, kSwizzle128, false)) !=
+            CCV_OK ||
+        (rc = encode_tiled_ex(&prm.tm_dyi, dyi, 4, dims, strides, box, es, kSwizzle128, false)) !=
+            CCV_OK) {
+      return rc;
+    }
+  }
+  {
+    const uint64_t dims[5] = {static_cast<uint64_t>(pb.q), static_cast<uint64_t>(pb.h),
+                              static_cast<uint64_t>(pb.c), static_cast<uint64_t>(pb.n),
+                              static_cast<uint64_t>(pb.s)};
+    const uint64_t row = static_cast<uint64_t>(w.qa) * 4;
+    const uint64_t strides[4] = {row, row * pb.h, row * pb.h * pb.c, row * pb.h * pb.c * pb.n};
+    const uint32_t box[5] = {32, 1, static_cast<uint32_t>(w.ct), 1, 1};
+    const uint32_t es[5] = {1, 1, 1, 1, 1};
+    if ((rc = encode_tiled_ex(&prm.tm_xr, xr, 5, dims, strides, box, es, kSwizzle128, false)) !=
+            CCV_OK ||
+        (rc = encode_tiled_ex(&prm.tm_xi, xi, 5, dims, strides, box, es, kSwizzle128, false)) !=
+            CCV_OK) {
+      return rc;
+    }
+  }
+  prm.partial = partial;
+  prm.dw_r = dw_r;
+  prm.dw_i = dw_i;
+  prm.status = device_status_ptr();
+  if (prm.status == nullptr) return CCV_ERR_CUDA;
+  prm.k = pb.k; prm.c = pb.c; prm.r = pb.r; prm.s = pb.s;
+  prm.sh = pb.sh; prm.sw = pb.sw; prm.ph = pb.ph; prm.pw = pb.pw;
+  prm.p = pb.p; prm.q = pb.q;
+  prm.tiles_c = w.tiles_c;
+  prm.splits = w.splits;
+  prm.qblocks = w.qblocks;
+  prm.steps = w.steps;
+  const int ctas = w.tiles * w.splits;
+  switch (w.ct) {
+    case 32: rc = launch_wgrad_kernel<32>(prm, ctas, stream); break;
+    case 64: rc = launch_wgrad_kernel<64>(prm, ctas, stream); break;
+    default: rc = launch_wgrad_kernel<128>(prm, ctas, stream); break;
+  }
+  if (rc != CCV_OK || w.splits == 1) return rc;
+  const long long total = static_cast<long long>(w.tiles) * kWgM * (w.ct / 4);
+  const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, sms * 16LL));
+  const cudaError_t e = launch_kernel(ccv_wgrad_reduce_kernel, dim3(grid), dim3(block), 0, stream,
+                                      1, static_cast<const float*>(partial), dw_r, dw_i, w.tiles,
+                                      w.splits, w.ct, w.tiles_c, pb.k, pb.c, pb.r * pb.s);
+  return e == cudaSuccess ? CCV_OK : cuda_error(e, "wgrad reduce launch");
+}
+
+}  // namespace ccv

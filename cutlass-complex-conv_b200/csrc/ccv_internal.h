@@ -118,6 +118,20 @@ int launch_fprop_planar_lw(const float* x_real, const float* x_imag, float* hr, 
 // Name of the kernel path a complex (forward()) call takes.
 const char* complex_kernel_name(const Problem& pb, int precision);
 
+// Kernels of ccv_backward.cu.
+// Packed image of the data-gradient filter (transposed K <-> C, flipped,
+// conjugated) for the forward kernels, from the forward's KCRS/KRSC planes.
+int launch_prepack_dgrad(const float* w_real, const float* w_imag, int layout, const Problem& pb,
+                         int precision, float* packed, cudaStream_t stream);
+// dy (complex64 [N][K][P][Q]) spread onto the stride grid: [N][K][hu][wu].
+int launch_zero_insert(const void* dy, void* up, const Problem& pb, int hu, int wu,
+                       cudaStream_t stream);
+// Weight gradient: scratch bytes, and the launch (layout kernels, the
+// tcgen05 kernel and, when the reduction is split, the split-order sum).
+size_t wgrad_workspace_bytes(const Problem& pb);
+int launch_wgrad(const void* x, const void* dy, float* dw_r, float* dw_i, const Problem& pb,
+                 void* ws, cudaStream_t stream);
+
 // Encodes a tiled tensor map through the driver entry point.
 // `swizzle_bytes` is 64 or 128 (the box's inner extent in bytes).
 int encode_tiled(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,

@@ -198,6 +198,39 @@ int ccv_forward_noalloc(const float* x_real, const float* x_imag,
                         float* y_real, float* y_imag, const ccv_conv_shape* shape,
                         ccv_stream_t stream);
 
+/* Backward - no counterpart in the reference, whose extension is forward
+ * only (README.md:143 lists backward as absent).  The gradients are those
+ * torch autograd gives for the reference's four-conv module
+ * (benchmarks/baseline.py:12-45) with upstream gradient dy, in PyTorch's
+ * complex convention:
+ *   dx[n,c,h,w] = sum_{k,r,s} conj(W[k,c,r,s]) dy[n,k,p,q]
+ *   dW[k,c,r,s] = sum_{n,p,q} dy[n,k,p,q] conj(x[n,c,h,w])
+ * (h = p*stride_h - pad_h + r, w = q*stride_w - pad_w + s); dw_real and
+ * dw_imag are the gradients of weight_real and weight_imag.  `shape` is the
+ * FORWARD problem.  dy: complex64 NKPQ, dx: complex64 NCHW, x: complex64
+ * NCHW, dw_real/dw_imag: fp32 KCRS; all dense.
+ *
+ * Data gradient: a forward convolution of dy (spread onto the stride grid
+ * with zeros for stride > 1) with the transposed, flipped, conjugated
+ * filter, whose packed image ccv_prepack_weights_dgrad builds (size
+ * ccv_packed_weight_bytes(shape, precision)).  Needs pad <= kernel size - 1
+ * per axis.  TF32 or 3xTF32. */
+int ccv_prepack_weights_dgrad(const float* w_real, const float* w_imag, int layout,
+                              const ccv_conv_shape* shape, int precision, void* packed,
+                              size_t packed_bytes, ccv_stream_t stream);
+size_t ccv_dgrad_complex_workspace_bytes(const ccv_conv_shape* shape, int precision);
+int ccv_dgrad_complex(const void* dy, const void* w_packed_dgrad, void* dx,
+                      const ccv_conv_shape* shape, int precision, void* workspace,
+                      size_t workspace_bytes, ccv_stream_t stream);
+
+/* Weight gradient (TF32 products, FP32 accumulation; the operands are
+ * rounded to TF32 first).  Writes every element of dw_real and dw_imag;
+ * deterministic. */
+size_t ccv_wgrad_complex_workspace_bytes(const ccv_conv_shape* shape);
+int ccv_wgrad_complex(const void* x, const void* dy, float* dw_real, float* dw_imag,
+                      const ccv_conv_shape* shape, void* workspace, size_t workspace_bytes,
+                      ccv_stream_t stream);
+
 /* Device status word of the current device: nonzero after an in-kernel
  * bounded wait ran out (a CCV_ERR_* code).  While it is set, fprop kernels
  * on that device exit without work.  The kernel that gives up also writes a
