@@ -84,8 +84,41 @@ def _aligned16(t):
     return t.data_ptr() % 16 == 0
 
 
+class _ComplexConv2dFunction(torch.autograd.Function):
+    """``forward()`` as an autograd node: the backward runs the library's data
+    gradient (``ccv_dgrad_complex``) and weight gradient
+    (``ccv_wgrad_complex``) kernels.  Gradients follow PyTorch's complex
+    convention (those torch autograd gives for the reference's four-conv
+    module, ``benchmarks/baseline.py:12-45``):
+    dx = conv_transpose(dy, conj(W)), dW = sum dy * conj(x),
+    d weight_real = Re dW, d weight_imag = Im dW, d bias = sum dy."""
+
+    @staticmethod
+    def forward(ctx, x, weight_real, weight_imag, bias_real, bias_imag, module):
+        ctx.module = module
+        ctx.save_for_backward(x)
+        return module._forward_impl(x)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x,) = ctx.saved_tensors
+        m = ctx.module
+        dy = dy.contiguous()
+        dx = dwr = dwi = dbr = dbi = None
+        if ctx.needs_input_grad[0]:
+            dx = m._data_grad(dy, x.shape[2], x.shape[3])
+        if ctx.needs_input_grad[1] or ctx.needs_input_grad[2]:
+            dwr, dwi = cutlass_complex_conv.wgrad_complex(
+                x, dy, m.kernel_size[0], m.kernel_size[1], m.stride[0], m.stride[1],
+                m.padding[0], m.padding[1])
+        if ctx.needs_input_grad[3] or ctx.needs_input_grad[4]:
+            db = dy.sum(dim=(0, 2, 3))
+            dbr, dbi = db.real.contiguous(), db.imag.contiguous()
+        return dx, dwr, dwi, dbr, dbi, None
+
+
 class ComplexConv2d(nn.Module):
-    """Inference-only complex-valued 2D convolution on B200 tensor cores.
+    """Complex-valued 2D convolution on B200 tensor cores.
 
     The public ``forward`` method accepts a ``torch.complex64`` tensor in NCHW
     format. ``forward_planar`` exposes the planar path and accepts separate
@@ -100,10 +133,17 @@ class ComplexConv2d(nn.Module):
     ``nn.Conv2d``'s bias: U(+-1/sqrt(in_channels * kernel_h * kernel_w))):
     ``y[:, k] += bias_real[k] + 1j * bias_imag[k]``.
 
+    ``forward`` is differentiable (an extension; the reference is inference
+    only): when grad mode is on and the input or a parameter requires grad,
+    the backward runs the library's data- and weight-gradient kernels
+    (parameters are created with ``requires_grad=False`` as in the
+    reference; set it to train them).  The weight gradient computes in TF32;
+    the data gradient in the layer's precision.  ``forward_planar`` stays
+    inference only.
+
     Current limitations (as in the reference):
       - CUDA only (an sm_100 / B200 device)
       - torch.complex64 only
-      - forward inference only (no autograd/backward)
       - dilation=1
       - groups=1
       - padding_mode="zeros"
@@ -224,6 +264,8 @@ class ComplexConv2d(nn.Module):
         self._w_packed = None
         self._packed_precision = None
         self._weight_version = None
+        self._w_packed_dgrad = None
+        self._dgrad_key = None
 
     def _apply(self, fn, recurse=True):
         # nn.Module.to()/cuda()/cpu() may replace or move Parameter storage.
@@ -321,6 +363,32 @@ class ComplexConv2d(nn.Module):
                 "input and ComplexConv2d weights must be on the same CUDA device"
             )
 
+        if torch.is_grad_enabled() and (
+            x.requires_grad
+            or self.weight_real.requires_grad
+            or self.weight_imag.requires_grad
+            or (self.bias_real is not None
+                and (self.bias_real.requires_grad or self.bias_imag.requires_grad))
+        ):
+            return _ComplexConv2dFunction.apply(
+                x, self.weight_real, self.weight_imag, self.bias_real, self.bias_imag, self)
+        return self._forward_impl(x)
+
+    def _data_grad(self, dy, in_h, in_w):
+        """dx of ``forward`` for the upstream gradient dy (complex64 NKPQ)."""
+        key = (self.weight_real._version, self.weight_imag._version, self.precision,
+               self.weight_real.device)
+        if self._w_packed_dgrad is None or self._dgrad_key != key:
+            self._w_packed_dgrad = cutlass_complex_conv.prepack_dgrad(
+                self.weight_real.detach().contiguous(), self.weight_imag.detach().contiguous(),
+                _PRECISIONS[self.precision])
+            self._dgrad_key = key
+        return cutlass_complex_conv.dgrad_complex_packed(
+            dy, self._w_packed_dgrad, self.in_channels, in_h, in_w, self.kernel_size[0],
+            self.kernel_size[1], self.stride[0], self.stride[1], self.padding[0],
+            self.padding[1], _PRECISIONS[self.precision])
+
+    def _forward_impl(self, x):
         self._ensure_prepacked()
 
         # Any layout is read in place (strided layout pass; the reference

@@ -228,6 +228,93 @@ torch::Tensor forward_complex_packed(torch::Tensor x, torch::Tensor w_packed, in
   return y;
 }
 
+// Packed image of the data-gradient filter (transposed, flipped,
+// conjugated) from KCRS weight planes; size as the forward image.
+torch::Tensor prepack_dgrad(torch::Tensor w_real, torch::Tensor w_imag, int64_t precision) {
+  CHECK_CUDA(w_real); CHECK_CUDA(w_imag); CHECK_FLOAT(w_real); CHECK_FLOAT(w_imag);
+  CHECK_CONTIGUOUS(w_real); CHECK_CONTIGUOUS(w_imag);
+  TORCH_CHECK(w_real.dim() == 4 && w_real.sizes() == w_imag.sizes(),
+              "weights must be two 4D tensors of identical shape");
+  TORCH_CHECK(w_real.device() == w_imag.device(), "weights must be on the same CUDA device");
+  c10::cuda::CUDAGuard guard(w_real.device());
+  const int64_t K = w_real.size(0), C = w_real.size(1), R = w_real.size(2), S = w_real.size(3);
+  // Padding R-1 / S-1 keeps the shape valid for every filter size.
+  ccv_conv_shape shp = make_shape(1, R, S, C, K, R, S, 1, 1, R - 1, S - 1);
+  const size_t bytes = ccv_packed_weight_bytes(&shp, static_cast<int>(precision));
+  check_rc(bytes == 0 ? ccv_check_shape(&shp) : CCV_OK, "weight shape check");
+  auto packed = torch::empty({static_cast<int64_t>(bytes / 4)}, w_real.options());
+  check_rc(ccv_prepack_weights_dgrad(w_real.data_ptr<float>(), w_imag.data_ptr<float>(),
+                                     CCV_WEIGHT_KCRS, &shp, static_cast<int>(precision),
+                                     packed.data_ptr(), bytes, current_stream()),
+           "ccv_prepack_weights_dgrad");
+  return packed;
+}
+
+// Data gradient: dy complex64 [N][K][P][Q] -> dx complex64 [N][C][H][W]
+// (H, W: the forward input's size).
+torch::Tensor dgrad_complex_packed(torch::Tensor dy, torch::Tensor w_packed_dgrad, int64_t C,
+                                   int64_t H, int64_t W, int64_t R, int64_t S, int64_t stride_h,
+                                   int64_t stride_w, int64_t pad_h, int64_t pad_w,
+                                   int64_t precision) {
+  CHECK_CUDA(dy); CHECK_CUDA(w_packed_dgrad); CHECK_FLOAT(w_packed_dgrad);
+  CHECK_CONTIGUOUS(w_packed_dgrad);
+  TORCH_CHECK(dy.scalar_type() == at::kComplexFloat, "dy must be complex64");
+  TORCH_CHECK(dy.dim() == 4, "dy must be a 4D NCHW tensor");
+  TORCH_CHECK(dy.device() == w_packed_dgrad.device(),
+              "gradient and weights must be on the same CUDA device");
+  c10::cuda::CUDAGuard guard(dy.device());
+  dy = dy.contiguous();
+  const int64_t N = dy.size(0), K = dy.size(1);
+  ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
+  int64_t P = 0, Q = 0;
+  check_rc(ccv_output_size(&shp, &P, &Q), "shape check");
+  TORCH_CHECK(dy.size(2) == P && dy.size(3) == Q, "dy does not match the forward output size");
+  TORCH_CHECK(static_cast<size_t>(w_packed_dgrad.numel()) * 4 >=
+                  ccv_packed_weight_bytes(&shp, static_cast<int>(precision)),
+              "packed weights do not match the problem");
+  const size_t ws_bytes = ccv_dgrad_complex_workspace_bytes(&shp, static_cast<int>(precision));
+  check_rc(ws_bytes == 0 ? CCV_ERR_UNSUPPORTED : CCV_OK, "data gradient");
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes)}, dy.options().dtype(torch::kUInt8));
+  auto dx = torch::empty({N, C, H, W}, dy.options());
+  check_rc(ccv_dgrad_complex(dy.data_ptr(), w_packed_dgrad.data_ptr(), dx.data_ptr(), &shp,
+                             static_cast<int>(precision), ws.data_ptr(), ws_bytes,
+                             current_stream()),
+           "ccv_dgrad_complex");
+  return dx;
+}
+
+// Weight gradient: x complex64 NCHW and dy complex64 NKPQ -> (dW_real,
+// dW_imag) fp32 KCRS.
+std::vector<torch::Tensor> wgrad_complex(torch::Tensor x, torch::Tensor dy, int64_t R, int64_t S,
+                                         int64_t stride_h, int64_t stride_w, int64_t pad_h,
+                                         int64_t pad_w) {
+  CHECK_CUDA(x); CHECK_CUDA(dy);
+  TORCH_CHECK(x.scalar_type() == at::kComplexFloat && dy.scalar_type() == at::kComplexFloat,
+              "x and dy must be complex64");
+  TORCH_CHECK(x.dim() == 4 && dy.dim() == 4, "x and dy must be 4D NCHW tensors");
+  TORCH_CHECK(x.device() == dy.device(), "x and dy must be on the same CUDA device");
+  c10::cuda::CUDAGuard guard(x.device());
+  x = x.contiguous();
+  dy = dy.contiguous();
+  const int64_t N = x.size(0), C = x.size(1), H = x.size(2), W = x.size(3), K = dy.size(1);
+  ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
+  int64_t P = 0, Q = 0;
+  check_rc(ccv_output_size(&shp, &P, &Q), "shape check");
+  TORCH_CHECK(dy.size(0) == N && dy.size(2) == P && dy.size(3) == Q,
+              "dy does not match the forward output size");
+  const size_t ws_bytes = ccv_wgrad_complex_workspace_bytes(&shp);
+  check_rc(ws_bytes == 0 ? ccv_check_shape(&shp) : CCV_OK, "weight gradient");
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes)}, x.options().dtype(torch::kUInt8));
+  auto fo = x.options().dtype(torch::kFloat);
+  auto dwr = torch::empty({K, C, R, S}, fo);
+  auto dwi = torch::empty({K, C, R, S}, fo);
+  check_rc(ccv_wgrad_complex(x.data_ptr(), dy.data_ptr(), dwr.data_ptr<float>(),
+                             dwi.data_ptr<float>(), &shp, ws.data_ptr(), ws_bytes,
+                             current_stream()),
+           "ccv_wgrad_complex");
+  return {dwr, dwi};
+}
+
 // Planar NHWC planes in, complex64 NKPQ out (the conv launch of forward()
 // without its layout pass).
 torch::Tensor forward_planar_to_complex_packed(torch::Tensor x_real, torch::Tensor x_imag,
@@ -353,6 +440,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("r"), pybind11::arg("s"), pybind11::arg("stride_h"),
         pybind11::arg("stride_w"), pybind11::arg("pad_h"), pybind11::arg("pad_w"),
         pybind11::arg("precision"));
+  m.def("prepack_dgrad", &prepack_dgrad, "Pack the data-gradient filter (KCRS planes)",
+        pybind11::arg("w_real"), pybind11::arg("w_imag"), pybind11::arg("precision"));
+  m.def("dgrad_complex_packed", &dgrad_complex_packed, "Data gradient, complex64 NCHW",
+        pybind11::arg("dy"), pybind11::arg("w_packed_dgrad"), pybind11::arg("in_channels"),
+        pybind11::arg("in_h"), pybind11::arg("in_w"), pybind11::arg("kernel_h"),
+        pybind11::arg("kernel_w"), pybind11::arg("stride_h"), pybind11::arg("stride_w"),
+        pybind11::arg("pad_h"), pybind11::arg("pad_w"), pybind11::arg("precision"));
+  m.def("wgrad_complex", &wgrad_complex, "Weight gradient -> (dW_real, dW_imag) KCRS",
+        pybind11::arg("x"), pybind11::arg("dy"), pybind11::arg("kernel_h"),
+        pybind11::arg("kernel_w"), pybind11::arg("stride_h"), pybind11::arg("stride_w"),
+        pybind11::arg("pad_h"), pybind11::arg("pad_w"));
   m.def("device_status", &device_status, pybind11::arg("device"));
   m.def("clear_device_status", &clear_device_status, pybind11::arg("device"));
   m.def("selftest_bounded_wait", &selftest_bounded_wait, pybind11::arg("device"),
