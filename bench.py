@@ -398,6 +398,34 @@ def measure_config(wname, precision, world, rank, dev, args, peaks):
             e["tflops_all_gpus"] = e["tflops"] * scale
             e["blocks"] = blocks
             res[name + ("_warm" if batch1 else "")] = e
+        if wname == "b64_128_128_56" and precision == "tf32":
+            # Backward of the headline layer (an extension: the reference is
+            # forward only): the data gradient and the weight gradient the
+            # autograd node of forward() runs, each with the forward's flop
+            # count; upstream gradients rotate like the inputs.
+            dys = [torch.randn((nb, k, p, q), dtype=torch.complex64, device=dev)
+                   for _ in range(nbuf)]
+
+            def dgrad():
+                layer._data_grad(dys[it[0] % nbuf], h, w)
+                it[0] += 1
+
+            def wgrad():
+                j = it[0] % nbuf
+                _C.wgrad_complex(xs[j], dys[j], r, s, st, st, pd, pd)
+                it[0] += 1
+
+            bw = {"method": "ComplexConv2d's autograd backward calls (_data_grad, "
+                            "_C.wgrad_complex), flops 8*N*P*Q*K*C*R*S each"}
+            for name, fn in (("dgrad", dgrad), ("wgrad", wgrad)):
+                for _ in range(args.warmup):
+                    fn()
+                t, blocks = timed_blocks(fn, args.steps, world, dev)
+                e = roofline_entry(flops_rank, alg_rank, t, precision, peaks)
+                e["blocks"] = blocks
+                bw[name] = e
+            res["backward"] = bw
+            del dys
         if batch1:
             # Device time per call: the same module calls captured in one CUDA
             # graph (a serving loop's form), replayed; what is left is the

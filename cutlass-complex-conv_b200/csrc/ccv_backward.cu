@@ -173,43 +173,53 @@ struct WgradParams {
   long long steps;  // reduction steps of a tile: N * P * qblocks
 };
 
-// Complex64 [planes][P][Q] -> TF32-rounded fp32 planes [planes][P][Qa].
+// Complex64 [rows][Q] -> TF32-rounded fp32 planes [rows][Qa] (rows = N*K*P).
+// One warp per row, lanes along q (32-bit index math inside a row).
 __global__ void ccv_wgrad_dy_planes_kernel(const float2* __restrict__ dy, float* __restrict__ yr,
                                            float* __restrict__ yi, long long rows, int Q,
                                            int Qa) {
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
-  const long long total = rows * Q;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const long long row = i / Q;
-    const int q = static_cast<int>(i - row * Q);
-    const float2 v = dy[i];
-    yr[row * Qa + q] = to_tf32_rna(v.x);
-    yi[row * Qa + q] = to_tf32_rna(v.y);
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  for (long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+       row < rows; row += nwarps) {
+    const float2* src = dy + row * Q;
+    float* dr = yr + row * Qa;
+    float* di = yi + row * Qa;
+    for (int q = lane; q < Q; q += 32) {
+      const float2 v = __ldg(src + q);
+      dr[q] = to_tf32_rna(v.x);
+      di[q] = to_tf32_rna(v.y);
+    }
   }
 }
 
 // Complex64 NCHW -> TF32-rounded fp32 planes [S][N][C][H][Qa], element
 // (s, .., q) = x[.., w = q*sw - pw + s] (0 outside the image), for q < Q.
+// One warp per input row (n, c, h): the row is read once from DRAM (the S
+// shifted copies re-read it from L1) and each copy is written with
+// consecutive lanes on consecutive q.
 __global__ void ccv_wgrad_x_planes_kernel(const float2* __restrict__ x, float* __restrict__ xr,
                                           float* __restrict__ xi, long long rows, int W, int S,
                                           int Q, int Qa, int sw, int pw) {
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
-  const long long total = static_cast<long long>(S) * rows * Q;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int q = static_cast<int>(i % Q);
-    const long long t = i / Q;  // (s, n, c, h)
-    const int s = static_cast<int>(t / rows);
-    const long long row = t - static_cast<long long>(s) * rows;
-    const int w = q * sw - pw + s;
-    float2 v = make_float2(0.f, 0.f);
-    if (w >= 0 && w < W) v = x[row * W + w];
-    const long long o = t * Qa + q;
-    xr[o] = to_tf32_rna(v.x);
-    xi[o] = to_tf32_rna(v.y);
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  for (long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+       row < rows; row += nwarps) {
+    const float2* src = x + row * W;
+    for (int s = 0; s < S; ++s) {
+      float* dr = xr + (static_cast<long long>(s) * rows + row) * Qa;
+      float* di = xi + (static_cast<long long>(s) * rows + row) * Qa;
+      for (int q = lane; q < Q; q += 32) {
+        const int w = q * sw - pw + s;
+        const float2 v = (w >= 0 && w < W) ? __ldg(src + w) : make_float2(0.f, 0.f);
+        dr[q] = to_tf32_rna(v.x);
+        di[q] = to_tf32_rna(v.y);
+      }
+    }
   }
 }
 
@@ -554,8 +564,7 @@ int launch_wgrad(const void* x, const void* dy, float* dw_r, float* dw_i, const 
   const int sms = device_sm_count();
   {
     const long long rows = static_cast<long long>(pb.n) * pb.k * pb.p;
-    const long long total = rows * pb.q;
-    const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, sms * 16LL));
+    const int grid = static_cast<int>(std::min<long long>((rows * 32 + block - 1) / block, sms * 16LL));
     const cudaError_t e =
         launch_kernel(ccv_wgrad_dy_planes_kernel, dim3(grid), dim3(block), 0, stream, 1,
                       static_cast<const float2*>(dy), dyr, dyi, rows, pb.q, w.qa);
@@ -563,8 +572,7 @@ int launch_wgrad(const void* x, const void* dy, float* dw_r, float* dw_i, const 
   }
   {
     const long long rows = static_cast<long long>(pb.n) * pb.c * pb.h;
-    const long long total = rows * pb.s * pb.q;
-    const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, sms * 16LL));
+    const int grid = static_cast<int>(std::min<long long>((rows * 32 + block - 1) / block, sms * 16LL));
     const cudaError_t e =
         launch_kernel(ccv_wgrad_x_planes_kernel, dim3(grid), dim3(block), 0, stream, 1,
                       static_cast<const float2*>(x), xr, xi, rows, pb.w, pb.s, pb.q, w.qa, pb.sw,
