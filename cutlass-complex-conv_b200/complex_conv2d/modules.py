@@ -381,6 +381,7 @@ class ComplexConv2d(nn.Module):
         if self._w_packed_dgrad is None or self._dgrad_key != key:
             self._w_packed_dgrad = cutlass_complex_conv.prepack_dgrad(
                 self.weight_real.detach().contiguous(), self.weight_imag.detach().contiguous(),
+                self.stride[0], self.stride[1], self.padding[0], self.padding[1],
                 _PRECISIONS[self.precision])
             self._dgrad_key = key
         return cutlass_complex_conv.dgrad_complex_packed(

@@ -228,9 +228,11 @@ torch::Tensor forward_complex_packed(torch::Tensor x, torch::Tensor w_packed, in
   return y;
 }
 
-// Packed image of the data-gradient filter (transposed, flipped,
-// conjugated) from KCRS weight planes; size as the forward image.
-torch::Tensor prepack_dgrad(torch::Tensor w_real, torch::Tensor w_imag, int64_t precision) {
+// Packed images of the data-gradient filter (transposed, flipped,
+// conjugated; one per phase of the stride grid) from KCRS weight planes, for
+// the layer's stride and padding; size as the forward image.
+torch::Tensor prepack_dgrad(torch::Tensor w_real, torch::Tensor w_imag, int64_t stride_h,
+                            int64_t stride_w, int64_t pad_h, int64_t pad_w, int64_t precision) {
   CHECK_CUDA(w_real); CHECK_CUDA(w_imag); CHECK_FLOAT(w_real); CHECK_FLOAT(w_imag);
   CHECK_CONTIGUOUS(w_real); CHECK_CONTIGUOUS(w_imag);
   TORCH_CHECK(w_real.dim() == 4 && w_real.sizes() == w_imag.sizes(),
@@ -238,8 +240,9 @@ torch::Tensor prepack_dgrad(torch::Tensor w_real, torch::Tensor w_imag, int64_t 
   TORCH_CHECK(w_real.device() == w_imag.device(), "weights must be on the same CUDA device");
   c10::cuda::CUDAGuard guard(w_real.device());
   const int64_t K = w_real.size(0), C = w_real.size(1), R = w_real.size(2), S = w_real.size(3);
-  // Padding R-1 / S-1 keeps the shape valid for every filter size.
-  ccv_conv_shape shp = make_shape(1, R, S, C, K, R, S, 1, 1, R - 1, S - 1);
+  // The image depends on the filter, stride and padding only; an input of
+  // R x S pixels keeps the shape valid for every filter size.
+  ccv_conv_shape shp = make_shape(1, R, S, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
   const size_t bytes = ccv_packed_weight_bytes(&shp, static_cast<int>(precision));
   check_rc(bytes == 0 ? ccv_check_shape(&shp) : CCV_OK, "weight shape check");
   auto packed = torch::empty({static_cast<int64_t>(bytes / 4)}, w_real.options());
@@ -441,7 +444,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("stride_w"), pybind11::arg("pad_h"), pybind11::arg("pad_w"),
         pybind11::arg("precision"));
   m.def("prepack_dgrad", &prepack_dgrad, "Pack the data-gradient filter (KCRS planes)",
-        pybind11::arg("w_real"), pybind11::arg("w_imag"), pybind11::arg("precision"));
+        pybind11::arg("w_real"), pybind11::arg("w_imag"), pybind11::arg("stride_h"),
+        pybind11::arg("stride_w"), pybind11::arg("pad_h"), pybind11::arg("pad_w"),
+        pybind11::arg("precision"));
   m.def("dgrad_complex_packed", &dgrad_complex_packed, "Data gradient, complex64 NCHW",
         pybind11::arg("dy"), pybind11::arg("w_packed_dgrad"), pybind11::arg("in_channels"),
         pybind11::arg("in_h"), pybind11::arg("in_w"), pybind11::arg("kernel_h"),

@@ -866,23 +866,51 @@ int ccv_reload_config(void) {
 namespace ccv {
 namespace {
 
-// The forward problem's data gradient as a forward problem: dy (spread onto
-// the stride grid, hu x wu) convolved with the transposed filter, stride 1,
-// padding R-1-ph / S-1-pw; its output is H x W.
-int dgrad_problem(const Problem& pb, ccv_conv_shape* out, int* hu, int* wu) {
-  if (pb.ph > pb.r - 1 || pb.pw > pb.s - 1) {
-    return set_error(CCV_ERR_UNSUPPORTED,
-                     "cannot implement the data gradient: padding above kernel size - 1");
-  }
-  // Rows/columns the forward's floor division left out keep a zero gradient.
-  const int eh = (pb.h + 2 * pb.ph - pb.r) % pb.sh;
-  const int ew = (pb.w + 2 * pb.pw - pb.s) % pb.sw;
-  *hu = (pb.p - 1) * pb.sh + 1 + eh;
-  *wu = (pb.q - 1) * pb.sw + 1 + ew;
+// Phase (a, b) of the data gradient as a forward problem: dy with the
+// phase's zero border (y.out + y.taps - 1 rows), the phase's sub-filter
+// (y.taps x x.taps taps), stride 1, no padding; its output is the phase's
+// y.out x x.out positions of dx.
+struct DgradPhase {
+  DgradAxis y, x;
+  ccv_conv_shape shape;
+  bool live = false;         // some filter tap reaches this phase
+  size_t filter_floats = 0;  // floats of its packed image(s)
+};
+
+DgradPhase dgrad_phase(const Problem& pb, int a, int b, int precision) {
+  DgradPhase ph;
+  ph.y = dgrad_axis(a, pb.sh, pb.ph, pb.r, pb.h);
+  ph.x = dgrad_axis(b, pb.sw, pb.pw, pb.s, pb.w);
+  ph.filter_floats = static_cast<size_t>(ph.y.taps) * ph.x.taps * 3 * pb.k * pb.c *
+                     (precision == CCV_PRECISION_3XTF32 ? 2 : 1);
+  ph.live = ph.y.taps > 0 && ph.x.taps > 0 && ph.y.out > 0 && ph.x.out > 0;
   ccv_conv_shape d;
   d.n = pb.n;
-  d.h = *hu;
-  d.w = *wu;
+  d.h = ph.y.out + ph.y.taps - 1;
+  d.w = ph.x.out + ph.x.taps - 1;
+  d.c = pb.k;
+  d.k = pb.c;
+  d.r = ph.y.taps;
+  d.s = ph.x.taps;
+  d.stride_h = 1;
+  d.stride_w = 1;
+  d.pad_h = 0;
+  d.pad_w = 0;
+  ph.shape = d;
+  return ph;
+}
+
+// Stride 1 with padding <= kernel size - 1: one phase whose zero border is
+// the forward's own padding, so dy is convolved in place (no copy).
+bool dgrad_direct(const Problem& pb) {
+  return pb.sh == 1 && pb.sw == 1 && pb.ph <= pb.r - 1 && pb.pw <= pb.s - 1;
+}
+
+ccv_conv_shape dgrad_direct_shape(const Problem& pb) {
+  ccv_conv_shape d;
+  d.n = pb.n;
+  d.h = pb.p;
+  d.w = pb.q;
   d.c = pb.k;
   d.k = pb.c;
   d.r = pb.r;
@@ -891,13 +919,33 @@ int dgrad_problem(const Problem& pb, ccv_conv_shape* out, int* hu, int* wu) {
   d.stride_w = 1;
   d.pad_h = pb.r - 1 - pb.ph;
   d.pad_w = pb.s - 1 - pb.pw;
-  *out = d;
-  return CCV_OK;
+  return d;
 }
 
-size_t zero_insert_bytes(const Problem& pb, int hu, int wu) {
-  if (pb.sh == 1 && pb.sw == 1) return 0;
-  return align256(static_cast<size_t>(pb.n) * pb.k * hu * wu * 8);
+// Scratch of the phase path: every phase's output (dx-sized in total), the
+// largest phase copy of dy and the largest forward workspace of a phase.
+struct DgradScratch {
+  size_t outputs = 0, pad = 0, fprop = 0;
+  size_t total() const { return outputs + pad + fprop; }
+};
+
+int dgrad_scratch(const Problem& pb, int precision, DgradScratch* out) {
+  DgradScratch sc;
+  sc.outputs = align256(static_cast<size_t>(pb.n) * pb.c * pb.h * pb.w * 8);
+  for (int a = 0; a < pb.sh; ++a) {
+    for (int b = 0; b < pb.sw; ++b) {
+      const DgradPhase ph = dgrad_phase(pb, a, b, precision);
+      if (!ph.live) continue;
+      Problem pp;
+      const int rc = make_problem(&ph.shape, &pp);
+      if (rc != CCV_OK) return rc;
+      sc.pad = std::max(sc.pad, align256(static_cast<size_t>(pb.n) * pb.k * ph.shape.h *
+                                         ph.shape.w * 8));
+      sc.fprop = std::max(sc.fprop, ccv_fprop_complex_workspace_bytes(&ph.shape, precision));
+    }
+  }
+  *out = sc;
+  return CCV_OK;
 }
 
 }  // namespace
@@ -934,10 +982,13 @@ int ccv_prepack_weights_dgrad(const float* w_real, const float* w_imag, int layo
 size_t ccv_dgrad_complex_workspace_bytes(const ccv_conv_shape* shape, int precision) {
   Problem pb;
   if (make_problem(shape, &pb) != CCV_OK) return 0;
-  ccv_conv_shape d;
-  int hu = 0, wu = 0;
-  if (dgrad_problem(pb, &d, &hu, &wu) != CCV_OK) return 0;
-  return zero_insert_bytes(pb, hu, wu) + ccv_fprop_complex_workspace_bytes(&d, precision);
+  if (dgrad_direct(pb)) {
+    const ccv_conv_shape d = dgrad_direct_shape(pb);
+    return ccv_fprop_complex_workspace_bytes(&d, precision);
+  }
+  DgradScratch sc;
+  if (dgrad_scratch(pb, precision, &sc) != CCV_OK) return 0;
+  return sc.total();
 }
 
 int ccv_dgrad_complex(const void* dy, const void* w_packed_dgrad, void* dx,
@@ -953,25 +1004,45 @@ int ccv_dgrad_complex(const void* dy, const void* w_packed_dgrad, void* dx,
   if (!aligned16(dy) || !aligned16(w_packed_dgrad) || !aligned16(dx)) {
     return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
   }
-  ccv_conv_shape d;
-  int hu = 0, wu = 0;
-  if ((rc = dgrad_problem(pb, &d, &hu, &wu)) != CCV_OK) return rc;
-  Problem pd;
-  if ((rc = make_problem(&d, &pd)) != CCV_OK) return rc;
-  const size_t up = zero_insert_bytes(pb, hu, wu);
-  if (workspace == nullptr || !aligned16(workspace) ||
-      workspace_bytes < up + complex_required_bytes(pd, precision)) {
-    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
+  if (workspace == nullptr || !aligned16(workspace)) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing or misaligned");
+  }
+  if (dgrad_direct(pb)) {
+    const ccv_conv_shape d = dgrad_direct_shape(pb);
+    return fprop_complex_impl(dy, nullptr, w_packed_dgrad, nullptr, nullptr, dx, &d, precision,
+                              workspace, workspace_bytes, stream);
+  }
+  DgradScratch sc;
+  if ((rc = dgrad_scratch(pb, precision, &sc)) != CCV_OK) return rc;
+  if (workspace_bytes < sc.total()) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace too small");
   }
   if ((rc = check_device()) != CCV_OK) return rc;
   if ((rc = check_status_clear()) != CCV_OK) return rc;
-  const void* src = dy;
-  if (up > 0) {
-    if ((rc = launch_zero_insert(dy, workspace, pb, hu, wu, st)) != CCV_OK) return rc;
-    src = workspace;
+  char* ws = static_cast<char*>(workspace);
+  char* outputs = ws;
+  char* padded = ws + sc.outputs;
+  char* fws = padded + sc.pad;
+  const float* filt = static_cast<const float*>(w_packed_dgrad);
+  size_t out_off = 0;  // bytes into `outputs`
+  for (int a = 0; a < pb.sh; ++a) {
+    for (int b = 0; b < pb.sw; ++b) {
+      const DgradPhase ph = dgrad_phase(pb, a, b, precision);
+      if (ph.live) {
+        if ((rc = launch_dgrad_phase_pad(dy, padded, pb, static_cast<int>(ph.shape.h),
+                                         static_cast<int>(ph.shape.w), ph.y.offset,
+                                         ph.x.offset, st)) != CCV_OK) {
+          return rc;
+        }
+        rc = fprop_complex_impl(padded, nullptr, filt, nullptr, nullptr, outputs + out_off,
+                                &ph.shape, precision, fws, sc.fprop, stream);
+        if (rc != CCV_OK) return rc;
+      }
+      filt += ph.filter_floats;
+      out_off += static_cast<size_t>(pb.n) * pb.c * ph.y.out * ph.x.out * 8;
+    }
   }
-  return fprop_complex_impl(src, nullptr, w_packed_dgrad, nullptr, nullptr, dx, &d, precision,
-                            static_cast<char*>(workspace) + up, workspace_bytes - up, stream);
+  return launch_dgrad_interleave(outputs, dx, pb, st);
 }
 
 size_t ccv_wgrad_complex_workspace_bytes(const ccv_conv_shape* shape) {

@@ -10,11 +10,15 @@
 // over h = p*sh - ph + r, w = q*sw - pw + s.
 //
 // dgrad is a forward convolution of dy with the filter transposed (K <-> C),
-// flipped (r -> R-1-r, s -> S-1-s) and conjugated, padding R-1-ph / S-1-pw;
-// for stride > 1, dy is first spread onto the stride grid with zeros between
-// (zero insertion), plus the rows/columns the forward's floor division left
-// out.  It runs on the forward kernels (ccv_fprop*.cu) with a packed image
-// of that filter (ccv_prepack_dgrad_kernel).
+// flipped (r -> R-1-r, s -> S-1-s) and conjugated, padding R-1-ph / S-1-pw,
+// on the forward kernels (ccv_fprop*.cu) with a packed image of that filter
+// (ccv_prepack_dgrad_kernel).  For stride > 1 the output splits into the
+// sh*sw phases of the stride grid (rows h = sh*i + a, columns w = sw*j + b):
+// phase (a, b) only meets filter rows r = ra + sh*t and columns
+// s = rb + sw*u, so it is a stride-1 convolution of dy with that sub-filter
+// (a copy of dy with the phase's zero border, ccv_dgrad_phase_pad_kernel);
+// ccv_dgrad_interleave_kernel writes the phases into dx.  Every filter tap
+// belongs to exactly one phase, so the phases together do the forward's MACs.
 //
 // wgrad is an implicit GEMM per filter tap (r, s): M = output channels k
 // (128-row tiles), N = input channels c, reduction over the output pixels
@@ -51,17 +55,19 @@ __device__ __forceinline__ float to_tf32_rna(float x) {
 }
 
 // ------------------------------------------------------------------ dgrad
-// Packed image of the dgrad filter W'[c][k][r'][s'] = conj(W[k][c][R-1-r'][S-1-s'])
-// in the forward's packed layout for the problem (K' = C, C' = K):
-// [tap'][plane][C][K], plane 0 = -W'_im = W_im, 1 = W'_re = W_re,
-// 2 = W'_im = -W_im (TF32-rounded; with `split`, the remainders follow as a
-// second image).
+// Packed image of one phase's dgrad filter: taps (u, v) of a TA x TB
+// sub-filter, W'[c][k][u][v] = conj(W[k][c][ra + sh*(TA-1-u)][rb + sw*(TB-1-v)])
+// (transposed, flipped, conjugated), in the forward's packed layout for the
+// problem (K' = C, C' = K): [tap'][plane][C][K], plane 0 = -W'_im = W_im,
+// 1 = W'_re = W_re, 2 = W'_im = -W_im (TF32-rounded; with `split`, the
+// remainders follow as a second image).  Stride 1: one phase, TA = R, TB = S.
 __global__ void ccv_prepack_dgrad_kernel(const float* __restrict__ wr,
                                          const float* __restrict__ wi, float* __restrict__ out,
-                                         int K, int C, int R, int S, int krsc, int split) {
+                                         int K, int C, int R, int S, int krsc, int split, int TA,
+                                         int TB, int ra, int rb, int sh, int sw) {
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
-  const long long total = static_cast<long long>(R) * S * K * C;
+  const long long total = static_cast<long long>(TA) * TB * K * C;
   const long long image = total * 3;
   const long long ck = static_cast<long long>(C) * K;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -71,8 +77,8 @@ __global__ void ccv_prepack_dgrad_kernel(const float* __restrict__ wr,
     long long t = i / K;
     const int c = static_cast<int>(t % C);
     const int tap = static_cast<int>(t / C);
-    const int r = R - 1 - tap / S;
-    const int s = S - 1 - tap % S;
+    const int r = ra + sh * (TA - 1 - tap / TB);
+    const int s = rb + sw * (TB - 1 - tap % TB);
     const long long src = krsc ? ((static_cast<long long>(k) * R + r) * S + s) * C + c
                                : ((static_cast<long long>(k) * C + c) * R + r) * S + s;
     const float xr = wr[src];
@@ -93,53 +99,131 @@ __global__ void ccv_prepack_dgrad_kernel(const float* __restrict__ wr,
   }
 }
 
-// complex64 [N][K][P][Q] -> complex64 [N][K][Hu][Wu]: dy on the stride grid
-// (dy[.., p, q] at (p*sh, q*sw)), zeros elsewhere.
-__global__ void ccv_zero_insert_kernel(const float2* __restrict__ dy, float2* __restrict__ up,
-                                       long long planes, int P, int Q, int Hu, int Wu, int sh,
-                                       int sw) {
+// complex64 [planes][P][Q] -> complex64 [planes][Hp][Wp], element (i, j) =
+// dy[i - oh][j - ow] (zero outside dy): the phase's zero border.
+__global__ void ccv_dgrad_phase_pad_kernel(const float2* __restrict__ dy, float2* __restrict__ out,
+                                           long long planes, int P, int Q, int Hp, int Wp,
+                                           int oh, int ow) {
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
-  const long long total = planes * Hu * Wu;
+  const long long total = planes * Hp * Wp;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int wu = static_cast<int>(i % Wu);
-    long long t = i / Wu;
-    const int hu = static_cast<int>(t % Hu);
-    const long long pl = t / Hu;
+    const int j = static_cast<int>(i % Wp);
+    long long t = i / Wp;
+    const int r = static_cast<int>(t % Hp);
+    const long long pl = t / Hp;
+    const int p = r - oh, q = j - ow;
+    out[i] = (p >= 0 && p < P && q >= 0 && q < Q) ? dy[(pl * P + p) * Q + q]
+                                                  : make_float2(0.f, 0.f);
+  }
+}
+
+// dx[n][c][h][w] = phase (h % sh, w % sw)'s output at (h / sh, w / sw), or 0
+// for a phase no filter tap reaches.  Phase outputs are [N][C][Ha][Wb]
+// complex64 blocks, back to back in (a, b) order at `phase_off` (elements).
+struct DgradPhaseTable {
+  long long off[64];
+  int ha[8], wb[8];
+  int live[64];
+};
+__global__ void ccv_dgrad_interleave_kernel(const float2* __restrict__ phases,
+                                            float2* __restrict__ dx, long long planes, int H,
+                                            int W, int sh, int sw,
+                                            const __grid_constant__ DgradPhaseTable tab) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const long long total = planes * H * W;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int w = static_cast<int>(i % W);
+    long long t = i / W;
+    const int h = static_cast<int>(t % H);
+    const long long pl = t / H;
+    const int a = h % sh, b = w % sw;
+    const int ph = a * sw + b;
     float2 v = make_float2(0.f, 0.f);
-    if (hu % sh == 0 && wu % sw == 0 && hu / sh < P && wu / sw < Q) {
-      v = dy[(pl * P + hu / sh) * Q + wu / sw];
+    if (tab.live[ph]) {
+      const int ha = tab.ha[a], wb = tab.wb[b];
+      v = phases[tab.off[ph] + (pl * ha + h / sh) * wb + w / sw];
     }
-    up[i] = v;
+    dx[i] = v;
   }
 }
 
 }  // namespace
 
-int launch_prepack_dgrad(const float* w_real, const float* w_imag, int layout, const Problem& pb,
-                         int precision, float* packed, cudaStream_t stream) {
-  const long long total = static_cast<long long>(pb.r) * pb.s * pb.k * pb.c;
-  const int block = 256;
-  const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, 4096));
-  const cudaError_t e = launch_kernel(ccv_prepack_dgrad_kernel, dim3(grid), dim3(block), 0, stream,
-                                      1, w_real, w_imag, packed, pb.k, pb.c, pb.r, pb.s,
-                                      layout == CCV_WEIGHT_KRSC ? 1 : 0,
-                                      precision == CCV_PRECISION_3XTF32 ? 1 : 0);
-  return e == cudaSuccess ? CCV_OK : cuda_error(e, "dgrad weight prepack launch");
+DgradAxis dgrad_axis(int a, int stride, int pad, int taps, int in_size) {
+  DgradAxis x;
+  x.first = (a + pad) % stride;
+  x.taps = x.first < taps ? (taps - x.first + stride - 1) / stride : 0;
+  const int d = (a + pad - x.first) / stride;  // dy index offset of the phase's first tap
+  x.offset = x.taps - 1 - d;
+  x.out = a < in_size ? (in_size - a + stride - 1) / stride : 0;
+  return x;
 }
 
-int launch_zero_insert(const void* dy, void* up, const Problem& pb, int hu, int wu,
-                       cudaStream_t stream) {
+int launch_prepack_dgrad(const float* w_real, const float* w_imag, int layout, const Problem& pb,
+                         int precision, float* packed, cudaStream_t stream) {
+  const int split = precision == CCV_PRECISION_3XTF32 ? 1 : 0;
+  const int block = 256;
+  float* out = packed;
+  for (int a = 0; a < pb.sh; ++a) {
+    const DgradAxis ya = dgrad_axis(a, pb.sh, pb.ph, pb.r, pb.h);
+    for (int b = 0; b < pb.sw; ++b) {
+      const DgradAxis xb = dgrad_axis(b, pb.sw, pb.pw, pb.s, pb.w);
+      const long long total = static_cast<long long>(ya.taps) * xb.taps * pb.k * pb.c;
+      if (total == 0) continue;
+      const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, 4096));
+      const cudaError_t e =
+          launch_kernel(ccv_prepack_dgrad_kernel, dim3(grid), dim3(block), 0, stream, 1, w_real,
+                        w_imag, out, pb.k, pb.c, pb.r, pb.s, layout == CCV_WEIGHT_KRSC ? 1 : 0,
+                        split, ya.taps, xb.taps, ya.first, xb.first, pb.sh, pb.sw);
+      if (e != cudaSuccess) return cuda_error(e, "dgrad weight prepack launch");
+      out += total * 3 * (split ? 2 : 1);
+    }
+  }
+  return CCV_OK;
+}
+
+int launch_dgrad_phase_pad(const void* dy, void* out, const Problem& pb, int hp, int wp, int oh,
+                           int ow, cudaStream_t stream) {
   const long long planes = static_cast<long long>(pb.n) * pb.k;
-  const long long total = planes * hu * wu;
+  const long long total = planes * hp * wp;
   const int block = 256;
   const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, 148 * 16));
   const cudaError_t e =
-      launch_kernel(ccv_zero_insert_kernel, dim3(grid), dim3(block), 0, stream, 1,
-                    static_cast<const float2*>(dy), static_cast<float2*>(up), planes, pb.p, pb.q,
-                    hu, wu, pb.sh, pb.sw);
-  return e == cudaSuccess ? CCV_OK : cuda_error(e, "dgrad zero-insertion launch");
+      launch_kernel(ccv_dgrad_phase_pad_kernel, dim3(grid), dim3(block), 0, stream, 1,
+                    static_cast<const float2*>(dy), static_cast<float2*>(out), planes, pb.p, pb.q,
+                    hp, wp, oh, ow);
+  return e == cudaSuccess ? CCV_OK : cuda_error(e, "dgrad phase copy launch");
+}
+
+int launch_dgrad_interleave(const void* phases, void* dx, const Problem& pb, cudaStream_t stream) {
+  DgradPhaseTable tab;
+  memset(&tab, 0, sizeof(tab));
+  long long off = 0;
+  for (int a = 0; a < pb.sh; ++a) {
+    const DgradAxis ya = dgrad_axis(a, pb.sh, pb.ph, pb.r, pb.h);
+    tab.ha[a] = ya.out;
+    for (int b = 0; b < pb.sw; ++b) {
+      const DgradAxis xb = dgrad_axis(b, pb.sw, pb.pw, pb.s, pb.w);
+      tab.wb[b] = xb.out;
+      const int ph = a * pb.sw + b;
+      tab.off[ph] = off;
+      tab.live[ph] = ya.taps > 0 && xb.taps > 0 && ya.out > 0 && xb.out > 0;
+      off += static_cast<long long>(pb.n) * pb.c * ya.out * xb.out;
+    }
+  }
+  const long long planes = static_cast<long long>(pb.n) * pb.c;
+  const long long total = planes * pb.h * pb.w;
+  const int block = 256;
+  const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, 148 * 16));
+  const cudaError_t e = launch_kernel(ccv_dgrad_interleave_kernel, dim3(grid), dim3(block), 0,
+                                      stream, 1, static_cast<const float2*>(phases),
+                                      static_cast<float2*>(dx), planes, pb.h, pb.w, pb.sh, pb.sw,
+                                      tab);
+  return e == cudaSuccess ? CCV_OK : cuda_error(e, "dgrad interleave launch");
 }
 
 // ------------------------------------------------------------------ wgrad

@@ -112,14 +112,34 @@ __device__ __forceinline__ void store_accumulator_tma(const FpropParams& prm, ui
                                                       int k0, bool valid, int c1, int c2, int c3,
                                                       uint8_t* stage, int lane, uint32_t& seq) {
   static_assert(NBUF == 1 || NBUF == 2, "one or two staging buffers");
-#pragma unroll 1
+  static_assert(KT % 32 == 0, "chunks are processed in pairs");
+  // TMEM reads run one chunk ahead: chunk ch+16's loads are issued before
+  // chunk ch is staged and stored, so their latency overlaps that work.
+  uint32_t nr[16], ni[16];
+  ptx::tmem_ld_32x32b_x16(t_acc, nr);
+  ptx::tmem_ld_32x32b_x16(t_acc + KT, ni);
+  ptx::tmem_wait_ld();
+  ptx::reg_fence(nr);
+  ptx::reg_fence(ni);
+#pragma unroll 2
   for (int ch = 0; ch < KT; ch += 16) {
     uint32_t vr[16], vi[16];
-    ptx::tmem_ld_32x32b_x16(t_acc + ch, vr);
-    ptx::tmem_ld_32x32b_x16(t_acc + KT + ch, vi);
-    ptx::tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      vr[j] = nr[j];
+      vi[j] = ni[j];
+    }
+    if (ch + 16 < KT) {
+      ptx::tmem_ld_32x32b_x16(t_acc + ch + 16, nr);
+      ptx::tmem_ld_32x32b_x16(t_acc + KT + ch + 16, ni);
+    }
     const bool go = valid && k0 + ch < prm.k;
-    if (!go) continue;
+    if (!go) {
+      ptx::tmem_wait_ld();
+      ptx::reg_fence(nr);
+      ptx::reg_fence(ni);
+      continue;
+    }
     add_bias<16>(prm, k0 + ch, vr, vi);
     float* sr = reinterpret_cast<float*>(stage + (NBUF == 2 ? (seq & 1u) * 4096u : 0u));
     float* si = sr + 32 * 16;
@@ -162,6 +182,9 @@ __device__ __forceinline__ void store_accumulator_tma(const FpropParams& prm, ui
       }
       ptx::bulk_commit_group();
     }
+    ptx::tmem_wait_ld();
+    ptx::reg_fence(nr);
+    ptx::reg_fence(ni);
   }
 }
 
@@ -230,12 +253,25 @@ __device__ __noinline__ bool split_piece_epilogue(const FpropParams& prm, WorkUn
   };
   {
     float4* dst = ws4 + block0(cid) + lane;
-#pragma unroll 1
+    // TMEM reads one chunk ahead of the stores (as in store_accumulator_tma).
+    uint32_t nr[16], ni[16];
+    ptx::tmem_ld_32x32b_x16(t_acc, nr);
+    ptx::tmem_ld_32x32b_x16(t_acc + KT, ni);
+    ptx::tmem_wait_ld();
+    ptx::reg_fence(nr);
+    ptx::reg_fence(ni);
+#pragma unroll 2
     for (int ch = 0; ch < KT; ch += 16) {
       uint32_t vr[16], vi[16];
-      ptx::tmem_ld_32x32b_x16(t_acc + ch, vr);
-      ptx::tmem_ld_32x32b_x16(t_acc + KT + ch, vi);
-      ptx::tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        vr[j] = nr[j];
+        vi[j] = ni[j];
+      }
+      if (ch + 16 < KT) {
+        ptx::tmem_ld_32x32b_x16(t_acc + ch + 16, nr);
+        ptx::tmem_ld_32x32b_x16(t_acc + KT + ch + 16, ni);
+      }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         float4* gd = dst + ((ch / 8 + h) * 4) * 32;
@@ -250,6 +286,9 @@ __device__ __noinline__ bool split_piece_epilogue(const FpropParams& prm, WorkUn
         __stcg(gd + 96, make_float4(__uint_as_float(m[4]), __uint_as_float(m[5]),
                                     __uint_as_float(m[6]), __uint_as_float(m[7])));
       }
+      ptx::tmem_wait_ld();
+      ptx::reg_fence(nr);
+      ptx::reg_fence(ni);
     }
   }
   // Publish this warp's rows, then count its slots.

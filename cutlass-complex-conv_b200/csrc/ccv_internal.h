@@ -119,13 +119,26 @@ int launch_fprop_planar_lw(const float* x_real, const float* x_imag, float* hr, 
 const char* complex_kernel_name(const Problem& pb, int precision);
 
 // Kernels of ccv_backward.cu.
-// Packed image of the data-gradient filter (transposed K <-> C, flipped,
-// conjugated) for the forward kernels, from the forward's KCRS/KRSC planes.
+// One axis of one phase of the data gradient: output positions
+// a, a + stride, ... (`out` of them) meet filter taps first, first + stride,
+// ... (`taps` of them, 0: none), and the phase's convolution reads dy with
+// its index shifted by `offset` (a copy of dy whose element i is dy[i - offset]).
+struct DgradAxis {
+  int first = 0, taps = 0, offset = 0, out = 0;
+};
+DgradAxis dgrad_axis(int a, int stride, int pad, int taps, int in_size);
+// Packed images of the data-gradient filter (transposed K <-> C, flipped,
+// conjugated), one per phase of the stride grid in (a, b) order (one for
+// stride 1), for the forward kernels, from the forward's KCRS/KRSC planes.
+// Their total size is the forward image's.
 int launch_prepack_dgrad(const float* w_real, const float* w_imag, int layout, const Problem& pb,
                          int precision, float* packed, cudaStream_t stream);
-// dy (complex64 [N][K][P][Q]) spread onto the stride grid: [N][K][hu][wu].
-int launch_zero_insert(const void* dy, void* up, const Problem& pb, int hu, int wu,
-                       cudaStream_t stream);
+// dy (complex64 [N][K][P][Q]) with a phase's zero border: [N][K][hp][wp],
+// element (i, j) = dy[i - oh][j - ow].
+int launch_dgrad_phase_pad(const void* dy, void* out, const Problem& pb, int hp, int wp, int oh,
+                           int ow, cudaStream_t stream);
+// dx from the phases' outputs ([N][C][Ha][Wb] blocks in (a, b) order).
+int launch_dgrad_interleave(const void* phases, void* dx, const Problem& pb, cudaStream_t stream);
 // Weight gradient: scratch bytes, and the launch (layout kernels, the
 // tcgen05 kernel and, when the reduction is split, the split-order sum).
 size_t wgrad_workspace_bytes(const Problem& pb);

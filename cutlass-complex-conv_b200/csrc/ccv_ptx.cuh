@@ -301,6 +301,15 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
                : "memory");
 }
 
+// Pins registers that an asynchronous tcgen05.ld wrote: an empty volatile asm
+// that reads and redefines each one, placed after tcgen05.wait::ld, so no use
+// of them can be scheduled before the wait.
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

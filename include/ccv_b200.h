@@ -210,11 +210,11 @@ int ccv_forward_noalloc(const float* x_real, const float* x_imag,
  * FORWARD problem.  dy: complex64 NKPQ, dx: complex64 NCHW, x: complex64
  * NCHW, dw_real/dw_imag: fp32 KCRS; all dense.
  *
- * Data gradient: a forward convolution of dy (spread onto the stride grid
- * with zeros for stride > 1) with the transposed, flipped, conjugated
- * filter, whose packed image ccv_prepack_weights_dgrad builds (size
- * ccv_packed_weight_bytes(shape, precision)).  Needs pad <= kernel size - 1
- * per axis.  TF32 or 3xTF32. */
+ * Data gradient: forward convolutions of dy with the transposed, flipped,
+ * conjugated filter - one per phase of the stride grid (stride 1: one, run
+ * on dy in place when pad <= kernel size - 1) - whose packed images
+ * ccv_prepack_weights_dgrad builds (total size
+ * ccv_packed_weight_bytes(shape, precision)).  TF32 or 3xTF32. */
 int ccv_prepack_weights_dgrad(const float* w_real, const float* w_imag, int layout,
                               const ccv_conv_shape* shape, int precision, void* packed,
                               size_t packed_bytes, ccv_stream_t stream);
