@@ -340,7 +340,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             __stcg(gd + 96, u4f(vi[8 * h + 4], vi[8 * h + 5], vi[8 * h + 6], vi[8 * h + 7]));
           }
         }
-        __threadfence();
+        // No fence: the cluster barrier below (arrive.release / wait.acquire
+        // at cluster scope, by every thread) orders these stores before the
+        // other CTAs of the cluster - the only readers - load them.
       }
     } else if (!skip && splits > 1) {
       // Split-K: park this CTA's partial accumulator row in shared memory
