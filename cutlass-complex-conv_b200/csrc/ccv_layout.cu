@@ -82,33 +82,32 @@ __global__ void ccv_split_planes_kernel(const float4* __restrict__ xr, const flo
   }
 }
 
-// complex64 NCHW -> two fp32 NHWC planes.  One block per (n, h) row and a
-// 32-channel x 64-pixel tile: every thread issues its 8 loads (256-byte runs
-// along W per warp) before touching shared memory, then writes 8 channel-
-// contiguous runs (128 bytes per warp and plane).  With xr_lo/xi_lo set,
-// writes tf32(x) and x - tf32(x) instead (3xTF32).
+// complex64 NCHW -> two fp32 NHWC planes.  One block per image and a
+// 32-channel x 64-pixel tile of the image's H*W pixels taken as one row (a
+// channel's pixels are contiguous in NCHW), so narrow images fill every
+// tile: every thread issues its 8 loads (256-byte runs per warp) before
+// touching shared memory, then writes 8 channel-contiguous runs (128 bytes
+// per warp and plane).  With xr_lo/xi_lo set, writes tf32(x) and
+// x - tf32(x) instead (3xTF32).
 constexpr int kLayoutW = 64;
 
 __global__ void __launch_bounds__(256) ccv_nchw_to_planar_kernel(
     const float2* __restrict__ x, float* __restrict__ xr, float* __restrict__ xi,
-    float* __restrict__ xr_lo, float* __restrict__ xi_lo, int C, int H, int W) {
+    float* __restrict__ xr_lo, float* __restrict__ xi_lo, int C, long long HW) {
   __shared__ float tr[32][kLayoutW + 1];
   __shared__ float ti[32][kLayoutW + 1];
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
-  const int nh = blockIdx.z;
-  const int n = nh / H;
-  const int h = nh - n * H;
-  const int w0 = blockIdx.x * kLayoutW;
+  const long long n = blockIdx.z;
+  const long long w0 = static_cast<long long>(blockIdx.x) * kLayoutW;  // first pixel of the tile
   const int c0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;
   float2 v[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int c = c0 + ty + 8 * (i & 3);
-    const int w = w0 + tx + 32 * (i >> 2);
-    v[i] = (c < C && w < W) ? __ldg(x + ((static_cast<long long>(n) * C + c) * H + h) * W + w)
-                            : make_float2(0.f, 0.f);
+    const long long w = w0 + tx + 32 * (i >> 2);
+    v[i] = (c < C && w < HW) ? __ldg(x + (n * C + c) * HW + w) : make_float2(0.f, 0.f);
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -123,9 +122,9 @@ __global__ void __launch_bounds__(256) ccv_nchw_to_planar_kernel(
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int wl = ty + 8 * i;
-    const int w = w0 + wl;
-    if (w < W) {
-      const long long o = ((static_cast<long long>(n) * H + h) * W + w) * C + c;
+    const long long w = w0 + wl;
+    if (w < HW) {
+      const long long o = (n * HW + w) * C + c;
       const float a = tr[tx][wl];
       const float b = ti[tx][wl];
       if (xr_lo != nullptr) {
@@ -253,13 +252,14 @@ int launch_prepack(const float* w_real, const float* w_imag, int layout, const P
 
 int launch_nchw_complex_to_planar(const float* x, float* xr, float* xi, float* xr_lo,
                                   float* xi_lo, const Problem& pb, cudaStream_t stream) {
-  const long long nh = static_cast<long long>(pb.n) * pb.h;
-  if (nh > 65535) return set_error(CCV_ERR_UNSUPPORTED, "N*H too large for the layout kernel");
-  dim3 grid((pb.w + kLayoutW - 1) / kLayoutW, (pb.c + 31) / 32, static_cast<unsigned>(nh));
+  if (pb.n > 65535) return set_error(CCV_ERR_UNSUPPORTED, "batch too large for the layout kernel");
+  const long long hw = static_cast<long long>(pb.h) * pb.w;
+  const long long tiles = (hw + kLayoutW - 1) / kLayoutW;
+  if (tiles > 0x7fffffffLL) return set_error(CCV_ERR_UNSUPPORTED, "image too large for the layout kernel");
+  dim3 grid(static_cast<unsigned>(tiles), (pb.c + 31) / 32, static_cast<unsigned>(pb.n));
   dim3 block(32, 8);
   cudaError_t e = launch_kernel(ccv_nchw_to_planar_kernel, grid, block, 0, stream, 0,
-                                reinterpret_cast<const float2*>(x), xr, xi, xr_lo, xi_lo, pb.c,
-                                pb.h, pb.w);
+                                reinterpret_cast<const float2*>(x), xr, xi, xr_lo, xi_lo, pb.c, hw);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_error(e, "layout kernel launch");
   return CCV_OK;
