@@ -117,6 +117,37 @@ class _ComplexConv2dFunction(torch.autograd.Function):
         return dx, dwr, dwi, dbr, dbi, None
 
 
+class _ComplexConv2dPlanarFunction(torch.autograd.Function):
+    """``forward_planar()`` as an autograd node (two real outputs): the same
+    gradients as ``_ComplexConv2dFunction`` on fp32 planes, from the library's
+    planar data- and weight-gradient kernels (``ccv_dgrad_planar``,
+    ``ccv_wgrad_planar``)."""
+
+    @staticmethod
+    def forward(ctx, x_real, x_imag, weight_real, weight_imag, bias_real, bias_imag, module):
+        ctx.module = module
+        ctx.save_for_backward(x_real, x_imag)
+        y_real, y_imag = module._forward_planar_impl(x_real, x_imag)
+        return y_real, y_imag
+
+    @staticmethod
+    def backward(ctx, dy_real, dy_imag):
+        x_real, x_imag = ctx.saved_tensors
+        m = ctx.module
+        dy_real = dy_real.contiguous()
+        dy_imag = dy_imag.contiguous()
+        dxr = dxi = dwr = dwi = dbr = dbi = None
+        if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
+            dxr, dxi = m._data_grad_planar(dy_real, dy_imag, x_real.shape[1], x_real.shape[2])
+        if ctx.needs_input_grad[2] or ctx.needs_input_grad[3]:
+            dwr, dwi = cutlass_complex_conv.wgrad_planar(
+                x_real, x_imag, dy_real, dy_imag, m.kernel_size[0], m.kernel_size[1],
+                m.stride[0], m.stride[1], m.padding[0], m.padding[1])
+        if ctx.needs_input_grad[4] or ctx.needs_input_grad[5]:
+            dbr, dbi = dy_real.sum(dim=(0, 1, 2)), dy_imag.sum(dim=(0, 1, 2))
+        return dxr, dxi, dwr, dwi, dbr, dbi, None
+
+
 class ComplexConv2d(nn.Module):
     """Complex-valued 2D convolution on B200 tensor cores.
 
@@ -138,8 +169,8 @@ class ComplexConv2d(nn.Module):
     the backward runs the library's data- and weight-gradient kernels
     (parameters are created with ``requires_grad=False`` as in the
     reference; set it to train them).  The weight gradient computes in TF32;
-    the data gradient in the layer's precision.  ``forward_planar`` stays
-    inference only.
+    the data gradient in the layer's precision.  ``forward_planar`` is
+    differentiable the same way (gradients of both planes).
 
     Current limitations (as in the reference):
       - CUDA only (an sm_100 / B200 device)
@@ -316,6 +347,38 @@ class ComplexConv2d(nn.Module):
         Returns:
             ``[y_real, y_imag]`` as contiguous NHWC float32 tensors.
         """
+        if torch.is_grad_enabled() and (
+            x_real.requires_grad
+            or x_imag.requires_grad
+            or self.weight_real.requires_grad
+            or self.weight_imag.requires_grad
+            or (self.bias_real is not None
+                and (self.bias_real.requires_grad or self.bias_imag.requires_grad))
+        ):
+            return list(_ComplexConv2dPlanarFunction.apply(
+                x_real, x_imag, self.weight_real, self.weight_imag, self.bias_real,
+                self.bias_imag, self))
+        return self._forward_planar_impl(x_real, x_imag)
+
+    def _packed_dgrad(self):
+        key = (self.weight_real._version, self.weight_imag._version, self.precision,
+               self.weight_real.device)
+        if self._w_packed_dgrad is None or self._dgrad_key != key:
+            self._w_packed_dgrad = cutlass_complex_conv.prepack_dgrad(
+                self.weight_real.detach().contiguous(), self.weight_imag.detach().contiguous(),
+                self.stride[0], self.stride[1], self.padding[0], self.padding[1],
+                _PRECISIONS[self.precision])
+            self._dgrad_key = key
+        return self._w_packed_dgrad
+
+    def _data_grad_planar(self, dy_real, dy_imag, in_h, in_w):
+        """(dx_real, dx_imag) of ``forward_planar`` for upstream planes dy (NPQK)."""
+        return cutlass_complex_conv.dgrad_planar_packed(
+            dy_real, dy_imag, self._packed_dgrad(), self.in_channels, in_h, in_w,
+            self.kernel_size[0], self.kernel_size[1], self.stride[0], self.stride[1],
+            self.padding[0], self.padding[1], _PRECISIONS[self.precision])
+
+    def _forward_planar_impl(self, x_real, x_imag):
         self._ensure_prepacked()
 
         # TMA needs 16-byte aligned bases; copy the rare misaligned view.
@@ -376,16 +439,8 @@ class ComplexConv2d(nn.Module):
 
     def _data_grad(self, dy, in_h, in_w):
         """dx of ``forward`` for the upstream gradient dy (complex64 NKPQ)."""
-        key = (self.weight_real._version, self.weight_imag._version, self.precision,
-               self.weight_real.device)
-        if self._w_packed_dgrad is None or self._dgrad_key != key:
-            self._w_packed_dgrad = cutlass_complex_conv.prepack_dgrad(
-                self.weight_real.detach().contiguous(), self.weight_imag.detach().contiguous(),
-                self.stride[0], self.stride[1], self.padding[0], self.padding[1],
-                _PRECISIONS[self.precision])
-            self._dgrad_key = key
         return cutlass_complex_conv.dgrad_complex_packed(
-            dy, self._w_packed_dgrad, self.in_channels, in_h, in_w, self.kernel_size[0],
+            dy, self._packed_dgrad(), self.in_channels, in_h, in_w, self.kernel_size[0],
             self.kernel_size[1], self.stride[0], self.stride[1], self.padding[0],
             self.padding[1], _PRECISIONS[self.precision])
 

@@ -318,6 +318,78 @@ std::vector<torch::Tensor> wgrad_complex(torch::Tensor x, torch::Tensor dy, int6
   return {dwr, dwi};
 }
 
+// Planar data gradient: dy planes NPQK -> dx planes NHWC [N][H][W][C].
+std::vector<torch::Tensor> dgrad_planar_packed(torch::Tensor dy_real, torch::Tensor dy_imag,
+                                               torch::Tensor w_packed_dgrad, int64_t C, int64_t H,
+                                               int64_t W, int64_t R, int64_t S,
+                                               int64_t stride_h, int64_t stride_w, int64_t pad_h,
+                                               int64_t pad_w, int64_t precision) {
+  CHECK_CUDA(dy_real); CHECK_CUDA(dy_imag); CHECK_CUDA(w_packed_dgrad);
+  CHECK_FLOAT(dy_real); CHECK_FLOAT(dy_imag); CHECK_FLOAT(w_packed_dgrad);
+  CHECK_CONTIGUOUS(w_packed_dgrad);
+  TORCH_CHECK(dy_real.dim() == 4 && dy_real.sizes() == dy_imag.sizes(),
+              "dy_real and dy_imag must be 4D NHWC tensors of identical shape");
+  c10::cuda::CUDAGuard guard(dy_real.device());
+  dy_real = dy_real.contiguous();
+  dy_imag = dy_imag.contiguous();
+  const int64_t N = dy_real.size(0), K = dy_real.size(3);
+  ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
+  int64_t P = 0, Q = 0;
+  check_rc(ccv_output_size(&shp, &P, &Q), "shape check");
+  TORCH_CHECK(dy_real.size(1) == P && dy_real.size(2) == Q,
+              "dy does not match the forward output size");
+  const size_t ws_bytes = ccv_dgrad_planar_workspace_bytes(&shp, static_cast<int>(precision));
+  torch::Tensor ws;
+  void* ws_ptr = nullptr;
+  if (ws_bytes > 0) {
+    ws = torch::empty({static_cast<int64_t>(ws_bytes)}, dy_real.options().dtype(torch::kUInt8));
+    ws_ptr = ws.data_ptr();
+  }
+  auto dxr = torch::empty({N, H, W, C}, dy_real.options());
+  auto dxi = torch::empty({N, H, W, C}, dy_real.options());
+  check_rc(ccv_dgrad_planar(dy_real.data_ptr<float>(), dy_imag.data_ptr<float>(),
+                            w_packed_dgrad.data_ptr(), dxr.data_ptr<float>(),
+                            dxi.data_ptr<float>(), &shp, static_cast<int>(precision), ws_ptr,
+                            ws_bytes, current_stream()),
+           "ccv_dgrad_planar");
+  return {dxr, dxi};
+}
+
+// Planar weight gradient: x planes NHWC and dy planes NPQK -> (dW_real,
+// dW_imag) fp32 KCRS.
+std::vector<torch::Tensor> wgrad_planar(torch::Tensor x_real, torch::Tensor x_imag,
+                                        torch::Tensor dy_real, torch::Tensor dy_imag, int64_t R,
+                                        int64_t S, int64_t stride_h, int64_t stride_w,
+                                        int64_t pad_h, int64_t pad_w) {
+  for (const auto* t : {&x_real, &x_imag, &dy_real, &dy_imag}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->dim() == 4,
+                "inputs must be 4D CUDA float32 tensors");
+  }
+  TORCH_CHECK(x_real.sizes() == x_imag.sizes() && dy_real.sizes() == dy_imag.sizes(),
+              "real and imaginary planes must have identical shapes");
+  c10::cuda::CUDAGuard guard(x_real.device());
+  x_real = x_real.contiguous(); x_imag = x_imag.contiguous();
+  dy_real = dy_real.contiguous(); dy_imag = dy_imag.contiguous();
+  const int64_t N = x_real.size(0), H = x_real.size(1), W = x_real.size(2), C = x_real.size(3);
+  const int64_t K = dy_real.size(3);
+  ccv_conv_shape shp = make_shape(N, H, W, C, K, R, S, stride_h, stride_w, pad_h, pad_w);
+  int64_t P = 0, Q = 0;
+  check_rc(ccv_output_size(&shp, &P, &Q), "shape check");
+  TORCH_CHECK(dy_real.size(0) == N && dy_real.size(1) == P && dy_real.size(2) == Q,
+              "dy does not match the forward output size");
+  const size_t ws_bytes = ccv_wgrad_planar_workspace_bytes(&shp);
+  check_rc(ws_bytes == 0 ? ccv_check_shape(&shp) : CCV_OK, "weight gradient");
+  auto ws = torch::empty({static_cast<int64_t>(ws_bytes)}, x_real.options().dtype(torch::kUInt8));
+  auto dwr = torch::empty({K, C, R, S}, x_real.options());
+  auto dwi = torch::empty({K, C, R, S}, x_real.options());
+  check_rc(ccv_wgrad_planar(x_real.data_ptr<float>(), x_imag.data_ptr<float>(),
+                            dy_real.data_ptr<float>(), dy_imag.data_ptr<float>(),
+                            dwr.data_ptr<float>(), dwi.data_ptr<float>(), &shp, ws.data_ptr(),
+                            ws_bytes, current_stream()),
+           "ccv_wgrad_planar");
+  return {dwr, dwi};
+}
+
 // Planar NHWC planes in, complex64 NKPQ out (the conv launch of forward()
 // without its layout pass).
 torch::Tensor forward_planar_to_complex_packed(torch::Tensor x_real, torch::Tensor x_imag,
@@ -452,6 +524,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         pybind11::arg("in_h"), pybind11::arg("in_w"), pybind11::arg("kernel_h"),
         pybind11::arg("kernel_w"), pybind11::arg("stride_h"), pybind11::arg("stride_w"),
         pybind11::arg("pad_h"), pybind11::arg("pad_w"), pybind11::arg("precision"));
+  m.def("dgrad_planar_packed", &dgrad_planar_packed, "Data gradient, fp32 NHWC planes",
+        pybind11::arg("dy_real"), pybind11::arg("dy_imag"), pybind11::arg("w_packed_dgrad"),
+        pybind11::arg("in_channels"), pybind11::arg("in_h"), pybind11::arg("in_w"),
+        pybind11::arg("kernel_h"), pybind11::arg("kernel_w"), pybind11::arg("stride_h"),
+        pybind11::arg("stride_w"), pybind11::arg("pad_h"), pybind11::arg("pad_w"),
+        pybind11::arg("precision"));
+  m.def("wgrad_planar", &wgrad_planar, "Weight gradient from planes -> (dW_real, dW_imag)",
+        pybind11::arg("x_real"), pybind11::arg("x_imag"), pybind11::arg("dy_real"),
+        pybind11::arg("dy_imag"), pybind11::arg("kernel_h"), pybind11::arg("kernel_w"),
+        pybind11::arg("stride_h"), pybind11::arg("stride_w"), pybind11::arg("pad_h"),
+        pybind11::arg("pad_w"));
   m.def("wgrad_complex", &wgrad_complex, "Weight gradient -> (dW_real, dW_imag) KCRS",
         pybind11::arg("x"), pybind11::arg("dy"), pybind11::arg("kernel_h"),
         pybind11::arg("kernel_w"), pybind11::arg("stride_h"), pybind11::arg("stride_w"),

@@ -929,7 +929,9 @@ struct DgradScratch {
   size_t total() const { return outputs + pad + fprop; }
 };
 
-int dgrad_scratch(const Problem& pb, int precision, DgradScratch* out) {
+// planar: the phase copies are two fp32 planes (each half of `pad`, 256-byte
+// aligned) and the forward workspace is the planar one.
+int dgrad_scratch(const Problem& pb, int precision, DgradScratch* out, bool planar = false) {
   DgradScratch sc;
   sc.outputs = align256(static_cast<size_t>(pb.n) * pb.c * pb.h * pb.w * 8);
   for (int a = 0; a < pb.sh; ++a) {
@@ -939,9 +941,10 @@ int dgrad_scratch(const Problem& pb, int precision, DgradScratch* out) {
       Problem pp;
       const int rc = make_problem(&ph.shape, &pp);
       if (rc != CCV_OK) return rc;
-      sc.pad = std::max(sc.pad, align256(static_cast<size_t>(pb.n) * pb.k * ph.shape.h *
-                                         ph.shape.w * 8));
-      sc.fprop = std::max(sc.fprop, ccv_fprop_complex_workspace_bytes(&ph.shape, precision));
+      sc.pad = std::max(sc.pad, 2 * align256(static_cast<size_t>(pb.n) * pb.k * ph.shape.h *
+                                             ph.shape.w * 4));
+      sc.fprop = std::max(sc.fprop, planar ? ccv_fprop_planar_workspace_bytes(&ph.shape, precision)
+                                           : ccv_fprop_complex_workspace_bytes(&ph.shape, precision));
     }
   }
   *out = sc;
@@ -1071,7 +1074,115 @@ int ccv_wgrad_complex(const void* x, const void* dy, float* dw_real, float* dw_i
   }
   if ((rc = check_device()) != CCV_OK) return rc;
   if ((rc = check_status_clear()) != CCV_OK) return rc;
-  return launch_wgrad(x, dy, dw_real, dw_imag, pb, workspace, st);
+  WgradSource src;
+  src.x = x;
+  src.dy = dy;
+  return launch_wgrad(src, dw_real, dw_imag, pb, workspace, st);
+}
+
+size_t ccv_wgrad_planar_workspace_bytes(const ccv_conv_shape* shape) {
+  return ccv_wgrad_complex_workspace_bytes(shape);
+}
+
+int ccv_wgrad_planar(const float* x_real, const float* x_imag, const float* dy_real,
+                     const float* dy_imag, float* dw_real, float* dw_imag,
+                     const ccv_conv_shape* shape, void* workspace, size_t workspace_bytes,
+                     ccv_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ensure_status_mirror(st);
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if (!x_real || !x_imag || !dy_real || !dy_imag || !dw_real || !dw_imag) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  }
+  if (!aligned16(x_real) || !aligned16(x_imag) || !aligned16(dy_real) || !aligned16(dy_imag) ||
+      !aligned16(dw_real) || !aligned16(dw_imag)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  }
+  if (workspace == nullptr || !aligned16(workspace) ||
+      workspace_bytes < wgrad_workspace_bytes(pb)) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing, misaligned or too small");
+  }
+  if ((rc = check_device()) != CCV_OK) return rc;
+  if ((rc = check_status_clear()) != CCV_OK) return rc;
+  WgradSource src;
+  src.x_real = x_real;
+  src.x_imag = x_imag;
+  src.dy_real = dy_real;
+  src.dy_imag = dy_imag;
+  return launch_wgrad(src, dw_real, dw_imag, pb, workspace, st);
+}
+
+size_t ccv_dgrad_planar_workspace_bytes(const ccv_conv_shape* shape, int precision) {
+  Problem pb;
+  if (make_problem(shape, &pb) != CCV_OK) return 0;
+  if (dgrad_direct(pb)) {
+    const ccv_conv_shape d = dgrad_direct_shape(pb);
+    return ccv_fprop_planar_workspace_bytes(&d, precision);
+  }
+  DgradScratch sc;
+  if (dgrad_scratch(pb, precision, &sc, true) != CCV_OK) return 0;
+  return sc.total();
+}
+
+int ccv_dgrad_planar(const float* dy_real, const float* dy_imag, const void* w_packed_dgrad,
+                     float* dx_real, float* dx_imag, const ccv_conv_shape* shape, int precision,
+                     void* workspace, size_t workspace_bytes, ccv_stream_t stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  ensure_status_mirror(st);
+  Problem pb;
+  int rc = make_problem(shape, &pb);
+  if (rc != CCV_OK) return rc;
+  if ((rc = check_precision(precision)) != CCV_OK) return rc;
+  if (!dy_real || !dy_imag || !w_packed_dgrad || !dx_real || !dx_imag) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "null tensor pointer");
+  }
+  if (!aligned16(dy_real) || !aligned16(dy_imag) || !aligned16(w_packed_dgrad) ||
+      !aligned16(dx_real) || !aligned16(dx_imag)) {
+    return set_error(CCV_ERR_INVALID_ARGUMENT, "tensor pointers must be 16-byte aligned");
+  }
+  if (dgrad_direct(pb)) {
+    const ccv_conv_shape d = dgrad_direct_shape(pb);
+    return fprop_planar_impl(dy_real, dy_imag, w_packed_dgrad, nullptr, nullptr, dx_real, dx_imag,
+                             &d, precision, workspace, workspace_bytes, stream);
+  }
+  if (workspace == nullptr || !aligned16(workspace)) {
+    return set_error(CCV_ERR_WORKSPACE, "workspace missing or misaligned");
+  }
+  DgradScratch sc;
+  if ((rc = dgrad_scratch(pb, precision, &sc, true)) != CCV_OK) return rc;
+  if (workspace_bytes < sc.total()) return set_error(CCV_ERR_WORKSPACE, "workspace too small");
+  if ((rc = check_device()) != CCV_OK) return rc;
+  if ((rc = check_status_clear()) != CCV_OK) return rc;
+  char* ws = static_cast<char*>(workspace);
+  float* outputs = reinterpret_cast<float*>(ws);
+  float* pad_r = reinterpret_cast<float*>(ws + sc.outputs);
+  float* pad_i = reinterpret_cast<float*>(ws + sc.outputs + sc.pad / 2);
+  char* fws = ws + sc.outputs + sc.pad;
+  const float* filt = static_cast<const float*>(w_packed_dgrad);
+  size_t out_off = 0;  // floats into `outputs`
+  for (int a = 0; a < pb.sh; ++a) {
+    for (int b = 0; b < pb.sw; ++b) {
+      const DgradPhase ph = dgrad_phase(pb, a, b, precision);
+      const size_t plane = static_cast<size_t>(pb.n) * ph.y.out * ph.x.out * pb.c;
+      if (ph.live) {
+        if ((rc = launch_dgrad_phase_pad_planar(dy_real, dy_imag, pad_r, pad_i, pb,
+                                                static_cast<int>(ph.shape.h),
+                                                static_cast<int>(ph.shape.w), ph.y.offset,
+                                                ph.x.offset, st)) != CCV_OK) {
+          return rc;
+        }
+        rc = fprop_planar_impl(pad_r, pad_i, filt, nullptr, nullptr, outputs + out_off,
+                               outputs + out_off + plane, &ph.shape, precision, fws, sc.fprop,
+                               stream);
+        if (rc != CCV_OK) return rc;
+      }
+      filt += ph.filter_floats;
+      out_off += 2 * plane;
+    }
+  }
+  return launch_dgrad_interleave_planar(outputs, dx_real, dx_imag, pb, st);
 }
 
 }  // extern "C"

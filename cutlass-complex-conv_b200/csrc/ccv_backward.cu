@@ -226,6 +226,117 @@ int launch_dgrad_interleave(const void* phases, void* dx, const Problem& pb, cud
   return e == cudaSuccess ? CCV_OK : cuda_error(e, "dgrad interleave launch");
 }
 
+// Planar (forward_planar) data gradient: the same phases on fp32 NHWC planes.
+namespace {
+
+// fp32 planes [N][P][Q][K] -> [N][Hp][Wp][K]: pixel (i, j) = dy[i - oh][j - ow]
+// (zero outside dy); 4 channels per thread.
+__global__ void ccv_dgrad_phase_pad_planar_kernel(const float4* __restrict__ yr,
+                                                  const float4* __restrict__ yi,
+                                                  float4* __restrict__ outr,
+                                                  float4* __restrict__ outi, long long n, int P,
+                                                  int Q, int K4, int Hp, int Wp, int oh, int ow) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const long long total = n * Hp * Wp * K4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int k4 = static_cast<int>(i % K4);
+    long long t = i / K4;
+    const int j = static_cast<int>(t % Wp);
+    t /= Wp;
+    const int r = static_cast<int>(t % Hp);
+    const long long img = t / Hp;
+    const int p = r - oh, q = j - ow;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (p >= 0 && p < P && q >= 0 && q < Q) {
+      const long long src = ((img * P + p) * Q + q) * K4 + k4;
+      a = yr[src];
+      b = yi[src];
+    }
+    outr[i] = a;
+    outi[i] = b;
+  }
+}
+
+// dx planes [N][H][W][C] from the phases' planar outputs ([N][Ha][Wb][C] per
+// phase and plane: for each phase its real block, then its imaginary block,
+// in (a, b) order at `tab.off`, counted in float4).
+__global__ void ccv_dgrad_interleave_planar_kernel(const float4* __restrict__ phases,
+                                                   float4* __restrict__ dxr,
+                                                   float4* __restrict__ dxi, long long n, int H,
+                                                   int W, int C4, int sh, int sw,
+                                                   const __grid_constant__ DgradPhaseTable tab) {
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const long long total = n * H * W * C4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c4 = static_cast<int>(i % C4);
+    long long t = i / C4;
+    const int w = static_cast<int>(t % W);
+    t /= W;
+    const int h = static_cast<int>(t % H);
+    const long long img = t / H;
+    const int a = h % sh, b = w % sw;
+    const int ph = a * sw + b;
+    float4 vr = make_float4(0.f, 0.f, 0.f, 0.f), vi = vr;
+    if (tab.live[ph]) {
+      const int ha = tab.ha[a], wb = tab.wb[b];
+      const long long plane = n * ha * wb * C4;
+      const long long e = ((img * ha + h / sh) * wb + w / sw) * C4 + c4;
+      vr = phases[tab.off[ph] + e];
+      vi = phases[tab.off[ph] + plane + e];
+    }
+    dxr[i] = vr;
+    dxi[i] = vi;
+  }
+}
+
+}  // namespace
+
+int launch_dgrad_phase_pad_planar(const float* dy_r, const float* dy_i, float* out_r,
+                                  float* out_i, const Problem& pb, int hp, int wp, int oh, int ow,
+                                  cudaStream_t stream) {
+  const long long total = static_cast<long long>(pb.n) * hp * wp * (pb.k / 4);
+  const int block = 256;
+  const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, 148 * 16));
+  const cudaError_t e = launch_kernel(
+      ccv_dgrad_phase_pad_planar_kernel, dim3(grid), dim3(block), 0, stream, 1,
+      reinterpret_cast<const float4*>(dy_r), reinterpret_cast<const float4*>(dy_i),
+      reinterpret_cast<float4*>(out_r), reinterpret_cast<float4*>(out_i),
+      static_cast<long long>(pb.n), pb.p, pb.q, pb.k / 4, hp, wp, oh, ow);
+  return e == cudaSuccess ? CCV_OK : cuda_error(e, "dgrad planar phase copy launch");
+}
+
+int launch_dgrad_interleave_planar(const float* phases, float* dx_r, float* dx_i, const Problem& pb,
+                                   cudaStream_t stream) {
+  DgradPhaseTable tab;
+  memset(&tab, 0, sizeof(tab));
+  long long off = 0;  // float4
+  for (int a = 0; a < pb.sh; ++a) {
+    const DgradAxis ya = dgrad_axis(a, pb.sh, pb.ph, pb.r, pb.h);
+    tab.ha[a] = ya.out;
+    for (int b = 0; b < pb.sw; ++b) {
+      const DgradAxis xb = dgrad_axis(b, pb.sw, pb.pw, pb.s, pb.w);
+      tab.wb[b] = xb.out;
+      const int ph = a * pb.sw + b;
+      tab.off[ph] = off;
+      tab.live[ph] = ya.taps > 0 && xb.taps > 0 && ya.out > 0 && xb.out > 0;
+      off += 2LL * pb.n * ya.out * xb.out * (pb.c / 4);
+    }
+  }
+  const long long total = static_cast<long long>(pb.n) * pb.h * pb.w * (pb.c / 4);
+  const int block = 256;
+  const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, 148 * 16));
+  const cudaError_t e = launch_kernel(
+      ccv_dgrad_interleave_planar_kernel, dim3(grid), dim3(block), 0, stream, 1,
+      reinterpret_cast<const float4*>(phases), reinterpret_cast<float4*>(dx_r),
+      reinterpret_cast<float4*>(dx_i), static_cast<long long>(pb.n), pb.h, pb.w, pb.c / 4, pb.sh,
+      pb.sw, tab);
+  return e == cudaSuccess ? CCV_OK : cuda_error(e, "dgrad planar interleave launch");
+}
+
 // ------------------------------------------------------------------ wgrad
 namespace {
 
@@ -303,6 +414,55 @@ __global__ void ccv_wgrad_x_planes_kernel(const float2* __restrict__ x, float* _
         dr[q] = to_tf32_rna(v.x);
         di[q] = to_tf32_rna(v.y);
       }
+    }
+  }
+}
+
+// fp32 planes [N][R][Win][Cn] (channels innermost: NHWC x, NPQK dy) ->
+// TF32-rounded planes [S][N][Cn][R][Qa], element (s, n, c, r, q) =
+// src[n][r][q*sw - pw + s][c] (0 outside 0..Win-1), for q < Q - the layout
+// the weight-gradient kernel reads, from planar inputs.  One block per
+// (row r, n, s) and tile of 32 columns x 32 channels, through shared memory:
+// loads coalesced along c, stores along q.
+__global__ void __launch_bounds__(256) ccv_wgrad_planar_transpose_kernel(
+    const float* __restrict__ sr, const float* __restrict__ si, float* __restrict__ dr,
+    float* __restrict__ di, int N, int R, int Win, int Cn, int Q, int Qa, int S, int sw, int pw) {
+  __shared__ float tr[32][33];
+  __shared__ float ti[32][33];
+  ptx::griddep_wait();
+  ptx::griddep_launch_dependents();
+  const int qt = (Q + 31) / 32;
+  const int q0 = (blockIdx.x % qt) * 32;
+  const int c0 = (blockIdx.x / qt) * 32;
+  const int r = blockIdx.y;
+  const int n = blockIdx.z / S;
+  const int s = blockIdx.z - n * S;
+  const int tx = threadIdx.x, ty = threadIdx.y;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int ql = ty + 8 * i;
+    const int q = q0 + ql;
+    const int w = q * sw - pw + s;
+    const int c = c0 + tx;
+    float a = 0.f, b = 0.f;
+    if (q < Q && w >= 0 && w < Win && c < Cn) {
+      const long long src = ((static_cast<long long>(n) * R + r) * Win + w) * Cn + c;
+      a = __ldg(sr + src);
+      b = __ldg(si + src);
+    }
+    tr[ql][tx] = a;
+    ti[ql][tx] = b;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int c = c0 + ty + 8 * i;
+    const int q = q0 + tx;
+    if (c < Cn && q < Q) {
+      const long long o =
+          (((static_cast<long long>(s) * N + n) * Cn + c) * R + r) * Qa + q;
+      dr[o] = to_tf32_rna(tr[tx][ty + 8 * i]);
+      di[o] = to_tf32_rna(ti[tx][ty + 8 * i]);
     }
   }
 }
@@ -633,8 +793,8 @@ size_t wgrad_workspace_bytes(const Problem& pb) {
   return 2 * w.dy_plane + 2 * w.x_plane + w.partial;
 }
 
-int launch_wgrad(const void* x, const void* dy, float* dw_r, float* dw_i, const Problem& pb,
-                 void* ws, cudaStream_t stream) {
+int launch_wgrad(const WgradSource& src, float* dw_r, float* dw_i, const Problem& pb, void* ws,
+                 cudaStream_t stream) {
   const WgradPlan w = plan_wgrad(pb);
   char* base = static_cast<char*>(ws);
   float* dyr = reinterpret_cast<float*>(base);
@@ -646,21 +806,35 @@ int launch_wgrad(const void* x, const void* dy, float* dw_r, float* dw_i, const 
                        : nullptr;
   const int block = 256;
   const int sms = device_sm_count();
-  {
-    const long long rows = static_cast<long long>(pb.n) * pb.k * pb.p;
-    const int grid = static_cast<int>(std::min<long long>((rows * 32 + block - 1) / block, sms * 16LL));
-    const cudaError_t e =
+  if (src.x_real != nullptr) {
+    // Planar inputs: dy NPQK and x NHWC planes, transposed through shared memory.
+    if (pb.n > 65535 / pb.s || pb.p > 65535 || pb.h > 65535) {
+      return set_error(CCV_ERR_UNSUPPORTED, "problem too large for the planar weight gradient");
+    }
+    const int qt = (pb.q + 31) / 32;
+    cudaError_t e = launch_kernel(
+        ccv_wgrad_planar_transpose_kernel,
+        dim3(static_cast<unsigned>(qt * ((pb.k + 31) / 32)), pb.p, pb.n), dim3(32, 8), 0, stream,
+        1, src.dy_real, src.dy_imag, dyr, dyi, pb.n, pb.p, pb.q, pb.k, pb.q, w.qa, 1, 1, 0);
+    if (e != cudaSuccess) return cuda_error(e, "wgrad planar dy layout launch");
+    e = launch_kernel(ccv_wgrad_planar_transpose_kernel,
+                      dim3(static_cast<unsigned>(qt * ((pb.c + 31) / 32)), pb.h, pb.n * pb.s),
+                      dim3(32, 8), 0, stream, 1, src.x_real, src.x_imag, xr, xi, pb.n, pb.h, pb.w,
+                      pb.c, pb.q, w.qa, pb.s, pb.sw, pb.pw);
+    if (e != cudaSuccess) return cuda_error(e, "wgrad planar x layout launch");
+  } else {
+    // Complex64 inputs: dy NKPQ and x NCHW, one warp per row.
+    const long long dy_rows = static_cast<long long>(pb.n) * pb.k * pb.p;
+    int grid = static_cast<int>(std::min<long long>((dy_rows * 32 + block - 1) / block, sms * 16LL));
+    cudaError_t e =
         launch_kernel(ccv_wgrad_dy_planes_kernel, dim3(grid), dim3(block), 0, stream, 1,
-                      static_cast<const float2*>(dy), dyr, dyi, rows, pb.q, w.qa);
+                      static_cast<const float2*>(src.dy), dyr, dyi, dy_rows, pb.q, w.qa);
     if (e != cudaSuccess) return cuda_error(e, "wgrad dy layout launch");
-  }
-  {
-    const long long rows = static_cast<long long>(pb.n) * pb.c * pb.h;
-    const int grid = static_cast<int>(std::min<long long>((rows * 32 + block - 1) / block, sms * 16LL));
-    const cudaError_t e =
-        launch_kernel(ccv_wgrad_x_planes_kernel, dim3(grid), dim3(block), 0, stream, 1,
-                      static_cast<const float2*>(x), xr, xi, rows, pb.w, pb.s, pb.q, w.qa, pb.sw,
-                      pb.pw);
+    const long long x_rows = static_cast<long long>(pb.n) * pb.c * pb.h;
+    grid = static_cast<int>(std::min<long long>((x_rows * 32 + block - 1) / block, sms * 16LL));
+    e = launch_kernel(ccv_wgrad_x_planes_kernel, dim3(grid), dim3(block), 0, stream, 1,
+                      static_cast<const float2*>(src.x), xr, xi, x_rows, pb.w, pb.s, pb.q, w.qa,
+                      pb.sw, pb.pw);
     if (e != cudaSuccess) return cuda_error(e, "wgrad x layout launch");
   }
   WgradParams prm;

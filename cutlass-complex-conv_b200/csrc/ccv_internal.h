@@ -142,8 +142,26 @@ int launch_dgrad_interleave(const void* phases, void* dx, const Problem& pb, cud
 // Weight gradient: scratch bytes, and the launch (layout kernels, the
 // tcgen05 kernel and, when the reduction is split, the split-order sum).
 size_t wgrad_workspace_bytes(const Problem& pb);
-int launch_wgrad(const void* x, const void* dy, float* dw_r, float* dw_i, const Problem& pb,
-                 void* ws, cudaStream_t stream);
+// Inputs of the weight gradient: complex64 x (NCHW) and dy (NKPQ), or fp32
+// planes x_real/x_imag (NHWC) and dy_real/dy_imag (NPQK).
+struct WgradSource {
+  const void* x = nullptr;
+  const void* dy = nullptr;
+  const float* x_real = nullptr;
+  const float* x_imag = nullptr;
+  const float* dy_real = nullptr;
+  const float* dy_imag = nullptr;
+};
+int launch_wgrad(const WgradSource& src, float* dw_r, float* dw_i, const Problem& pb, void* ws,
+                 cudaStream_t stream);
+// Planar data gradient pieces: dy planes with a phase's zero border, and dx
+// planes from the phases' planar outputs (real block, then imaginary block,
+// per phase in (a, b) order).
+int launch_dgrad_phase_pad_planar(const float* dy_r, const float* dy_i, float* out_r,
+                                  float* out_i, const Problem& pb, int hp, int wp, int oh, int ow,
+                                  cudaStream_t stream);
+int launch_dgrad_interleave_planar(const float* phases, float* dx_r, float* dx_i, const Problem& pb,
+                                   cudaStream_t stream);
 
 // Encodes a tiled tensor map through the driver entry point.
 // `swizzle_bytes` is 64 or 128 (the box's inner extent in bytes).

@@ -231,6 +231,19 @@ int ccv_wgrad_complex(const void* x, const void* dy, float* dw_real, float* dw_i
                       const ccv_conv_shape* shape, void* workspace, size_t workspace_bytes,
                       ccv_stream_t stream);
 
+/* The same gradients for the planar path (forward_planar): dy_real/dy_imag
+ * fp32 NPQK planes, dx_real/dx_imag fp32 NHWC planes, x_real/x_imag fp32
+ * NHWC planes; the packed filter of ccv_prepack_weights_dgrad. */
+size_t ccv_dgrad_planar_workspace_bytes(const ccv_conv_shape* shape, int precision);
+int ccv_dgrad_planar(const float* dy_real, const float* dy_imag, const void* w_packed_dgrad,
+                     float* dx_real, float* dx_imag, const ccv_conv_shape* shape, int precision,
+                     void* workspace, size_t workspace_bytes, ccv_stream_t stream);
+size_t ccv_wgrad_planar_workspace_bytes(const ccv_conv_shape* shape);
+int ccv_wgrad_planar(const float* x_real, const float* x_imag, const float* dy_real,
+                     const float* dy_imag, float* dw_real, float* dw_imag,
+                     const ccv_conv_shape* shape, void* workspace, size_t workspace_bytes,
+                     ccv_stream_t stream);
+
 /* Device status word of the current device: nonzero after an in-kernel
  * bounded wait ran out (a CCV_ERR_* code).  While it is set, fprop kernels
  * on that device exit without work.  The kernel that gives up also writes a

@@ -82,6 +82,10 @@ def load():
         "ccv_dgrad_complex": (ctypes.c_int, [vp, vp, vp, sp, ctypes.c_int, vp, sz, vp]),
         "ccv_wgrad_complex_workspace_bytes": (sz, [sp]),
         "ccv_wgrad_complex": (ctypes.c_int, [vp, vp, vp, vp, sp, vp, sz, vp]),
+        "ccv_dgrad_planar_workspace_bytes": (sz, [sp, ctypes.c_int]),
+        "ccv_dgrad_planar": (ctypes.c_int, [vp, vp, vp, vp, vp, sp, ctypes.c_int, vp, sz, vp]),
+        "ccv_wgrad_planar_workspace_bytes": (sz, [sp]),
+        "ccv_wgrad_planar": (ctypes.c_int, [vp, vp, vp, vp, vp, vp, sp, vp, sz, vp]),
         "ccv_get_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int)]),
         "ccv_clear_device_status": (ctypes.c_int, []),
         "ccv_selftest_bounded_wait": (ctypes.c_int, [vp, vp]),

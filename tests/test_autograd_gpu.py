@@ -105,3 +105,23 @@ def test_weight_edit_refreshes_data_gradient_filter():
         (dx,) = torch.autograd.grad(layer(xd), xd, grad_outputs=dy.to(DEV))
         rx, _, _ = oracle.backward_autograd_fp64(case, x, wr * scale, wi, dy)
         assert oracle.rel_frobenius(dx.cpu(), rx) <= 1e-3
+
+
+@pytest.mark.parametrize("case", CASES[:2], ids=IDS[:2])
+def test_forward_planar_gradients(case):
+    layer, x, wr, wi = _layer(case)
+    layer.weight_real.requires_grad_(True)
+    layer.weight_imag.requires_grad_(True)
+    xr = x.real.permute(0, 2, 3, 1).contiguous().to(DEV).requires_grad_(True)
+    xi = x.imag.permute(0, 2, 3, 1).contiguous().to(DEV).requires_grad_(True)
+    yr, yi = layer.forward_planar(xr, xi)
+    dy = _dy(case)
+    dyr = dy.real.permute(0, 2, 3, 1).contiguous().to(DEV)
+    dyi = dy.imag.permute(0, 2, 3, 1).contiguous().to(DEV)
+    gxr, gxi, gwr, gwi = torch.autograd.grad(
+        (yr, yi), (xr, xi, layer.weight_real, layer.weight_imag), grad_outputs=(dyr, dyi))
+    rx, rwr, rwi = oracle.backward_autograd_fp64(case, x, wr, wi, dy)
+    dx = oracle.planar_nhwc_to_complex_nchw(gxr, gxi).cpu()
+    assert oracle.rel_frobenius(dx, rx) <= 1e-3
+    got = torch.complex(gwr.cpu().double(), gwi.cpu().double())
+    assert oracle.rel_frobenius(got, torch.complex(rwr, rwi)) <= 1e-3

@@ -166,3 +166,47 @@ def test_dgrad_phases(case):
     dx = dgrad(case, wr, wi, dy)
     assert torch.isfinite(torch.view_as_real(dx)).all()
     assert oracle.rel_frobenius(dx, ref_dx) <= 1e-3
+
+
+def _planes(t):
+    """complex64 NCHW -> (real, imag) fp32 NHWC planes on the device."""
+    t = t.to(DEV)
+    return (t.real.permute(0, 2, 3, 1).contiguous(), t.imag.permute(0, 2, 3, 1).contiguous())
+
+
+@pytest.mark.parametrize("case", CASES[:8] + [oracle.ConvCase(1, 8, 8, 8, 8, 3, 3, 1, 1, 3, 3)],
+                         ids=IDS[:8] + ["pad3_k3"])
+def test_planar_gradients_match_oracle(case):
+    """ccv_dgrad_planar / ccv_wgrad_planar (the forward_planar layouts)."""
+    lib = ccv_abi.load()
+    shp = ccv_abi.shape_of(case)
+    x, wr, wi = oracle.make_inputs(case)
+    dy = _dy(case)
+    rx, rwr, rwi = oracle.backward_autograd_fp64(case, x, wr, wi, dy)
+    nb = lib.ccv_packed_weight_bytes(ctypes.byref(shp), 0)
+    packed = torch.empty(nb // 4, dtype=torch.float32, device=DEV)
+    wr_d, wi_d = wr.to(DEV).contiguous(), wi.to(DEV).contiguous()
+    ccv_abi.check(lib.ccv_prepack_weights_dgrad(_ptr(wr_d), _ptr(wi_d), ccv_abi.CCV_WEIGHT_KCRS,
+                                                ctypes.byref(shp), 0, _ptr(packed), nb,
+                                                _stream()), "dgrad prepack")
+    dyr, dyi = _planes(dy)
+    xr, xi = _planes(x)
+    wsb = lib.ccv_dgrad_planar_workspace_bytes(ctypes.byref(shp), 0)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device=DEV)
+    dxr = torch.full((case.n, case.h, case.w, case.c), float("nan"), device=DEV)
+    dxi = torch.full_like(dxr, float("nan"))
+    ccv_abi.check(lib.ccv_dgrad_planar(_ptr(dyr), _ptr(dyi), _ptr(packed), _ptr(dxr), _ptr(dxi),
+                                       ctypes.byref(shp), 0, _ptr(ws), wsb, _stream()),
+                  "dgrad planar")
+    wwb = lib.ccv_wgrad_planar_workspace_bytes(ctypes.byref(shp))
+    wws = torch.empty(wwb, dtype=torch.uint8, device=DEV)
+    dwr = torch.full((case.k, case.c, case.r, case.s), float("nan"), device=DEV)
+    dwi = torch.full_like(dwr, float("nan"))
+    ccv_abi.check(lib.ccv_wgrad_planar(_ptr(xr), _ptr(xi), _ptr(dyr), _ptr(dyi), _ptr(dwr),
+                                       _ptr(dwi), ctypes.byref(shp), _ptr(wws), wwb, _stream()),
+                  "wgrad planar")
+    torch.cuda.synchronize()
+    dx = oracle.planar_nhwc_to_complex_nchw(dxr, dxi).cpu()
+    assert oracle.rel_frobenius(dx, rx) <= 1e-3
+    got = torch.complex(dwr.cpu().double(), dwi.cpu().double())
+    assert oracle.rel_frobenius(got, torch.complex(rwr, rwi)) <= 1e-3
