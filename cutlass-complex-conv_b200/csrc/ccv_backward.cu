@@ -526,7 +526,7 @@ __global__ void __launch_bounds__(kWgThreads, 1)
   }
   if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
   ptx::tc_fence_before();
-  __syncthreads();
+  ptx::cta_sync();
   ptx::tc_fence_after();
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
@@ -674,8 +674,9 @@ __global__ void __launch_bounds__(kWgThreads, 1)
     }
     ptx::tc_fence_before();
   }
-  __syncthreads();
+  ptx::cta_sync();
   if (warp == 1) {
+    __syncwarp();  // tcgen05.dealloc is warp-collective
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, Cf::kTmemCols);
   }

@@ -165,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // word's host copy before it launches again.
   if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
   ptx::tc_fence_before();
-  __syncthreads();
+  ptx::cta_sync();
   ptx::tc_fence_after();
   // Everything above may overlap the previous kernel on the stream
   // (programmatic dependent launch); the operands and outputs are touched
@@ -408,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tc_fence_before();
   }
 
-  __syncthreads();
+  ptx::cta_sync();
   if (splits > 1) {
     // ---------------------------------------------------------- cluster reduce
     // Every partial is parked.  Only the tile rows that hold an output pixel
@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       vm = __ballot_sync(0xffffffffu, v);
       if (lane == 0) vmask[warp] = vm;
     }
-    __syncthreads();
+    ptx::cta_sync();
     if (v) {
       int idx = __popc(vm & ((1u << lane) - 1u));
       for (int w2 = 0; w2 < warp; ++w2) idx += __popc(vmask[w2]);
@@ -575,6 +575,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (warp == 1) {
+    __syncwarp();  // tcgen05.dealloc is warp-collective
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, C::kTmemCols);
   }
@@ -978,7 +979,7 @@ __global__ void ccv_selftest_wait_kernel(int* status, int mirror) {
     ptx::mbar_init(b, 1);
     ptx::fence_mbar_init();
   }
-  __syncthreads();
+  ptx::cta_sync();
   if (threadIdx.x == 0) {
     // Nothing ever arrives on `bar`: the bounded wait must give up.
     const bool ok = mirror ? ptx::mbar_wait_bounded<false, true>(b, 0, status, CCV_ERR_DEVICE_TIMEOUT)

@@ -133,7 +133,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
   if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
-  __syncthreads();
+  ptx::cta_sync();
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
   const int rs = prm.r * prm.s;
@@ -366,7 +366,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32
     }
   }
 
-  __syncthreads();
+  ptx::cta_sync();
   if constexpr (LW) {
     // The last CTA to finish leaves the conversion counters zero.
     if (threadIdx.x == 0) {
@@ -388,6 +388,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads2 + (LW ? 32
   ptx::tc_fence_before();
   ptx::cluster_sync();
   if (warp == 1) {
+    __syncwarp();  // tcgen05.dealloc is warp-collective
     ptx::tc_fence_after();
     ptx::tmem_dealloc_pair(tmem_base, C::kTmemCols);
   }

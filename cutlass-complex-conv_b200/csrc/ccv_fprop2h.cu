@@ -143,7 +143,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<LW>(), 
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
   if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
-  __syncthreads();
+  ptx::cta_sync();
   const uint32_t tmem_base = *tmem_holder;
   const bool skip = flags[0] != 0;
   const int per_img = prm.tiles_bp * prm.tiles_bq;
@@ -163,7 +163,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<LW>(), 
         flags[1] = 1;
       }
       ptx::fence_proxy_async_shared();
-      __syncthreads();
+      ptx::cta_sync();
     } else if (!skip && prm.lw_prefix > 0) {
       layout_warp(prm, lane, true);
     }
@@ -405,7 +405,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<LW>(), 
     }
   }
 
-  __syncthreads();
+  ptx::cta_sync();
   if constexpr (LW) {
     // The last CTA to finish leaves the conversion counters zero.
     if (threadIdx.x == 0) {
@@ -428,6 +428,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(halo_threads<LW>(), 
   ptx::tc_fence_before();
   ptx::cluster_sync();
   if (warp == 1) {
+    __syncwarp();  // tcgen05.dealloc is warp-collective
     ptx::tc_fence_after();
     ptx::tmem_dealloc_pair(tmem_base, C::kTmemCols);
   }

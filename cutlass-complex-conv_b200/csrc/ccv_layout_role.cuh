@@ -342,7 +342,7 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
     for (int i = 0; i < kLwTmaMaxImages; ++i) cnt[i] = 0u;
     for (int b = 0; b < nbuf; ++b) load(b, atomicAdd(ctr, 1u));
   }
-  __syncthreads();
+  ptx::cta_sync();
   bool ok = true;
 #pragma unroll 1
   for (int k = 0;; ++k) {
@@ -360,7 +360,7 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
                                                     prm.status, CCV_ERR_DEVICE_TIMEOUT);
     const int ob = k & 1;
     if (tid == 0 && k >= 2) ptx::bulk_wait_read_le1();  // the store of k-2 has read its buffer
-    if (__syncthreads_or(!got)) {
+    if (ptx::cta_sync_or(!got)) {
       ok = false;
       break;
     }
@@ -382,7 +382,7 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
       oii[p0 + kLwBoxCh] = v.w;
     }
     ptx::fence_proxy_async_shared();
-    __syncthreads();
+    ptx::cta_sync();
     if (tid == 0) {
       const uint32_t o = out_u + static_cast<uint32_t>(ob) * 2u * kLwBoxOutPlane;
       ptx::tma_store_4d(&prm.tm_pr, o, c0, w0, h0, img);
@@ -407,7 +407,7 @@ __device__ __forceinline__ bool lw_tma_prefix(const FpropParams& prm, uint8_t* b
       }
     }
   }
-  __syncthreads();
+  ptx::cta_sync();
   return ok;
 }
 

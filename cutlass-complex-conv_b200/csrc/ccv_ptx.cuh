@@ -432,9 +432,35 @@ __device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t addr) {
   return v;
 }
 
+// Cluster-wide barrier.  The non-.aligned forms count threads, so a warp
+// whose lanes arrive at different times (one lane ran a role loop alone) is
+// still waited for in full.
 __device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\t"
-               "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.arrive.release;\n\t"
+               "barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// CTA-wide barrier that counts threads, not warps.  __syncthreads() is the
+// .aligned form, which is undefined unless every lane of a warp reaches it
+// together.  After a branch that one lane runs alone (a producer or MMA loop,
+// a bulk wait) the other lanes get there first; on B200 the aligned form then
+// let thread 0 of the single-CTA kernel past the barrier about 1 us before an
+// epilogue warp had arrived (%globaltimer stamps on both sides).  Every
+// barrier that follows such a branch is this one.
+__device__ __forceinline__ void cta_sync() { asm volatile("barrier.sync 0;" ::: "memory"); }
+
+// cta_sync() that also returns whether `v` was true in any thread.
+__device__ __forceinline__ bool cta_sync_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.or.pred q, 0, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(v))
+      : "memory");
+  return r != 0;
 }
 
 // Arrive on an mbarrier that may live in another CTA of the cluster.
