@@ -44,6 +44,7 @@ namespace ccv {
 namespace {
 
 constexpr int kThreads = 192;
+constexpr int kMaxSplits = 16;  // CTAs per cluster (non-portable above 8)
 constexpr int kBlockC = 32;      // input channels per K step (128-byte rows)
 constexpr int kRowBytes = kBlockC * 4;
 constexpr int kABytes = kBlockM * kRowBytes;  // one activation plane per stage
@@ -601,22 +602,21 @@ cudaError_t prepare_variant() {
   return err[dev & 63];
 }
 
-// Clusters of 1, 2, 4, 8 and 16 CTAs of the KT-wide single-CTA kernel the
-// device can hold at once (0: that size cannot be launched), queried once
-// per device.  Clusters of 16 take 16 SMs of one GPC, so B200 holds only
-// about 7 of them - fewer than it has SMs for.
+// Clusters of 1..16 CTAs of the KT-wide single-CTA kernel the device can
+// hold at once (index = cluster size; 0: that size cannot be launched),
+// queried once per device.  A cluster takes its SMs from one GPC, so B200
+// holds only about 7 clusters of 16 - fewer than it has SMs for.
 template <int KT>
 const int* cluster_capacity() {
   using C = Cfg<KT>;
   auto kern = ccv_fprop_tf32_kernel<KT, false, false>;
   static std::once_flag once[64];
-  static int caps[64][5] = {};
+  static int caps[64][kMaxSplits + 1] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   std::call_once(once[dev & 63], [&]() {
     if (prepare_variant<KT, false, false>() != cudaSuccess) return;
-    for (int l = 0; l < 5; ++l) {
-      const int size = 1 << l;
+    for (int size = 1; size <= kMaxSplits; ++size) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(static_cast<unsigned>(size), 1, 1);
       cfg.blockDim = dim3(kThreads, 1, 1);
@@ -630,7 +630,7 @@ const int* cluster_capacity() {
       cfg.numAttrs = 1;
       int n = 0;
       if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0) {
-        caps[dev & 63][l] = n;
+        caps[dev & 63][size] = n;
       } else {
         cudaGetLastError();
       }
@@ -686,24 +686,34 @@ size_t single_l2_bytes(int tiles, int splits, int kt) {
   return static_cast<size_t>(tiles) * splits * kBlockM * 2 * kt * sizeof(float);
 }
 
-// Picks the channel tile (32, 64 or 128) and the split (1, 2, 4 or 8 CTAs
-// per tile) that put the most CTAs to work - at most one per SM, and only
-// as many clusters as the device holds at once (a second wave of clusters
-// doubles the time) - preferring the wider tile on a tie (fewer activation
-// re-reads).  Measured on B200 over the batch-1 layers (graph replay, every
-// tile x split): clusters of 16 were slower than clusters of 8 with the same
-// CTA count (256->512 @ 7x7: 12.7 vs 12.4 us; 128->256 @ 14x14: 14.4 vs
-// 11.2 us), and a split too wide for one wave of clusters ran 2x slower.
-// With workspace room (`ws_bytes`; SIZE_MAX: unbounded) the split's partial
-// sums meet in L2, else over distributed shared memory (~1 us slower on the
-// deep layers).  CCV_KT pins the tile; CCV_SPLITK caps the split.
+// Picks the channel tile (32, 64 or 128) and the split (1..16 CTAs per tile,
+// one cluster) by an estimate of the launch's time on B200:
+//   ceil(K steps / split) x step time(tile)          the slowest CTA's loop
+// + rows x 2*tile x 4 B / 100 GB/s                    partial (or output) rows out
+// + 1.5 us when split                                 cluster barrier + sums
+// with step times 0.55 / 0.60 / 0.80 us for tiles of 32 / 64 / 128, rows the
+// tile's output rows rounded up to a warp's 32.  Only plans of one wave fit:
+// at most one CTA per SM and no more clusters than the device holds at once
+// (a second wave of clusters doubled the time).  The constants come from a
+// graph-replay sweep of every tile x split on the four batch-1 layers, where
+// the estimate ranks the fastest plan first on each: 32->64 @ 56x56 tile 64
+// split 5 (10.2 us; split 4: 10.8), 64->128 @ 28x28 64/9 (9.4; 64/8: 9.8),
+// 128->256 @ 14x14 64/9 (10.2; 64/8: 10.8), 256->512 @ 7x7 128/16 (10.5;
+// 64/8: 12.1) - a split that divides the K steps evenly leaves no CTA a step
+// behind the others at the barrier.  With workspace room (`ws_bytes`;
+// SIZE_MAX: unbounded) the partial sums meet in L2, else over distributed
+// shared memory (~1 us slower on the deep layers).  CCV_KT pins the tile;
+// CCV_SPLITK caps the split.
 SinglePlan plan_single_cta(const Problem& pb, const Tiling& t, size_t ws_bytes) {
   SinglePlan best;
-  long long best_ctas = -1;
+  double best_us = 1e30;
   const int sms = device_sm_count();
   const int ksteps = ((pb.c + kBlockC - 1) / kBlockC) * pb.r * pb.s;
   const int pin = knobs().kt;
-  const int cap = knobs().splitk > 0 ? std::min(knobs().splitk, 8) : 8;
+  const int cap = knobs().splitk > 0 ? std::min(knobs().splitk, kMaxSplits) : kMaxSplits;
+  const long long m_total = static_cast<long long>(pb.n) * pb.p * pb.q;
+  const long long rows_per_tile = (m_total + t.tiles_m - 1) / t.tiles_m;
+  const double rows = static_cast<double>(std::min<long long>(kBlockM, (rows_per_tile + 31) / 32 * 32));
   for (int kt = 128; kt >= 32; kt /= 2) {
     if (pin == 32 || pin == 64 || pin == 128) {
       if (kt != pin) continue;
@@ -713,20 +723,20 @@ SinglePlan plan_single_cta(const Problem& pb, const Tiling& t, size_t ws_bytes) 
     const int tiles_n = (pb.k + kt - 1) / kt;
     const long long tiles = static_cast<long long>(t.tiles_m) * tiles_n;
     const int* caps = cluster_capacity_kt(kt);
-    int s = 1;
-    for (int l = 1; l < 4; ++l) {
-      const int c = 1 << l;
-      if (c > cap || c > ksteps || tiles * c > sms || caps[l] < tiles) break;
-      s = c;
-    }
-    const long long ctas = tiles * s;
-    if (ctas > best_ctas) {  // ties keep the wider tile (visited first)
-      best_ctas = ctas;
-      best.kt = kt;
-      best.splits = s;
-      const size_t need = s > 1 ? single_l2_bytes(static_cast<int>(tiles), s, kt) : 0;
-      best.l2 = s > 1 && ws_bytes >= need;
-      best.ws_bytes = best.l2 ? need : 0;
+    const double step_us = kt == 128 ? 0.80 : (kt == 64 ? 0.60 : 0.55);
+    const double out_us = rows * 2.0 * kt * 4.0 / 100e3;
+    for (int sp = 1; sp <= cap && sp <= ksteps; ++sp) {
+      if (tiles * sp > sms && sp > 1) break;
+      if (sp > 1 && caps[sp] < tiles) continue;
+      const double us = ((ksteps + sp - 1) / sp) * step_us + out_us + (sp > 1 ? 1.5 : 0.0);
+      if (us < best_us - 1e-9) {  // ties keep the wider tile and the smaller split
+        best_us = us;
+        best.kt = kt;
+        best.splits = sp;
+        const size_t need = sp > 1 ? single_l2_bytes(static_cast<int>(tiles), sp, kt) : 0;
+        best.l2 = sp > 1 && ws_bytes >= need;
+        best.ws_bytes = best.l2 ? need : 0;
+      }
     }
   }
   return best;

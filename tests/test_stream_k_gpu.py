@@ -187,3 +187,35 @@ def test_single_cta_split_through_l2_matches_dsmem(case):
     assert not torch.isnan(y_l2.real).any() and not torch.isnan(y_l2.imag).any()
     assert torch.equal(y_l2, y_dsmem)
     assert oracle.rel_frobenius(y_l2, oracle.oracle_fp64(case, x, wr, wi)) <= TOL[TF32]
+
+
+@pytest.mark.parametrize("case,kt,splits",
+                         [(C(1, 256, 7, 7, 512, 3, 3, 1, 1, 1, 1), 128, s) for s in (3, 5, 7, 11, 16)]
+                         + [(C(1, 64, 28, 28, 128, 3, 3, 1, 1, 1, 1), 64, 9),
+                            (C(1, 32, 56, 56, 64, 3, 3, 1, 1, 1, 1), 64, 5),
+                            (C(2, 40, 9, 13, 24, 3, 3, 1, 1, 1, 1), 32, 6)],
+                         ids=lambda v: str(v) if isinstance(v, int) else f"{v.c}_{v.k}_{v.h}")
+def test_single_cta_any_split(case, kt, splits):
+    """Cluster splits of any size up to 16 CTAs (not only powers of two): the
+    K steps divide unevenly for most sizes, the partials still sum in rank
+    order - bitwise equal through L2 and over distributed shared memory - and
+    within the TF32 bar of the fp64 oracle.  CCV_SPLITK caps the split and
+    the plan takes the largest that shortens the slowest CTA's loop."""
+    keys = ("CCV_KT", "CCV_SPLITK", "CCV_FORCE_KERNEL")
+    old = {k: os.environ.get(k) for k in keys}
+    os.environ.update({"CCV_KT": str(kt), "CCV_SPLITK": str(splits), "CCV_FORCE_KERNEL": "1"})
+    try:
+        x, wr, wi = oracle.make_inputs(case, input_seed=83)
+        packed = abi_prepack(case, wr, wi)
+        y_l2 = planar(case, x, packed, TF32, full_workspace=True)
+        y_dsmem = planar(case, x, packed, TF32, full_workspace=False)
+    finally:
+        for k, v in old.items():
+            if v is None:
+                os.environ.pop(k, None)
+            else:
+                os.environ[k] = v
+    assert not torch.isnan(y_l2.real).any() and not torch.isnan(y_l2.imag).any()
+    assert torch.equal(y_l2, y_dsmem)
+    assert oracle.rel_frobenius(y_l2, oracle.oracle_fp64(case, x, wr, wi)) <= TOL[TF32]
+    assert device_status() == 0, "a bounded in-kernel wait ran out"
