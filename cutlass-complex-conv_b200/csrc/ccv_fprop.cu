@@ -132,17 +132,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int k0 = n_tile * KT;
   const int rs = prm.r * prm.s;
 
-  if (warp == 0 && lane == 0) {
-    // Every weight byte of this CTA's K range is read once, from HBM: ask
-    // for all of it now, before the prologue and the wait for the previous
-    // kernel, so the stream of the whole grid is in flight at once instead
-    // of `kStages` boxes per CTA at a time.  The loads below then hit L2.
-    for (int t = kbeg; t < kend; ++t) {
-      const int cb = t / rs;
-      ptx::tma_prefetch_l2_4d(&prm.tm_w, cb * kBlockC, k0, 1, t - cb * rs);
-    }
-  }
+  // Prologue, spread over warps so that its latencies overlap: thread 0
+  // asks for the tensor-map descriptors first (the first TMA issue waits for
+  // them otherwise) and initialises the barriers, warp 1 allocates TMEM,
+  // warp 3 reads the status word.
   if (threadIdx.x == 0) {
+    ptx::prefetch_tmap(&prm.tm_w);
+    ptx::prefetch_tmap(&prm.tm_xr);
+    ptx::prefetch_tmap(&prm.tm_xi);
     flags[1] = 0;
     for (int i = 0; i < C::kStages; ++i) {
       ptx::mbar_init(full_bar(i), 1);
@@ -150,11 +147,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     ptx::mbar_init(acc_bar, 1);
     ptx::fence_mbar_init();
-  }
-  if (warp == 0 && lane == 0) {
-    ptx::prefetch_tmap(&prm.tm_xr);
-    ptx::prefetch_tmap(&prm.tm_xi);
-    ptx::prefetch_tmap(&prm.tm_w);
   }
   if (warp == 1) {
     ptx::tmem_alloc(ptx::smem_u32(tmem_holder), C::kTmemCols);
@@ -164,10 +156,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the previous kernel's tail (programmatic dependent launch).  No kernel
   // writes it except on a timeout, which the host also sees through the
   // word's host copy before it launches again.
-  if (threadIdx.x == 0) flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
+  if (warp == 3 && lane == 0) {
+    flags[0] = *reinterpret_cast<volatile int*>(prm.status) != 0 ? 1 : 0;
+  }
   ptx::tc_fence_before();
   ptx::cta_sync();
   ptx::tc_fence_after();
+  if (warp == 2 && lane == 0) {
+    // Every weight byte of this CTA's K range is read once, from HBM: ask
+    // for all of it now, before the wait for the previous kernel, so the
+    // stream of the whole grid is in flight at once instead of `kStages`
+    // boxes per CTA at a time; the producer's loads then hit L2.  An
+    // epilogue warp issues it: it is idle until the accumulator is ready.
+    for (int t = kbeg; t < kend; ++t) {
+      const int cb = t / rs;
+      ptx::tma_prefetch_l2_4d(&prm.tm_w, cb * kBlockC, k0, 1, t - cb * rs);
+    }
+  }
   // Everything above may overlap the previous kernel on the stream
   // (programmatic dependent launch); the operands and outputs are touched
   // only below.

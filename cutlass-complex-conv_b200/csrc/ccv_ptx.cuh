@@ -441,12 +441,12 @@ __device__ __forceinline__ void cluster_sync() {
 }
 
 // CTA-wide barrier that counts threads, not warps.  __syncthreads() is the
-// .aligned form, which is undefined unless every lane of a warp reaches it
-// together.  After a branch that one lane runs alone (a producer or MMA loop,
-// a bulk wait) the other lanes get there first; on B200 the aligned form then
-// let thread 0 of the single-CTA kernel past the barrier about 1 us before an
-// epilogue warp had arrived (%globaltimer stamps on both sides).  Every
-// barrier that follows such a branch is this one.
+// .aligned form, which PTX leaves undefined unless every lane of a warp
+// reaches it together; after a branch that one lane runs alone (a producer or
+// MMA loop, a bulk wait) the other lanes get there first.  The compiler's
+// reconvergence made the aligned form wait in a B200 test (a lane held 2 us
+// before the barrier; every thread read its flag after it), but only this
+// form is defined there, so every barrier that follows such a branch is it.
 __device__ __forceinline__ void cta_sync() { asm volatile("barrier.sync 0;" ::: "memory"); }
 
 // cta_sync() that also returns whether `v` was true in any thread.
