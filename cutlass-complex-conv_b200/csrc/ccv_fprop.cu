@@ -802,9 +802,11 @@ bool layout_warps_pay(const Problem& pb, int precision) {
   // CCV_LW=0: never; CCV_LW=1: wherever a pair kernel runs; unset: when
   //   * the grid runs at least two waves of tiles (below that the first
   //     wave needs most images at once),
-  //   * the input is at least 128 MB (below that the layout pass's cost is
+  //   * the input is at least 96 MB (below that the layout pass's cost is
   //     small and the layout warps' traffic during the convolution costs as
-  //     much or more: 51-103 MB inputs won in one of four B200 runs), and
+  //     much or more; at 103 MB - batch 32 of the 56x56 layer - they win
+  //     ~4 % once the stream-K split is off, which layout-warp launches now
+  //     skip: 226 / 232 / 225 -> 215 / 218 / 222 us in three B200 runs), and
   //   * there are at least 500 flops per input byte, K*R*S*(P*Q)/(H*W) per
   //     pass (the layout warps convert ~1 TB/s; below that - stride 2 at
   //     C = 64 - they hold the MMAs back and a pass at the copy rate wins).
@@ -821,7 +823,7 @@ bool layout_warps_pay(const Problem& pb, int precision) {
   const double flops_per_byte = static_cast<double>(pb.k) * pb.r * pb.s * pb.p * pb.q /
                                 (static_cast<double>(pb.h) * pb.w) *
                                 (precision == CCV_PRECISION_3XTF32 ? 3 : 1);
-  if (in_bytes < 128.0 * 1024 * 1024 || flops_per_byte < 500.0) return false;
+  if (in_bytes < 96.0 * 1024 * 1024 || flops_per_byte < 500.0) return false;
   // Pixels per cluster tile: two CTAs of 128 (halo: two sub-boxes each for
   // KT <= 64).
   const int kt = fam == kPairHalo ? th.kt : t.kt;

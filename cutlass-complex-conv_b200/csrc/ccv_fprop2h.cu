@@ -465,9 +465,13 @@ int launchh_variant(FpropParams& prm, int smem_bytes, void* ws, size_t ws_bytes,
   int rc;
   int launched = 0;
   if (LW) {
-    // Layout warps: the stream-K range runs first, so its first image is
-    // converted first.
-    launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc);
+    // Layout warps: no stream-K split by default (CCV_STREAMK=1 forces it).
+    // Its partial sums and the split tiles' waits for their images cost the
+    // layout-warp launches more than the tail they remove: batch 32 of the
+    // 56x56 layer 231 us with the split, 215-222 us without, batch 64 equal
+    // within noise (B200).  When forced, the stream-K range runs first, so
+    // its first image is converted first.
+    launched = launch_clusters(prm, clusters, slots, KT, ws, ws_bytes, stream, &rc, 101);
     if (rc != CCV_OK) return rc;
     prm.lw_first_img = 0;
     if (prm.sk_slots > 0) {

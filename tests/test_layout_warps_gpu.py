@@ -158,10 +158,12 @@ def test_layout_warps_not_taken(knobs):
     os.environ.pop("CCV_HALO")
     # Batch-1 layers run the single-CTA kernel: layout pass first.
     assert kernel_name(C(1, 64, 28, 28, 128, 3, 3, 1, 1, 1, 1)) == "layout_pass+single_cta"
-    # Default: inputs of at least 128 MB, at least two waves of tiles and
+    # Default: inputs of at least 96 MB, at least two waves of tiles and
     # 500 flops per input byte.
     os.environ.pop("CCV_LW")
     assert kernel_name(C(8, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == "layout_pass+halo_pair"
+    assert kernel_name(C(16, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == "layout_pass+halo_pair"
+    assert kernel_name(C(32, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == "halo_pair_layout_warps"
     assert kernel_name(C(64, 128, 56, 56, 128, 3, 3, 1, 1, 1, 1)) == "halo_pair_layout_warps"
     assert kernel_name(C(8, 64, 320, 320, 64, 3, 3, 1, 1, 1, 1)) == "halo_pair_layout_warps"
     assert kernel_name(C(32, 64, 56, 56, 64, 3, 3, 1, 1, 1, 1)) == "layout_pass+halo_pair"
@@ -176,10 +178,11 @@ def test_layout_warps_not_taken(knobs):
 @pytest.mark.parametrize("name,case", [CASES[0], ("b3_c64_ragged", C(3, 64, 45, 29, 96, 3, 3, 1, 1, 1, 1))],
                          ids=[CASES[0][0], "b3_c64_ragged"])
 def test_layout_warps_with_stream_k(knobs, name, case):
-    # Default stream-K policy (a partial last wave is split): the split range
-    # runs first, so the layout warps convert its images first.  Same plan,
-    # same sums as the layout pass + kernel.
-    os.environ.pop("CCV_STREAMK")
+    # Stream-K forced (CCV_STREAMK=1: a partial last wave is split; layout-warp
+    # launches skip the split by default): the split range runs first, so the
+    # layout warps convert its images first.  Same plan, same sums as the
+    # layout pass + kernel under the same setting.
+    os.environ["CCV_STREAMK"] = "1"
     prec = ccv_abi.CCV_PRECISION_TF32
     x, wr, wi = oracle.make_inputs(case, input_seed=63)
     packed = abi_prepack(case, wr, wi)
