@@ -400,19 +400,27 @@ __global__ void ccv_wgrad_x_planes_kernel(const float2* __restrict__ x, float* _
                                           int Q, int Qa, int sw, int pw) {
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
+  // One warp per input row; a lane writes two adjacent output columns per
+  // pass as one 8-byte store (64 columns per warp pass; Qa is a multiple of
+  // 4, so every pair starts 8-byte aligned).  Columns Q..Qa-1 get zeros
+  // (the weight-gradient kernel's tensor map ends at Q, so they are never
+  // read).
   const int lane = threadIdx.x & 31;
   const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
   for (long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
        row < rows; row += nwarps) {
     const float2* src = x + row * W;
-    for (int s = 0; s < S; ++s) {
-      float* dr = xr + (static_cast<long long>(s) * rows + row) * Qa;
-      float* di = xi + (static_cast<long long>(s) * rows + row) * Qa;
-      for (int q = lane; q < Q; q += 32) {
-        const int w = q * sw - pw + s;
-        const float2 v = (w >= 0 && w < W) ? __ldg(src + w) : make_float2(0.f, 0.f);
-        dr[q] = to_tf32_rna(v.x);
-        di[q] = to_tf32_rna(v.y);
+    for (int q = 2 * lane; q < Qa; q += 64) {
+#pragma unroll 1
+      for (int s = 0; s < S; ++s) {
+        const int w0 = q * sw - pw + s;
+        const int w1 = w0 + sw;
+        const float2 v0 = (q < Q && w0 >= 0 && w0 < W) ? __ldg(src + w0) : make_float2(0.f, 0.f);
+        const float2 v1 =
+            (q + 1 < Q && w1 >= 0 && w1 < W) ? __ldg(src + w1) : make_float2(0.f, 0.f);
+        const long long o = (static_cast<long long>(s) * rows + row) * Qa + q;
+        *reinterpret_cast<float2*>(xr + o) = make_float2(to_tf32_rna(v0.x), to_tf32_rna(v1.x));
+        *reinterpret_cast<float2*>(xi + o) = make_float2(to_tf32_rna(v0.y), to_tf32_rna(v1.y));
       }
     }
   }
