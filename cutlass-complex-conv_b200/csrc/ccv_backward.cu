@@ -106,16 +106,25 @@ __global__ void ccv_dgrad_phase_pad_kernel(const float2* __restrict__ dy, float2
                                            int oh, int ow) {
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
-  const long long total = planes * Hp * Wp;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int j = static_cast<int>(i % Wp);
-    long long t = i / Wp;
-    const int r = static_cast<int>(t % Hp);
-    const long long pl = t / Hp;
-    const int p = r - oh, q = j - ow;
-    out[i] = (p >= 0 && p < P && q >= 0 && q < Q) ? dy[(pl * P + p) * Q + q]
-                                                  : make_float2(0.f, 0.f);
+  // One warp per output row: the row's plane and dy row are derived once,
+  // the lanes copy along the row.
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  const long long rows = planes * Hp;
+  for (long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+       row < rows; row += nwarps) {
+    const long long pl = row / Hp;
+    const int p = static_cast<int>(row - pl * Hp) - oh;
+    float2* dst = out + row * Wp;
+    if (p < 0 || p >= P) {
+      for (int j = lane; j < Wp; j += 32) dst[j] = make_float2(0.f, 0.f);
+      continue;
+    }
+    const float2* src = dy + (pl * P + p) * Q;
+    for (int j = lane; j < Wp; j += 32) {
+      const int q = j - ow;
+      dst[j] = (q >= 0 && q < Q) ? __ldg(src + q) : make_float2(0.f, 0.f);
+    }
   }
 }
 
@@ -133,21 +142,25 @@ __global__ void ccv_dgrad_interleave_kernel(const float2* __restrict__ phases,
                                             const __grid_constant__ DgradPhaseTable tab) {
   ptx::griddep_wait();
   ptx::griddep_launch_dependents();
-  const long long total = planes * H * W;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int w = static_cast<int>(i % W);
-    long long t = i / W;
-    const int h = static_cast<int>(t % H);
-    const long long pl = t / H;
-    const int a = h % sh, b = w % sw;
-    const int ph = a * sw + b;
-    float2 v = make_float2(0.f, 0.f);
-    if (tab.live[ph]) {
-      const int ha = tab.ha[a], wb = tab.wb[b];
-      v = phases[tab.off[ph] + (pl * ha + h / sh) * wb + w / sw];
+  // One warp per dx row: the row's plane and phase row are derived once,
+  // the lanes fill the row column by column.
+  const int lane = threadIdx.x & 31;
+  const long long nwarps = (static_cast<long long>(gridDim.x) * blockDim.x) >> 5;
+  const long long rows = planes * H;
+  for (long long row = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+       row < rows; row += nwarps) {
+    const long long pl = row / H;
+    const int h = static_cast<int>(row - pl * H);
+    const int a = h % sh, hh = h / sh;
+    const long long prow = pl * tab.ha[a] + hh;
+    float2* dst = dx + row * W;
+    for (int w = lane; w < W; w += 32) {
+      const int b = w % sw;
+      const int ph = a * sw + b;
+      float2 v = make_float2(0.f, 0.f);
+      if (tab.live[ph]) v = phases[tab.off[ph] + prow * tab.wb[b] + w / sw];
+      dst[w] = v;
     }
-    dx[i] = v;
   }
 }
 
@@ -189,9 +202,9 @@ int launch_prepack_dgrad(const float* w_real, const float* w_imag, int layout, c
 int launch_dgrad_phase_pad(const void* dy, void* out, const Problem& pb, int hp, int wp, int oh,
                            int ow, cudaStream_t stream) {
   const long long planes = static_cast<long long>(pb.n) * pb.k;
-  const long long total = planes * hp * wp;
+  const long long rows = planes * hp;  // one warp per row
   const int block = 256;
-  const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, 148 * 16));
+  const int grid = static_cast<int>(std::min<long long>((rows * 32 + block - 1) / block, 148 * 16));
   const cudaError_t e =
       launch_kernel(ccv_dgrad_phase_pad_kernel, dim3(grid), dim3(block), 0, stream, 1,
                     static_cast<const float2*>(dy), static_cast<float2*>(out), planes, pb.p, pb.q,
@@ -216,9 +229,9 @@ int launch_dgrad_interleave(const void* phases, void* dx, const Problem& pb, cud
     }
   }
   const long long planes = static_cast<long long>(pb.n) * pb.c;
-  const long long total = planes * pb.h * pb.w;
+  const long long rows = planes * pb.h;  // one warp per row
   const int block = 256;
-  const int grid = static_cast<int>(std::min<long long>((total + block - 1) / block, 148 * 16));
+  const int grid = static_cast<int>(std::min<long long>((rows * 32 + block - 1) / block, 148 * 16));
   const cudaError_t e = launch_kernel(ccv_dgrad_interleave_kernel, dim3(grid), dim3(block), 0,
                                       stream, 1, static_cast<const float2*>(phases),
                                       static_cast<float2*>(dx), planes, pb.h, pb.w, pb.sh, pb.sw,
